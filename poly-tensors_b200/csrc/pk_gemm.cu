@@ -1,0 +1,861 @@
+// Polynomial (block-Toeplitz) matrix product  C_k = sum_{i+j=k} A_i B_j,  k = 0..n.
+//
+// Replaces plain_polynomial_product(matrix=True) (src/polytensors/_plain.py:118-128),
+// which issues (n+1)(n+2)/2 separate GEMMs plus n(n+1)/2 full-size additions.  Here
+// output plane k is one GEMM over a concatenated reduction axis: the k+1 products
+// A_i B_{k-i} are accumulated in the same tensor-memory accumulator, so every output
+// plane is written once and no partial sums ever reach HBM.
+//
+// Paths
+//   float32 / bf16 / f16 : tcgen05.mma kind::f16 (TMEM accumulators, TMA-fed, persistent,
+//                          warp-specialised).  float32 operands are split into bf16
+//                          hi + lo; each product is a_hi b_hi + a_hi b_lo + a_lo b_hi.
+//   float64 / complex128 : mma.sync m16n8k4 f64 (DMMA); a complex product is a sum of
+//                          real products over planar re / im / -im sub-planes.
+#include <algorithm>
+#include <vector>
+
+#include "pk_common.cuh"
+#include "pk_gemm_prep.cuh"
+
+namespace pk {
+
+// =====================================================================================
+// Operand staging (see pk_gemm_prep.cuh)
+
+template <int KIND>
+struct StageTraits;
+template <>
+struct StageTraits<STAGE_SPLIT_BF16> {
+    using T = float;
+    static constexpr int NOUT = 2;
+};
+template <>
+struct StageTraits<STAGE_COPY_16> {
+    using T = uint16_t;
+    static constexpr int NOUT = 1;
+};
+template <>
+struct StageTraits<STAGE_F64> {
+    using T = double;
+    static constexpr int NOUT = 1;
+};
+template <>
+struct StageTraits<STAGE_C128_A> {
+    using T = double2;
+    static constexpr int NOUT = 3;
+};
+template <>
+struct StageTraits<STAGE_C128_B> {
+    using T = double2;
+    static constexpr int NOUT = 2;
+};
+
+template <typename T>
+__device__ __forceinline__ T zero_of() {
+    return T{};
+}
+
+// Grid: x = ceil(Kp/64) k-tiles, y = ceil(rows/32) row tiles, z = batch * planes.
+// Only planes whose kind equals KIND are processed by this instantiation.
+template <int KIND>
+__global__ void __launch_bounds__(256) stage_kernel(const StageParams p) {
+    using T = typename StageTraits<KIND>::T;
+    __shared__ T tile[32][65];
+    const int z = blockIdx.z;
+    const int pi = z % p.planes;
+    const int64_t b = z / p.planes;
+    const StagePlane pl = p.plane[pi];
+    if (pl.kind != KIND) return;
+    const T* src = static_cast<const T*>(pl.src) + b * p.s_b;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32;
+    const int64_t k0 = static_cast<int64_t>(blockIdx.x) * 64;
+    const int t = threadIdx.x;
+
+    if (p.s_k == 1 || p.s_r != 1) {
+        // k is the fast index of the source (or neither is): threads sweep k.
+        const int tx = t & 63, ty = t >> 6;
+        for (int rr = ty; rr < 32; rr += 4) {
+            const int64_t r = r0 + rr, k = k0 + tx;
+            tile[rr][tx] = (r < p.rows && k < p.K) ? src[r * p.s_r + k * p.s_k] : zero_of<T>();
+        }
+    } else {
+        // rows are the fast index of the source: threads sweep rows, then transpose.
+        const int tx = t & 31, ty = t >> 5;
+        for (int kk = ty; kk < 64; kk += 8) {
+            const int64_t r = r0 + tx, k = k0 + kk;
+            tile[tx][kk] = (r < p.rows && k < p.K) ? src[r * p.s_r + k * p.s_k] : zero_of<T>();
+        }
+    }
+    __syncthreads();
+
+    const int lane = t & 31, warp = t >> 5;
+    const int64_t sub0 = b * p.subs_per_batch + pl.dst_sub;
+    for (int rr = warp; rr < 32; rr += 8) {
+        const int64_t r = r0 + rr;
+        const int64_t k = k0 + 2 * lane;
+        if (r >= p.rows || k >= p.Kp) continue;  // Kp is even, so k+1 < Kp as well
+        const T v0 = tile[rr][2 * lane], v1 = tile[rr][2 * lane + 1];
+        if constexpr (KIND == STAGE_SPLIT_BF16) {
+            __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.dst);
+            const __nv_bfloat16 h0 = __float2bfloat16_rn(v0), h1 = __float2bfloat16_rn(v1);
+            const __nv_bfloat16 l0 = __float2bfloat16_rn(v0 - __bfloat162float(h0));
+            const __nv_bfloat16 l1 = __float2bfloat16_rn(v1 - __bfloat162float(h1));
+            const int64_t base_hi = ((sub0 + 0) * p.rows + r) * p.Kp + k;
+            const int64_t base_lo = ((sub0 + 1) * p.rows + r) * p.Kp + k;
+            *reinterpret_cast<__nv_bfloat162*>(dst + base_hi) = __halves2bfloat162(h0, h1);
+            *reinterpret_cast<__nv_bfloat162*>(dst + base_lo) = __halves2bfloat162(l0, l1);
+        } else if constexpr (KIND == STAGE_COPY_16) {
+            uint16_t* dst = static_cast<uint16_t*>(p.dst);
+            const int64_t base = (sub0 * p.rows + r) * p.Kp + k;
+            *reinterpret_cast<uint32_t*>(dst + base) = static_cast<uint32_t>(v0) | (static_cast<uint32_t>(v1) << 16);
+        } else if constexpr (KIND == STAGE_F64) {
+            double* dst = static_cast<double*>(p.dst);
+            const int64_t base = (sub0 * p.rows + r) * p.Kp + k;
+            *reinterpret_cast<double2*>(dst + base) = make_double2(v0, v1);
+        } else {
+            double* dst = static_cast<double*>(p.dst);
+            const int64_t base_re = ((sub0 + 0) * p.rows + r) * p.Kp + k;
+            const int64_t base_im = ((sub0 + 1) * p.rows + r) * p.Kp + k;
+            *reinterpret_cast<double2*>(dst + base_re) = make_double2(v0.x, v1.x);
+            *reinterpret_cast<double2*>(dst + base_im) = make_double2(v0.y, v1.y);
+            if constexpr (KIND == STAGE_C128_A) {
+                const int64_t base_ni = ((sub0 + 2) * p.rows + r) * p.Kp + k;
+                *reinterpret_cast<double2*>(dst + base_ni) = make_double2(-v0.y, -v1.y);
+            }
+        }
+    }
+}
+
+static int launch_stage(const StageParams& p, int64_t batch, bool has_kind[5], cudaStream_t stream) {
+    if (p.rows == 0 || p.Kp == 0 || batch == 0) return PK_OK;
+    const int64_t gx = ceil_div(p.Kp, 64), gy = ceil_div(p.rows, 32), gz = batch * p.planes;
+    if (gy > 65535 || gz > 65535) return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: operand too large to stage");
+    dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy), static_cast<unsigned>(gz));
+    if (has_kind[STAGE_SPLIT_BF16]) stage_kernel<STAGE_SPLIT_BF16><<<grid, 256, 0, stream>>>(p);
+    if (has_kind[STAGE_COPY_16]) stage_kernel<STAGE_COPY_16><<<grid, 256, 0, stream>>>(p);
+    if (has_kind[STAGE_F64]) stage_kernel<STAGE_F64><<<grid, 256, 0, stream>>>(p);
+    if (has_kind[STAGE_C128_A]) stage_kernel<STAGE_C128_A><<<grid, 256, 0, stream>>>(p);
+    if (has_kind[STAGE_C128_B]) stage_kernel<STAGE_C128_B><<<grid, 256, 0, stream>>>(p);
+    PK_CHECK_LAUNCH("pk_poly_gemm: stage kernel launch");
+    return PK_OK;
+}
+
+// =====================================================================================
+// tcgen05 path
+
+constexpr int TC_BM = 128;
+constexpr int TC_BK = 64;  // 64 bf16 = one 128-byte swizzle row
+constexpr int TC_THREADS = 192;  // warp 0: TMA, warp 1: MMA + TMEM owner, warps 2-5: epilogue
+
+struct TcParams {
+    int planes, batch;
+    int M, N;
+    int kblocks;
+    int tiles_m, tiles_n, group_m;
+    int total_tiles;
+    int out_kind;  // 0 = f32, 1 = bf16, 2 = f16
+    int vec_ok;    // output rows 16-byte aligned: vectorised stores allowed
+    int64_t c_bs, c_rs;
+    void* c[PK_MAX_PLANES];
+    int* status;
+};
+
+struct TileCoord {
+    int plane, b, tm, tn;
+};
+
+// Tiles are ordered heaviest first (output plane n has n+1 products), then by batch,
+// then in groups of `group_m` row tiles so that CTAs running concurrently share
+// operand tiles in L2.
+__device__ __forceinline__ TileCoord decode_tile(const TcParams& p, int t) {
+    TileCoord c;
+    const int per_b = p.tiles_m * p.tiles_n;
+    const int per_plane = p.batch * per_b;
+    c.plane = p.planes - 1 - t / per_plane;
+    int r = t % per_plane;
+    c.b = r / per_b;
+    r %= per_b;
+    const int span = p.group_m * p.tiles_n;
+    const int first_m = (r / span) * p.group_m;
+    const int gsize = min(p.tiles_m - first_m, p.group_m);
+    c.tm = first_m + (r % span) % gsize;
+    c.tn = (r % span) / gsize;
+    return c;
+}
+
+template <int BN, bool SPLIT>
+struct TcConfig {
+    static constexpr int NSUB = SPLIT ? 2 : 1;
+    static constexpr int A_BYTES = TC_BM * TC_BK * 2;
+    static constexpr int B_BYTES = BN * TC_BK * 2;
+    static constexpr int STAGE_BYTES = NSUB * (A_BYTES + B_BYTES);
+    static constexpr int STAGES = (196 * 1024) / STAGE_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+    static_assert(STAGES >= 2, "need at least two pipeline stages");
+    static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+};
+
+__device__ __forceinline__ void store_row_chunk(const TcParams& p, int plane, int b, int row, int col0,
+                                                const uint32_t (&r)[32]) {
+    if (row >= p.M) return;
+    const int64_t off = static_cast<int64_t>(b) * p.c_bs + static_cast<int64_t>(row) * p.c_rs + col0;
+    const bool full = (col0 + 32 <= p.N) && p.vec_ok;
+    if (p.out_kind == 0) {
+        float* dst = static_cast<float*>(p.c[plane]) + off;
+        if (full) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                                  __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+        } else {
+            for (int j = 0; j < 32 && col0 + j < p.N; ++j) dst[j] = __uint_as_float(r[j]);
+        }
+    } else {
+        uint16_t* dst = static_cast<uint16_t*>(p.c[plane]) + off;
+        uint32_t packed[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const float x0 = __uint_as_float(r[2 * j]), x1 = __uint_as_float(r[2 * j + 1]);
+            uint16_t h0, h1;
+            if (p.out_kind == 1) {
+                h0 = __bfloat16_as_ushort(__float2bfloat16_rn(x0));
+                h1 = __bfloat16_as_ushort(__float2bfloat16_rn(x1));
+            } else {
+                h0 = __half_as_ushort(__float2half_rn(x0));
+                h1 = __half_as_ushort(__float2half_rn(x1));
+            }
+            packed[j] = static_cast<uint32_t>(h0) | (static_cast<uint32_t>(h1) << 16);
+        }
+        if (full) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+                *reinterpret_cast<uint4*>(dst + 2 * j) = make_uint4(packed[j], packed[j + 1], packed[j + 2], packed[j + 3]);
+        } else {
+            for (int j = 0; j < 32 && col0 + j < p.N; ++j)
+                dst[j] = static_cast<uint16_t>((packed[j / 2] >> (16 * (j & 1))) & 0xFFFFu);
+        }
+    }
+}
+
+template <int BN, bool SPLIT>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_poly_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        const TcParams p) {
+    using Cfg = TcConfig<BN, SPLIT>;
+    constexpr int STAGES = Cfg::STAGES;
+    constexpr int NSUB = Cfg::NSUB;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+    uint64_t* empty_bar = full_bar + STAGES;
+    uint64_t* acc_full = empty_bar + STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* drain_bar = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&acc_full[s], 1);
+            mbar_init(&acc_empty[s], 128);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&map_a);
+        tma_prefetch_desc(&map_b);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0;
+            int issued_parity[STAGES];
+#pragma unroll
+            for (int s = 0; s < STAGES; ++s) issued_parity[s] = -1;
+            bool ok = true;
+            for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+                const TileCoord tc = decode_tile(p, t);
+                for (int i = 0; i <= tc.plane && ok; ++i) {
+                    const int j = tc.plane - i;
+                    const int za = (tc.b * p.planes + i) * NSUB;
+                    const int zb = (tc.b * p.planes + j) * NSUB;
+                    for (int kb = 0; kb < p.kblocks; ++kb) {
+                        if (!mbar_wait_or_abort(&empty_bar[stage], phase ^ 1, abort_flag, p.status, 101)) {
+                            ok = false;
+                            break;
+                        }
+                        uint8_t* st = smem + stage * Cfg::STAGE_BYTES;
+                        mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+#pragma unroll
+                        for (int h = 0; h < NSUB; ++h)
+                            tma_load_3d(st + h * Cfg::A_BYTES, &map_a, &full_bar[stage], kb * TC_BK, tc.tm * TC_BM, za + h);
+#pragma unroll
+                        for (int h = 0; h < NSUB; ++h)
+                            tma_load_3d(st + NSUB * Cfg::A_BYTES + h * Cfg::B_BYTES, &map_b, &full_bar[stage], kb * TC_BK,
+                                        tc.tn * BN, zb + h);
+                        issued_parity[stage] = static_cast<int>(phase);
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                }
+            }
+            if (!ok) {
+                // Let copies already in flight land before the CTA (and its shared memory) exits:
+                // the last load issued into stage s completes phase issued_parity[s] of full_bar[s].
+                for (int s = 0; s < STAGES; ++s) {
+                    if (issued_parity[s] < 0) continue;
+                    const uint64_t t0 = pk_globaltimer();
+                    while (!mbar_try_wait(&full_bar[s], static_cast<uint32_t>(issued_parity[s])) &&
+                           pk_globaltimer() - t0 < 1000000000ull) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = f16_idesc(1u, TC_BM, BN);
+            uint32_t stage = 0, phase = 0;
+            uint32_t abuf = 0, aphase = 0;
+            bool ok = true;
+            bool issued = false;
+            for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+                const TileCoord tc = decode_tile(p, t);
+                if (!mbar_wait_or_abort(&acc_empty[abuf], aphase ^ 1, abort_flag, p.status, 102)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + abuf * BN;
+                const int iters = (tc.plane + 1) * p.kblocks;
+                for (int it = 0; it < iters; ++it) {
+                    if (!mbar_wait_or_abort(&full_bar[stage], phase, abort_flag, p.status, 103)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t st = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+                    const uint32_t a_hi = st, a_lo = st + Cfg::A_BYTES;
+                    const uint32_t b_hi = st + NSUB * Cfg::A_BYTES, b_lo = b_hi + Cfg::B_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < TC_BK / 16; ++kk) {
+                        const uint32_t koff = kk * 32;  // 16 bf16 = 32 bytes along the swizzled row
+                        tc_mma_f16(d_tmem, sw128_kmajor_desc(a_hi + koff), sw128_kmajor_desc(b_hi + koff), idesc,
+                                   (it > 0 || kk > 0) ? 1u : 0u);
+                        if constexpr (SPLIT) {
+                            tc_mma_f16(d_tmem, sw128_kmajor_desc(a_hi + koff), sw128_kmajor_desc(b_lo + koff), idesc, 1u);
+                            tc_mma_f16(d_tmem, sw128_kmajor_desc(a_lo + koff), sw128_kmajor_desc(b_hi + koff), idesc, 1u);
+                        }
+                    }
+                    issued = true;
+                    tc_commit(&empty_bar[stage]);  // frees this smem stage once the MMAs above retire
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&acc_full[abuf]);  // accumulator ready for the epilogue
+                if (++abuf == 2) {
+                    abuf = 0;
+                    aphase ^= 1;
+                }
+            }
+            if (!ok && issued) {
+                // Drain: wait (bounded) until every MMA issued so far has retired, so that none
+                // still writes TMEM or reads shared memory when the CTA releases them.
+                tc_commit(drain_bar);
+                const uint64_t t0 = pk_globaltimer();
+                while (!mbar_try_wait(drain_bar, 0) && pk_globaltimer() - t0 < 1000000000ull) {
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue: TMEM -> registers -> global ----------------
+        const uint32_t lane_base = 32u * (warp & 3);
+        uint32_t abuf = 0, aphase = 0;
+        for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+            const TileCoord tc = decode_tile(p, t);
+            if (!mbar_wait_or_abort(&acc_full[abuf], aphase, abort_flag, p.status, 104)) break;
+            tc_fence_after();
+            const int row = tc.tm * TC_BM + lane_base + lane;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_base + (lane_base << 16) + abuf * BN + c * 32, r);
+                tmem_ld_wait();
+                store_row_chunk(p, tc.plane, tc.b, row, tc.tn * BN + c * 32, r);
+            }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[abuf]);
+            if (++abuf == 2) {
+                abuf = 0;
+                aphase ^= 1;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    }
+}
+
+static int encode_operand_map(CUtensorMap* map, void* base, int64_t rows, int64_t Kp, int64_t depth, int box_rows) {
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(Kp), static_cast<cuuint64_t>(rows),
+                                static_cast<cuuint64_t>(depth)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(Kp * 2), static_cast<cuuint64_t>(rows * Kp * 2)};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(TC_BK), static_cast<cuuint32_t>(box_rows), 1u};
+    CUresult r = encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+    if (r != CUDA_SUCCESS) return fail(PK_ERR_CUDA, "pk_poly_gemm: cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+    return PK_OK;
+}
+
+template <int BN, bool SPLIT>
+static int launch_tc(TcParams& p, void* ws_a, void* ws_b, int64_t Kp, cudaStream_t stream) {
+    using Cfg = TcConfig<BN, SPLIT>;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(tc_poly_gemm_kernel<BN, SPLIT>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_fail(e, "pk_poly_gemm: cudaFuncSetAttribute");
+        attr_set[dev] = true;
+    }
+    const int64_t depth = static_cast<int64_t>(p.batch) * p.planes * Cfg::NSUB;
+    CUtensorMap map_a, map_b;
+    int rc = encode_operand_map(&map_a, ws_a, p.M, Kp, depth, TC_BM);
+    if (rc) return rc;
+    rc = encode_operand_map(&map_b, ws_b, p.N, Kp, depth, BN);
+    if (rc) return rc;
+    p.tiles_m = static_cast<int>(ceil_div(p.M, TC_BM));
+    p.tiles_n = static_cast<int>(ceil_div(p.N, BN));
+    p.group_m = 8;
+    const int64_t total = static_cast<int64_t>(p.tiles_m) * p.tiles_n * p.batch * p.planes;
+    if (total > 0x7fffffff) return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: too many tiles");
+    p.total_tiles = static_cast<int>(total);
+    const int grid = static_cast<int>(std::min<int64_t>(total, num_sms()));
+    void* tok;
+    prof_begin("poly_gemm", stream, &tok);
+    tc_poly_gemm_kernel<BN, SPLIT><<<grid, TC_THREADS, Cfg::SMEM_BYTES, stream>>>(map_a, map_b, p);
+    prof_end("poly_gemm", stream, tok);
+    PK_CHECK_LAUNCH("pk_poly_gemm: tcgen05 kernel launch");
+    return PK_OK;
+}
+
+// =====================================================================================
+// DMMA path (float64, complex128)
+
+constexpr int DM_BM = 128, DM_BN = 128, DM_BK = 16, DM_LD = 20, DM_STAGES = 3;
+constexpr int DM_THREADS = 256;
+constexpr int DM_MAX_OUT = 2 * PK_MAX_PLANES;
+constexpr int DM_MAX_SEG = 2 * PK_MAX_PLANES * (PK_MAX_PLANES + 1);
+
+struct DmOut {
+    double* ptr;   // plane base (as doubles)
+    int mult;      // 1 for a float64 plane, 2 for an interleaved complex128 plane
+    int part;      // 0 = real part / real plane, 1 = imaginary part
+    int seg_begin, seg_end;
+};
+
+struct DmParams {
+    int M, N;
+    int batch;
+    int64_t Kp;
+    int kblocks;
+    int n_out;
+    int64_t a_subs, b_subs;  // sub-planes per batch entry
+    const double* ws_a;
+    const double* ws_b;
+    int64_t c_bs, c_rs;
+    DmOut out[DM_MAX_OUT];
+    uint8_t seg_a[DM_MAX_SEG];
+    uint8_t seg_b[DM_MAX_SEG];
+    int order[DM_MAX_OUT];  // output sub-planes, heaviest first
+};
+
+__device__ __forceinline__ void cp_async_16(void* smem, const void* gmem, bool valid) {
+    const int n = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void dmma_16x8x4(double (&d)[4], double a0, double a1, double b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k4.row.col.f64.f64.f64.f64 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
+        : "+d"(d[0]), "+d"(d[1]), "+d"(d[2]), "+d"(d[3])
+        : "d"(a0), "d"(a1), "d"(b0));
+}
+
+// Grid: x = N tiles, y = M tiles, z = batch * n_out (heaviest output sub-planes first).
+__global__ void __launch_bounds__(DM_THREADS, 1) dmma_poly_gemm_kernel(const DmParams p) {
+    extern __shared__ __align__(16) double dsm[];
+    double* sA = dsm;                                 // [STAGES][BM][LD]
+    double* sB = dsm + DM_STAGES * DM_BM * DM_LD;     // [STAGES][BN][LD]
+
+    const int zo = blockIdx.z / p.batch;  // z = (output rank) * batch + b: heaviest outputs launch first
+    const int64_t b = blockIdx.z % p.batch;
+    const DmOut out = p.out[p.order[zo]];
+    const int m0 = blockIdx.y * DM_BM, n0 = blockIdx.x * DM_BN;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int wm = warp >> 2, wn = warp & 3;  // 2 x 4 warps, 64 x 32 each
+    const int g = lane >> 2, tg = lane & 3;
+
+    double acc[4][4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.0;
+
+    const int nseg = out.seg_end - out.seg_begin;
+    const int total = nseg * p.kblocks;
+
+    auto load_stage = [&](int it, int st) {
+        const int s = out.seg_begin + it / p.kblocks;
+        const int kb = it % p.kblocks;
+        const double* ga = p.ws_a + ((b * p.a_subs + p.seg_a[s]) * p.M) * p.Kp + static_cast<int64_t>(kb) * DM_BK;
+        const double* gb = p.ws_b + ((b * p.b_subs + p.seg_b[s]) * p.N) * p.Kp + static_cast<int64_t>(kb) * DM_BK;
+        double* da = sA + st * DM_BM * DM_LD;
+        double* db = sB + st * DM_BN * DM_LD;
+#pragma unroll
+        for (int c = tid; c < DM_BM * DM_BK / 2; c += DM_THREADS) {
+            const int r = c >> 3, kc = (c & 7) * 2;
+            const bool va = (m0 + r) < p.M;
+            cp_async_16(da + r * DM_LD + kc, va ? ga + static_cast<int64_t>(m0 + r) * p.Kp + kc : p.ws_a, va);
+            const bool vb = (n0 + r) < p.N;
+            cp_async_16(db + r * DM_LD + kc, vb ? gb + static_cast<int64_t>(n0 + r) * p.Kp + kc : p.ws_b, vb);
+        }
+    };
+
+#pragma unroll
+    for (int s = 0; s < DM_STAGES - 1; ++s) {
+        if (s < total) load_stage(s, s);
+        cp_async_commit();
+    }
+    for (int it = 0; it < total; ++it) {
+        cp_async_wait<DM_STAGES - 2>();
+        __syncthreads();
+        const int nxt = it + DM_STAGES - 1;
+        if (nxt < total) load_stage(nxt, nxt % DM_STAGES);
+        cp_async_commit();
+        const double* a = sA + (it % DM_STAGES) * DM_BM * DM_LD + (wm * 64) * DM_LD;
+        const double* bb = sB + (it % DM_STAGES) * DM_BN * DM_LD + (wn * 32) * DM_LD;
+#pragma unroll
+        for (int kk = 0; kk < DM_BK; kk += 4) {
+            double af[4][2], bf[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                af[i][0] = a[(i * 16 + g) * DM_LD + kk + tg];
+                af[i][1] = a[(i * 16 + g + 8) * DM_LD + kk + tg];
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) bf[j] = bb[(j * 8 + g) * DM_LD + kk + tg];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) dmma_16x8x4(acc[i][j], af[i][0], af[i][1], bf[j]);
+        }
+    }
+    cp_async_wait<0>();
+
+    // Epilogue: rows g / g+8, columns 2*tg, 2*tg+1 of each 16 x 8 fragment.
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int row = m0 + wm * 64 + i * 16 + g + ((e >> 1) ? 8 : 0);
+                const int col = n0 + wn * 32 + j * 8 + tg * 2 + (e & 1);
+                if (row < p.M && col < p.N) {
+                    const int64_t idx = b * p.c_bs + static_cast<int64_t>(row) * p.c_rs + col;
+                    out.ptr[idx * out.mult + out.part] = acc[i][j][e];
+                }
+            }
+        }
+    }
+}
+
+// Zero-fill output planes for K == 0 (an empty sum).
+__global__ void zero_planes_kernel(void* const* planes_dev_unused, char* base, int64_t rows, int64_t cols,
+                                   int64_t rs, int64_t bs, int64_t batch, int elem_bytes) {
+    const int64_t total = batch * rows * cols;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t b = i / (rows * cols), r = (i / cols) % rows, c = i % cols;
+        char* dst = base + (b * bs + r * rs + c) * elem_bytes;
+        for (int e = 0; e < elem_bytes; ++e) dst[e] = 0;
+    }
+}
+
+static int elem_size(int dtype) {
+    switch (dtype) {
+        case PK_F32: return 4;
+        case PK_F64: return 8;
+        case PK_BF16:
+        case PK_F16: return 2;
+        case PK_C128: return 16;
+    }
+    return 0;
+}
+
+struct GemmPlan {
+    int64_t Kp = 0;
+    int64_t a_subs = 0, b_subs = 0;  // per batch entry
+    size_t a_bytes = 0, b_bytes = 0, total = 0;
+    std::vector<int> a_first, b_first;  // first sub-plane of each plane
+};
+
+static GemmPlan plan_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K, int acf, int bcf) {
+    GemmPlan g;
+    const int P = degree + 1;
+    g.a_first.resize(P);
+    g.b_first.resize(P);
+    int64_t esz;
+    if (dtype == PK_F32 || dtype == PK_BF16 || dtype == PK_F16) {
+        g.Kp = round_up(std::max<int64_t>(K, 1), 8);
+        const int ns = dtype == PK_F32 ? 2 : 1;
+        for (int p = 0; p < P; ++p) {
+            g.a_first[p] = p * ns;
+            g.b_first[p] = p * ns;
+        }
+        g.a_subs = g.b_subs = static_cast<int64_t>(P) * ns;
+        esz = 2;
+    } else {
+        g.Kp = round_up(std::max<int64_t>(K, 1), 16);
+        for (int p = 0; p < P; ++p) {
+            const bool ca = dtype == PK_C128 && p >= acf, cb = dtype == PK_C128 && p >= bcf;
+            g.a_first[p] = static_cast<int>(g.a_subs);
+            g.a_subs += ca ? 3 : 1;
+            g.b_first[p] = static_cast<int>(g.b_subs);
+            g.b_subs += cb ? 2 : 1;
+        }
+        esz = 8;
+    }
+    g.a_bytes = static_cast<size_t>(round_up(batch * g.a_subs * M * g.Kp * esz, 1024));
+    g.b_bytes = static_cast<size_t>(round_up(batch * g.b_subs * N * g.Kp * esz, 1024));
+    g.total = g.a_bytes + g.b_bytes + 1024;  // +1024: alignment slack for the caller's pointer
+    return g;
+}
+
+}  // namespace pk
+
+using namespace pk;
+
+extern "C" {
+
+size_t pk_poly_gemm_workspace_size(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K,
+                                   int a_complex_from, int b_complex_from) {
+    if (degree < 0 || degree >= PK_MAX_PLANES || batch < 0 || M < 0 || N < 0 || K < 0) return 0;
+    if (elem_size(dtype) == 0) return 0;
+    return plan_gemm(dtype, degree, batch, M, N, K, a_complex_from, b_complex_from).total;
+}
+
+int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K, const void* const* a_planes,
+                 int64_t a_bs, int64_t a_rs, int64_t a_cs, const void* const* b_planes, int64_t b_bs, int64_t b_rs,
+                 int64_t b_cs, void* const* c_planes, int64_t c_bs, int64_t c_rs, int a_complex_from,
+                 int b_complex_from, void* workspace, size_t workspace_bytes, void* stream_ptr) {
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    if (degree < 0 || degree >= PK_MAX_PLANES)
+        return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: degree must be in [0, " + std::to_string(PK_MAX_PLANES - 1) + "]");
+    if (batch < 0 || M < 0 || N < 0 || K < 0) return fail(PK_ERR_ARG, "pk_poly_gemm: negative size");
+    const int esz = elem_size(dtype);
+    if (esz == 0) return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: unknown dtype " + std::to_string(dtype));
+    if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff)
+        return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: dimension exceeds 2^31-1");
+    const int P = degree + 1;
+    if (!a_planes || !b_planes || !c_planes) return fail(PK_ERR_ARG, "pk_poly_gemm: null plane array");
+    for (int p = 0; p < P; ++p)
+        if (!a_planes[p] || !b_planes[p] || !c_planes[p]) return fail(PK_ERR_ARG, "pk_poly_gemm: null plane pointer");
+    if (dtype != PK_C128) {
+        a_complex_from = P;
+        b_complex_from = P;
+    } else {
+        a_complex_from = std::max(0, std::min(a_complex_from, P));
+        b_complex_from = std::max(0, std::min(b_complex_from, P));
+    }
+    if (batch == 0 || M == 0 || N == 0) return PK_OK;
+
+    if (K == 0) {
+        for (int p = 0; p < P; ++p) {
+            const bool cplx = dtype == PK_C128 && (p >= a_complex_from || p >= b_complex_from);
+            const int e = dtype == PK_C128 ? (cplx ? 16 : 8) : esz;
+            zero_planes_kernel<<<592, 256, 0, stream>>>(nullptr, static_cast<char*>(c_planes[p]), M, N, c_rs, c_bs,
+                                                        batch, e);
+        }
+        PK_CHECK_LAUNCH("pk_poly_gemm: zero fill");
+        return PK_OK;
+    }
+
+    const GemmPlan g = plan_gemm(dtype, degree, batch, M, N, K, a_complex_from, b_complex_from);
+    if (!workspace || workspace_bytes < g.total)
+        return fail(PK_ERR_WORKSPACE, "pk_poly_gemm: workspace of " + std::to_string(g.total) + " bytes required");
+    char* ws = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(workspace) + 1023) & ~uintptr_t(1023));
+    void* ws_a = ws;
+    void* ws_b = ws + g.a_bytes;
+
+    // ---- stage operands into K-major sub-planes
+    StageParams sa{}, sb{};
+    bool kinds_a[5] = {false, false, false, false, false}, kinds_b[5] = {false, false, false, false, false};
+    for (int p = 0; p < P; ++p) {
+        int ka, kb;
+        if (dtype == PK_F32) ka = kb = STAGE_SPLIT_BF16;
+        else if (dtype == PK_BF16 || dtype == PK_F16) ka = kb = STAGE_COPY_16;
+        else {
+            ka = (dtype == PK_C128 && p >= a_complex_from) ? STAGE_C128_A : STAGE_F64;
+            kb = (dtype == PK_C128 && p >= b_complex_from) ? STAGE_C128_B : STAGE_F64;
+        }
+        sa.plane[p] = {a_planes[p], g.a_first[p], ka};
+        sb.plane[p] = {b_planes[p], g.b_first[p], kb};
+        kinds_a[ka] = true;
+        kinds_b[kb] = true;
+    }
+    sa.planes = sb.planes = P;
+    sa.rows = M; sa.K = K; sa.Kp = g.Kp; sa.s_b = a_bs; sa.s_r = a_rs; sa.s_k = a_cs;
+    sa.subs_per_batch = g.a_subs; sa.dst = ws_a;
+    sb.rows = N; sb.K = K; sb.Kp = g.Kp; sb.s_b = b_bs; sb.s_r = b_cs; sb.s_k = b_rs;
+    sb.subs_per_batch = g.b_subs; sb.dst = ws_b;
+    sa.elem_bytes = sb.elem_bytes = (dtype == PK_F64 || dtype == PK_C128) ? 8 : 2;
+    int rc = launch_stage(sa, batch, kinds_a, stream);
+    if (rc) return rc;
+    rc = launch_stage(sb, batch, kinds_b, stream);
+    if (rc) return rc;
+
+    if (dtype == PK_F32 || dtype == PK_BF16 || dtype == PK_F16) {
+        if (batch * P * 2 > 0x7fffffff) return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: batch too large");
+        TcParams tp{};
+        tp.planes = P;
+        tp.batch = static_cast<int>(batch);
+        tp.M = static_cast<int>(M);
+        tp.N = static_cast<int>(N);
+        tp.kblocks = static_cast<int>(ceil_div(g.Kp, TC_BK));
+        tp.out_kind = dtype == PK_F32 ? 0 : (dtype == PK_BF16 ? 1 : 2);
+        tp.c_bs = c_bs;
+        tp.c_rs = c_rs;
+        const int align_elems = 16 / esz;
+        bool vec = (c_rs % align_elems == 0) && (c_bs % align_elems == 0);
+        for (int p = 0; p < P; ++p) {
+            tp.c[p] = c_planes[p];
+            if (reinterpret_cast<uintptr_t>(c_planes[p]) % 16 != 0) vec = false;
+        }
+        tp.vec_ok = vec ? 1 : 0;
+        tp.status = device_status_ptr();
+        const int64_t tiles256 = ceil_div(M, TC_BM) * ceil_div(N, 256) * batch * P;
+        const bool wide = tiles256 >= 2 * num_sms();
+        if (dtype == PK_F32) {
+            return wide ? launch_tc<256, true>(tp, ws_a, ws_b, g.Kp, stream)
+                        : launch_tc<128, true>(tp, ws_a, ws_b, g.Kp, stream);
+        }
+        if (dtype == PK_F16) {
+            return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: float16 planes are not implemented yet");
+        }
+        return wide ? launch_tc<256, false>(tp, ws_a, ws_b, g.Kp, stream)
+                    : launch_tc<128, false>(tp, ws_a, ws_b, g.Kp, stream);
+    }
+
+    // ---- DMMA path: build the per-output segment lists
+    DmParams dp{};
+    dp.M = static_cast<int>(M);
+    dp.N = static_cast<int>(N);
+    dp.batch = static_cast<int>(batch);
+    dp.Kp = g.Kp;
+    dp.kblocks = static_cast<int>(g.Kp / DM_BK);
+    dp.a_subs = g.a_subs;
+    dp.b_subs = g.b_subs;
+    dp.ws_a = static_cast<const double*>(ws_a);
+    dp.ws_b = static_cast<const double*>(ws_b);
+    dp.c_bs = c_bs;
+    dp.c_rs = c_rs;
+    int nseg = 0, nout = 0;
+    for (int k = 0; k < P; ++k) {
+        const bool out_complex = dtype == PK_C128 && (k >= a_complex_from || k >= b_complex_from);
+        for (int part = 0; part < (out_complex ? 2 : 1); ++part) {
+            DmOut& o = dp.out[nout];
+            o.ptr = static_cast<double*>(c_planes[k]);
+            o.mult = out_complex ? 2 : 1;
+            o.part = part;
+            o.seg_begin = nseg;
+            for (int i = 0; i <= k; ++i) {
+                const int j = k - i;
+                const bool ca = dtype == PK_C128 && i >= a_complex_from;
+                const bool cb = dtype == PK_C128 && j >= b_complex_from;
+                const int ar = g.a_first[i], ai = ar + 1, ani = ar + 2;
+                const int br = g.b_first[j], bi = br + 1;
+                auto add = [&](int sa_, int sb_) {
+                    dp.seg_a[nseg] = static_cast<uint8_t>(sa_);
+                    dp.seg_b[nseg] = static_cast<uint8_t>(sb_);
+                    ++nseg;
+                };
+                if (part == 0) {  // real part: re*re - im*im
+                    add(ar, br);
+                    if (ca && cb) add(ani, bi);
+                } else {  // imaginary part: re*im + im*re
+                    if (cb) add(ar, bi);
+                    if (ca) add(ai, br);
+                }
+            }
+            o.seg_end = nseg;
+            ++nout;
+        }
+    }
+    dp.n_out = nout;
+    std::vector<int> order(nout);
+    for (int i = 0; i < nout; ++i) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](int x, int y) {
+        return (dp.out[x].seg_end - dp.out[x].seg_begin) > (dp.out[y].seg_end - dp.out[y].seg_begin);
+    });
+    for (int i = 0; i < nout; ++i) dp.order[i] = order[i];
+    const int smem = DM_STAGES * (DM_BM + DM_BN) * DM_LD * static_cast<int>(sizeof(double));
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(dmma_poly_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return cuda_fail(e, "pk_poly_gemm: cudaFuncSetAttribute (dmma)");
+        attr_set[dev] = true;
+    }
+    const int64_t gz = batch * nout;
+    if (gz > 65535 || ceil_div(M, DM_BM) > 65535) return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: grid too large");
+    dim3 grid(static_cast<unsigned>(ceil_div(N, DM_BN)), static_cast<unsigned>(ceil_div(M, DM_BM)),
+              static_cast<unsigned>(gz));
+    void* tok;
+    prof_begin("poly_gemm", stream, &tok);
+    dmma_poly_gemm_kernel<<<grid, DM_THREADS, smem, stream>>>(dp);
+    prof_end("poly_gemm", stream, tok);
+    PK_CHECK_LAUNCH("pk_poly_gemm: dmma kernel launch");
+    return PK_OK;
+}
+
+}  // extern "C"

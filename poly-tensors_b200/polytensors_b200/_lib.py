@@ -1,0 +1,81 @@
+"""ctypes binding of libpolykern.so (the C ABI declared in include/polykern.h).
+
+The library is loaded lazily on first use.  There is no fallback: if the shared
+library is missing or CUDA is unavailable, every kernel entry point raises.
+"""
+
+import ctypes
+import pathlib
+import threading
+
+LIB_PATH = pathlib.Path(__file__).resolve().parent / "lib" / "libpolykern.so"
+
+# enum pk_dtype
+PK_F32, PK_F64, PK_BF16, PK_F16, PK_C128 = 0, 1, 2, 3, 4
+PK_MAX_PLANES = 16
+
+_i32, _i64, _sz, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p
+_pp = ctypes.POINTER(ctypes.c_void_p)
+
+# name -> (restype, argtypes); every symbol declared in include/polykern.h
+SIGNATURES = {
+    "pk_version": (ctypes.c_char_p, []),
+    "pk_last_error": (ctypes.c_char_p, []),
+    "pk_device_status": (_i32, [_i32]),
+    "pk_profile_enable": (_i32, [_i32]),
+    "pk_profile_query": (_i32, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
+    "pk_poly_gemm_workspace_size": (_sz, [_i32, _i32, _i64, _i64, _i64, _i64, _i32, _i32]),
+    "pk_poly_gemm": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64,
+                            _pp, _i64, _i64, _i64,
+                            _pp, _i64, _i64, _i64,
+                            _pp, _i64, _i64,
+                            _i32, _i32, _vp, _sz, _vp]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load():
+    """Load libpolykern.so and bind every exported entry point (raises if unavailable)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(f"{LIB_PATH} is not built; run polytensors_b200._build.build() "
+                                   "(this package has no CPU fallback)")
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (restype, argtypes) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = restype
+                fn.argtypes = argtypes
+            _lib = lib
+    return _lib
+
+
+def last_error():
+    return load().pk_last_error().decode(errors="replace")
+
+
+def check(status, what):
+    """Raise RuntimeError carrying pk_last_error() for a nonzero status."""
+    if status != 0:
+        raise RuntimeError(f"{what} failed ({status}): {last_error()}")
+
+
+def profile_enable(on=True):
+    load().pk_profile_enable(1 if on else 0)
+
+
+def profile_query(kernel):
+    """(total milliseconds, launches) of the event-timed launches of ``kernel`` since the last query."""
+    ms, n = ctypes.c_double(), ctypes.c_int64()
+    check(load().pk_profile_query(kernel.encode(), ctypes.byref(ms), ctypes.byref(n)), "pk_profile_query")
+    return ms.value, n.value
+
+
+def pointer_array(tensors):
+    arr = (ctypes.c_void_p * len(tensors))(*[t.data_ptr() for t in tensors])
+    return ctypes.cast(arr, _pp), arr

@@ -1,0 +1,121 @@
+"""Parity of the polynomial matrix product (pk_poly_gemm) with the CPU oracle.
+
+Tolerances (per coefficient plane, max |got - want| / max |want|): float32 1e-4,
+float64 / complex128 1e-10, bfloat16 storage 2e-2."""
+
+import math
+
+import pytest
+import torch
+
+from oracle import polyref as ref
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: 1e-4, torch.float64: 1e-10, torch.complex128: 1e-10, torch.bfloat16: 2e-2}
+
+
+def series(shape, n, seed, dtype=torch.float32, complex_from=None):
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for k in range(n + 1):
+        x = torch.randn(*shape, generator=g, dtype=torch.float64) / math.factorial(k)
+        if complex_from is not None and k >= complex_from:
+            x = torch.complex(x, torch.randn(*shape, generator=g, dtype=torch.float64) / math.factorial(k))
+        out.append(x if x.is_complex() else x.to(dtype))
+    return out
+
+
+def cuda(planes):
+    return [p.cuda() for p in planes]
+
+
+def check(A, B, tol, got=None):
+    from polytensors_b200 import _kernels
+
+    got = _kernels.poly_matmul(cuda(A), cuda(B)) if got is None else got
+    want = ref.poly_matmul([a.double() if not a.is_complex() else a for a in A],
+                           [b.double() if not b.is_complex() else b for b in B])
+    for g, w in zip(got, want):
+        assert g.shape == w.shape
+    errs = ref.plane_errors(got, want)
+    assert max(errs) <= tol, errs
+    return errs
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_f32_square_1024(n):
+    A, B = series((1024, 1024), n, 1), series((1024, 1024), n, 2)
+    check(A, B, TOL[torch.float32])
+
+
+@pytest.mark.parametrize("M,N,K,n", [(257, 129, 200, 3), (1, 300, 77, 2), (130, 1, 64, 1), (64, 96, 8, 0),
+                                     (333, 517, 1031, 2)])
+def test_f32_ragged(M, N, K, n):
+    A, B = series((M, K), n, 3), series((K, N), n, 4)
+    check(A, B, TOL[torch.float32])
+
+
+def test_f32_transposed_and_batched():
+    from polytensors_b200 import _kernels
+
+    A = series((3, 100, 70), 2, 5)
+    W = series((3, 90, 70), 2, 6)                     # B = W^T: a non-contiguous operand
+    Bt = [w.transpose(-2, -1) for w in W]
+    got = _kernels.poly_matmul(cuda(A), [w.cuda().transpose(-2, -1) for w in W])
+    check(A, Bt, TOL[torch.float32], got=got)
+
+
+def test_f32_large_wide_tiles():
+    A, B = series((2048, 4096), 2, 7), series((4096, 3072), 2, 8)
+    check(A, B, TOL[torch.float32])
+
+
+@pytest.mark.parametrize("M,N,K,n", [(256, 320, 192, 3), (129, 65, 33, 2), (1, 1, 1, 4)])
+def test_f64(M, N, K, n):
+    A, B = series((M, K), n, 9, torch.float64), series((K, N), n, 10, torch.float64)
+    check(A, B, TOL[torch.float64])
+
+
+def test_c128_directions():
+    A = series((128, 80), 2, 11, complex_from=1)
+    B = series((80, 96), 2, 12, complex_from=1)
+    check(A, B, TOL[torch.complex128])
+
+
+def test_c128_one_side_complex():
+    A = series((64, 48), 3, 13, torch.float64)
+    B = series((48, 40), 3, 14, complex_from=1)
+    check(A, B, TOL[torch.complex128])
+
+
+def test_bf16_storage():
+    A, B = series((512, 384), 2, 15, torch.bfloat16), series((384, 256), 2, 16, torch.bfloat16)
+    check(A, B, TOL[torch.bfloat16])
+
+
+def test_empty_reduction_and_empty_output():
+    from polytensors_b200 import _kernels
+
+    A, B = series((5, 0), 2, 17), series((0, 7), 2, 18)
+    got = _kernels.poly_matmul(cuda(A), cuda(B))
+    assert all(torch.count_nonzero(g).item() == 0 and g.shape == (5, 7) for g in got)
+    got = _kernels.poly_matmul(cuda(series((0, 4), 1, 19)), cuda(series((4, 3), 1, 20)))
+    assert all(g.shape == (0, 3) for g in got)
+
+
+def test_golden_vectors(golden):
+    from polytensors_b200 import _kernels
+
+    for name, tol in (("matmul_f64_n2", 1e-10), ("matmul_f64_n4", 1e-10), ("matmul_f32_n4", 1e-4),
+                      ("bmm_f64_n3", 1e-10), ("matmul_c128_n2", 1e-10)):
+        g = golden(name)
+        got = _kernels.poly_matmul(cuda(g["A"]), cuda(g["B"]))
+        errs = ref.plane_errors(got, g["C"])
+        assert max(errs) <= tol, (name, errs)
+
+
+def test_device_status_clean():
+    from polytensors_b200 import _lib
+
+    assert _lib.load().pk_device_status(1) == 0

@@ -1,0 +1,115 @@
+"""Pin the CPU oracle (oracle/polyref.py) against golden vectors produced by the
+reference implementation itself (tests/golden/make_golden.py)."""
+
+import math
+
+import pytest
+import torch
+
+from oracle import polyref as ref
+
+
+def assert_series_close(got, want, tol):
+    errs = ref.plane_errors(got, want)
+    assert len(got) == len(want)
+    assert max(errs) <= tol, errs
+
+
+@pytest.mark.parametrize("name", ["matmul_f64_n2", "matmul_f64_n4", "bmm_f64_n3"])
+def test_matmul_forward_backward_f64(golden, name):
+    g = golden(name)
+    assert_series_close(ref.poly_matmul(g["A"], g["B"]), g["C"], 1e-13)
+    dA, dB = ref.series_vjp(ref.poly_matmul, [g["A"], g["B"]], g["G"])
+    assert_series_close(dA, g["dA"], 1e-13)
+    assert_series_close(dB, g["dB"], 1e-13)
+
+
+def test_matmul_f32(golden):
+    g = golden("matmul_f32_n4")
+    assert_series_close(ref.poly_matmul(g["A"], g["B"]), g["C"], 1e-6)
+    A64 = [a.double() for a in g["A"]]
+    B64 = [b.double() for b in g["B"]]
+    assert_series_close(ref.poly_matmul(A64, B64), g["C"], 1e-6)
+
+
+def test_matmul_complex_directions(golden):
+    g = golden("matmul_c128_n2")
+    C = ref.poly_matmul(g["A"], g["B"])
+    assert C[0].dtype == torch.float64 and C[1].dtype == torch.complex128
+    assert_series_close(C, g["C"], 1e-13)
+
+
+@pytest.mark.parametrize("name,tol", [("rmsnorm_f64_n3", 1e-12), ("rmsnorm_f32_n3", 2e-6)])
+def test_rmsnorm(golden, name, tol):
+    g = golden(name)
+    fn = lambda X, W: ref.rms_norm(X, (32,), W)
+    assert_series_close(fn(g["X"], g["W"]), g["Y"], tol)
+    dX, dW = ref.series_vjp(fn, [g["X"], g["W"]], g["G"])
+    assert_series_close(dX, g["dX"], tol * 10)
+    assert_series_close(dW, g["dW"], tol * 10)
+
+
+def test_gelu(golden):
+    g = golden("gelu_f64_n4")
+    assert_series_close(ref.gelu(g["X"]), g["Y"], 1e-13)
+    assert_series_close(ref.series_vjp(ref.gelu, [g["X"]], g["G"])[0], g["dX"], 1e-12)
+    # the explicit plain-range backward rule agrees with the identity
+    D = len(g["X"]) - 1
+    assert_series_close(ref.gelu_backward(g["G"], g["X"]), g["dX"], 1e-12)
+
+
+def test_cross_entropy(golden):
+    g = golden("ce_f64_n4")
+    ce = ref.cross_entropy(g["X"], g["target"])
+    assert_series_close(ce, g["CE"], 1e-13)
+    n = len(g["X"]) - 1
+    lam = [torch.tensor(1.0, dtype=torch.float64), torch.tensor(-0.5, dtype=torch.float64)] + \
+          [torch.tensor(0.0, dtype=torch.float64)] * (n - 1)
+    assert_series_close(ref.cauchy(ce, lam), g["loss"], 1e-13)
+    # d loss / d logits: the loss-gradient series seeding is (1, 0, ...) times (1 - 0.5 Z)
+    dX = ref.cross_entropy_backward(g["X"], g["target"], lam)
+    assert_series_close(dX, g["dX"], 1e-12)
+
+
+def test_cross_entropy_none(golden):
+    g = golden("ce_none_f64_n4")
+    assert_series_close(ref.cross_entropy(g["X"], g["target"], reduction="none"), g["CE"], 1e-13)
+    dX = ref.cross_entropy_backward(g["X"], g["target"], g["G"], reduction="none")
+    assert_series_close(dX, g["dX"], 1e-12)
+    fn = lambda X: ref.cross_entropy(X, g["target"], reduction="none")
+    assert_series_close(ref.series_vjp(fn, [g["X"]], g["G"])[0], g["dX"], 1e-12)
+
+
+@pytest.mark.parametrize("name,kw", [("attn_causal_f64_n3", dict(is_causal=True)),
+                                     ("attn_full_f64_n3", dict(scale=0.3))])
+def test_attention(golden, name, kw):
+    g = golden(name)
+    fn = lambda Q, K, V: ref.attention(Q, K, V, **kw)
+    assert_series_close(fn(g["Q"], g["K"], g["V"]), g["O"], 1e-12)
+    dQ, dK, dV = ref.series_vjp(fn, [g["Q"], g["K"], g["V"]], g["G"])
+    assert_series_close(dQ, g["dQ"], 1e-11)
+    assert_series_close(dK, g["dK"], 1e-11)
+    assert_series_close(dV, g["dV"], 1e-11)
+
+
+def test_series_ops(golden):
+    g = golden("series_ops_f64_n5")
+    X, Xp, Y, Yp = g["X"], g["Xp"], g["Y"], g["Yp"]
+    checks = {
+        "mul": ref.cauchy(X, Y),
+        "div": ref.series_quotient(X, Yp),
+        "add": [x + 2.5 * y for x, y in zip(X, Y)],
+        "exp": ref.series_exp(X),
+        "log": ref.series_log(Xp),
+        "rsqrt": ref.series_rsqrt(Xp),
+        "tanh": ref.activation(X, "tanh"),
+        "sigmoid": ref.activation(X, "sigmoid"),
+        "gelu": ref.gelu(X),
+        "softmax": ref.softmax_family(X, -1)[0],
+        "log_softmax": ref.softmax_family(X, -1)[1],
+        "sum1": [x.sum(dim=1) for x in X],
+        "mean0": [x.mean(dim=0) for x in X],
+        "square": ref.cauchy(X, X),
+    }
+    for key, got in checks.items():
+        assert_series_close(got, g[key], 1e-12)
