@@ -78,14 +78,14 @@ def test_f64(M, N, K, n):
 
 
 def test_c128_directions():
-    A = series((128, 80), 2, 11, complex_from=1)
-    B = series((80, 96), 2, 12, complex_from=1)
+    A = series((128, 80), 2, 11, torch.float64, complex_from=1)
+    B = series((80, 96), 2, 12, torch.float64, complex_from=1)
     check(A, B, TOL[torch.complex128])
 
 
 def test_c128_one_side_complex():
     A = series((64, 48), 3, 13, torch.float64)
-    B = series((48, 40), 3, 14, complex_from=1)
+    B = series((48, 40), 3, 14, torch.float64, complex_from=1)
     check(A, B, TOL[torch.complex128])
 
 
