@@ -35,6 +35,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 WORKLOADS = {
     "poly_matmul": dict(M=8192, N=8192, K=8192, degree=4, dtype="float32"),
     "poly_matmul_f64": dict(M=4096, N=4096, K=4096, degree=2, dtype="float64"),
+    "poly_matmul_2048": dict(M=2048, N=2048, K=2048, degree=4, dtype="float32"),
 }
 
 

@@ -696,9 +696,6 @@ int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int
     if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff)
         return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: dimension exceeds 2^31-1");
     const int P = degree + 1;
-    if (!a_planes || !b_planes || !c_planes) return fail(PK_ERR_ARG, "pk_poly_gemm: null plane array");
-    for (int p = 0; p < P; ++p)
-        if (!a_planes[p] || !b_planes[p] || !c_planes[p]) return fail(PK_ERR_ARG, "pk_poly_gemm: null plane pointer");
     if (dtype != PK_C128) {
         a_complex_from = P;
         b_complex_from = P;
@@ -706,9 +703,12 @@ int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int
         a_complex_from = std::max(0, std::min(a_complex_from, P));
         b_complex_from = std::max(0, std::min(b_complex_from, P));
     }
-    if (batch == 0 || M == 0 || N == 0) return PK_OK;
+    if (batch == 0 || M == 0 || N == 0) return PK_OK;  // empty output: nothing to read or write
+    if (!c_planes) return fail(PK_ERR_ARG, "pk_poly_gemm: null output plane array");
+    for (int p = 0; p < P; ++p)
+        if (!c_planes[p]) return fail(PK_ERR_ARG, "pk_poly_gemm: null output plane pointer");
 
-    if (K == 0) {
+    if (K == 0) {  // empty reduction: the operands may have no storage at all
         for (int p = 0; p < P; ++p) {
             const bool cplx = dtype == PK_C128 && (p >= a_complex_from || p >= b_complex_from);
             const int e = dtype == PK_C128 ? (cplx ? 16 : 8) : esz;
@@ -719,6 +719,9 @@ int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int
         return PK_OK;
     }
 
+    if (!a_planes || !b_planes) return fail(PK_ERR_ARG, "pk_poly_gemm: null operand plane array");
+    for (int p = 0; p < P; ++p)
+        if (!a_planes[p] || !b_planes[p]) return fail(PK_ERR_ARG, "pk_poly_gemm: null operand plane pointer");
     const GemmPlan g = plan_gemm(dtype, degree, batch, M, N, K, a_complex_from, b_complex_from);
     if (!workspace || workspace_bytes < g.total)
         return fail(PK_ERR_WORKSPACE, "pk_poly_gemm: workspace of " + std::to_string(g.total) + " bytes required");
