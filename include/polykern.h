@@ -107,6 +107,25 @@ PK_API int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t
                  int a_complex_from, int b_complex_from,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * pk_poly_gemm without a workspace argument, for callers that cannot allocate device
+ * memory (a plugin host that owns every allocation, a process that must not grow its
+ * device footprint after start-up, code with no allocator to link).  The scratch comes
+ * from a fixed PK_NOALLOC_SCRATCH_BYTES array in the library's device memory, held on
+ * every GPU that loads the library until the process exits.  Products needing more
+ * scratch than that (pk_poly_gemm_workspace_size) fail with PK_ERR_UNSUPPORTED.  The
+ * first call on a device looks up the array's address; make it before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race, so order
+ * them on one stream.  Allocates nothing.
+ * No counterpart in the reference (an addition of this library).
+ */
+#define PK_NOALLOC_SCRATCH_BYTES (64ull << 20)
+PK_API int pk_poly_gemm_noalloc(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K,
+                                const void* const* a_planes, int64_t a_bs, int64_t a_rs, int64_t a_cs,
+                                const void* const* b_planes, int64_t b_bs, int64_t b_rs, int64_t b_cs,
+                                void* const* c_planes, int64_t c_bs, int64_t c_rs,
+                                int a_complex_from, int b_complex_from, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

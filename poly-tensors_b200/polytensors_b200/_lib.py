@@ -30,6 +30,11 @@ SIGNATURES = {
                             _pp, _i64, _i64, _i64,
                             _pp, _i64, _i64,
                             _i32, _i32, _vp, _sz, _vp]),
+    "pk_poly_gemm_noalloc": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64,
+                                    _pp, _i64, _i64, _i64,
+                                    _pp, _i64, _i64, _i64,
+                                    _pp, _i64, _i64,
+                                    _i32, _i32, _vp]),
 }
 
 _lock = threading.Lock()
