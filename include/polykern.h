@@ -107,6 +107,119 @@ PK_API int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t
                  int a_complex_from, int b_complex_from,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------------------------
+ * Elementwise series operations.  out = f(a) or f(a, b) for every element, all planes
+ * at once.  Shapes broadcast through strides (0 for a broadcast dimension, at most 6
+ * dimensions); out, a and b share `shape` and the storage dtype (PK_F32, PK_F64,
+ * PK_BF16, PK_F16; bf16/f16 compute in float).  a_planes / b_planes is degree+1 for a
+ * series operand or 1 for a constant operand (its higher coefficients are zero).  out
+ * may alias a (in-place update, e.g. an SGD step) when their strides are equal.
+ */
+enum pk_series_op {
+    PK_OP_COPY = 0,        /* out = a */
+    PK_OP_AFFINE = 1,      /* out = p0*a + p1 (p1 on the constant term): neg, scale, add/rsub scalar */
+    PK_OP_EXP = 2,         /* src/polytensors/_plain.py:153-159 */
+    PK_OP_LOG = 3,         /* src/polytensors/_plain.py:162-171 */
+    PK_OP_SQRT = 4,        /* src/polytensors/_series.py:72-81, _plain.py:294-298 */
+    PK_OP_RSQRT = 5,       /* src/polytensors/_series.py:83-96 */
+    PK_OP_RECIPROCAL = 6,  /* src/polytensors/_range_ops.py:157-158 */
+    PK_OP_TANH = 7,        /* src/polytensors/_plain.py:303-304 */
+    PK_OP_SIGMOID = 8,     /* src/polytensors/_plain.py:303-304 */
+    PK_OP_GELU = 9,        /* exact GELU, src/polytensors/_plain.py:305-309 */
+    PK_OP_POWI = 10,       /* a^p0, p0 a nonnegative integer, src/polytensors/_dispatch.py:419-429 */
+    PK_OP_ADD = 32,        /* out = a + p0*b, src/polytensors/_range_ops.py:137-142 */
+    PK_OP_MUL = 33,        /* Cauchy product, src/polytensors/_range_ops.py:143-144 */
+    PK_OP_DIV = 34,        /* series quotient, src/polytensors/_range_ops.py:86-93 */
+    PK_OP_GELU_BWD = 35,   /* a = gradient, b = input: a * gelu'(b), src/polytensors/_plain.py:310-315 */
+    PK_OP_TANH_BWD = 36,   /* a = gradient, b = output: a * (1 - b^2), src/polytensors/_plain.py:316-320 */
+    PK_OP_SIGMOID_BWD = 37 /* a = gradient, b = output: a * b * (1 - b), src/polytensors/_plain.py:321-325 */
+};
+PK_API int pk_series_map(int op, int dtype, int degree, int ndim, const int64_t* shape,
+                         void* const* out, const int64_t* out_strides,
+                         const void* const* a, int a_planes, const int64_t* a_strides,
+                         const void* const* b, int b_planes, const int64_t* b_strides,
+                         double p0, double p1, void* stream);
+
+/*
+ * out[o, i] = scale * sum_r x[o, r, i] for every plane; x is contiguous [outer][red][inner],
+ * out contiguous [outer][inner].  Replaces the per-plane sum/mean of
+ * src/polytensors/_range_ops.py:178-193 (mean: scale = 1/count).  float32 / float64.
+ */
+PK_API int pk_series_reduce(int dtype, int degree, int64_t outer, int64_t red, int64_t inner,
+                            const void* const* x, void* const* out, double scale, void* stream);
+
+/*
+ * Embedding rows: out[i, :] = src[idx[i], :] (gather, src/polytensors/_dispatch.py:530-532) and
+ * its backward out[idx[i], :] += src[i, :] over a zeroed (n_rows, dim) output, skipping
+ * idx == padding_idx (src/polytensors/_dispatch.py:683-685).  idx is a device int64 array;
+ * out-of-range indices are skipped and reported through pk_device_status.  float32 / float64.
+ */
+PK_API int pk_series_gather_rows(int dtype, int degree, int64_t n_idx, int64_t dim, const int64_t* idx,
+                                 const void* const* src, int64_t src_rs, int64_t n_rows,
+                                 void* const* out, void* stream);
+PK_API int pk_series_scatter_add_rows(int dtype, int degree, int64_t n_idx, int64_t dim, const int64_t* idx,
+                                      int64_t padding_idx, const void* const* src, int64_t src_rs,
+                                      int64_t n_rows, void* const* out, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Row-wise series kernels over a (rows, cols) view: plane k of row r starts at
+ * planes[k] + r * row_stride and its cols elements are contiguous.
+ */
+
+/*
+ * RMSNorm: y = x (*) rsqrt(mean_row(x (*) x) + eps) (*) w, (*) the truncated Cauchy product.
+ * Replaces the decomposition of src/polytensors/_decompositions.py:14-22 and generalises the
+ * degree-1 kernels of src/polytensors/_norm_kernels.py:6-38 (gate src/polytensors/_fused_norm.py:11-21).
+ * w: NULL (no weight), or w_planes = 1 (constant weight) / degree+1 planes of cols elements.
+ * rstd (optional): receives the per-row rsqrt series, [rows][degree+1] in float (float64 for PK_F64),
+ * which pk_rmsnorm_bwd needs.
+ */
+PK_API int pk_rmsnorm_fwd(int dtype, int degree, int64_t rows, int64_t cols,
+                          const void* const* x, int64_t x_rs, const void* const* w, int w_planes,
+                          double eps, void* const* y, int64_t y_rs, void* rstd, void* stream);
+/*
+ * Gradient series of pk_rmsnorm_fwd for the output-gradient series g: dx, and (if dw is not NULL)
+ * dw (degree+1 planes of cols elements; needs a workspace of pk_rmsnorm_bwd_workspace_size bytes).
+ */
+PK_API size_t pk_rmsnorm_bwd_workspace_size(int dtype, int degree, int64_t rows, int64_t cols);
+PK_API int pk_rmsnorm_bwd(int dtype, int degree, int64_t rows, int64_t cols,
+                          const void* const* x, int64_t x_rs, const void* const* w, int w_planes,
+                          const void* const* g, int64_t g_rs, const void* rstd,
+                          void* const* dx, int64_t dx_rs, void* const* dw,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Softmax / log-softmax along rows (log = 1 for log_softmax), and their backward rules:
+ * src/polytensors/_plain.py:262-273 (forward), :342-347 (softmax backward), :348-354
+ * (log-softmax backward; y is the forward output).
+ */
+PK_API int pk_softmax_fwd(int dtype, int degree, int64_t rows, int64_t cols,
+                          const void* const* x, int64_t x_rs, int log, void* const* y, int64_t y_rs,
+                          void* stream);
+PK_API int pk_softmax_bwd(int dtype, int degree, int64_t rows, int64_t cols,
+                          const void* const* g, int64_t g_rs, const void* const* y, int64_t y_rs, int log,
+                          void* const* dx, int64_t dx_rs, void* stream);
+
+/*
+ * Cross entropy of (rows, cols) logits series with int64 class targets (device array):
+ * loss[k][r] = -log_softmax_k(z[r])[target[r]], 0 where target == ignore_index; softcap > 0
+ * first maps z -> softcap * tanh(z / softcap) as a series.  Loss planes and the per-row
+ * statistics (stats: [rows][degree+1]) are float for PK_F32/PK_BF16/PK_F16 and double for PK_F64.
+ * pk_cross_entropy_bwd: dz = d/dz of sum_r <g[.][r], loss[.][r]> as a series, for the per-row
+ * gradient series g (same precision as the loss); rows with target == ignore_index get 0.
+ * Replaces F.cross_entropy = log_softmax + nll_loss in plain range (src/polytensors/_plain.py:326-332,
+ * src/polytensors/_dispatch.py:537-562) and generalises the degree-1 fused kernels
+ * (src/polytensors/_cross_entropy_kernels.py:19-85, src/polytensors/_fused_cross_entropy.py:54-76).
+ */
+PK_API int pk_cross_entropy_fwd(int dtype, int degree, int64_t rows, int64_t cols,
+                                const void* const* z, int64_t z_rs, const int64_t* target,
+                                int64_t ignore_index, double softcap, void* const* loss, void* stats,
+                                void* stream);
+PK_API int pk_cross_entropy_bwd(int dtype, int degree, int64_t rows, int64_t cols,
+                                const void* const* z, int64_t z_rs, const int64_t* target,
+                                int64_t ignore_index, double softcap, const void* stats,
+                                const void* const* g, void* const* dz, int64_t dz_rs, void* stream);
+
 /*
  * pk_poly_gemm without a workspace argument, for callers that cannot allocate device
  * memory (a plugin host that owns every allocation, a process that must not grow its

@@ -1,0 +1,353 @@
+// Softmax family and cross entropy of series along the last dimension.
+//
+// For a row of logits series x(c) (c = class) with base log-sum-exp lse_0, the reference
+// (src/polytensors/_plain.py:262-273) forms E = exp(x - lse_0) as series, Z = sum_c E,
+// log Z, and log_softmax = x - log Z.  Because exp(x(c)) = exp(x_0(c)) e(c) with e the
+// exponential of the directions only, Z_k = sum_c exp(x_0(c) - m) e_k(c) / S_0 for any
+// shift m: one streaming pass with an online maximum (the flash-softmax rescaling applied
+// to all n+1 sums at once) yields lse_0 and the log-normaliser series logz_1..n.  A second
+// pass writes log_softmax_k = x_k - logz_k (k >= 1), x_0 - lse_0 (k = 0), or its exponential.
+//
+// Cross entropy never writes log_softmax: loss_k = logz_k - x_k[y] (loss_0 = lse_0 - x_0[y]),
+// and its backward is dx = g (*) P - g e_y with P the softmax series recomputed per
+// element (src/polytensors/_plain.py:348-354 after the NLL scatter of
+// src/polytensors/_dispatch.py:556-562), optionally through a softcap z -> c tanh(z/c)
+// (src/polytensors/_cross_entropy_kernels.py:7-17, generalised to any degree).
+#include <algorithm>
+
+#include "pk_rows.cuh"
+
+namespace pk {
+
+struct SoftmaxParams {
+    int np;
+    int64_t rows, cols;
+    int64_t x_rs, y_rs, g_rs;
+    int log;              // softmax: write log_softmax (1) or softmax (0)
+    double softcap;       // cross entropy: 0 = none
+    int64_t ignore_index;
+    const int64_t* target;
+    const void* x[PK_MAX_PLANES];
+    const void* y[PK_MAX_PLANES];   // backward: forward output
+    const void* g[PK_MAX_PLANES];   // backward: incoming gradient (per element, or per row for CE)
+    void* out[PK_MAX_PLANES];
+    void* stats;                    // CE: [rows][np] (lse_0, logz_1..n), compute type
+};
+
+template <int NP, typename T, typename C>
+__device__ __forceinline__ void load_row_elem(const void* const* planes, int np, int64_t off, C (&v)[NP]) {
+#pragma unroll
+    for (int k = 0; k < NP; ++k) v[k] = k < np ? to_c<C>(static_cast<const T*>(planes[k])[off]) : C(0);
+}
+
+// z -> c tanh(z / c) as a series; d receives the derivative series 1 - tanh^2(z / c).
+template <int NP, typename C>
+__device__ __forceinline__ void softcap_series(C (&z)[NP], C cap, C (&d)[NP]) {
+    C u[NP], t[NP];
+    const C inv = C(1) / cap;
+#pragma unroll
+    for (int k = 0; k < NP; ++k) u[k] = z[k] * inv;
+    s_tanh<NP, C>(u, t, d);
+#pragma unroll
+    for (int k = 0; k < NP; ++k) z[k] = cap * t[k];
+}
+
+// Pass 1 of every kernel here: the online log-sum-exp state of a row.
+template <typename T, int NP, typename C>
+__device__ __forceinline__ void row_lse(const SoftmaxParams& p, int64_t xb, C* scratch, C (&lse)[NP]) {
+    C m = -INFINITY, S[NP];
+#pragma unroll
+    for (int k = 0; k < NP; ++k) S[k] = C(0);
+    for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
+        C x[NP];
+        load_row_elem<NP, T, C>(p.x, p.np, xb + c, x);
+        if (p.softcap != 0.0) {
+            C d[NP];
+            softcap_series<NP, C>(x, C(p.softcap), d);
+        }
+        lse_accumulate<NP, C>(m, S, x);
+    }
+    block_lse_combine<NP, C>(m, S, scratch);
+    lse_finish<NP, C>(m, S, lse);
+}
+
+template <typename T, int NP>
+__global__ void __launch_bounds__(512) softmax_fwd_kernel(const SoftmaxParams p) {
+    using C = typename Compute<T>::type;
+    __shared__ C scratch[16 * (NP + 1)];
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        const int64_t xb = row * p.x_rs, yb = row * p.y_rs;
+        C lse[NP];
+        row_lse<T, NP, C>(p, xb, scratch, lse);
+        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
+            C x[NP], ls[NP];
+            load_row_elem<NP, T, C>(p.x, p.np, xb + c, x);
+            ls[0] = x[0] - lse[0];
+#pragma unroll
+            for (int k = 1; k < NP; ++k) ls[k] = x[k] - lse[k];
+            if (!p.log) s_exp<NP, C>(ls, ls);
+#pragma unroll
+            for (int k = 0; k < NP; ++k)
+                if (k < p.np) static_cast<T*>(p.out[k])[yb + c] = from_c<T>(ls[k]);
+        }
+    }
+}
+
+// log: dx = G - exp(Y) (*) sum_row G        (src/polytensors/_plain.py:348-354)
+// not log: dx = Y (*) (G - sum_row G (*) Y)   (src/polytensors/_plain.py:342-347)
+template <typename T, int NP>
+__global__ void __launch_bounds__(512) softmax_bwd_kernel(const SoftmaxParams p) {
+    using C = typename Compute<T>::type;
+    __shared__ C scratch[16 * NP];
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        const int64_t gb = row * p.g_rs, yb = row * p.y_rs, ob = row * p.x_rs;
+        C s[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) s[k] = C(0);
+        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
+            C g[NP];
+            load_row_elem<NP, T, C>(p.g, p.np, gb + c, g);
+            if (p.log) {
+#pragma unroll
+                for (int k = 0; k < NP; ++k) s[k] += g[k];
+            } else {
+                C y[NP], t[NP];
+                load_row_elem<NP, T, C>(p.y, p.np, yb + c, y);
+                s_mul<NP, C>(g, y, t);
+#pragma unroll
+                for (int k = 0; k < NP; ++k) s[k] += t[k];
+            }
+        }
+        block_sum<NP, C>(s, scratch);
+        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
+            C g[NP], y[NP], r[NP];
+            load_row_elem<NP, T, C>(p.g, p.np, gb + c, g);
+            load_row_elem<NP, T, C>(p.y, p.np, yb + c, y);
+            if (p.log) {
+                C e[NP], t[NP];
+                s_exp<NP, C>(y, e);
+                s_mul<NP, C>(e, s, t);
+#pragma unroll
+                for (int k = 0; k < NP; ++k) r[k] = g[k] - t[k];
+            } else {
+                C d[NP];
+#pragma unroll
+                for (int k = 0; k < NP; ++k) d[k] = g[k] - s[k];
+                s_mul<NP, C>(y, d, r);
+            }
+#pragma unroll
+            for (int k = 0; k < NP; ++k)
+                if (k < p.np) static_cast<T*>(p.out[k])[ob + c] = from_c<T>(r[k]);
+        }
+    }
+}
+
+// Cross entropy forward: per-row loss series and the row statistics for backward.
+template <typename T, int NP>
+__global__ void __launch_bounds__(512) ce_fwd_kernel(const SoftmaxParams p) {
+    using C = typename Compute<T>::type;
+    __shared__ C scratch[16 * (NP + 1)];
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        const int64_t xb = row * p.x_rs;
+        C lse[NP];
+        row_lse<T, NP, C>(p, xb, scratch, lse);
+        if (threadIdx.x == 0) {
+            const int64_t y = p.target[row];
+            const bool valid = y != p.ignore_index && y >= 0 && y < p.cols;
+            C zy[NP];
+#pragma unroll
+            for (int k = 0; k < NP; ++k) zy[k] = C(0);
+            if (valid) {
+                load_row_elem<NP, T, C>(p.x, p.np, xb + y, zy);
+                if (p.softcap != 0.0) {
+                    C d[NP];
+                    softcap_series<NP, C>(zy, C(p.softcap), d);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < NP; ++k) {
+                if (k >= p.np) continue;
+                static_cast<C*>(p.out[k])[row] = valid ? lse[k] - zy[k] : C(0);
+                static_cast<C*>(p.stats)[row * p.np + k] = lse[k];
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// Cross entropy backward: dz = d (*) [g (*) P - g e_y], d = softcap derivative series (or 1).
+template <typename T, int NP>
+__global__ void __launch_bounds__(512) ce_bwd_kernel(const SoftmaxParams p) {
+    using C = typename Compute<T>::type;
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        const int64_t y = p.target[row];
+        const bool valid = y != p.ignore_index && y >= 0 && y < p.cols;
+        C g[NP], lse[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+            g[k] = (valid && k < p.np) ? static_cast<const C*>(p.g[k])[row] : C(0);
+            lse[k] = k < p.np ? static_cast<const C*>(p.stats)[row * p.np + k] : C(0);
+        }
+        const int64_t xb = row * p.x_rs, ob = row * p.y_rs;
+        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
+            C z[NP], d[NP], ls[NP], P[NP], r[NP];
+            load_row_elem<NP, T, C>(p.x, p.np, xb + c, z);
+            if (p.softcap != 0.0) softcap_series<NP, C>(z, C(p.softcap), d);
+            ls[0] = z[0] - lse[0];
+#pragma unroll
+            for (int k = 1; k < NP; ++k) ls[k] = z[k] - lse[k];
+            s_exp<NP, C>(ls, P);
+            s_mul<NP, C>(g, P, r);
+            if (c == y) {
+#pragma unroll
+                for (int k = 0; k < NP; ++k) r[k] -= g[k];
+            }
+            if (p.softcap != 0.0) s_mul<NP, C>(r, d, r);
+#pragma unroll
+            for (int k = 0; k < NP; ++k)
+                if (k < p.np) static_cast<T*>(p.out[k])[ob + c] = from_c<T>(r[k]);
+        }
+    }
+}
+
+enum { SM_FWD = 0, SM_BWD = 1, CE_FWD = 2, CE_BWD = 3 };
+
+static int row_threads(int64_t cols) { return cols >= 4096 ? 512 : (cols >= 1024 ? 256 : 128); }
+
+template <typename T, int NP>
+static void launch_rows(int which, const SoftmaxParams& p, cudaStream_t s) {
+    const int threads = row_threads(p.cols);
+    const int grid = static_cast<int>(std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * 8));
+    switch (which) {
+        case SM_FWD: softmax_fwd_kernel<T, NP><<<grid, threads, 0, s>>>(p); break;
+        case SM_BWD: softmax_bwd_kernel<T, NP><<<grid, threads, 0, s>>>(p); break;
+        case CE_FWD: ce_fwd_kernel<T, NP><<<grid, threads, 0, s>>>(p); break;
+        default: ce_bwd_kernel<T, NP><<<grid, threads, 0, s>>>(p); break;
+    }
+}
+
+template <typename T>
+static void launch_rows_np(int which, const SoftmaxParams& p, cudaStream_t s) {
+    switch (p.np) {
+        case 1: launch_rows<T, 1>(which, p, s); break;
+        case 2: launch_rows<T, 2>(which, p, s); break;
+        case 3: launch_rows<T, 3>(which, p, s); break;
+        case 4: launch_rows<T, 4>(which, p, s); break;
+        case 5: launch_rows<T, 5>(which, p, s); break;
+        case 6: launch_rows<T, 6>(which, p, s); break;
+        case 7: case 8: case 9: launch_rows<T, 9>(which, p, s); break;
+        default: launch_rows<T, 16>(which, p, s); break;
+    }
+}
+
+static int dispatch_rows(int which, int dtype, const SoftmaxParams& p, void* stream, const char* what) {
+    if (p.rows == 0 || p.cols == 0) return PK_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    void* tok;
+    prof_begin(what, s, &tok);
+    switch (dtype) {
+        case PK_F32: launch_rows_np<float>(which, p, s); break;
+        case PK_F64: launch_rows_np<double>(which, p, s); break;
+        case PK_BF16: launch_rows_np<__nv_bfloat16>(which, p, s); break;
+        case PK_F16: launch_rows_np<__half>(which, p, s); break;
+        default: return fail(PK_ERR_UNSUPPORTED, std::string(what) + ": unsupported dtype");
+    }
+    prof_end(what, s, tok);
+    PK_CHECK_LAUNCH(what);
+    return PK_OK;
+}
+
+static int check_common(int degree, int64_t rows, int64_t cols, const char* what) {
+    if (degree < 0 || degree >= PK_MAX_PLANES) return fail(PK_ERR_UNSUPPORTED, std::string(what) + ": degree out of range");
+    if (rows < 0 || cols < 0) return fail(PK_ERR_ARG, std::string(what) + ": negative extent");
+    return PK_OK;
+}
+
+}  // namespace pk
+
+using namespace pk;
+
+extern "C" {
+
+int pk_softmax_fwd(int dtype, int degree, int64_t rows, int64_t cols, const void* const* x, int64_t x_rs, int log,
+                   void* const* y, int64_t y_rs, void* stream) {
+    if (int rc = check_common(degree, rows, cols, "pk_softmax_fwd")) return rc;
+    SoftmaxParams p{};
+    p.np = degree + 1;
+    p.rows = rows;
+    p.cols = cols;
+    p.x_rs = x_rs;
+    p.y_rs = y_rs;
+    p.log = log;
+    for (int k = 0; k < p.np; ++k) {
+        p.x[k] = x[k];
+        p.out[k] = y[k];
+    }
+    return dispatch_rows(SM_FWD, dtype, p, stream, "softmax_fwd");
+}
+
+int pk_softmax_bwd(int dtype, int degree, int64_t rows, int64_t cols, const void* const* g, int64_t g_rs,
+                   const void* const* y, int64_t y_rs, int log, void* const* dx, int64_t dx_rs, void* stream) {
+    if (int rc = check_common(degree, rows, cols, "pk_softmax_bwd")) return rc;
+    SoftmaxParams p{};
+    p.np = degree + 1;
+    p.rows = rows;
+    p.cols = cols;
+    p.g_rs = g_rs;
+    p.y_rs = y_rs;
+    p.x_rs = dx_rs;
+    p.log = log;
+    for (int k = 0; k < p.np; ++k) {
+        p.g[k] = g[k];
+        p.y[k] = y[k];
+        p.out[k] = dx[k];
+    }
+    return dispatch_rows(SM_BWD, dtype, p, stream, "softmax_bwd");
+}
+
+int pk_cross_entropy_fwd(int dtype, int degree, int64_t rows, int64_t cols, const void* const* z, int64_t z_rs,
+                         const int64_t* target, int64_t ignore_index, double softcap, void* const* loss, void* stats,
+                         void* stream) {
+    if (int rc = check_common(degree, rows, cols, "pk_cross_entropy_fwd")) return rc;
+    if (!target || !stats) return fail(PK_ERR_ARG, "pk_cross_entropy_fwd: null target or stats");
+    if (cols == 0) return fail(PK_ERR_ARG, "pk_cross_entropy_fwd: no classes");
+    SoftmaxParams p{};
+    p.np = degree + 1;
+    p.rows = rows;
+    p.cols = cols;
+    p.x_rs = z_rs;
+    p.target = target;
+    p.ignore_index = ignore_index;
+    p.softcap = softcap;
+    p.stats = stats;
+    for (int k = 0; k < p.np; ++k) {
+        p.x[k] = z[k];
+        p.out[k] = loss[k];
+    }
+    return dispatch_rows(CE_FWD, dtype, p, stream, "cross_entropy_fwd");
+}
+
+int pk_cross_entropy_bwd(int dtype, int degree, int64_t rows, int64_t cols, const void* const* z, int64_t z_rs,
+                         const int64_t* target, int64_t ignore_index, double softcap, const void* stats,
+                         const void* const* g, void* const* dz, int64_t dz_rs, void* stream) {
+    if (int rc = check_common(degree, rows, cols, "pk_cross_entropy_bwd")) return rc;
+    if (!target || !stats) return fail(PK_ERR_ARG, "pk_cross_entropy_bwd: null target or stats");
+    SoftmaxParams p{};
+    p.np = degree + 1;
+    p.rows = rows;
+    p.cols = cols;
+    p.x_rs = z_rs;
+    p.y_rs = dz_rs;
+    p.target = target;
+    p.ignore_index = ignore_index;
+    p.softcap = softcap;
+    p.stats = const_cast<void*>(stats);
+    for (int k = 0; k < p.np; ++k) {
+        p.x[k] = z[k];
+        p.g[k] = g[k];
+        p.out[k] = dz[k];
+    }
+    return dispatch_rows(CE_BWD, dtype, p, stream, "cross_entropy_bwd");
+}
+
+}  // extern "C"

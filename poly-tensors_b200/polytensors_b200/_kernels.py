@@ -109,3 +109,258 @@ def poly_matmul(a_planes, b_planes):
                               acf, bcf, ws.data_ptr(), ws.numel(), _stream(a0.device))
     _lib.check(status, "pk_poly_gemm")
     return outs
+
+
+# ------------------------------------------------------------------------------------
+# elementwise series operations, reductions, gathers
+
+def dtype_code(dtype):
+    code = _DTYPE_CODE.get(dtype)
+    if code is None:
+        raise NotImplementedError(f"polykern: coefficient dtype {dtype} is not supported by the kernels")
+    return code
+
+
+def _same_strides(planes):
+    s = planes[0].stride()
+    return all(p.stride() == s for p in planes)
+
+
+def _collapse(shape, *stride_sets):
+    """Merge adjacent dimensions that are contiguous with each other in every operand."""
+    dims = [(shape[d], [st[d] for st in stride_sets]) for d in range(len(shape)) if shape[d] != 1]
+    if not dims:
+        return [1], [[0] for _ in stride_sets]
+    out = [dims[0]]
+    for size, strides in dims[1:]:
+        psize, pstrides = out[-1]
+        if all(ps == s * size for ps, s in zip(pstrides, strides)):
+            out[-1] = (psize * size, strides)
+        else:
+            out.append((size, strides))
+    return [d[0] for d in out], [[d[1][i] for d in out] for i in range(len(stride_sets))]
+
+
+def series_map(op, degree, a, b=None, p0=0.0, p1=0.0, out=None):
+    """One elementwise series operation over all planes (pk_series_map).
+
+    ``a``/``b`` are lists of planes (degree+1 planes, or 1 plane for a constant operand);
+    they broadcast against each other.  Returns the ``out`` planes (allocated contiguous
+    when not given; an in-place update passes ``out=a``)."""
+    np_ = degree + 1
+    if np_ > _lib.PK_MAX_PLANES:
+        raise NotImplementedError(f"polykern: degree {degree} exceeds {_lib.PK_MAX_PLANES - 1}")
+    opcode = _lib.OP[op]
+    planes = list(a) + (list(b) if b is not None else []) + (list(out) if out is not None else [])
+    _require_cuda(planes, f"series {op}")
+    dtype = a[0].dtype
+    code = dtype_code(dtype)
+    shape = a[0].shape if b is None else torch.broadcast_shapes(a[0].shape, b[0].shape)
+    if out is not None:
+        shape = out[0].shape
+    a = [x.expand(shape) for x in a]
+    if not _same_strides(a):
+        a = [x.contiguous() for x in a]
+    if b is not None:
+        b = [x.to(dtype).expand(shape) for x in b]
+        if not _same_strides(b):
+            b = [x.contiguous() for x in b]
+    if out is None:
+        out = [torch.empty(shape, dtype=dtype, device=a[0].device) for _ in range(np_)]
+    elif not _same_strides(out):
+        raise NotImplementedError("series update into planes with differing layouts")
+    if any(o.dtype != dtype for o in out):
+        raise NotImplementedError("series update into planes of another dtype")
+    if out[0].numel() == 0:
+        return out
+    sets = [out[0].stride(), a[0].stride()] + ([b[0].stride()] if b is not None else [])
+    cshape, cstrides = _collapse(list(shape), *sets)
+    if len(cshape) > 6:
+        raise NotImplementedError("series operation on more than 6 non-mergeable dimensions")
+    shp, ks = _lib.int64_array(cshape)
+    so, k1 = _lib.int64_array(cstrides[0])
+    sa, k2 = _lib.int64_array(cstrides[1])
+    sb, k3 = _lib.int64_array(cstrides[2] if b is not None else [0] * len(cshape))
+    po, kp1 = _lib.pointer_array(out)
+    pa, kp2 = _lib.pointer_array(a)
+    pb, kp3 = _lib.pointer_array(b if b is not None else [None])
+    status = _lib.load().pk_series_map(opcode, code, degree, len(cshape), shp, po, so, pa, len(a), sa,
+                                        pb if b is not None else None, len(b) if b is not None else 0, sb,
+                                        float(p0), float(p1), _stream(a[0].device))
+    _lib.check(status, f"pk_series_map({op})")
+    return out
+
+
+def series_reduce(planes, outer, red, inner, scale=1.0):
+    """out[o, i] = scale * sum_r x[o, r, i] for contiguous planes viewed as (outer, red, inner)."""
+    x = [p.contiguous() for p in planes]
+    _require_cuda(x, "series reduction")
+    code = dtype_code(x[0].dtype)
+    out = [torch.empty(outer * inner, dtype=x[0].dtype, device=x[0].device) for _ in x]
+    px, k1 = _lib.pointer_array(x)
+    po, k2 = _lib.pointer_array(out)
+    status = _lib.load().pk_series_reduce(code, len(x) - 1, outer, red, inner, px, po, float(scale),
+                                          _stream(x[0].device))
+    _lib.check(status, "pk_series_reduce")
+    return out
+
+
+def gather_rows(weight_planes, idx):
+    """out[i, :] = W[idx[i], :] per plane (embedding)."""
+    w = weight_planes if _same_strides(weight_planes) and weight_planes[0].stride(-1) == 1 else \
+        [p.contiguous() for p in weight_planes]
+    _require_cuda((*w, idx), "embedding")
+    V, d = w[0].shape
+    flat = idx.reshape(-1).to(torch.int64).contiguous()
+    out = [torch.empty(flat.numel(), d, dtype=w[0].dtype, device=w[0].device) for _ in w]
+    pw, k1 = _lib.pointer_array(w)
+    po, k2 = _lib.pointer_array(out)
+    status = _lib.load().pk_series_gather_rows(dtype_code(w[0].dtype), len(w) - 1, flat.numel(), d,
+                                               flat.data_ptr(), pw, w[0].stride(0), V, po, _stream(w[0].device))
+    _lib.check(status, "pk_series_gather_rows")
+    return [o.view(*idx.shape, d) for o in out]
+
+
+def scatter_add_rows(grad_planes, idx, num_rows, padding_idx=-1):
+    """out[idx[i], :] += G[i, :] over zeroed (num_rows, d) planes (embedding backward)."""
+    d = grad_planes[0].shape[-1]
+    g = [p.reshape(-1, d) for p in grad_planes]
+    if not _same_strides(g) or g[0].stride(-1) != 1:
+        g = [p.contiguous() for p in g]
+    flat = idx.reshape(-1).to(torch.int64).contiguous()
+    _require_cuda((*g, flat), "embedding backward")
+    out = [torch.empty(num_rows, d, dtype=g[0].dtype, device=g[0].device) for _ in g]
+    pg, k1 = _lib.pointer_array(g)
+    po, k2 = _lib.pointer_array(out)
+    status = _lib.load().pk_series_scatter_add_rows(dtype_code(g[0].dtype), len(g) - 1, flat.numel(), d,
+                                                    flat.data_ptr(), padding_idx, pg, g[0].stride(0), num_rows,
+                                                    po, _stream(g[0].device))
+    _lib.check(status, "pk_series_scatter_add_rows")
+    return out
+
+
+# ------------------------------------------------------------------------------------
+# row-wise kernels: planes viewed as (rows, cols) with contiguous rows
+
+def _rows(planes, cols):
+    x = [p.reshape(-1, cols) if p.is_contiguous() else p.contiguous().view(-1, cols) for p in planes]
+    if not _same_strides(x) or x[0].stride(-1) != 1:
+        x = [p.contiguous() for p in x]
+    return x
+
+
+def compute_dtype(dtype):
+    return torch.float64 if dtype == torch.float64 else torch.float32
+
+
+def rmsnorm_fwd(x_planes, cols, w_planes, eps):
+    x = _rows(x_planes, cols)
+    _require_cuda(x, "rms_norm")
+    code = dtype_code(x[0].dtype)
+    rows = x[0].shape[0]
+    y = [torch.empty_like(p) for p in x]
+    rstd = torch.empty(rows, len(x), dtype=compute_dtype(x[0].dtype), device=x[0].device)
+    w = None
+    if w_planes is not None:
+        w = [p.to(x[0].dtype).reshape(-1).contiguous() for p in w_planes]
+    px, k1 = _lib.pointer_array(x)
+    pw, k2 = _lib.pointer_array(w) if w is not None else (None, None)
+    py, k3 = _lib.pointer_array(y)
+    status = _lib.load().pk_rmsnorm_fwd(code, len(x) - 1, rows, cols, px, x[0].stride(0), pw,
+                                        len(w) if w is not None else 0, float(eps), py, y[0].stride(0),
+                                        rstd.data_ptr(), _stream(x[0].device))
+    _lib.check(status, "pk_rmsnorm_fwd")
+    return [t.view(x_planes[0].shape) for t in y], rstd
+
+
+def rmsnorm_bwd(x_planes, cols, w_planes, g_planes, rstd, want_dw):
+    x = _rows(x_planes, cols)
+    g = _rows([p.to(x[0].dtype).expand(x_planes[0].shape) for p in g_planes], cols)
+    code = dtype_code(x[0].dtype)
+    rows = x[0].shape[0]
+    dx = [torch.empty_like(p) for p in x]
+    w = None
+    if w_planes is not None:
+        w = [p.to(x[0].dtype).reshape(-1).contiguous() for p in w_planes]
+    dw = [torch.empty(cols, dtype=x[0].dtype, device=x[0].device) for _ in x] if want_dw else None
+    lib = _lib.load()
+    ws = None
+    if want_dw:
+        ws = torch.empty(lib.pk_rmsnorm_bwd_workspace_size(code, len(x) - 1, rows, cols), dtype=torch.uint8,
+                         device=x[0].device)
+    px, k1 = _lib.pointer_array(x)
+    pw, k2 = _lib.pointer_array(w) if w is not None else (None, None)
+    pg, k3 = _lib.pointer_array(g)
+    pdx, k4 = _lib.pointer_array(dx)
+    pdw, k5 = _lib.pointer_array(dw) if dw is not None else (None, None)
+    status = lib.pk_rmsnorm_bwd(code, len(x) - 1, rows, cols, px, x[0].stride(0), pw,
+                                len(w) if w is not None else 0, pg, g[0].stride(0), rstd.data_ptr(), pdx,
+                                dx[0].stride(0), pdw, ws.data_ptr() if ws is not None else None,
+                                ws.numel() if ws is not None else 0, _stream(x[0].device))
+    _lib.check(status, "pk_rmsnorm_bwd")
+    return [t.view(x_planes[0].shape) for t in dx], dw
+
+
+def softmax_fwd(x_planes, log):
+    """Softmax (or log-softmax) series along the last dimension."""
+    cols = x_planes[0].shape[-1]
+    x = _rows(x_planes, cols)
+    _require_cuda(x, "softmax")
+    y = [torch.empty_like(p) for p in x]
+    px, k1 = _lib.pointer_array(x)
+    py, k2 = _lib.pointer_array(y)
+    status = _lib.load().pk_softmax_fwd(dtype_code(x[0].dtype), len(x) - 1, x[0].shape[0], cols, px,
+                                        x[0].stride(0), 1 if log else 0, py, y[0].stride(0), _stream(x[0].device))
+    _lib.check(status, "pk_softmax_fwd")
+    return [t.view(x_planes[0].shape) for t in y]
+
+
+def softmax_bwd(g_planes, y_planes, log):
+    cols = y_planes[0].shape[-1]
+    y = _rows(y_planes, cols)
+    g = _rows([p.to(y[0].dtype).expand(y_planes[0].shape) for p in g_planes], cols)
+    _require_cuda((*y, *g), "softmax backward")
+    dx = [torch.empty_like(p) for p in y]
+    pg, k1 = _lib.pointer_array(g)
+    py, k2 = _lib.pointer_array(y)
+    pd, k3 = _lib.pointer_array(dx)
+    status = _lib.load().pk_softmax_bwd(dtype_code(y[0].dtype), len(y) - 1, y[0].shape[0], cols, pg,
+                                        g[0].stride(0), py, y[0].stride(0), 1 if log else 0, pd, dx[0].stride(0),
+                                        _stream(y[0].device))
+    _lib.check(status, "pk_softmax_bwd")
+    return [t.view(y_planes[0].shape) for t in dx]
+
+
+def cross_entropy_fwd(z_planes, target, ignore_index, softcap):
+    """Per-row loss series (float32, or float64 for float64 logits) and row statistics."""
+    rows, cols = z_planes[0].shape
+    z = z_planes if (_same_strides(z_planes) and z_planes[0].stride(-1) == 1) else [p.contiguous() for p in z_planes]
+    t = target.to(torch.int64).contiguous()
+    _require_cuda((*z, t), "cross_entropy")
+    cdt = compute_dtype(z[0].dtype)
+    loss = [torch.empty(rows, dtype=cdt, device=z[0].device) for _ in z]
+    stats = torch.empty(rows, len(z), dtype=cdt, device=z[0].device)
+    pz, k1 = _lib.pointer_array(z)
+    pl, k2 = _lib.pointer_array(loss)
+    status = _lib.load().pk_cross_entropy_fwd(dtype_code(z[0].dtype), len(z) - 1, rows, cols, pz, z[0].stride(0),
+                                              t.data_ptr(), int(ignore_index), float(softcap or 0.0), pl,
+                                              stats.data_ptr(), _stream(z[0].device))
+    _lib.check(status, "pk_cross_entropy_fwd")
+    return loss, stats
+
+
+def cross_entropy_bwd(z_planes, target, ignore_index, softcap, stats, g_planes):
+    rows, cols = z_planes[0].shape
+    z = z_planes if (_same_strides(z_planes) and z_planes[0].stride(-1) == 1) else [p.contiguous() for p in z_planes]
+    t = target.to(torch.int64).contiguous()
+    cdt = stats.dtype
+    g = [p.to(cdt).expand(rows).contiguous() for p in g_planes]
+    dz = [torch.empty(rows, cols, dtype=z[0].dtype, device=z[0].device) for _ in z]
+    pz, k1 = _lib.pointer_array(z)
+    pg, k2 = _lib.pointer_array(g)
+    pd, k3 = _lib.pointer_array(dz)
+    status = _lib.load().pk_cross_entropy_bwd(dtype_code(z[0].dtype), len(z) - 1, rows, cols, pz, z[0].stride(0),
+                                              t.data_ptr(), int(ignore_index), float(softcap or 0.0),
+                                              stats.data_ptr(), pg, pd, cols, _stream(z[0].device))
+    _lib.check(status, "pk_cross_entropy_bwd")
+    return dz

@@ -12,10 +12,14 @@ LIB_PATH = pathlib.Path(__file__).resolve().parent / "lib" / "libpolykern.so"
 
 # enum pk_dtype
 PK_F32, PK_F64, PK_BF16, PK_F16, PK_C128 = 0, 1, 2, 3, 4
+# enum pk_series_op
+OP = dict(copy=0, affine=1, exp=2, log=3, sqrt=4, rsqrt=5, reciprocal=6, tanh=7, sigmoid=8, gelu=9, powi=10,
+          add=32, mul=33, div=34, gelu_bwd=35, tanh_bwd=36, sigmoid_bwd=37)
 PK_MAX_PLANES = 16
 
 _i32, _i64, _sz, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p
 _pp = ctypes.POINTER(ctypes.c_void_p)
+_p64 = ctypes.POINTER(ctypes.c_int64)
 
 # name -> (restype, argtypes); every symbol declared in include/polykern.h
 SIGNATURES = {
@@ -30,6 +34,21 @@ SIGNATURES = {
                             _pp, _i64, _i64, _i64,
                             _pp, _i64, _i64,
                             _i32, _i32, _vp, _sz, _vp]),
+    "pk_series_map": (_i32, [_i32, _i32, _i32, _i32, _p64, _pp, _p64, _pp, _i32, _p64, _pp, _i32, _p64,
+                             ctypes.c_double, ctypes.c_double, _vp]),
+    "pk_series_reduce": (_i32, [_i32, _i32, _i64, _i64, _i64, _pp, _pp, ctypes.c_double, _vp]),
+    "pk_series_gather_rows": (_i32, [_i32, _i32, _i64, _i64, _vp, _pp, _i64, _i64, _pp, _vp]),
+    "pk_series_scatter_add_rows": (_i32, [_i32, _i32, _i64, _i64, _vp, _i64, _pp, _i64, _i64, _pp, _vp]),
+    "pk_rmsnorm_fwd": (_i32, [_i32, _i32, _i64, _i64, _pp, _i64, _pp, _i32, ctypes.c_double, _pp, _i64, _vp, _vp]),
+    "pk_rmsnorm_bwd_workspace_size": (_sz, [_i32, _i32, _i64, _i64]),
+    "pk_rmsnorm_bwd": (_i32, [_i32, _i32, _i64, _i64, _pp, _i64, _pp, _i32, _pp, _i64, _vp, _pp, _i64, _pp,
+                              _vp, _sz, _vp]),
+    "pk_softmax_fwd": (_i32, [_i32, _i32, _i64, _i64, _pp, _i64, _i32, _pp, _i64, _vp]),
+    "pk_softmax_bwd": (_i32, [_i32, _i32, _i64, _i64, _pp, _i64, _pp, _i64, _i32, _pp, _i64, _vp]),
+    "pk_cross_entropy_fwd": (_i32, [_i32, _i32, _i64, _i64, _pp, _i64, _vp, _i64, ctypes.c_double, _pp, _vp,
+                                    _vp]),
+    "pk_cross_entropy_bwd": (_i32, [_i32, _i32, _i64, _i64, _pp, _i64, _vp, _i64, ctypes.c_double, _vp, _pp,
+                                    _pp, _i64, _vp]),
     "pk_poly_gemm_noalloc": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64,
                                     _pp, _i64, _i64, _i64,
                                     _pp, _i64, _i64, _i64,
@@ -82,5 +101,10 @@ def profile_query(kernel):
 
 
 def pointer_array(tensors):
-    arr = (ctypes.c_void_p * len(tensors))(*[t.data_ptr() for t in tensors])
+    arr = (ctypes.c_void_p * len(tensors))(*[t.data_ptr() if t is not None else None for t in tensors])
     return ctypes.cast(arr, _pp), arr
+
+
+def int64_array(values):
+    arr = (ctypes.c_int64 * max(len(values), 1))(*values)
+    return ctypes.cast(arr, _p64), arr

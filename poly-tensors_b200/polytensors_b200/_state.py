@@ -1,0 +1,9 @@
+"""Context-local switches of the PolyTensor API (the reference's ContextVars)."""
+
+import contextvars
+
+retention_scopes = contextvars.ContextVar("polytensor_retention_scopes", default=())
+plain_range = contextvars.ContextVar("polytensor_plain_range", default=False)
+fused_attention = contextvars.ContextVar("polytensor_fused_attention", default=True)
+fused_cross_entropy = contextvars.ContextVar("polytensor_fused_cross_entropy", default=True)
+coefficient_autograd = contextvars.ContextVar("polytensor_coefficient_autograd", default=False)

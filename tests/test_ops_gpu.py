@@ -1,0 +1,235 @@
+"""Parity of the series kernels, reached through the PolyTensor API, with the reference's
+own outputs (golden vectors) and the CPU oracle.
+
+Tolerances, per coefficient plane (max |got - want| / max |want|): float64 1e-10,
+float32 1e-4."""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from gpu_util import assert_close, coeffs, cuda, poly, series
+from oracle import polyref as ref
+
+pytestmark = pytest.mark.gpu
+
+F64, F32 = 1e-10, 1e-4
+
+
+def test_elementwise_series_ops_golden(golden):
+    from polytensors_b200 import PolyTensor
+
+    g = golden("series_ops_f64_n5")
+    x, xp, y, yp = (poly(g[k]) for k in ("X", "Xp", "Y", "Yp"))
+    with PolyTensor.plain_range():
+        got = {
+            "mul": x * y, "div": x / yp, "add": x + 2.5 * y, "exp": torch.exp(x), "log": torch.log(xp),
+            "rsqrt": torch.rsqrt(xp), "tanh": torch.tanh(x), "sigmoid": torch.sigmoid(x), "gelu": F.gelu(x),
+            "softmax": torch.softmax(x, dim=-1), "log_softmax": torch.log_softmax(x, dim=-1),
+            "sum1": x.sum(dim=1), "mean0": x.mean(dim=0), "square": x.square(),
+        }
+    for key, value in got.items():
+        assert_close(coeffs(value), g[key], F64, key)
+
+
+@pytest.mark.parametrize("n", [1, 3, 8])
+def test_elementwise_f32_against_oracle(n):
+    from polytensors_b200 import PolyTensor
+
+    X = series((64, 257), n, 1, torch.float32)
+    Y = series((64, 257), n, 2, torch.float32)
+    Yp = [Y[0].abs() + 0.5] + Y[1:]
+    X64, Y64, Yp64 = ([p.double() for p in s] for s in (X, Y, Yp))
+    with PolyTensor.plain_range():
+        x, y, yp = poly(X), poly(Y), poly(Yp)
+        checks = [
+            (x * y, ref.cauchy(X64, Y64)), (x / yp, ref.series_quotient(X64, Yp64)),
+            (torch.exp(x), ref.series_exp(X64)), (torch.tanh(x), ref.activation(X64, "tanh")),
+            (torch.sigmoid(x), ref.activation(X64, "sigmoid")), (F.gelu(x), ref.gelu(X64)),
+            (torch.rsqrt(yp), ref.series_rsqrt(Yp64)), (torch.log(yp), ref.series_log(Yp64)),
+            (x.sum(dim=0), [p.sum(dim=0) for p in X64]), (x.mean(), [p.mean() for p in X64]),
+            (torch.softmax(x, dim=0), ref.softmax_family(X64, 0)[0]),
+            (x ** 3, ref.cauchy(ref.cauchy(X64, X64), X64)),
+            (1 - 0.5 * x, [1 - 0.5 * X64[0]] + [-0.5 * p for p in X64[1:]]),
+        ]
+    for i, (got, want) in enumerate(checks):
+        assert_close(coeffs(got), want, F32, f"check {i}")
+
+
+def test_broadcast_and_inplace_sgd_update():
+    from polytensors_b200 import PolyTensor
+
+    X = series((8, 5), 3, 3, torch.float32)
+    b = series((5,), 3, 4, torch.float32)
+    with PolyTensor.plain_range():
+        x, bias = poly(X), poly(b)
+        assert_close(coeffs(x + bias), [p + q for p, q in zip(X, b)], 1e-6)
+        w = poly(X)
+        g = poly(series((8, 5), 3, 5, torch.float32))
+        planes_before = [p.data_ptr() for p in w.coeffs]
+        w.add_(g, alpha=-0.1)
+        assert [p.data_ptr() for p in w.coeffs] == planes_before
+        G = series((8, 5), 3, 5, torch.float32)
+        assert_close(coeffs(w), [p - 0.1 * q for p, q in zip(X, G)], 1e-6)
+
+
+def test_matmul_backward_golden(golden):
+    from polytensors_b200 import PolyTensor
+
+    for name in ("matmul_f64_n2", "bmm_f64_n3"):
+        g = golden(name)
+        with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+            a, b = poly(g["A"], requires_grad=True), poly(g["B"], requires_grad=True)
+            c = a @ b
+            c.backward(poly(g["G"]))
+            assert_close(coeffs(c), g["C"], F64, name)
+            assert_close(coeffs(a.grad), g["dA"], F64, name + " dA")
+            assert_close(coeffs(b.grad), g["dB"], F64, name + " dB")
+
+
+@pytest.mark.parametrize("name,tol", [("rmsnorm_f64_n3", F64), ("rmsnorm_f32_n3", F32)])
+def test_rmsnorm_golden(golden, name, tol):
+    from polytensors_b200 import PolyTensor
+
+    g = golden(name)
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        x, w = poly(g["X"], requires_grad=True), poly(g["W"], requires_grad=True)
+        y = F.rms_norm(x, (32,), w)
+        y.backward(poly(g["G"]))
+        assert_close(coeffs(y), g["Y"], tol, "y")
+        assert_close(coeffs(x.grad), g["dX"], tol * 10, "dx")
+        assert_close(coeffs(w.grad), g["dW"], tol * 10, "dw")
+
+
+def test_rmsnorm_f32_config_width():
+    from polytensors_b200 import PolyTensor
+
+    n, H = 4, 4096
+    X = series((64, H), n, 6, torch.float32)
+    w0 = 1 + 0.02 * torch.randn(H, generator=torch.Generator().manual_seed(7))
+    W = [w0] + [torch.zeros(H) for _ in range(n)]
+    G = series((64, H), n, 8, torch.float32)
+    X64, W64, G64 = ([p.double() for p in s] for s in (X, W, G))
+    fn = lambda Xs, Ws: ref.rms_norm(Xs, (H,), Ws)
+    want_y = fn(X64, W64)
+    want_dx, want_dw = ref.series_vjp(fn, [X64, W64], G64)
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        x, w = poly(X, requires_grad=True), poly(W, requires_grad=True)
+        y = F.rms_norm(x, (H,), w)
+        y.backward(poly(G))
+    assert_close(coeffs(y), want_y, F32, "y")
+    assert_close(coeffs(x.grad), want_dx, F32, "dx")
+    assert_close(coeffs(w.grad), want_dw, F32, "dw")
+
+
+def test_gelu_golden(golden):
+    from polytensors_b200 import PolyTensor
+
+    g = golden("gelu_f64_n4")
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        x = poly(g["X"], requires_grad=True)
+        y = F.gelu(x)
+        y.backward(poly(g["G"]))
+    assert_close(coeffs(y), g["Y"], F64)
+    assert_close(coeffs(x.grad), g["dX"], F64)
+
+
+def test_cross_entropy_golden(golden):
+    from polytensors_b200 import PolyTensor
+
+    g = golden("ce_f64_n4")
+    n = len(g["X"]) - 1
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        Z = PolyTensor((torch.tensor(0.0, dtype=torch.float64, device="cuda"), 1.0), degree=n)
+        x = poly(g["X"], requires_grad=True)
+        ce = F.cross_entropy(x, g["target"].cuda())
+        loss = ce * (1 - 0.5 * Z)
+        loss.backward()
+    assert_close(coeffs(ce), g["CE"], F64, "ce")
+    assert_close(coeffs(loss), g["loss"], F64, "loss")
+    assert_close(coeffs(x.grad), g["dX"], F64, "dx")
+    g = golden("ce_none_f64_n4")
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        x = poly(g["X"], requires_grad=True)
+        per_row = F.cross_entropy(x, g["target"].cuda(), reduction="none")
+        per_row.backward(poly(g["G"]))
+    assert_close(coeffs(per_row), g["CE"], F64, "ce none")
+    assert_close(coeffs(x.grad), g["dX"], F64, "dx none")
+
+
+def test_cross_entropy_unfused_path_matches(golden):
+    from polytensors_b200 import PolyTensor
+
+    g = golden("ce_f64_n4")
+    with PolyTensor.plain_range(), PolyTensor.fused_cross_entropy(False), PolyTensor.retain_wrappers():
+        x = poly(g["X"], requires_grad=True)
+        ce = F.cross_entropy(x, g["target"].cuda())
+        ce.backward()
+    assert_close(coeffs(ce), g["CE"], F64, "ce")
+    lam = [torch.tensor(1.0, dtype=torch.float64)] + [torch.tensor(0.0, dtype=torch.float64)] * (len(g["X"]) - 1)
+    want = ref.cross_entropy_backward(g["X"], g["target"], lam)
+    assert_close(coeffs(x.grad), want, F64, "dx")
+
+
+def test_cross_entropy_f32_vocab_and_softcap():
+    from polytensors_b200 import PolyTensor
+
+    n, N, C = 4, 96, 32000
+    X = series((N, C), n, 9, torch.float32)
+    target = torch.randint(0, C, (N,), generator=torch.Generator().manual_seed(10))
+    target[::7] = -100
+    X64 = [p.double() for p in X]
+    want = ref.cross_entropy(X64, target)
+    lam = [torch.tensor(1.0, dtype=torch.float64)] + [torch.tensor(0.0, dtype=torch.float64)] * n
+    want_dx = ref.cross_entropy_backward(X64, target, lam)
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        x = poly(X, requires_grad=True)
+        ce = F.cross_entropy(x, target.cuda())
+        ce.backward()
+    assert_close(coeffs(ce), want, F32, "ce")
+    assert_close(coeffs(x.grad), want_dx, F32, "dx")
+    # softcap: the cap is a series tanh applied before the loss
+    cap = 30.0
+    capped = [cap * t for t in ref.activation([p / cap for p in X64], "tanh")]
+    want = ref.cross_entropy(capped, target, reduction="sum")
+    fn = lambda Xs: ref.cross_entropy([cap * t for t in ref.activation([p / cap for p in Xs], "tanh")], target,
+                                      reduction="sum")
+    want_dx = ref.series_vjp(fn, [X64], lam)[0]
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        x = poly(X, requires_grad=True)
+        ce = PolyTensor.cross_entropy(x, target.cuda(), softcap=cap, reduction="sum")
+        ce.backward()
+    assert_close(coeffs(ce), want, F32, "softcap ce")
+    assert_close(coeffs(x.grad), want_dx, F32, "softcap dx")
+
+
+@pytest.mark.parametrize("name,kw", [("attn_causal_f64_n3", dict(is_causal=True)),
+                                     ("attn_full_f64_n3", dict(scale=0.3))])
+def test_attention_golden(golden, name, kw):
+    from polytensors_b200 import PolyTensor
+
+    g = golden(name)
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        q, k, v = (poly(g[key], requires_grad=True) for key in ("Q", "K", "V"))
+        o = F.scaled_dot_product_attention(q, k, v, **kw)
+        o.backward(poly(g["G"]))
+    assert_close(coeffs(o), g["O"], F64, "o")
+    assert_close(coeffs(q.grad), g["dQ"], 1e-9, "dq")
+    assert_close(coeffs(k.grad), g["dK"], 1e-9, "dk")
+    assert_close(coeffs(v.grad), g["dV"], 1e-9, "dv")
+
+
+def test_embedding_forward_backward():
+    from polytensors_b200 import PolyTensor
+
+    n, V, d = 3, 50, 16
+    W = series((V, d), n, 11, torch.float32)
+    ids = torch.randint(0, V, (4, 7), generator=torch.Generator().manual_seed(12))
+    G = series((4, 7, d), n, 13, torch.float32)
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        w = poly(W, requires_grad=True)
+        e = F.embedding(ids.cuda(), w)
+        e.backward(poly(G))
+    assert_close(coeffs(e), [p[ids] for p in W], 1e-7)
+    want = [torch.zeros(V, d).index_add_(0, ids.reshape(-1), g.reshape(-1, d)) for g in G]
+    assert_close(coeffs(w.grad), want, 1e-6)

@@ -1,0 +1,149 @@
+"""Host-side behaviour of the PolyTensor mirror that needs no GPU: construction rules,
+context managers, retention scopes, error behaviour (mirrors the reference's
+tests/test_tensor.py and tests/test_retention.py where they do not compute)."""
+
+import pytest
+import torch
+
+import polytensors_b200
+from polytensors_b200 import PolyTensor
+
+
+def test_only_public_export():
+    assert polytensors_b200.__all__ == ["PolyTensor"]
+
+
+def test_validation():
+    with pytest.raises(ValueError, match="at least one"):
+        PolyTensor([])
+    for degree in (-1, -3):
+        with pytest.raises(ValueError):
+            PolyTensor([1.0], degree=degree)
+    for degree in (True, 1.2):
+        with pytest.raises(TypeError):
+            PolyTensor([1.0], degree=degree)
+    with pytest.raises(ValueError, match="at least"):
+        PolyTensor([1.0, 2.0], degree=0)
+    with pytest.raises(TypeError, match="floating-point"):
+        PolyTensor([torch.tensor(1)])
+    with pytest.raises(ValueError, match="same device"):
+        PolyTensor([torch.tensor(1.0), torch.empty((), device="meta")])
+    with pytest.raises(TypeError, match="nested"):
+        PolyTensor([PolyTensor([1.0])])
+
+
+def test_integer_literals_and_constant_padding():
+    x = PolyTensor([1, 2], degree=4)
+    assert x.dtype == torch.get_default_dtype()
+    assert [c.item() for c in x.coeffs] == [1, 2, 0, 0, 0]
+    constant = PolyTensor.constant(2, degree=3)
+    assert [c.item() for c in constant.coeffs] == [2, 0, 0, 0]
+    with pytest.raises(ValueError, match="no tangent"):
+        _ = PolyTensor([1.0]).tangent
+
+
+def test_complex_direction_dtypes():
+    x = PolyTensor([torch.tensor(1.0, dtype=torch.float64), 2 + 3j], degree=3)
+    assert x.dtype == torch.float64
+    assert all(c.dtype == torch.complex128 for c in x.coeffs[1:])
+    assert x.tangent == 2 + 3j
+
+
+def test_overlapping_orders_get_independent_storage():
+    zero = torch.tensor(0.0)
+    x = PolyTensor([torch.tensor(1.0), zero, zero], degree=2)
+    assert not torch._C._overlaps(x.coeffs[1], x.coeffs[2])
+
+
+def test_constructor_broadcasting_materialises_coefficients():
+    x = PolyTensor((torch.tensor([1.0, 2.0]), torch.tensor(1.0)), degree=2)
+    assert all(c.shape == (2,) for c in x.coeffs)
+    assert x.coeffs[1].stride() == (1,)
+
+
+def test_python_direction_does_not_round_through_float32():
+    direction = 0.12345678912345678
+    x = PolyTensor((torch.tensor(0.0, dtype=torch.float64), direction))
+    assert x.tangent.item() == direction
+    z = PolyTensor((torch.tensor(0.0, dtype=torch.float64), complex(direction, direction)))
+    assert z.tangent.item() == complex(direction, direction)
+
+
+def test_backward_requires_explicit_gradient_for_vector():
+    x = PolyTensor([torch.tensor([1.0, 2.0])], degree=1, requires_grad=True)
+    with pytest.raises(RuntimeError, match="scalar"):
+        x.backward()
+
+
+def test_unimplemented_operation_fails_explicitly():
+    x = PolyTensor([torch.eye(2)], degree=1)
+    with pytest.raises(NotImplementedError, match="PolyTensor"):
+        torch.linalg.det(x)
+
+
+def test_series_arithmetic_has_no_cpu_fallback():
+    x = PolyTensor((torch.randn(3), torch.randn(3)), degree=2)
+    for op in (lambda: x * x, lambda: torch.exp(x), lambda: x.sum(), lambda: x @ x):
+        with pytest.raises(NotImplementedError, match="CUDA"):
+            op()
+
+
+def test_views_are_per_coefficient():
+    x = PolyTensor((torch.arange(6.0).view(2, 3), torch.ones(2, 3)), degree=1)
+    t = x.t()
+    assert t.shape == (3, 2) and t.degree == 1
+    assert torch.equal(t.coeffs[0], torch.arange(6.0).view(2, 3).t())
+    v = x.view(6)
+    assert v.shape == (6,) and torch.equal(v.coeffs[1], torch.ones(6))
+    s = x[1]
+    assert s.shape == (3,) and torch.equal(s.value, torch.tensor([3.0, 4.0, 5.0]))
+
+
+def test_degree_mismatch_raises():
+    a = PolyTensor((torch.ones(2),), degree=1)
+    b = PolyTensor((torch.ones(2),), degree=2)
+    with pytest.raises(ValueError, match="same degree"):
+        torch.cat([a, b])
+
+
+def test_inplace_update_of_ordinary_tensor_with_polytensor_raises():
+    a = torch.zeros(2)
+    b = PolyTensor((torch.ones(2),), degree=1)
+    with pytest.raises(RuntimeError, match="regular Tensor in-place"):
+        a.add_(b)
+
+
+def test_retention_scopes_nest_and_isolate():
+    x = PolyTensor((torch.randn(4, 3), torch.randn(4, 3)), degree=1)
+    with PolyTensor.retain_wrappers() as outer:
+        x.t()
+        before = len(outer)
+        assert before >= 1
+        with PolyTensor.retain_wrappers(isolated=True) as inner:
+            x.t()
+            assert len(inner) >= 1
+        assert len(inner) == 0 and len(outer) == before
+        with PolyTensor.retain_wrappers() as nested:
+            x.t()
+            assert len(nested) >= 1
+        assert len(outer) > before
+    assert len(outer) == 0
+
+
+def test_context_managers_are_context_local():
+    from polytensors_b200 import _state
+
+    assert not _state.plain_range.get()
+    with PolyTensor.plain_range():
+        assert _state.plain_range.get()
+        with PolyTensor.fused_attention(False), PolyTensor.fused_cross_entropy(False):
+            assert not _state.fused_attention.get() and not _state.fused_cross_entropy.get()
+        assert _state.fused_attention.get() and _state.fused_cross_entropy.get()
+    assert not _state.plain_range.get()
+
+
+def test_coefficient_autograd_mode_raises_explicitly():
+    x = PolyTensor((torch.randn(2), torch.randn(2)), degree=1)
+    with PolyTensor.coefficient_autograd():
+        with pytest.raises(NotImplementedError, match="coefficient_autograd"):
+            x.t()
