@@ -221,6 +221,24 @@ PK_API int pk_cross_entropy_bwd(int dtype, int degree, int64_t rows, int64_t col
                                 const void* const* g, void* const* dz, int64_t dz_rs, void* stream);
 
 /*
+ * Attention score kernels for series attention built from pk_poly_gemm contractions
+ * (the reference's decomposition, src/polytensors/_decompositions.py:28-43, evaluated a
+ * block of heads at a time).  Rows are score rows of (rows / q_len) matrices; row r is query
+ * r % q_len; with causal != 0, keys beyond query + causal_shift are masked out.
+ * pk_attn_probs: P = softmax(scale * scores) as series (src/polytensors/_plain.py:262-273),
+ *   stats [rows][degree+1] = (lse_0, logz_1..n), float (double for PK_F64).
+ * pk_attn_dscores: d scores = scale * P (*) (dP - dsum) from the probabilities P of pk_attn_probs,
+ *   dsum [rows][degree+1] = sum_d dO (*) O (src/polytensors/_plain.py:342-347); masked entries
+ *   (P = 0) get zero.  dscores may alias dprobs.
+ */
+PK_API int pk_attn_probs(int dtype, int degree, int64_t rows, int64_t cols, int64_t q_len,
+                         const void* const* scores, int64_t s_rs, double scale, int causal,
+                         int64_t causal_shift, void* const* probs, int64_t p_rs, void* stats, void* stream);
+PK_API int pk_attn_dscores(int dtype, int degree, int64_t rows, int64_t cols,
+                           const void* const* probs, int64_t p_rs, const void* const* dprobs, int64_t dp_rs,
+                           const void* dsum, double scale, void* const* dscores, int64_t ds_rs, void* stream);
+
+/*
  * pk_poly_gemm without a workspace argument, for callers that cannot allocate device
  * memory (a plugin host that owns every allocation, a process that must not grow its
  * device footprint after start-up, code with no allocator to link).  The scratch comes

@@ -31,7 +31,13 @@ struct SoftmaxParams {
     const void* y[PK_MAX_PLANES];   // backward: forward output
     const void* g[PK_MAX_PLANES];   // backward: incoming gradient (per element, or per row for CE)
     void* out[PK_MAX_PLANES];
-    void* stats;                    // CE: [rows][np] (lse_0, logz_1..n), compute type
+    void* stats;                    // CE / attention: [rows][np] (lse_0, logz_1..n), compute type
+    // attention score rows: row r is query (r % q_len) of its matrix; entries scale * x,
+    // masked (causal: key > query + causal_shift) entries excluded
+    double scale;
+    int causal;
+    int64_t q_len, causal_shift;
+    const void* dsum;               // attention backward: [rows][np] sum_d dO (*) O, compute type
 };
 
 template <int NP, typename T, typename C>
@@ -210,7 +216,90 @@ __global__ void __launch_bounds__(512) ce_bwd_kernel(const SoftmaxParams p) {
     }
 }
 
-enum { SM_FWD = 0, SM_BWD = 1, CE_FWD = 2, CE_BWD = 3 };
+// Attention probabilities from raw score series x = Q K^T (all planes):  P = softmax(scale * x)
+// along keys with causal masking, written as series; stats receive (lse_0, logz_1..n) per row.
+template <typename T, int NP>
+__global__ void __launch_bounds__(512) attn_probs_kernel(const SoftmaxParams p) {
+    using C = typename Compute<T>::type;
+    __shared__ C scratch[16 * (NP + 1)];
+    const C sc = C(p.scale);
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        const int64_t xb = row * p.x_rs, yb = row * p.y_rs;
+        const int64_t limit = p.causal ? (row % p.q_len) + p.causal_shift : p.cols - 1;  // last admissible key
+        C m = -INFINITY, S[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) S[k] = C(0);
+        for (int64_t c = threadIdx.x; c < p.cols && c <= limit; c += blockDim.x) {
+            C x[NP];
+            load_row_elem<NP, T, C>(p.x, p.np, xb + c, x);
+#pragma unroll
+            for (int k = 0; k < NP; ++k) x[k] *= sc;
+            lse_accumulate<NP, C>(m, S, x);
+        }
+        block_lse_combine<NP, C>(m, S, scratch);
+        C lse[NP];
+        const bool empty = !(S[0] > C(0));
+        if (empty) {
+#pragma unroll
+            for (int k = 0; k < NP; ++k) lse[k] = C(0);
+            lse[0] = INFINITY;  // a row without admissible keys: P = 0 (and 0 output)
+        } else {
+            lse_finish<NP, C>(m, S, lse);
+        }
+        if (threadIdx.x == 0) {
+#pragma unroll
+            for (int k = 0; k < NP; ++k)
+                if (k < p.np) static_cast<C*>(p.stats)[row * p.np + k] = lse[k];
+        }
+        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
+            C P[NP];
+            if (c <= limit && !empty) {
+                C x[NP];
+                load_row_elem<NP, T, C>(p.x, p.np, xb + c, x);
+                P[0] = x[0] * sc - lse[0];
+#pragma unroll
+                for (int k = 1; k < NP; ++k) P[k] = x[k] * sc - lse[k];
+                s_exp<NP, C>(P, P);
+            } else {
+#pragma unroll
+                for (int k = 0; k < NP; ++k) P[k] = C(0);
+            }
+#pragma unroll
+            for (int k = 0; k < NP; ++k)
+                if (k < p.np) static_cast<T*>(p.out[k])[yb + c] = from_c<T>(P[k]);
+        }
+    }
+}
+
+// Score gradient of attention, the series form of the softmax backward
+// (src/polytensors/_plain.py:342-347) through the score scaling:
+//   d scores = scale * P (*) (dP - dsum_row),   dsum_row = sum_d dO (*) O.
+// P arrives in p.y, dP in p.g, the output goes to p.out (may alias p.g); masked entries
+// have P = 0 and so get a zero gradient.
+template <typename T, int NP>
+__global__ void __launch_bounds__(256) attn_dscores_kernel(const SoftmaxParams p) {
+    using C = typename Compute<T>::type;
+    const C sc = C(p.scale);
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        const int64_t yb = row * p.y_rs, gb = row * p.g_rs, ob = row * p.x_rs;
+        C ds[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) ds[k] = k < p.np ? static_cast<const C*>(p.dsum)[row * p.np + k] : C(0);
+        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
+            C P[NP], g[NP], r[NP];
+            load_row_elem<NP, T, C>(p.y, p.np, yb + c, P);
+            load_row_elem<NP, T, C>(p.g, p.np, gb + c, g);
+#pragma unroll
+            for (int k = 0; k < NP; ++k) g[k] -= ds[k];
+            s_mul<NP, C>(P, g, r);
+#pragma unroll
+            for (int k = 0; k < NP; ++k)
+                if (k < p.np) static_cast<T*>(p.out[k])[ob + c] = from_c<T>(r[k] * sc);
+        }
+    }
+}
+
+enum { SM_FWD = 0, SM_BWD = 1, CE_FWD = 2, CE_BWD = 3, ATTN_P = 4, ATTN_DS = 5 };
 
 static int row_threads(int64_t cols) { return cols >= 4096 ? 512 : (cols >= 1024 ? 256 : 128); }
 
@@ -222,6 +311,8 @@ static void launch_rows(int which, const SoftmaxParams& p, cudaStream_t s) {
         case SM_FWD: softmax_fwd_kernel<T, NP><<<grid, threads, 0, s>>>(p); break;
         case SM_BWD: softmax_bwd_kernel<T, NP><<<grid, threads, 0, s>>>(p); break;
         case CE_FWD: ce_fwd_kernel<T, NP><<<grid, threads, 0, s>>>(p); break;
+        case ATTN_P: attn_probs_kernel<T, NP><<<grid, threads, 0, s>>>(p); break;
+        case ATTN_DS: attn_dscores_kernel<T, NP><<<grid, std::min(threads, 256), 0, s>>>(p); break;
         default: ce_bwd_kernel<T, NP><<<grid, threads, 0, s>>>(p); break;
     }
 }
@@ -348,6 +439,51 @@ int pk_cross_entropy_bwd(int dtype, int degree, int64_t rows, int64_t cols, cons
         p.out[k] = dz[k];
     }
     return dispatch_rows(CE_BWD, dtype, p, stream, "cross_entropy_bwd");
+}
+
+int pk_attn_probs(int dtype, int degree, int64_t rows, int64_t cols, int64_t q_len, const void* const* scores,
+                  int64_t s_rs, double scale, int causal, int64_t causal_shift, void* const* probs, int64_t p_rs,
+                  void* stats, void* stream) {
+    if (int rc = check_common(degree, rows, cols, "pk_attn_probs")) return rc;
+    if (!stats || q_len <= 0) return fail(PK_ERR_ARG, "pk_attn_probs: null stats or bad q_len");
+    SoftmaxParams p{};
+    p.np = degree + 1;
+    p.rows = rows;
+    p.cols = cols;
+    p.x_rs = s_rs;
+    p.y_rs = p_rs;
+    p.scale = scale;
+    p.causal = causal;
+    p.q_len = q_len;
+    p.causal_shift = causal_shift;
+    p.stats = stats;
+    for (int k = 0; k < p.np; ++k) {
+        p.x[k] = scores[k];
+        p.out[k] = probs[k];
+    }
+    return dispatch_rows(ATTN_P, dtype, p, stream, "attn_probs");
+}
+
+int pk_attn_dscores(int dtype, int degree, int64_t rows, int64_t cols, const void* const* probs, int64_t p_rs,
+                    const void* const* dprobs, int64_t dp_rs, const void* dsum, double scale, void* const* dscores,
+                    int64_t ds_rs, void* stream) {
+    if (int rc = check_common(degree, rows, cols, "pk_attn_dscores")) return rc;
+    if (!dsum) return fail(PK_ERR_ARG, "pk_attn_dscores: null dsum");
+    SoftmaxParams p{};
+    p.np = degree + 1;
+    p.rows = rows;
+    p.cols = cols;
+    p.y_rs = p_rs;
+    p.g_rs = dp_rs;
+    p.x_rs = ds_rs;
+    p.scale = scale;
+    p.dsum = dsum;
+    for (int k = 0; k < p.np; ++k) {
+        p.y[k] = probs[k];
+        p.g[k] = dprobs[k];
+        p.out[k] = dscores[k];
+    }
+    return dispatch_rows(ATTN_DS, dtype, p, stream, "attn_dscores");
 }
 
 }  // extern "C"

@@ -49,6 +49,10 @@ SIGNATURES = {
                                     _vp]),
     "pk_cross_entropy_bwd": (_i32, [_i32, _i32, _i64, _i64, _pp, _i64, _vp, _i64, ctypes.c_double, _vp, _pp,
                                     _pp, _i64, _vp]),
+    "pk_attn_probs": (_i32, [_i32, _i32, _i64, _i64, _i64, _pp, _i64, ctypes.c_double, _i32, _i64, _pp, _i64,
+                             _vp, _vp]),
+    "pk_attn_dscores": (_i32, [_i32, _i32, _i64, _i64, _pp, _i64, _pp, _i64, _vp, ctypes.c_double, _pp, _i64,
+                               _vp]),
     "pk_poly_gemm_noalloc": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64,
                                     _pp, _i64, _i64, _i64,
                                     _pp, _i64, _i64, _i64,

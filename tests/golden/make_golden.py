@@ -197,9 +197,11 @@ def tiny_transformer_config():
     return dict(layers=2, d=16, heads=2, mlp=64, vocab=50, seq=8, batch=2, degree=3, steps=3, lr=0.1, lam=0.5)
 
 
-def case_tiny_transformer():
+def case_tiny_transformer(dtype=torch.float32, name="tiny_transformer_f32_n3"):
     """A reduced decoder step loop in the layout of the benchmark transformer: RMSNorm, separate
-    q/k/v linears, causal SDPA, GELU MLP, untied head, loss CE*(1 - lam*Z), SGD(foreach=False)."""
+    q/k/v linears, causal SDPA, GELU MLP, untied head, loss CE*(1 - lam*Z), SGD(foreach=False).
+    The float64 run starts from the float32 initial values and serves as the accuracy yardstick
+    for float32 results (small coefficients of the loss lose many digits to float32 rounding)."""
     cfg = tiny_transformer_config()
     n, d, H, V, T, Bt = cfg["degree"], cfg["d"], cfg["heads"], cfg["vocab"], cfg["seq"], cfg["batch"]
     g = torch.Generator().manual_seed(100)
@@ -208,7 +210,7 @@ def case_tiny_transformer():
     def param(name, *shape, ones=False):
         base = torch.ones(*shape) if ones else 0.02 * torch.randn(*shape, generator=g)
         init[name] = base.clone()
-        return torch.nn.Parameter(PolyTensor((base,), degree=n))
+        return torch.nn.Parameter(PolyTensor((base.to(dtype),), degree=n))
 
     P = {"emb": param("emb", V, d)}
     for l in range(cfg["layers"]):
@@ -243,8 +245,7 @@ def case_tiny_transformer():
                 loss.backward()
                 opt.step()
                 losses.append(coeffs(loss))
-    save("tiny_transformer_f32_n3", config=cfg, init=init, ids=ids, losses=losses,
-         final={k: coeffs(p) for k, p in P.items()})
+    save(name, config=cfg, init=init, ids=ids, losses=losses, final={k: coeffs(p) for k, p in P.items()})
 
 
 if __name__ == "__main__":
@@ -263,3 +264,4 @@ if __name__ == "__main__":
     case_readme_fit(plain=False)
     case_readme_fit(plain=True)
     case_tiny_transformer()
+    case_tiny_transformer(torch.float64, "tiny_transformer_f64_n3")

@@ -233,3 +233,35 @@ def test_embedding_forward_backward():
     assert_close(coeffs(e), [p[ids] for p in W], 1e-7)
     want = [torch.zeros(V, d).index_add_(0, ids.reshape(-1), g.reshape(-1, d)) for g in G]
     assert_close(coeffs(w.grad), want, 1e-6)
+
+
+@pytest.mark.parametrize("dtype,tol,causal", [(torch.float32, F32, True), (torch.float32, F32, False),
+                                              (torch.float64, F64, True), (torch.bfloat16, 3e-2, True)])
+def test_attention_against_oracle(dtype, tol, causal):
+    from polytensors_b200 import PolyTensor
+
+    n, shape = 3, (2, 3, 200, 64)
+    Q, Kp, V, G = (series(shape, n, s, dtype) for s in (21, 22, 23, 24))
+    ref64 = [[p.double() for p in s] for s in (Q, Kp, V, G)]
+    fn = lambda q, k, v: ref.attention(q, k, v, is_causal=causal)
+    want_o = fn(*ref64[:3])
+    want = ref.series_vjp(fn, ref64[:3], ref64[3])
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        q, k, v = (poly(s, requires_grad=True) for s in (Q, Kp, V))
+        o = F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+        o.backward(poly(G))
+    assert_close(coeffs(o), want_o, tol, "o")
+    for name, t, w in (("dq", q, want[0]), ("dk", k, want[1]), ("dv", v, want[2])):
+        assert_close(coeffs(t.grad), w, tol * (10 if dtype == torch.float64 else 1), name)
+
+
+def test_attention_fused_and_decomposed_paths_agree():
+    from polytensors_b200 import PolyTensor
+
+    n, shape = 2, (1, 2, 96, 32)
+    Q, Kp, V = (series(shape, n, s, torch.float64) for s in (31, 32, 33))
+    outs = []
+    for enabled in (True, False):
+        with PolyTensor.plain_range(), PolyTensor.fused_attention(enabled):
+            outs.append(coeffs(F.scaled_dot_product_attention(poly(Q), poly(Kp), poly(V), is_causal=True)))
+    assert_close(outs[0], outs[1], F64)

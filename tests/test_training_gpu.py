@@ -69,12 +69,23 @@ def run_tiny_transformer(g, device="cuda"):
     return P, losses
 
 
+def _as_accurate(got, ref32, ref64, what):
+    """Per plane: |got - ref64| <= max(1e-4 * max|ref64|, 3 * |ref32 - ref64|), i.e. the float32
+    GPU result is within the float32 tolerance of the float64 reference, or at least as accurate
+    (within 3x) as the reference's own float32 result."""
+    for k, (g, a, b) in enumerate(zip(got, ref32, ref64)):
+        g, a, b = g.double(), a.double(), b.double()
+        err = (g - b).abs().max().item()
+        ref_err = (a - b).abs().max().item()
+        scale = b.abs().max().item()
+        assert err <= max(1e-4 * scale, 3 * ref_err), (what, k, err, ref_err, scale)
+
+
 def test_tiny_transformer_matches_reference(golden):
-    g = golden("tiny_transformer_f32_n3")
-    P, losses = run_tiny_transformer(g)
-    for step, (got, want) in enumerate(zip(losses, g["losses"])):
-        assert_close(got, want, 1e-4, f"loss step {step}")
-    for name, want in g["final"].items():
+    g32, g64 = golden("tiny_transformer_f32_n3"), golden("tiny_transformer_f64_n3")
+    P, losses = run_tiny_transformer(g32)
+    for step, got in enumerate(losses):
+        _as_accurate(got, g32["losses"][step], g64["losses"][step], f"loss step {step}")
+    for name in g32["final"]:
         got = [c.detach().cpu() for c in P[name].coeffs]
-        # zero-initialised higher planes: compare against the plane max-norm of the update
-        assert_close(got, want, 2e-4, name)
+        _as_accurate(got, g32["final"][name], g64["final"][name], name)
