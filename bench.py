@@ -240,6 +240,268 @@ def run_matmul(args, cfg, rank, world, device):
 
 
 # ------------------------------------------------------------------------------------
+# secondary workloads (configs[2..4] and the configs[1] sweep); not the driver's default
+
+def _series_poly(shape, n, seed, dtype, device, requires_grad=False):
+    from polytensors_b200 import PolyTensor
+
+    planes = [p.to(device) for p in make_series(shape, n, seed, dtype)]
+    return PolyTensor(tuple(planes), requires_grad=requires_grad)
+
+
+def _timed(fn, steps, warmup, device, world):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream(device)
+    with ClockSampler(device.index) as clocks:
+        start.record(stream)
+        for _ in range(steps):
+            fn()
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    barrier(world)
+    return max_over_ranks(start.elapsed_time(end) / steps, world, device), clocks.summary()
+
+
+def _kernel_rates(names_bytes, steps):
+    """Per-kernel achieved GB/s from the library's event timings: {name: (GB/s, ms per launch)}."""
+    from polytensors_b200 import _lib
+
+    out = {}
+    for name, nbytes in names_bytes.items():
+        ms, launches = _lib.profile_query(name)
+        if launches:
+            per = ms / launches
+            out[name] = {"GB/s": nbytes / (per / 1e3) / 1e9, "ms_per_launch": per, "launches": launches,
+                         "algorithmic_bytes": nbytes}
+    return out
+
+
+def run_norm_ce(args, rank, world, device):
+    """RMSNorm(w) -> GELU -> linear(32000) -> cross entropy, forward + backward, degree 4."""
+    import torch.nn.functional as F
+    from polytensors_b200 import PolyTensor, _lib
+
+    n, R, H, V = 4, args.rows, 4096, 32000
+    x = _series_poly((R, H), n, 1, torch.float32, device, requires_grad=True)
+    g = torch.Generator().manual_seed(2)
+    w = PolyTensor(((1 + 0.02 * torch.randn(H, generator=g)).to(device),), degree=n, requires_grad=True)
+    W = PolyTensor(((0.02 * torch.randn(V, H, generator=g)).to(device),), degree=n, requires_grad=True)
+    target = torch.randint(0, V, (R,), generator=g).to(device)
+
+    def step():
+        for t in (x, w, W):
+            t.grad = None
+        with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+            h = F.gelu(F.rms_norm(x, (H,), w))
+            loss = F.cross_entropy(F.linear(h, W), target)
+            loss.backward()
+
+    for _ in range(args.warmup):
+        step()
+    for name in ("rmsnorm_fwd", "rmsnorm_bwd", "cross_entropy_fwd", "cross_entropy_bwd", "poly_gemm", "series_map"):
+        _lib.profile_query(name)
+    _lib.profile_enable(True)
+    ms, clocks = _timed(step, args.steps, 0, device, world)
+    _lib.profile_enable(False)
+    P = n + 1
+    rates = _kernel_rates({"rmsnorm_fwd": 2 * P * R * H * 4, "rmsnorm_bwd": 3 * P * R * H * 4,
+                           "cross_entropy_fwd": P * R * V * 4, "cross_entropy_bwd": 2 * P * R * V * 4}, args.steps)
+    gms, glaunch = _lib.profile_query("poly_gemm")
+    T = (n + 1) * (n + 2) / 2
+    gemm_flops = 3 * 2 * R * H * V * T   # forward + the two backward products
+    mem_bytes = sum(r["algorithmic_bytes"] * r["launches"] for r in rates.values())
+    mem_ms = sum(r["ms_per_launch"] * r["launches"] for r in rates.values())
+    pk, source = peaks()
+    value = mem_bytes / (mem_ms / 1e3) / 1e9
+    return {
+        "metric": "norm/CE kernels GB/s (configs[2]: RMSNorm+GELU+linear(32000)+CE fwd+bwd, degree 4, float32)",
+        "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: planes N(0,1)/k!, seeded",
+        "config": {"workload": f"norm_gelu_linear_ce rows={R} hidden={H} vocab={V} degree {n}",
+                   "l2": "inputs larger than L2"},
+        "kernels": rates,
+        "linear": {"TFLOP/s": gemm_flops / (gms / 1e3) / 1e12 if glaunch else None, "launches": glaunch},
+        "roofline": {"bound": "hbm", "achieved": value, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": value / pk["hbm_gbs"], "traffic": None, "peak_source": f"hbm_gbs ({source})"},
+        "clocks": clocks,
+    }
+
+
+def attention_flops(B, H, L, D, n):
+    T = (n + 1) * (n + 2) / 2
+    pairs = L * (L + 1) / 2
+    return 6 * T * 2 * B * H * pairs * D   # forward 2 contractions, backward 4 (no recompute counted)
+
+
+def run_attention(args, rank, world, device):
+    """causal series attention (8, 32, L, 128), degree 3, forward + backward."""
+    import torch.nn.functional as F
+    from polytensors_b200 import PolyTensor
+
+    n, B, H, L, D = 3, 8, 32, args.seq, 128
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
+    q, k, v = (_series_poly((B, H, L, D), n, s, dtype, device, requires_grad=True) for s in (1, 2, 3))
+    G = _series_poly((B, H, L, D), n, 4, dtype, device)
+
+    def step():
+        for t in (q, k, v):
+            t.grad = None
+        with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+            o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+            o.backward(G)
+
+    ms, clocks = _timed(step, args.steps, args.warmup, device, world)
+    flops = attention_flops(B, H, L, D, n)
+    pk, source = peaks()
+    value = world * flops / (ms / 1e3) / 1e12
+    return {
+        "metric": f"poly-attention coeff TFLOP/s (configs[3]: causal, (8, 32, {L}, 128), degree 3, {args.dtype}, fwd+bwd)",
+        "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.dtype,
+        "data": "synthetic: planes N(0,1)/k!, seeded",
+        "config": {"workload": f"attention B=8 H=32 L={L} D=128 degree 3 causal {args.dtype}",
+                   "flops": "12*T*B*H*L(L+1)/2*D (causal pairs, no recompute)"},
+        "roofline": {"bound": "tensor", "achieved": value / world, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": value / world / pk["bf16_tflops"], "traffic": None,
+                     "peak_source": f"bf16_tflops ({source})"},
+        "clocks": clocks,
+    }
+
+
+class TinyGPT:
+    """decoder-only transformer with PolyTensor parameters (degree 3, float32):
+    embedding, 12 x [RMSNorm, q/k/v/o linears, causal SDPA, RMSNorm, GELU MLP], RMSNorm, untied head."""
+
+    def __init__(self, device, layers=12, d=768, heads=12, mlp=3072, vocab=32000, degree=3, seed=0):
+        from polytensors_b200 import PolyTensor
+
+        g = torch.Generator().manual_seed(seed)
+        self.layers, self.d, self.heads, self.vocab, self.degree = layers, d, heads, vocab, degree
+
+        def param(*shape, ones=False):
+            base = torch.ones(*shape) if ones else 0.02 * torch.randn(*shape, generator=g)
+            return torch.nn.Parameter(PolyTensor((base.to(device),), degree=degree))
+
+        self.p = {"emb": param(vocab, d)}
+        for l in range(layers):
+            self.p[f"n1.{l}"], self.p[f"n2.{l}"] = param(d, ones=True), param(d, ones=True)
+            for nm in ("wq", "wk", "wv", "wo"):
+                self.p[f"{nm}.{l}"] = param(d, d)
+            self.p[f"w1.{l}"], self.p[f"w2.{l}"] = param(mlp, d), param(d, mlp)
+        self.p["nf"] = param(d, ones=True)
+        self.p["head"] = param(vocab, d)
+
+    def parameters(self):
+        return list(self.p.values())
+
+    def loss(self, inp, tgt, Z, lam):
+        import torch.nn.functional as F
+
+        P, d, H = self.p, self.d, self.heads
+        Bt, T = inp.shape
+        x = F.embedding(inp, P["emb"])
+        for l in range(self.layers):
+            h = F.rms_norm(x, (d,), P[f"n1.{l}"])
+            q, k, v = (F.linear(h, P[f"{nm}.{l}"]).view(Bt, T, H, d // H).transpose(1, 2) for nm in ("wq", "wk", "wv"))
+            a = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(1, 2).reshape(Bt, T, d)
+            x = x + F.linear(a, P[f"wo.{l}"])
+            h = F.rms_norm(x, (d,), P[f"n2.{l}"])
+            x = x + F.linear(F.gelu(F.linear(h, P[f"w1.{l}"])), P[f"w2.{l}"])
+        logits = F.linear(F.rms_norm(x, (d,), P["nf"]), P["head"])
+        return F.cross_entropy(logits.reshape(-1, self.vocab), tgt.reshape(-1)) * (1 - lam * Z)
+
+
+def run_train(args, rank, world, device):
+    """global batch 64 x seq 1024 sharded over the ranks, micro-batches of args.micro
+    sequences per rank with gradient accumulation, one bucketed NCCL all-reduce of the gradient
+    series, SGD(lr=0.1, foreach=False).  Times args.micro_batches micro-batches per rank (a
+    bounded fraction of a step) plus the all-reduce and update, and reports tokens/s and the
+    steps/s they extrapolate to."""
+    from polytensors_b200 import PolyTensor
+    from polytensors_b200.parallel import allreduce_gradients
+
+    seq, global_batch, n = 1024, 64, 3
+    model = TinyGPT(device, layers=args.layers)
+    opt = torch.optim.SGD(model.parameters(), lr=0.1, foreach=False)
+    Z = PolyTensor((torch.tensor(0.0, device=device), 1.0), degree=n)
+    per_rank = global_batch // world
+    g = torch.Generator().manual_seed(1234)
+    ids = torch.randint(0, 32000, (global_batch, seq + 1), generator=g)[rank * per_rank:(rank + 1) * per_rank]
+    ids = ids.to(device)
+    micro = min(args.micro, per_rank)
+    n_micro = min(args.micro_batches, per_rank // micro)
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        with PolyTensor.plain_range():
+            for m in range(n_micro):
+                chunk = ids[m * micro:(m + 1) * micro]
+                with PolyTensor.retain_wrappers():
+                    loss = model.loss(chunk[:, :-1], chunk[:, 1:], Z, 0.5) * (micro / per_rank)
+                    loss.backward()
+            allreduce_gradients(model.parameters())
+            with PolyTensor.retain_wrappers():
+                opt.step()
+
+    ms, clocks = _timed(step, args.steps, args.warmup, device, world)
+    tokens = world * n_micro * micro * seq
+    tps = tokens / (ms / 1e3)
+    return {
+        "metric": "train tokens/s (configs[4]: 12-layer d768 PolyTensor transformer, degree 3, float32)",
+        "value": tps, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: uniform random token ids, N(0,0.02) weights with zero higher coefficients",
+        "config": {"workload": f"transformer layers={args.layers} d=768 heads=12 mlp=3072 vocab=32000 seq=1024 "
+                               f"global_batch=64 degree 3", "parallelism": f"dp{world}",
+                   "micro_batch": micro, "micro_batches_timed_per_rank": n_micro},
+        "extrapolated_steps_per_s": tps / (global_batch * seq),
+        "clocks": clocks,
+    }
+
+
+def run_matmul_sweep(args, rank, world, device):
+    """every size / degree / dtype point, one line per point in 'sweep'."""
+    from polytensors_b200 import _kernels
+
+    points = []
+    for dtype in ("float32", "float64"):
+        for N in (1024, 4096, 8192):
+            for n in (2, 4, 8):
+                if dtype == "float64" and N == 8192 and n == 8 and not args.full_sweep:
+                    continue
+                points.append((dtype, N, n))
+    points.append(("complex128", 4096, 2))
+    out = []
+    for dtype, N, n in points:
+        if dtype == "complex128":
+            A = [torch.randn(N, N, dtype=torch.float64, device=device)] + \
+                [torch.complex(torch.randn(N, N, dtype=torch.float64, device=device),
+                               torch.randn(N, N, dtype=torch.float64, device=device)) / math.factorial(k)
+                 for k in range(1, n + 1)]
+            B = [a.clone() for a in A]
+            T = 1 + 4 * n + 4 * ((n + 1) * (n + 2) // 2 - 1 - 2 * n)
+            flops = 2.0 * N ** 3 * T
+        else:
+            dt = getattr(torch, dtype)
+            A = [t.to(device) for t in make_series((N, N), n, 1, dt)]
+            B = [t.to(device) for t in make_series((N, N), n, 2, dt)]
+            flops = matmul_flops(N, N, N, n)
+        steps = max(1, min(args.steps, int(2e14 // flops) or 1))
+        ms, _ = _timed(lambda: _kernels.poly_matmul(A, B), steps, 1, device, world)
+        out.append({"dtype": dtype, "M=N=K": N, "degree": n, "ms": ms,
+                    "coeff_TFLOP/s": flops / (ms / 1e3) / 1e12})
+        del A, B
+        torch.cuda.empty_cache()
+    return {"metric": "poly-matmul coeff TFLOP/s sweep (configs[1])", "value": None, "unit": "TFLOP/s",
+            "n_gpus": world, "sweep": out, "higher_is_better": True}
+
+
+# ------------------------------------------------------------------------------------
 
 def barrier(world):
     if world > 1:
@@ -281,11 +543,19 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="poly_matmul", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="poly_matmul",
+                    choices=sorted(WORKLOADS) + ["norm_ce", "attention", "train", "poly_matmul_sweep"])
     ap.add_argument("--impl", default="polykern", choices=["polykern", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=16384, help="norm_ce: rows (batch*seq)")
+    ap.add_argument("--seq", type=int, default=4096, help="attention: sequence length")
+    ap.add_argument("--dtype", default="f32", choices=["f32", "bf16"], help="attention: storage dtype")
+    ap.add_argument("--layers", type=int, default=12, help="train: transformer layers")
+    ap.add_argument("--micro", type=int, default=8, help="train: sequences per micro-batch")
+    ap.add_argument("--micro-batches", type=int, default=1, help="train: micro-batches timed per rank and step")
+    ap.add_argument("--full-sweep", action="store_true")
     args = ap.parse_args()
-    cfg = WORKLOADS[args.workload]
+    cfg = WORKLOADS.get(args.workload)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -293,7 +563,11 @@ def main():
 
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(reference_arm(args, cfg)), flush=True)
+            if cfg is None:
+                print(json.dumps({"impl": "reference", "unavailable": f"--impl reference times the default workload; "
+                                  f"see --workload {args.workload} --cpu-only"}), flush=True)
+            else:
+                print(json.dumps(reference_arm(args, cfg)), flush=True)
         return
 
     if args.warmup < 3:
@@ -305,6 +579,15 @@ def main():
 
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=device)
+    secondary = {"norm_ce": run_norm_ce, "attention": run_attention, "train": run_train,
+                 "poly_matmul_sweep": run_matmul_sweep}
+    if args.workload in secondary:
+        result = secondary[args.workload](args, rank, world, device)
+        if rank == 0:
+            print(json.dumps(result), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
     result = run_matmul(args, cfg, rank, world, device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, desc = cpu_matmul_rate(cfg, os.cpu_count() or 1)

@@ -354,6 +354,8 @@ int pk_series_map(int op, int dtype, int degree, int ndim, const int64_t* shape,
                (!binary || dense(ndim, shape, b_strides));
     const int grid = grid_for(p.numel);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    void* tok;
+    prof_begin("series_map", s, &tok);
     switch (dtype) {
         case PK_F32: launch_map_t<float>(p, grid, s); break;
         case PK_F64: launch_map_t<double>(p, grid, s); break;
@@ -361,6 +363,7 @@ int pk_series_map(int op, int dtype, int degree, int ndim, const int64_t* shape,
         case PK_F16: launch_map_t<__half>(p, grid, s); break;
         default: return fail(PK_ERR_UNSUPPORTED, "pk_series_map: unsupported dtype");
     }
+    prof_end("series_map", s, tok);
     PK_CHECK_LAUNCH("pk_series_map");
     return PK_OK;
 }

@@ -183,7 +183,10 @@ static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, siz
     const int threads = norm_threads(p.cols);
     if (!backward) {
         const int grid = static_cast<int>(std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * 8));
+        void* tok;
+        prof_begin("rmsnorm_fwd", s, &tok);
         rmsnorm_fwd_kernel<T, NP><<<grid, threads, 0, s>>>(p);
+        prof_end("rmsnorm_fwd", s, tok);
         PK_CHECK_LAUNCH("pk_rmsnorm_fwd");
         return PK_OK;
     }
@@ -202,7 +205,10 @@ static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, siz
         if (!ws || ws_bytes < need) return fail(PK_ERR_WORKSPACE, "pk_rmsnorm_bwd: workspace too small");
         p.dw_part = ws;
     }
+    void* tok;
+    prof_begin("rmsnorm_bwd", s, &tok);
     rmsnorm_bwd_kernel<T, NP><<<grid, threads, smem, s>>>(p);
+    prof_end("rmsnorm_bwd", s, tok);
     PK_CHECK_LAUNCH("pk_rmsnorm_bwd");
     if (dw) {
         NormParams q = p;

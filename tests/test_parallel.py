@@ -1,0 +1,95 @@
+"""Data-parallel gradient averaging on world_size-2 gloo process groups (CPU), including a
+rank that fails before the collective: the surviving rank must end with an error from the
+short process-group timeout instead of hanging."""
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _init(rank, world, port, timeout_s=30):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _average_worker(rank, world, port, queue):
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "poly-tensors_b200"))
+    from polytensors_b200 import PolyTensor
+    from polytensors_b200.parallel import allreduce_gradients
+
+    _init(rank, world, port)
+    try:
+        params = []
+        for i, shape in enumerate([(5, 3), (7,), (2, 2, 2)]):
+            p = PolyTensor(tuple(torch.zeros(shape) for _ in range(4)), requires_grad=True)
+            p.grad = PolyTensor(tuple(torch.full(shape, float(rank * 10 + i * 100 + k)) for k in range(4)))
+            params.append(p)
+        allreduce_gradients(params, bucket_bytes=64)   # several buckets
+        got = [[c.clone() for c in p.grad.coeffs] for p in params]
+        queue.put((rank, got))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_allreduce_averages_every_plane():
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_average_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank in range(world):
+        for i, planes in enumerate(results[rank]):
+            for k, c in enumerate(planes):
+                assert torch.all(c == (0 + 10) / 2 + i * 100 + k)
+
+
+def _failing_worker(rank, world, port, queue):
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "poly-tensors_b200"))
+    from polytensors_b200 import PolyTensor
+    from polytensors_b200.parallel import allreduce_gradients
+
+    _init(rank, world, port, timeout_s=5)
+    p = PolyTensor((torch.zeros(4), torch.zeros(4)), requires_grad=True)
+    p.grad = PolyTensor((torch.ones(4), torch.ones(4)))
+    if rank == 1:
+        os._exit(3)   # the rank dies between steps, before the collective
+    try:
+        allreduce_gradients([p])
+        queue.put((rank, "completed"))
+    except Exception as e:   # the short timeout ends the collective with an error
+        queue.put((rank, "error: " + type(e).__name__))
+
+
+def test_failed_rank_surfaces_as_error_not_hang():
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_failing_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    rank, message = queue.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert procs[1].exitcode == 3
+    assert rank == 0 and message.startswith("error"), message
