@@ -325,7 +325,8 @@ def run_norm_ce(args, rank, world, device):
         "config": {"workload": f"norm_gelu_linear_ce rows={R} hidden={H} vocab={V} degree {n}",
                    "l2": "inputs larger than L2"},
         "kernels": rates,
-        "linear": {"TFLOP/s": gemm_flops / (gms / 1e3) / 1e12 if glaunch else None, "launches": glaunch},
+        "linear": {"TFLOP/s": gemm_flops * (glaunch / 3) / (gms / 1e3) / 1e12 if glaunch else None,
+                   "launches": glaunch, "flops_per_step": gemm_flops},
         "roofline": {"bound": "hbm", "achieved": value, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": value / pk["hbm_gbs"], "traffic": None, "peak_source": f"hbm_gbs ({source})"},
         "clocks": clocks,
@@ -419,9 +420,8 @@ class TinyGPT:
 def run_train(args, rank, world, device):
     """global batch 64 x seq 1024 sharded over the ranks, micro-batches of args.micro
     sequences per rank with gradient accumulation, one bucketed NCCL all-reduce of the gradient
-    series, SGD(lr=0.1, foreach=False).  Times args.micro_batches micro-batches per rank (a
-    bounded fraction of a step) plus the all-reduce and update, and reports tokens/s and the
-    steps/s they extrapolate to."""
+    series, SGD(lr=0.1, foreach=False).  A timed step is the whole global batch (unless
+    --micro-batches bounds it); reports tokens/s and steps/s."""
     from polytensors_b200 import PolyTensor
     from polytensors_b200.parallel import allreduce_gradients
 
@@ -434,7 +434,7 @@ def run_train(args, rank, world, device):
     ids = torch.randint(0, 32000, (global_batch, seq + 1), generator=g)[rank * per_rank:(rank + 1) * per_rank]
     ids = ids.to(device)
     micro = min(args.micro, per_rank)
-    n_micro = min(args.micro_batches, per_rank // micro)
+    n_micro = per_rank // micro if args.micro_batches <= 0 else min(args.micro_batches, per_rank // micro)
 
     def step():
         opt.zero_grad(set_to_none=True)
@@ -459,6 +459,7 @@ def run_train(args, rank, world, device):
         "config": {"workload": f"transformer layers={args.layers} d=768 heads=12 mlp=3072 vocab=32000 seq=1024 "
                                f"global_batch=64 degree 3", "parallelism": f"dp{world}",
                    "micro_batch": micro, "micro_batches_timed_per_rank": n_micro},
+        "steps_per_s": tps / (global_batch * seq) if n_micro * micro == per_rank else None,
         "extrapolated_steps_per_s": tps / (global_batch * seq),
         "clocks": clocks,
     }
@@ -552,7 +553,8 @@ def main():
     ap.add_argument("--dtype", default="f32", choices=["f32", "bf16"], help="attention: storage dtype")
     ap.add_argument("--layers", type=int, default=12, help="train: transformer layers")
     ap.add_argument("--micro", type=int, default=8, help="train: sequences per micro-batch")
-    ap.add_argument("--micro-batches", type=int, default=1, help="train: micro-batches timed per rank and step")
+    ap.add_argument("--micro-batches", type=int, default=0,
+                    help="train: micro-batches per rank and step (0 = the whole global batch)")
     ap.add_argument("--full-sweep", action="store_true")
     args = ap.parse_args()
     cfg = WORKLOADS.get(args.workload)

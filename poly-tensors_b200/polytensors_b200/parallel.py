@@ -29,6 +29,8 @@ def allreduce_gradients(params, group=None, bucket_bytes=512 << 20):
     ``bucket_bytes`` per dtype, each reduced by one collective and unpacked again, so the
     collective count per step is small and independent of the series degree.  Every rank
     must call this with the same parameters in the same order."""
+    if not (dist.is_available() and dist.is_initialized()):
+        return
     world = dist.get_world_size(group)
     if world == 1:
         return
