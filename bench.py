@@ -356,8 +356,20 @@ def run_attention(args, rank, world, device):
             o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
             o.backward(G)
 
+    def forward_only():
+        with torch.no_grad(), PolyTensor.plain_range():
+            F.scaled_dot_product_attention(q, k, v, is_causal=True)
+
+    from polytensors_b200 import _lib
+
+    _lib.profile_query("flash_attn_fwd")
+    _lib.profile_enable(True)
+    fwd_ms, _ = _timed(forward_only, args.steps, 1, device, world)
+    _lib.profile_enable(False)
+    kms, klaunch = _lib.profile_query("flash_attn_fwd")
     ms, clocks = _timed(step, args.steps, args.warmup, device, world)
     flops = attention_flops(B, H, L, D, n)
+    fwd_flops = flops / 3
     pk, source = peaks()
     value = world * flops / (ms / 1e3) / 1e12
     return {
@@ -370,6 +382,9 @@ def run_attention(args, rank, world, device):
         "roofline": {"bound": "tensor", "achieved": value / world, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": value / world / pk["bf16_tflops"], "traffic": None,
                      "peak_source": f"bf16_tflops ({source})"},
+        "forward": {"ms": fwd_ms, "TFLOP/s": fwd_flops / (fwd_ms / 1e3) / 1e12,
+                    "fused_kernel_ms": kms / klaunch if klaunch else None,
+                    "fused_kernel_TFLOP/s": fwd_flops / (kms / klaunch / 1e3) / 1e12 if klaunch else None},
         "clocks": clocks,
     }
 

@@ -239,6 +239,18 @@ PK_API int pk_attn_dscores(int dtype, int degree, int64_t rows, int64_t cols,
                            const void* dsum, double scale, void* const* dscores, int64_t ds_rs, void* stream);
 
 /*
+ * Series flash attention forward in one kernel: O = softmax(scale * Q K^T, causal) V with
+ * truncated Cauchy products, bfloat16 planes, fp32 accumulation, degree <= 3, head dim 64 or
+ * 128.  q/o: [bh][L][D], k/v: [bh][S][D], contiguous, 16-byte aligned.  Key index j is
+ * admissible for query i when j <= i (causal != 0).  Generalises the degree-1 Triton forward
+ * (src/polytensors/_attention_kernels.py:27-82) and replaces the decomposition of
+ * src/polytensors/_decompositions.py:28-43 (whose (L, S) score series it never forms).
+ */
+PK_API int pk_flash_attn_fwd(int dtype, int degree, int64_t bh, int64_t L, int64_t S, int64_t D,
+                             const void* const* q, const void* const* k, const void* const* v,
+                             void* const* o, int causal, double scale, void* stream);
+
+/*
  * pk_poly_gemm without a workspace argument, for callers that cannot allocate device
  * memory (a plugin host that owns every allocation, a process that must not grow its
  * device footprint after start-up, code with no allocator to link).  The scratch comes

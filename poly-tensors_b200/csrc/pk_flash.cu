@@ -1,0 +1,469 @@
+// Series flash attention, forward: O = softmax(scale * Q K^T, causal) V with every product
+// a truncated Cauchy product, in one kernel (bfloat16 storage, fp32 accumulation).
+//
+// The reference evaluates this as its SDPA decomposition (src/polytensors/_decompositions.py:28-43)
+// with the full (L, S) score series materialised per coefficient plane; its degree-1 Triton
+// kernel (src/polytensors/_attention_kernels.py:27-82) is the single-kernel form for degree 1.
+// Here, for degree n <= 3, one CTA owns 128 query rows and a 64-wide slice of the output
+// columns and streams 64-key blocks:
+//
+//   S_k   = sum_{a+b=k} Q_a K_b^T                 tcgen05 (A = Q, B = K from shared memory),
+//                                                  all n+1 planes accumulated in TMEM
+//   E     = exp(scale*S - m) as a series           4 softmax warps, one query row per thread:
+//                                                  E_0 = exp(scale*S_0 - m), e = exp of the
+//                                                  directions; l_k += sum_keys E_k
+//   O~_k += sum_{a+b=k} E_a V_b                   tcgen05 with A = E (bf16) written back into
+//                                                  TMEM over the spent score columns, B = V read
+//                                                  MN-major straight from the caller's planes
+//   O     = O~ (/) l                               series division in the epilogue
+//
+// The running maximum m is only raised (and O~, l rescaled) when a block's maximum exceeds it
+// by more than FA_TAU, so most blocks skip the TMEM read-modify-write of O~; a stale m only
+// scales E by at most e^FA_TAU, which fp32 accumulation absorbs.
+#include <algorithm>
+#include <cstring>
+
+#include "pk_common.cuh"
+#include "pk_series.cuh"
+
+namespace pk {
+
+constexpr int FA_BM = 128;           // query rows per CTA
+constexpr int FA_BN = 64;            // keys per block
+constexpr int FA_DS = 64;            // output columns per CTA
+constexpr int FA_STAGES = 10;
+constexpr int FA_TILE = 64 * 64 * 2;        // K chunk [64 keys][64 d] or V slice [64 keys][64 d], bf16
+constexpr int FA_QTILE = FA_BM * 64 * 2;    // Q chunk [128][64], bf16
+constexpr float FA_TAU = 8.0f;
+constexpr int FA_THREADS = 192;
+constexpr int FA_MAX_NP = 4;
+
+struct FlashMaps {
+    CUtensorMap q[FA_MAX_NP];
+    CUtensorMap k[FA_MAX_NP];
+    CUtensorMap v[FA_MAX_NP];
+};
+
+struct FlashParams {
+    int bh, L, S, D;
+    int n_slices, q_tiles, causal;
+    float scale;
+    void* o[FA_MAX_NP];
+    int* status;
+};
+
+template <int NP>
+struct FlashCfg {
+    static constexpr int S_COLS = NP * FA_BN;     // score / probability planes
+    static constexpr int O_BASE = S_COLS;
+    static constexpr int USED = 2 * NP * 64;
+    static constexpr int TMEM_COLS = USED <= 128 ? 128 : (USED <= 256 ? 256 : 512);
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(lo))) |
+           (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(hi))) << 16);
+}
+
+template <int NP, int DCH>
+__global__ void __launch_bounds__(FA_THREADS, 1)
+    flash_fwd_kernel(const __grid_constant__ FlashMaps maps, const FlashParams p) {
+    using Cfg = FlashCfg<NP>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sq = smem;
+    uint8_t* ring = sq + NP * DCH * FA_QTILE;
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + FA_STAGES * FA_TILE);
+    uint64_t* empty = full + FA_STAGES;
+    uint64_t* q_full = empty + FA_STAGES;
+    uint64_t* s_full = q_full + 1;
+    uint64_t* p_ready = s_full + 1;
+    uint64_t* pv_done = p_ready + 1;
+    uint64_t* drain = pv_done + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int slice = blockIdx.x % p.n_slices;
+    const int qt = p.q_tiles - 1 - static_cast<int>(blockIdx.x) / p.n_slices;  // heaviest (latest) tiles first
+    const int bh = blockIdx.y;
+    const int q0 = qt * FA_BM;
+    int nblocks = (p.S + FA_BN - 1) / FA_BN;
+    if (p.causal) nblocks = min(nblocks, (min(q0 + FA_BM, p.L) - 1) / FA_BN + 1);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < FA_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(q_full, 1);
+        mbar_init(s_full, 1);
+        mbar_init(p_ready, 128);
+        mbar_init(pv_done, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            mbar_arrive_expect_tx(q_full, NP * DCH * FA_QTILE);
+            for (int a = 0; a < NP; ++a)
+                for (int c = 0; c < DCH; ++c)
+                    tma_load_3d(sq + (a * DCH + c) * FA_QTILE, &maps.q[a], q_full, c * 64, q0, bh);
+            uint32_t stage = 0, phase = 0;
+            int issued_parity[FA_STAGES];
+#pragma unroll
+            for (int s = 0; s < FA_STAGES; ++s) issued_parity[s] = -1;
+            bool ok = true;
+            for (int j = 0; j < nblocks && ok; ++j) {
+                for (int t = 0; t < NP * DCH + NP && ok; ++t) {
+                    if (!mbar_wait_or_abort(&empty[stage], phase ^ 1, abort_flag, p.status, 401)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* dst = ring + stage * FA_TILE;
+                    mbar_arrive_expect_tx(&full[stage], FA_TILE);
+                    if (t < NP * DCH) {
+                        const int b = t / DCH, c = t % DCH;
+                        tma_load_3d(dst, &maps.k[b], &full[stage], c * 64, j * FA_BN, bh);
+                    } else {
+                        const int b = t - NP * DCH;
+                        tma_load_3d(dst, &maps.v[b], &full[stage], slice * FA_DS, j * FA_BN, bh);
+                    }
+                    issued_parity[stage] = static_cast<int>(phase);
+                    if (++stage == FA_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            {
+                // Let every copy issued (Q included) land before the CTA can exit.
+                const uint64_t t0 = pk_globaltimer();
+                while (!mbar_try_wait(q_full, 0) && pk_globaltimer() - t0 < 1000000000ull) {
+                }
+            }
+            if (!ok) {
+                for (int s = 0; s < FA_STAGES; ++s) {
+                    if (issued_parity[s] < 0) continue;
+                    const uint64_t t0 = pk_globaltimer();
+                    while (!mbar_try_wait(&full[s], static_cast<uint32_t>(issued_parity[s])) &&
+                           pk_globaltimer() - t0 < 1000000000ull) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc_qk = f16_idesc(1u, FA_BM, FA_BN);
+            constexpr uint32_t idesc_pv = f16_idesc(1u, FA_BM, FA_DS) | (1u << 16);  // B (V) MN-major
+            uint32_t stage = 0, phase = 0;
+            bool ok = mbar_wait_or_abort(q_full, 0, abort_flag, p.status, 402);
+            bool issued = false;
+            for (int j = 0; j < nblocks && ok; ++j) {
+                if (j > 0 && !mbar_wait_or_abort(pv_done, (j - 1) & 1, abort_flag, p.status, 403)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                // S_k = sum_{a+b=k} Q_a K_b^T over the head dimension (DCH chunks of 64)
+                for (int b = 0; b < NP && ok; ++b) {
+                    for (int c = 0; c < DCH; ++c) {
+                        if (!mbar_wait_or_abort(&full[stage], phase, abort_flag, p.status, 404)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t kt = smem_u32(ring + stage * FA_TILE);
+                        for (int a = 0; a + b < NP; ++a) {
+                            const uint32_t qtile = smem_u32(sq + (a * DCH + c) * FA_QTILE);
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk)
+                                tc_mma_f16(tmem + (a + b) * FA_BN, sw128_kmajor_desc(qtile + kk * 32),
+                                           sw128_kmajor_desc(kt + kk * 32), idesc_qk,
+                                           (b == 0 && c == 0 && kk == 0) ? 0u : 1u);
+                        }
+                        issued = true;
+                        tc_commit(&empty[stage]);
+                        if (++stage == FA_STAGES) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                }
+                if (!ok) break;
+                tc_commit(s_full);
+                if (!mbar_wait_or_abort(p_ready, j & 1, abort_flag, p.status, 405)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                // O~_k += sum_{a+b=k} E_a V_b, E_a in TMEM (bf16 pairs over the spent S_a columns)
+                for (int b = 0; b < NP && ok; ++b) {
+                    if (!mbar_wait_or_abort(&full[stage], phase, abort_flag, p.status, 406)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t vt = smem_u32(ring + stage * FA_TILE);
+                    for (int a = 0; a + b < NP; ++a) {
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            tc_mma_f16_ts(tmem + Cfg::O_BASE + (a + b) * FA_DS, tmem + a * FA_BN + kk * 8,
+                                          sw128_mnmajor_desc(vt + kk * 2048), idesc_pv,
+                                          (j == 0 && b == 0 && kk == 0) ? 0u : 1u);
+                    }
+                    tc_commit(&empty[stage]);
+                    if (++stage == FA_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(pv_done);
+            }
+            if (!ok && issued) {
+                tc_commit(drain);
+                const uint64_t t0 = pk_globaltimer();
+                while (!mbar_try_wait(drain, 0) && pk_globaltimer() - t0 < 1000000000ull) {
+                }
+            }
+        }
+    } else {
+        // ---------------- softmax + epilogue: one query row per thread ----------------
+        const uint32_t lane_base = 32u * (warp & 3);
+        const uint32_t trow = tmem + (lane_base << 16);
+        const int q = q0 + static_cast<int>(lane_base) + lane;
+        const float sc = p.scale;
+        float m_used = -INFINITY;
+        float l[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) l[k] = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nblocks; ++j) {
+            if (!mbar_wait_or_abort(s_full, j & 1, abort_flag, p.status, 407)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int key0 = j * FA_BN;
+            const int last_key = p.causal ? min(q, p.S - 1) : p.S - 1;
+            // sweep 1: block maximum of scale * S_0 over admissible keys
+            float bmax = -INFINITY;
+#pragma unroll
+            for (int ch = 0; ch < FA_BN / 16; ++ch) {
+                uint32_t r[16];
+                tmem_ld_32x32b_x16(trow + ch * 16, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int t = 0; t < 16; ++t)
+                    if (key0 + ch * 16 + t <= last_key) bmax = fmaxf(bmax, sc * __uint_as_float(r[t]));
+            }
+            float f = 1.f;
+            bool rescale = false;
+            if (bmax > -INFINITY && (m_used == -INFINITY || bmax > m_used + FA_TAU)) {
+                if (m_used != -INFINITY) {
+                    f = __expf(m_used - bmax);
+                    rescale = true;
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) l[k] *= f;
+                }
+                m_used = bmax;
+            }
+            // sweep 2: E = exp(scale * S - m) as a series; accumulate l; write E (bf16) over S
+#pragma unroll 1
+            for (int ch = 0; ch < FA_BN / 16; ++ch) {
+                uint32_t r[NP][16];
+#pragma unroll
+                for (int k = 0; k < NP; ++k) tmem_ld_32x32b_x16(trow + k * FA_BN + ch * 16, r[k]);
+                tmem_ld_wait();
+                uint32_t packed[NP][8];
+#pragma unroll
+                for (int t = 0; t < 16; t += 2) {
+                    float e2[2][NP];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const int key = key0 + ch * 16 + t + u;
+                        float x[NP], e[NP];
+#pragma unroll
+                        for (int k = 0; k < NP; ++k) x[k] = sc * __uint_as_float(r[k][t + u]);
+                        if (key <= last_key && m_used > -INFINITY) {
+                            s_exp_dir<NP, float>(x, e);
+                            const float w = __expf(x[0] - m_used);
+#pragma unroll
+                            for (int k = 0; k < NP; ++k) e[k] *= w;
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < NP; ++k) e[k] = 0.f;
+                        }
+#pragma unroll
+                        for (int k = 0; k < NP; ++k) {
+                            l[k] += e[k];
+                            e2[u][k] = e[k];
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) packed[k][t / 2] = pack_bf16x2(e2[0][k], e2[1][k]);
+                }
+#pragma unroll
+                for (int k = 0; k < NP; ++k) tmem_st_32x32b_x8(trow + k * FA_BN + ch * 8, packed[k]);
+            }
+            // rescale O~ rows whose maximum moved (warp-collective TMEM access)
+            if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+                for (int k = 0; k < NP; ++k) {
+#pragma unroll 1
+                    for (int ch = 0; ch < FA_DS / 16; ++ch) {
+                        uint32_t r[16];
+                        const uint32_t addr = trow + Cfg::O_BASE + k * FA_DS + ch * 16;
+                        tmem_ld_32x32b_x16(addr, r);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int t = 0; t < 16; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * f);
+                        tmem_st_32x32b_x16(addr, r);
+                    }
+                }
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(p_ready);
+        }
+        // epilogue: O = O~ (/) l, written as bf16 into this CTA's column slice
+        if (ok && mbar_wait_or_abort(pv_done, (nblocks - 1) & 1, abort_flag, p.status, 408)) {
+            tc_fence_after();
+            const float inv = l[0] > 0.f ? 1.f / l[0] : 0.f;
+#pragma unroll 1
+            for (int ch = 0; ch < FA_DS / 16; ++ch) {
+                uint32_t r[NP][16];
+#pragma unroll
+                for (int k = 0; k < NP; ++k) tmem_ld_32x32b_x16(trow + Cfg::O_BASE + k * FA_DS + ch * 16, r[k]);
+                tmem_ld_wait();
+                float o[NP][16];
+#pragma unroll
+                for (int t = 0; t < 16; ++t) {
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) {
+                        float acc = __uint_as_float(r[k][t]);
+#pragma unroll
+                        for (int c2 = 1; c2 <= k; ++c2) acc -= l[c2] * o[k - c2][t];
+                        o[k][t] = acc * inv;
+                    }
+                }
+                if (q < p.L) {
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) {
+                        uint32_t w[8];
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) w[t] = pack_bf16x2(o[k][2 * t], o[k][2 * t + 1]);
+                        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.o[k]) +
+                                             (static_cast<int64_t>(bh) * p.L + q) * p.D + slice * FA_DS + ch * 16;
+                        uint4* d4 = reinterpret_cast<uint4*>(dst);
+                        d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                        d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    }
+}
+
+static int encode_plane_map(CUtensorMap* map, const void* base, int64_t rows, int64_t D, int64_t bh, int box_rows) {
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows),
+                                static_cast<cuuint64_t>(bh)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(rows * D * 2)};
+    const cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(box_rows), 1u};
+    CUresult r = encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+    if (r != CUDA_SUCCESS)
+        return fail(PK_ERR_CUDA, "pk_flash_attn_fwd: cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+    return PK_OK;
+}
+
+template <int NP, int DCH>
+static int launch_flash(const FlashMaps& maps, const FlashParams& p, cudaStream_t s) {
+    const int smem = NP * DCH * FA_QTILE + FA_STAGES * FA_TILE + 1024 + 512;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel<NP, DCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return cuda_fail(e, "pk_flash_attn_fwd: cudaFuncSetAttribute");
+        attr_set[dev] = true;
+    }
+    dim3 grid(static_cast<unsigned>(p.q_tiles * p.n_slices), static_cast<unsigned>(p.bh));
+    void* tok;
+    prof_begin("flash_attn_fwd", s, &tok);
+    flash_fwd_kernel<NP, DCH><<<grid, FA_THREADS, smem, s>>>(maps, p);
+    prof_end("flash_attn_fwd", s, tok);
+    PK_CHECK_LAUNCH("pk_flash_attn_fwd");
+    return PK_OK;
+}
+
+}  // namespace pk
+
+using namespace pk;
+
+extern "C" int pk_flash_attn_fwd(int dtype, int degree, int64_t bh, int64_t L, int64_t S, int64_t D,
+                                 const void* const* q, const void* const* k, const void* const* v, void* const* o,
+                                 int causal, double scale, void* stream) {
+    if (dtype != PK_BF16) return fail(PK_ERR_UNSUPPORTED, "pk_flash_attn_fwd: bfloat16 planes only");
+    if (degree < 0 || degree >= FA_MAX_NP) return fail(PK_ERR_UNSUPPORTED, "pk_flash_attn_fwd: degree must be <= 3");
+    if (D != 64 && D != 128) return fail(PK_ERR_UNSUPPORTED, "pk_flash_attn_fwd: head dimension must be 64 or 128");
+    if (bh <= 0 || L <= 0 || S <= 0) return bh == 0 || L == 0 ? PK_OK : fail(PK_ERR_ARG, "pk_flash_attn_fwd: empty keys");
+    if (bh > 65535 || L > (1LL << 30) || S > (1LL << 30)) return fail(PK_ERR_UNSUPPORTED, "pk_flash_attn_fwd: too large");
+    const int NP = degree + 1;
+    FlashMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    for (int a = 0; a < NP; ++a) {
+        if (!q[a] || !k[a] || !v[a] || !o[a]) return fail(PK_ERR_ARG, "pk_flash_attn_fwd: null plane");
+        if ((reinterpret_cast<uintptr_t>(q[a]) | reinterpret_cast<uintptr_t>(k[a]) | reinterpret_cast<uintptr_t>(v[a]) |
+             reinterpret_cast<uintptr_t>(o[a])) % 16)
+            return fail(PK_ERR_ARG, "pk_flash_attn_fwd: planes must be 16-byte aligned");
+        int rc = encode_plane_map(&maps.q[a], q[a], L, D, bh, FA_BM);
+        if (!rc) rc = encode_plane_map(&maps.k[a], k[a], S, D, bh, FA_BN);
+        if (!rc) rc = encode_plane_map(&maps.v[a], v[a], S, D, bh, FA_BN);
+        if (rc) return rc;
+    }
+    FlashParams p{};
+    p.bh = static_cast<int>(bh);
+    p.L = static_cast<int>(L);
+    p.S = static_cast<int>(S);
+    p.D = static_cast<int>(D);
+    p.n_slices = static_cast<int>(D / FA_DS);
+    p.q_tiles = static_cast<int>(ceil_div(L, FA_BM));
+    p.causal = causal ? 1 : 0;
+    p.scale = static_cast<float>(scale);
+    for (int a = 0; a < NP; ++a) p.o[a] = o[a];
+    p.status = device_status_ptr();
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int dch = static_cast<int>(D / 64);
+#define PK_FLASH(NPV)                                                              \
+    case NPV: return dch == 1 ? launch_flash<NPV, 1>(maps, p, s) : launch_flash<NPV, 2>(maps, p, s);
+    switch (NP) {
+        PK_FLASH(1)
+        PK_FLASH(2)
+        PK_FLASH(3)
+        PK_FLASH(4)
+    }
+#undef PK_FLASH
+    return fail(PK_ERR_UNSUPPORTED, "pk_flash_attn_fwd: degree");
+}

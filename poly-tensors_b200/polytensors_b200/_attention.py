@@ -92,8 +92,32 @@ def _probs(Sc, L, scale, causal):
     return stats
 
 
+def flash_eligible(Q, Kp, V):
+    """Whether the single-kernel forward (pk_flash_attn_fwd) applies: bfloat16 planes, degree <= 3,
+    head dim 64 or 128 for queries, keys and values alike."""
+    D = Q[0].shape[-1]
+    return (Q[0].dtype == torch.bfloat16 and len(Q) <= 4 and D in (64, 128)
+            and Kp[0].shape[-1] == D and V[0].shape[-1] == D)
+
+
+def flash_forward(Q, Kp, V, causal, scale):
+    BH, L, D = Q[0].shape
+    S = Kp[0].shape[1]
+    O = [torch.empty_like(q) for q in Q]
+    pq, k1 = _lib.pointer_array(Q)
+    pk_, k2 = _lib.pointer_array(Kp)
+    pv, k3 = _lib.pointer_array(V)
+    po, k4 = _lib.pointer_array(O)
+    status = _lib.load().pk_flash_attn_fwd(_lib.PK_BF16, len(Q) - 1, BH, L, S, D, pq, pk_, pv, po,
+                                           1 if causal else 0, float(scale), K._stream(Q[0].device))
+    _lib.check(status, "pk_flash_attn_fwd")
+    return O
+
+
 def forward_planes(Q, Kp, V, causal, scale):
     """O planes (BH, L, Dv) for flattened (BH, T, D) planes."""
+    if flash_eligible(Q, Kp, V):
+        return flash_forward(Q, Kp, V, causal, scale)
     BH, L, _ = Q[0].shape
     S = Kp[0].shape[1]
     hb = _block_heads(L, S, len(Q), Q[0].element_size(), BH)

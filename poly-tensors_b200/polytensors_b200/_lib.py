@@ -53,6 +53,8 @@ SIGNATURES = {
                              _vp, _vp]),
     "pk_attn_dscores": (_i32, [_i32, _i32, _i64, _i64, _pp, _i64, _pp, _i64, _vp, ctypes.c_double, _pp, _i64,
                                _vp]),
+    "pk_flash_attn_fwd": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64, _pp, _pp, _pp, _pp, _i32, ctypes.c_double,
+                                 _vp]),
     "pk_poly_gemm_noalloc": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64,
                                     _pp, _i64, _i64, _i64,
                                     _pp, _i64, _i64, _i64,

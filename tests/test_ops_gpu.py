@@ -265,3 +265,22 @@ def test_attention_fused_and_decomposed_paths_agree():
         with PolyTensor.plain_range(), PolyTensor.fused_attention(enabled):
             outs.append(coeffs(F.scaled_dot_product_attention(poly(Q), poly(Kp), poly(V), is_causal=True)))
     assert_close(outs[0], outs[1], F64)
+
+
+@pytest.mark.parametrize("n,shape,causal", [(3, (2, 3, 300, 128), True), (3, (1, 2, 256, 64), False),
+                                            (1, (2, 2, 130, 64), True), (2, (1, 1, 64, 128), True),
+                                            (0, (1, 2, 200, 128), False)])
+def test_flash_forward_bf16_against_oracle(n, shape, causal):
+    """The single-kernel bf16 forward (pk_flash_attn_fwd) against the float64 oracle of the reference
+    decomposition on the same bf16-rounded inputs; tolerance 3e-2 of the plane max-norm."""
+    from polytensors_b200 import PolyTensor, _attention
+
+    Q, Kp, V = (series(shape, n, s, torch.bfloat16) for s in (41, 42, 43))
+    flat = [_attention._flat([p.cuda() for p in X], shape) for X in (Q, Kp, V)]
+    assert _attention.flash_eligible(*flat)
+    got = _attention.flash_forward(*flat, causal, 1 / shape[-1] ** 0.5)
+    want = ref.attention(*[[p.double() for p in X] for X in (Q, Kp, V)], is_causal=causal)
+    assert_close([g.view(shape).float() for g in got], want, 3e-2)
+    with PolyTensor.plain_range():
+        o = F.scaled_dot_product_attention(poly(Q), poly(Kp), poly(V), is_causal=causal)
+    assert_close(coeffs(o), want, 3e-2, "through the API")
