@@ -339,6 +339,26 @@ def attention_flops(B, H, L, D, n):
     return 6 * T * 2 * B * H * pairs * D   # forward 2 contractions, backward 4 (no recompute counted)
 
 
+def run_attention_fwd(args, rank, world, device):
+    """Forward only of configs[3] (profiling aid): (args.batch, 32, L, 128), degree 3, causal."""
+    import torch.nn.functional as F
+    from polytensors_b200 import PolyTensor
+
+    n, B, H, L, D = 3, args.batch, 32, args.seq, 128
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
+    q, k, v = (_series_poly((B, H, L, D), n, s, dtype, device) for s in (1, 2, 3))
+
+    def step():
+        with torch.no_grad(), PolyTensor.plain_range():
+            F.scaled_dot_product_attention(q, k, v, is_causal=True)
+
+    ms, clocks = _timed(step, args.steps, args.warmup, device, world)
+    flops = attention_flops(B, H, L, D, n) / 3
+    return {"metric": "poly-attention forward coeff TFLOP/s", "value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s",
+            "ms_per_step": ms, "config": {"workload": f"attention_fwd B={B} H=32 L={L} D=128 degree 3 causal {args.dtype}"},
+            "clocks": clocks}
+
+
 def run_attention(args, rank, world, device):
     """causal series attention (8, 32, L, 128), degree 3, forward + backward."""
     import torch.nn.functional as F
@@ -560,11 +580,13 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="poly_matmul",
-                    choices=sorted(WORKLOADS) + ["norm_ce", "attention", "train", "poly_matmul_sweep"])
+                    choices=sorted(WORKLOADS) + ["norm_ce", "attention", "attention_fwd", "train",
+                                                 "poly_matmul_sweep"])
     ap.add_argument("--impl", default="polykern", choices=["polykern", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rows", type=int, default=16384, help="norm_ce: rows (batch*seq)")
     ap.add_argument("--seq", type=int, default=4096, help="attention: sequence length")
+    ap.add_argument("--batch", type=int, default=8, help="attention_fwd: batch")
     ap.add_argument("--dtype", default="f32", choices=["f32", "bf16"], help="attention: storage dtype")
     ap.add_argument("--layers", type=int, default=12, help="train: transformer layers")
     ap.add_argument("--micro", type=int, default=8, help="train: sequences per micro-batch")
@@ -596,7 +618,8 @@ def main():
 
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=device)
-    secondary = {"norm_ce": run_norm_ce, "attention": run_attention, "train": run_train,
+    secondary = {"norm_ce": run_norm_ce, "attention": run_attention, "attention_fwd": run_attention_fwd,
+                 "train": run_train,
                  "poly_matmul_sweep": run_matmul_sweep}
     if args.workload in secondary:
         result = secondary[args.workload](args, rank, world, device)
