@@ -9,7 +9,10 @@
 //
 //   S_k   = sum_{a+b=k} Q_a K_b^T                 tcgen05 (A = Q, B = K from shared memory),
 //                                                  all n+1 planes accumulated in TMEM
-//   E     = exp(scale*S - m) as a series           4 softmax warps, one query row per thread:
+//   E     = exp(scale*S - m) as a series           16 softmax warps: 4 per TMEM lane quadrant
+//                                                  (32 query rows), each owning 16 of the 64
+//                                                  keys; row maxima and normaliser partials
+//                                                  combine through shared memory.
 //                                                  E_0 = exp(scale*S_0 - m), e = exp of the
 //                                                  directions; l_k += sum_keys E_k
 //   O~_k += sum_{a+b=k} E_a V_b                   tcgen05 with A = E (bf16) written back into
@@ -35,7 +38,8 @@ constexpr int FA_STAGES = 10;
 constexpr int FA_TILE = 64 * 64 * 2;        // K chunk [64 keys][64 d] or V slice [64 keys][64 d], bf16
 constexpr int FA_QTILE = FA_BM * 64 * 2;    // Q chunk [128][64], bf16
 constexpr float FA_TAU = 8.0f;
-constexpr int FA_THREADS = 192;
+constexpr int FA_SOFTMAX_WARPS = 16;         // 4 per TMEM lane quadrant, each owning 16 keys of a block
+constexpr int FA_THREADS = 64 + 32 * FA_SOFTMAX_WARPS;
 constexpr int FA_MAX_NP = 4;
 
 struct FlashMaps {
@@ -82,6 +86,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     uint64_t* drain = pv_done + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* red = reinterpret_cast<float*>(tmem_slot + 4);  // [4 key groups][128 rows][NP + 1]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int slice = blockIdx.x % p.n_slices;
@@ -98,7 +103,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         }
         mbar_init(q_full, 1);
         mbar_init(s_full, 1);
-        mbar_init(p_ready, 128);
+        mbar_init(p_ready, 32 * FA_SOFTMAX_WARPS);
         mbar_init(pv_done, 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -209,7 +214,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                // O~_k += sum_{a+b=k} E_a V_b, E_a in TMEM (bf16 pairs over the spent S_a columns)
+                // O~_k += sum_{a+b=k} E_a V_b, E_a in TMEM: the bf16 pairs of keys 16kk..16kk+15 sit in
+                // columns 16kk..16kk+7 of S_a (written by the warp that owned those scores)
                 for (int b = 0; b < NP && ok; ++b) {
                     if (!mbar_wait_or_abort(&full[stage], phase, abort_flag, p.status, 406)) {
                         ok = false;
@@ -220,7 +226,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                     for (int a = 0; a + b < NP; ++a) {
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
-                            tc_mma_f16_ts(tmem + Cfg::O_BASE + (a + b) * FA_DS, tmem + a * FA_BN + kk * 8,
+                            tc_mma_f16_ts(tmem + Cfg::O_BASE + (a + b) * FA_DS, tmem + a * FA_BN + kk * 16,
                                           sw128_mnmajor_desc(vt + kk * 2048), idesc_pv,
                                           (j == 0 && b == 0 && kk == 0) ? 0u : 1u);
                     }
@@ -241,15 +247,21 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             }
         }
     } else {
-        // ---------------- softmax + epilogue: one query row per thread ----------------
-        const uint32_t lane_base = 32u * (warp & 3);
+        // ---------------- softmax + epilogue ----------------
+        // warp w (2..17) accesses TMEM lanes 32*(w%4)..+31 (query rows); key group g = (w-2)/4
+        // owns keys 16g..16g+15 of every block and output columns 16g..16g+15 of the slice.
+        const int quad = warp & 3;
+        const int g = (warp - 2) >> 2;
+        const uint32_t lane_base = 32u * quad;
+        const int row = static_cast<int>(lane_base) + lane;
         const uint32_t trow = tmem + (lane_base << 16);
-        const int q = q0 + static_cast<int>(lane_base) + lane;
+        const int q = q0 + row;
         const float sc = p.scale;
         float m_used = -INFINITY;
         float l[NP];
 #pragma unroll
         for (int k = 0; k < NP; ++k) l[k] = 0.f;
+        auto quad_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(1 + quad), "r"(128) : "memory"); };
         bool ok = true;
         for (int j = 0; j < nblocks; ++j) {
             if (!mbar_wait_or_abort(s_full, j & 1, abort_flag, p.status, 407)) {
@@ -257,19 +269,22 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                 break;
             }
             tc_fence_after();
-            const int key0 = j * FA_BN;
+            const int key0 = j * FA_BN + g * 16;
             const int last_key = p.causal ? min(q, p.S - 1) : p.S - 1;
-            // sweep 1: block maximum of scale * S_0 over admissible keys
+            uint32_t r[NP][16];
+#pragma unroll
+            for (int k = 0; k < NP; ++k) tmem_ld_32x32b_x16(trow + k * FA_BN + g * 16, r[k]);
+            tmem_ld_wait();
+            float pmax = -INFINITY;
+#pragma unroll
+            for (int t = 0; t < 16; ++t)
+                if (key0 + t <= last_key) pmax = fmaxf(pmax, sc * __uint_as_float(r[0][t]));
+            red[(g * 128 + row) * (NP + 1)] = pmax;
+            quad_sync();
             float bmax = -INFINITY;
 #pragma unroll
-            for (int ch = 0; ch < FA_BN / 16; ++ch) {
-                uint32_t r[16];
-                tmem_ld_32x32b_x16(trow + ch * 16, r);
-                tmem_ld_wait();
-#pragma unroll
-                for (int t = 0; t < 16; ++t)
-                    if (key0 + ch * 16 + t <= last_key) bmax = fmaxf(bmax, sc * __uint_as_float(r[t]));
-            }
+            for (int gg = 0; gg < 4; ++gg) bmax = fmaxf(bmax, red[(gg * 128 + row) * (NP + 1)]);
+            quad_sync();  // the partial maxima are read before the next block overwrites them
             float f = 1.f;
             bool rescale = false;
             if (bmax > -INFINITY && (m_used == -INFINITY || bmax > m_used + FA_TAU)) {
@@ -281,73 +296,73 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                 }
                 m_used = bmax;
             }
-            // sweep 2: E = exp(scale * S - m) as a series; accumulate l; write E (bf16) over S
-#pragma unroll 1
-            for (int ch = 0; ch < FA_BN / 16; ++ch) {
-                uint32_t r[NP][16];
+            // E = exp(scale * S - m) as a series for this warp's 16 keys; bf16 pairs written over
+            // the first 8 of its own 16 score columns in every plane
+            uint32_t packed[NP][8];
 #pragma unroll
-                for (int k = 0; k < NP; ++k) tmem_ld_32x32b_x16(trow + k * FA_BN + ch * 16, r[k]);
-                tmem_ld_wait();
-                uint32_t packed[NP][8];
+            for (int t = 0; t < 16; t += 2) {
+                float e2[2][NP];
 #pragma unroll
-                for (int t = 0; t < 16; t += 2) {
-                    float e2[2][NP];
+                for (int u = 0; u < 2; ++u) {
+                    float x[NP], e[NP];
 #pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int key = key0 + ch * 16 + t + u;
-                        float x[NP], e[NP];
+                    for (int k = 0; k < NP; ++k) x[k] = sc * __uint_as_float(r[k][t + u]);
+                    if (key0 + t + u <= last_key && m_used > -INFINITY) {
+                        s_exp_dir<NP, float>(x, e);
+                        const float w = __expf(x[0] - m_used);
 #pragma unroll
-                        for (int k = 0; k < NP; ++k) x[k] = sc * __uint_as_float(r[k][t + u]);
-                        if (key <= last_key && m_used > -INFINITY) {
-                            s_exp_dir<NP, float>(x, e);
-                            const float w = __expf(x[0] - m_used);
+                        for (int k = 0; k < NP; ++k) e[k] *= w;
+                    } else {
 #pragma unroll
-                            for (int k = 0; k < NP; ++k) e[k] *= w;
-                        } else {
-#pragma unroll
-                            for (int k = 0; k < NP; ++k) e[k] = 0.f;
-                        }
-#pragma unroll
-                        for (int k = 0; k < NP; ++k) {
-                            l[k] += e[k];
-                            e2[u][k] = e[k];
-                        }
+                        for (int k = 0; k < NP; ++k) e[k] = 0.f;
                     }
 #pragma unroll
-                    for (int k = 0; k < NP; ++k) packed[k][t / 2] = pack_bf16x2(e2[0][k], e2[1][k]);
+                    for (int k = 0; k < NP; ++k) {
+                        l[k] += e[k];
+                        e2[u][k] = e[k];
+                    }
                 }
 #pragma unroll
-                for (int k = 0; k < NP; ++k) tmem_st_32x32b_x8(trow + k * FA_BN + ch * 8, packed[k]);
+                for (int k = 0; k < NP; ++k) packed[k][t / 2] = pack_bf16x2(e2[0][k], e2[1][k]);
             }
-            // rescale O~ rows whose maximum moved (warp-collective TMEM access)
-            if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-                for (int k = 0; k < NP; ++k) {
-#pragma unroll 1
-                    for (int ch = 0; ch < FA_DS / 16; ++ch) {
-                        uint32_t r[16];
-                        const uint32_t addr = trow + Cfg::O_BASE + k * FA_DS + ch * 16;
-                        tmem_ld_32x32b_x16(addr, r);
-                        tmem_ld_wait();
 #pragma unroll
-                        for (int t = 0; t < 16; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * f);
-                        tmem_st_32x32b_x16(addr, r);
-                    }
+            for (int k = 0; k < NP; ++k) tmem_st_32x32b_x8(trow + k * FA_BN + g * 16, packed[k]);
+            // rescale this warp's 16 columns of every O~ plane where the row maximum moved
+            if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+                for (int k = 0; k < NP; ++k) {
+                    uint32_t o[16];
+                    const uint32_t addr = trow + Cfg::O_BASE + k * FA_DS + g * 16;
+                    tmem_ld_32x32b_x16(addr, o);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * f);
+                    tmem_st_32x32b_x16(addr, o);
                 }
             }
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(p_ready);
         }
-        // epilogue: O = O~ (/) l, written as bf16 into this CTA's column slice
-        if (ok && mbar_wait_or_abort(pv_done, (nblocks - 1) & 1, abort_flag, p.status, 408)) {
-            tc_fence_after();
-            const float inv = l[0] > 0.f ? 1.f / l[0] : 0.f;
-#pragma unroll 1
-            for (int ch = 0; ch < FA_DS / 16; ++ch) {
+        // epilogue: combine the four normaliser partials of each row, O = O~ (/) l for this
+        // warp's 16 output columns, written as bf16
+        if (ok) {
+#pragma unroll
+            for (int k = 0; k < NP; ++k) red[(g * 128 + row) * (NP + 1) + 1 + k] = l[k];
+            quad_sync();
+            float lt[NP];
+#pragma unroll
+            for (int k = 0; k < NP; ++k) {
+                lt[k] = 0.f;
+#pragma unroll
+                for (int gg = 0; gg < 4; ++gg) lt[k] += red[(gg * 128 + row) * (NP + 1) + 1 + k];
+            }
+            if (mbar_wait_or_abort(pv_done, (nblocks - 1) & 1, abort_flag, p.status, 408)) {
+                tc_fence_after();
+                const float inv = lt[0] > 0.f ? 1.f / lt[0] : 0.f;
                 uint32_t r[NP][16];
 #pragma unroll
-                for (int k = 0; k < NP; ++k) tmem_ld_32x32b_x16(trow + Cfg::O_BASE + k * FA_DS + ch * 16, r[k]);
+                for (int k = 0; k < NP; ++k) tmem_ld_32x32b_x16(trow + Cfg::O_BASE + k * FA_DS + g * 16, r[k]);
                 tmem_ld_wait();
                 float o[NP][16];
 #pragma unroll
@@ -356,7 +371,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                     for (int k = 0; k < NP; ++k) {
                         float acc = __uint_as_float(r[k][t]);
 #pragma unroll
-                        for (int c2 = 1; c2 <= k; ++c2) acc -= l[c2] * o[k - c2][t];
+                        for (int c2 = 1; c2 <= k; ++c2) acc -= lt[c2] * o[k - c2][t];
                         o[k][t] = acc * inv;
                     }
                 }
@@ -367,7 +382,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 #pragma unroll
                         for (int t = 0; t < 8; ++t) w[t] = pack_bf16x2(o[k][2 * t], o[k][2 * t + 1]);
                         __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.o[k]) +
-                                             (static_cast<int64_t>(bh) * p.L + q) * p.D + slice * FA_DS + ch * 16;
+                                             (static_cast<int64_t>(bh) * p.L + q) * p.D + slice * FA_DS + g * 16;
                         uint4* d4 = reinterpret_cast<uint4*>(dst);
                         d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
                         d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
@@ -400,7 +415,7 @@ static int encode_plane_map(CUtensorMap* map, const void* base, int64_t rows, in
 
 template <int NP, int DCH>
 static int launch_flash(const FlashMaps& maps, const FlashParams& p, cudaStream_t s) {
-    const int smem = NP * DCH * FA_QTILE + FA_STAGES * FA_TILE + 1024 + 512;
+    const int smem = NP * DCH * FA_QTILE + FA_STAGES * FA_TILE + 1024 + 512 + 4 * 128 * (NP + 1) * 4;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);

@@ -11,6 +11,12 @@
 
 namespace pk {
 
+// 1/k for the series recurrences (k is a compile-time constant after unrolling).
+template <typename C>
+__device__ __forceinline__ constexpr C inv_int(int k) {
+    return C(1.0 / static_cast<double>(k));
+}
+
 // Storage <-> compute conversions.  bf16 / f16 planes are computed in float.
 template <typename T> struct Compute { using type = T; };
 template <> struct Compute<__nv_bfloat16> { using type = float; };
@@ -78,7 +84,7 @@ __device__ __forceinline__ void s_exp(const C (&x)[NP], C (&y)[NP]) {
         C acc = C(0);
 #pragma unroll
         for (int i = 1; i <= k; ++i) acc += C(i) * x[i] * r[k - i];
-        r[k] = acc / C(k);
+        r[k] = acc * inv_int<C>(k);
     }
 #pragma unroll
     for (int k = 0; k < NP; ++k) y[k] = r[k];
@@ -93,7 +99,7 @@ __device__ __forceinline__ void s_exp_dir(const C (&x)[NP], C (&e)[NP]) {
         C acc = C(0);
 #pragma unroll
         for (int i = 1; i <= k; ++i) acc += C(i) * x[i] * e[k - i];
-        e[k] = acc / C(k);
+        e[k] = acc * inv_int<C>(k);
     }
 }
 
@@ -107,7 +113,7 @@ __device__ __forceinline__ void s_log1(const C (&u)[NP], C (&y)[NP]) {
         C acc = u[k] * C(k);
 #pragma unroll
         for (int i = 1; i < k; ++i) acc -= C(i) * y[i] * u[k - i];
-        y[k] = acc / C(k);
+        y[k] = acc * inv_int<C>(k);
     }
 }
 
@@ -139,7 +145,7 @@ __device__ __forceinline__ void s_rsqrt(const C (&x)[NP], C (&y)[NP]) {
         C acc = C(0);
 #pragma unroll
         for (int i = 1; i <= k; ++i) acc += C(2 * k - i) * u[i] * r[k - i];
-        r[k] = -acc / C(2 * k);
+        r[k] = -acc * inv_int<C>(2 * k);
     }
 #pragma unroll
     for (int k = 0; k < NP; ++k) y[k] = r[k];
@@ -175,7 +181,7 @@ __device__ __forceinline__ void s_tanh(const C (&x)[NP], C (&y)[NP], C (&g)[NP])
         C acc = C(0);
 #pragma unroll
         for (int i = 1; i <= k; ++i) acc += C(i) * x[i] * gg[k - i];
-        r[k] = acc / C(k);
+        r[k] = acc * inv_int<C>(k);
         C sq = C(0);
 #pragma unroll
         for (int i = 0; i <= k; ++i) sq += r[i] * r[k - i];
@@ -198,7 +204,7 @@ __device__ __forceinline__ void s_sigmoid(const C (&x)[NP], C (&y)[NP], C (&g)[N
         C acc = C(0);
 #pragma unroll
         for (int i = 1; i <= k; ++i) acc += C(i) * x[i] * gg[k - i];
-        r[k] = acc / C(k);
+        r[k] = acc * inv_int<C>(k);
         C p = r[k] * (C(1) - r[0]);
 #pragma unroll
         for (int i = 0; i < k; ++i) p -= r[i] * r[k - i];
@@ -229,8 +235,8 @@ __device__ __forceinline__ void s_gelu(const C (&x)[NP], C (&y)[NP], C (&d)[NP])
             a += C(i) * x[i] * phi[k - i];
             b += C(i) * x[i] * w[k - i];
         }
-        Phi[k] = a / C(k);
-        phi[k] = -b / C(k);
+        Phi[k] = a * inv_int<C>(k);
+        phi[k] = -b * inv_int<C>(k);
         C ww = C(0);
 #pragma unroll
         for (int i = 0; i <= k; ++i) ww += x[i] * phi[k - i];
