@@ -27,6 +27,7 @@ struct NormParams {
     void* y[PK_MAX_PLANES];   // forward output / backward dx
     void* dw_part;            // backward: [gridDim.x][np][cols] partial weight gradients (compute type)
     void* rstd;               // [rows][np] rsqrt series per row (compute type)
+    int vec;                  // planes and row strides allow ROW_VEC-element vector access
 };
 
 template <int NP, typename T, typename C>
@@ -42,6 +43,19 @@ __device__ __forceinline__ void load_weight(const NormParams& p, int64_t c, C (&
     if (p.w_np == 0) w[0] = C(1);
 }
 
+template <int NP, typename T, typename C>
+__device__ __forceinline__ void load_weight4(const NormParams& p, int64_t c0, int valid, C (&w)[ROW_VEC][NP]) {
+    if (p.w_np == 0) {
+#pragma unroll
+        for (int u = 0; u < ROW_VEC; ++u) {
+#pragma unroll
+            for (int k = 0; k < NP; ++k) w[u][k] = C(k == 0 ? 1 : 0);
+        }
+        return;
+    }
+    load_planes4<NP, T, C>(p.w, p.w_np, c0, valid, p.vec != 0, w);
+}
+
 template <typename T, int NP>
 __global__ void __launch_bounds__(512) rmsnorm_fwd_kernel(const NormParams p) {
     using C = typename Compute<T>::type;
@@ -51,12 +65,18 @@ __global__ void __launch_bounds__(512) rmsnorm_fwd_kernel(const NormParams p) {
         C acc[NP];
 #pragma unroll
         for (int k = 0; k < NP; ++k) acc[k] = C(0);
-        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
-            C x[NP], sq[NP];
-            load_elem<NP, T, C>(p.x, p.np, xb + c, x);
-            s_mul<NP, C>(x, x, sq);
+        for (int64_t c0 = static_cast<int64_t>(threadIdx.x) * ROW_VEC; c0 < p.cols;
+             c0 += static_cast<int64_t>(blockDim.x) * ROW_VEC) {
+            const int valid = vec_count(p.cols, c0);
+            C x[ROW_VEC][NP];
+            load_planes4<NP, T, C>(p.x, p.np, xb + c0, valid, p.vec != 0, x);
 #pragma unroll
-            for (int k = 0; k < NP; ++k) acc[k] += sq[k];
+            for (int u = 0; u < ROW_VEC; ++u) {
+                C sq[NP];
+                s_mul<NP, C>(x[u], x[u], sq);
+#pragma unroll
+                for (int k = 0; k < NP; ++k) acc[k] += sq[k];
+            }
         }
         block_sum<NP, C>(acc, scratch);
         C m[NP], r[NP];
@@ -71,17 +91,18 @@ __global__ void __launch_bounds__(512) rmsnorm_fwd_kernel(const NormParams p) {
                 if (k == static_cast<int>(threadIdx.x)) static_cast<C*>(p.rstd)[row * p.np + k] = r[k];
         }
         const int64_t yb = row * p.y_rs;
-        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
-            C x[NP], w[NP], t[NP];
-            load_elem<NP, T, C>(p.x, p.np, xb + c, x);
-            s_mul<NP, C>(x, r, t);
-            if (p.w_np) {
-                load_weight<NP, T, C>(p, c, w);
-                s_mul<NP, C>(t, w, t);
-            }
+        for (int64_t c0 = static_cast<int64_t>(threadIdx.x) * ROW_VEC; c0 < p.cols;
+             c0 += static_cast<int64_t>(blockDim.x) * ROW_VEC) {
+            const int valid = vec_count(p.cols, c0);
+            C x[ROW_VEC][NP], w[ROW_VEC][NP], t[ROW_VEC][NP];
+            load_planes4<NP, T, C>(p.x, p.np, xb + c0, valid, p.vec != 0, x);
+            if (p.w_np) load_weight4<NP, T, C>(p, c0, valid, w);
 #pragma unroll
-            for (int k = 0; k < NP; ++k)
-                if (k < p.np) static_cast<T*>(p.y[k])[yb + c] = from_c<T>(t[k]);
+            for (int u = 0; u < ROW_VEC; ++u) {
+                s_mul<NP, C>(x[u], r, t[u]);
+                if (p.w_np) s_mul<NP, C>(t[u], w[u], t[u]);
+            }
+            store_planes4<NP, T, C>(p.y, p.np, yb + c0, valid, p.vec != 0, t);
         }
     }
 }
@@ -106,20 +127,25 @@ __global__ void __launch_bounds__(512) rmsnorm_bwd_kernel(const NormParams p) {
         C d[NP];
 #pragma unroll
         for (int k = 0; k < NP; ++k) d[k] = C(0);
-        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
-            C x[NP], g[NP], w[NP], gy[NP], t[NP];
-            load_elem<NP, T, C>(p.x, p.np, xb + c, x);
-            load_elem<NP, T, C>(p.g, p.np, gb + c, g);
-            if (p.w_np) {
-                load_weight<NP, T, C>(p, c, w);
-                s_mul<NP, C>(g, w, gy);
-            } else {
+        for (int64_t c0 = static_cast<int64_t>(threadIdx.x) * ROW_VEC; c0 < p.cols;
+             c0 += static_cast<int64_t>(blockDim.x) * ROW_VEC) {
+            const int valid = vec_count(p.cols, c0);
+            C x[ROW_VEC][NP], g[ROW_VEC][NP], w[ROW_VEC][NP];
+            load_planes4<NP, T, C>(p.x, p.np, xb + c0, valid, p.vec != 0, x);
+            load_planes4<NP, T, C>(p.g, p.np, gb + c0, valid, p.vec != 0, g);
+            if (p.w_np) load_weight4<NP, T, C>(p, c0, valid, w);
 #pragma unroll
-                for (int k = 0; k < NP; ++k) gy[k] = g[k];
+            for (int u = 0; u < ROW_VEC; ++u) {
+                C gy[NP], t[NP];
+                if (p.w_np) s_mul<NP, C>(g[u], w[u], gy);
+                else {
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) gy[k] = g[u][k];
+                }
+                s_mul<NP, C>(gy, x[u], t);
+#pragma unroll
+                for (int k = 0; k < NP; ++k) d[k] += t[k];
             }
-            s_mul<NP, C>(gy, x, t);
-#pragma unroll
-            for (int k = 0; k < NP; ++k) d[k] += t[k];
         }
         block_sum<NP, C>(d, scratch);
         C r2[NP], r3[NP], coef[NP];
@@ -129,29 +155,34 @@ __global__ void __launch_bounds__(512) rmsnorm_bwd_kernel(const NormParams p) {
 #pragma unroll
         for (int k = 0; k < NP; ++k) coef[k] *= inv_cols;
         const int64_t yb = row * p.y_rs;
-        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
-            C x[NP], g[NP], w[NP], gy[NP], a[NP], b[NP];
-            load_elem<NP, T, C>(p.x, p.np, xb + c, x);
-            load_elem<NP, T, C>(p.g, p.np, gb + c, g);
-            if (p.w_np) {
-                load_weight<NP, T, C>(p, c, w);
-                s_mul<NP, C>(g, w, gy);
-            } else {
+        for (int64_t c0 = static_cast<int64_t>(threadIdx.x) * ROW_VEC; c0 < p.cols;
+             c0 += static_cast<int64_t>(blockDim.x) * ROW_VEC) {
+            const int valid = vec_count(p.cols, c0);
+            C x[ROW_VEC][NP], g[ROW_VEC][NP], w[ROW_VEC][NP], out[ROW_VEC][NP];
+            load_planes4<NP, T, C>(p.x, p.np, xb + c0, valid, p.vec != 0, x);
+            load_planes4<NP, T, C>(p.g, p.np, gb + c0, valid, p.vec != 0, g);
+            if (p.w_np) load_weight4<NP, T, C>(p, c0, valid, w);
 #pragma unroll
-                for (int k = 0; k < NP; ++k) gy[k] = g[k];
+            for (int u = 0; u < ROW_VEC; ++u) {
+                C gy[NP], a[NP], b[NP];
+                if (p.w_np) s_mul<NP, C>(g[u], w[u], gy);
+                else {
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) gy[k] = g[u][k];
+                }
+                s_mul<NP, C>(r, gy, a);
+                s_mul<NP, C>(coef, x[u], b);
+#pragma unroll
+                for (int k = 0; k < NP; ++k) out[u][k] = a[k] - b[k];
+                if (want_dw && u < valid) {
+                    C xr[NP], gx[NP];
+                    s_mul<NP, C>(x[u], r, xr);
+                    s_mul<NP, C>(g[u], xr, gx);
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) dwp[k * p.cols + c0 + u] += gx[k];
+                }
             }
-            s_mul<NP, C>(r, gy, a);
-            s_mul<NP, C>(coef, x, b);
-#pragma unroll
-            for (int k = 0; k < NP; ++k)
-                if (k < p.np) static_cast<T*>(p.y[k])[yb + c] = from_c<T>(a[k] - b[k]);
-            if (want_dw) {
-                C xr[NP], gx[NP];
-                s_mul<NP, C>(x, r, xr);
-                s_mul<NP, C>(g, xr, gx);
-#pragma unroll
-                for (int k = 0; k < NP; ++k) dwp[k * p.cols + c] += gx[k];
-            }
+            store_planes4<NP, T, C>(p.y, p.np, yb + c0, valid, p.vec != 0, out);
         }
     }
     if (want_dw) {
@@ -180,6 +211,14 @@ static int norm_threads(int64_t cols) { return cols >= 2048 ? 512 : (cols >= 512
 template <typename T, int NP>
 static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, size_t ws_bytes, cudaStream_t s) {
     using C = typename Compute<T>::type;
+    {
+        const int eb = static_cast<int>(sizeof(T));
+        bool ok = p.cols % ROW_VEC == 0 && row_vec_ok(p.x, p.np, p.x_rs, eb) &&
+                  row_vec_ok(reinterpret_cast<const void* const*>(p.y), p.np, p.y_rs, eb);
+        if (backward) ok = ok && row_vec_ok(p.g, p.np, p.g_rs, eb);
+        if (p.w_np) ok = ok && row_vec_ok(p.w, p.w_np, 0, eb);
+        p.vec = ok ? 1 : 0;
+    }
     const int threads = norm_threads(p.cols);
     if (!backward) {
         const int grid = static_cast<int>(std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * 8));

@@ -38,6 +38,7 @@ struct SoftmaxParams {
     int causal;
     int64_t q_len, causal_shift;
     const void* dsum;               // attention backward: [rows][np] sum_d dO (*) O, compute type
+    int vec;                        // every plane and row stride allows ROW_VEC-element vector access
 };
 
 template <int NP, typename T, typename C>
@@ -58,20 +59,28 @@ __device__ __forceinline__ void softcap_series(C (&z)[NP], C cap, C (&d)[NP]) {
     for (int k = 0; k < NP; ++k) z[k] = cap * t[k];
 }
 
-// Pass 1 of every kernel here: the online log-sum-exp state of a row.
+// Pass 1 of every kernel here: the online log-sum-exp state of a row (keys <= limit when limit >= 0).
 template <typename T, int NP, typename C>
-__device__ __forceinline__ void row_lse(const SoftmaxParams& p, int64_t xb, C* scratch, C (&lse)[NP]) {
+__device__ __forceinline__ void row_lse(const SoftmaxParams& p, int64_t xb, C* scratch, C (&lse)[NP],
+                                        C scale = C(1), int64_t limit = -1) {
     C m = -INFINITY, S[NP];
 #pragma unroll
     for (int k = 0; k < NP; ++k) S[k] = C(0);
-    for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
-        C x[NP];
-        load_row_elem<NP, T, C>(p.x, p.np, xb + c, x);
-        if (p.softcap != 0.0) {
-            C d[NP];
-            softcap_series<NP, C>(x, C(p.softcap), d);
+    const int64_t end = (limit < 0 || limit >= p.cols) ? p.cols : limit + 1;  // limit < 0: every key
+    for (int64_t c0 = static_cast<int64_t>(threadIdx.x) * ROW_VEC; c0 < end; c0 += static_cast<int64_t>(blockDim.x) * ROW_VEC) {
+        const int valid = vec_count(end, c0);
+        C x[ROW_VEC][NP];
+        load_planes4<NP, T, C>(p.x, p.np, xb + c0, valid, p.vec != 0, x);
+#pragma unroll
+        for (int u = 0; u < ROW_VEC; ++u) {
+#pragma unroll
+            for (int k = 0; k < NP; ++k) x[u][k] *= scale;
+            if (p.softcap != 0.0) {
+                C d[NP];
+                softcap_series<NP, C>(x[u], C(p.softcap), d);
+            }
         }
-        lse_accumulate<NP, C>(m, S, x);
+        lse_accumulate4<NP, C>(m, S, x, valid);
     }
     block_lse_combine<NP, C>(m, S, scratch);
     lse_finish<NP, C>(m, S, lse);
@@ -85,16 +94,19 @@ __global__ void __launch_bounds__(512) softmax_fwd_kernel(const SoftmaxParams p)
         const int64_t xb = row * p.x_rs, yb = row * p.y_rs;
         C lse[NP];
         row_lse<T, NP, C>(p, xb, scratch, lse);
-        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
-            C x[NP], ls[NP];
-            load_row_elem<NP, T, C>(p.x, p.np, xb + c, x);
-            ls[0] = x[0] - lse[0];
+        for (int64_t c0 = static_cast<int64_t>(threadIdx.x) * ROW_VEC; c0 < p.cols;
+             c0 += static_cast<int64_t>(blockDim.x) * ROW_VEC) {
+            const int valid = vec_count(p.cols, c0);
+            C x[ROW_VEC][NP];
+            load_planes4<NP, T, C>(p.x, p.np, xb + c0, valid, p.vec != 0, x);
 #pragma unroll
-            for (int k = 1; k < NP; ++k) ls[k] = x[k] - lse[k];
-            if (!p.log) s_exp<NP, C>(ls, ls);
+            for (int u = 0; u < ROW_VEC; ++u) {
+                x[u][0] -= lse[0];
 #pragma unroll
-            for (int k = 0; k < NP; ++k)
-                if (k < p.np) static_cast<T*>(p.out[k])[yb + c] = from_c<T>(ls[k]);
+                for (int k = 1; k < NP; ++k) x[u][k] -= lse[k];
+                if (!p.log) s_exp<NP, C>(x[u], x[u]);
+            }
+            store_planes4<NP, T, C>(p.out, p.np, yb + c0, valid, p.vec != 0, x);
         }
     }
 }
@@ -110,40 +122,48 @@ __global__ void __launch_bounds__(512) softmax_bwd_kernel(const SoftmaxParams p)
         C s[NP];
 #pragma unroll
         for (int k = 0; k < NP; ++k) s[k] = C(0);
-        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
-            C g[NP];
-            load_row_elem<NP, T, C>(p.g, p.np, gb + c, g);
-            if (p.log) {
+        for (int64_t c0 = static_cast<int64_t>(threadIdx.x) * ROW_VEC; c0 < p.cols;
+             c0 += static_cast<int64_t>(blockDim.x) * ROW_VEC) {
+            const int valid = vec_count(p.cols, c0);
+            C g[ROW_VEC][NP], y[ROW_VEC][NP];
+            load_planes4<NP, T, C>(p.g, p.np, gb + c0, valid, p.vec != 0, g);
+            if (!p.log) load_planes4<NP, T, C>(p.y, p.np, yb + c0, valid, p.vec != 0, y);
 #pragma unroll
-                for (int k = 0; k < NP; ++k) s[k] += g[k];
-            } else {
-                C y[NP], t[NP];
-                load_row_elem<NP, T, C>(p.y, p.np, yb + c, y);
-                s_mul<NP, C>(g, y, t);
+            for (int u = 0; u < ROW_VEC; ++u) {
+                if (p.log) {
 #pragma unroll
-                for (int k = 0; k < NP; ++k) s[k] += t[k];
+                    for (int k = 0; k < NP; ++k) s[k] += g[u][k];
+                } else {
+                    C t[NP];
+                    s_mul<NP, C>(g[u], y[u], t);
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) s[k] += t[k];
+                }
             }
         }
         block_sum<NP, C>(s, scratch);
-        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
-            C g[NP], y[NP], r[NP];
-            load_row_elem<NP, T, C>(p.g, p.np, gb + c, g);
-            load_row_elem<NP, T, C>(p.y, p.np, yb + c, y);
-            if (p.log) {
-                C e[NP], t[NP];
-                s_exp<NP, C>(y, e);
-                s_mul<NP, C>(e, s, t);
+        for (int64_t c0 = static_cast<int64_t>(threadIdx.x) * ROW_VEC; c0 < p.cols;
+             c0 += static_cast<int64_t>(blockDim.x) * ROW_VEC) {
+            const int valid = vec_count(p.cols, c0);
+            C g[ROW_VEC][NP], y[ROW_VEC][NP], r[ROW_VEC][NP];
+            load_planes4<NP, T, C>(p.g, p.np, gb + c0, valid, p.vec != 0, g);
+            load_planes4<NP, T, C>(p.y, p.np, yb + c0, valid, p.vec != 0, y);
 #pragma unroll
-                for (int k = 0; k < NP; ++k) r[k] = g[k] - t[k];
-            } else {
-                C d[NP];
+            for (int u = 0; u < ROW_VEC; ++u) {
+                if (p.log) {
+                    C e[NP], t[NP];
+                    s_exp<NP, C>(y[u], e);
+                    s_mul<NP, C>(e, s, t);
 #pragma unroll
-                for (int k = 0; k < NP; ++k) d[k] = g[k] - s[k];
-                s_mul<NP, C>(y, d, r);
+                    for (int k = 0; k < NP; ++k) r[u][k] = g[u][k] - t[k];
+                } else {
+                    C d[NP];
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) d[k] = g[u][k] - s[k];
+                    s_mul<NP, C>(y[u], d, r[u]);
+                }
             }
-#pragma unroll
-            for (int k = 0; k < NP; ++k)
-                if (k < p.np) static_cast<T*>(p.out[k])[ob + c] = from_c<T>(r[k]);
+            store_planes4<NP, T, C>(p.out, p.np, ob + c0, valid, p.vec != 0, r);
         }
     }
 }
@@ -195,23 +215,27 @@ __global__ void __launch_bounds__(512) ce_bwd_kernel(const SoftmaxParams p) {
             lse[k] = k < p.np ? static_cast<const C*>(p.stats)[row * p.np + k] : C(0);
         }
         const int64_t xb = row * p.x_rs, ob = row * p.y_rs;
-        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
-            C z[NP], d[NP], ls[NP], P[NP], r[NP];
-            load_row_elem<NP, T, C>(p.x, p.np, xb + c, z);
-            if (p.softcap != 0.0) softcap_series<NP, C>(z, C(p.softcap), d);
-            ls[0] = z[0] - lse[0];
+        for (int64_t c0 = static_cast<int64_t>(threadIdx.x) * ROW_VEC; c0 < p.cols;
+             c0 += static_cast<int64_t>(blockDim.x) * ROW_VEC) {
+            const int valid = vec_count(p.cols, c0);
+            C z[ROW_VEC][NP], r[ROW_VEC][NP];
+            load_planes4<NP, T, C>(p.x, p.np, xb + c0, valid, p.vec != 0, z);
 #pragma unroll
-            for (int k = 1; k < NP; ++k) ls[k] = z[k] - lse[k];
-            s_exp<NP, C>(ls, P);
-            s_mul<NP, C>(g, P, r);
-            if (c == y) {
+            for (int u = 0; u < ROW_VEC; ++u) {
+                C d[NP], ls[NP], P[NP];
+                if (p.softcap != 0.0) softcap_series<NP, C>(z[u], C(p.softcap), d);
+                ls[0] = z[u][0] - lse[0];
 #pragma unroll
-                for (int k = 0; k < NP; ++k) r[k] -= g[k];
+                for (int k = 1; k < NP; ++k) ls[k] = z[u][k] - lse[k];
+                s_exp<NP, C>(ls, P);
+                s_mul<NP, C>(g, P, r[u]);
+                if (c0 + u == y) {
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) r[u][k] -= g[k];
+                }
+                if (p.softcap != 0.0) s_mul<NP, C>(r[u], d, r[u]);
             }
-            if (p.softcap != 0.0) s_mul<NP, C>(r, d, r);
-#pragma unroll
-            for (int k = 0; k < NP; ++k)
-                if (k < p.np) static_cast<T*>(p.out[k])[ob + c] = from_c<T>(r[k]);
+            store_planes4<NP, T, C>(p.out, p.np, ob + c0, valid, p.vec != 0, r);
         }
     }
 }
@@ -226,47 +250,37 @@ __global__ void __launch_bounds__(512) attn_probs_kernel(const SoftmaxParams p) 
     for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
         const int64_t xb = row * p.x_rs, yb = row * p.y_rs;
         const int64_t limit = p.causal ? (row % p.q_len) + p.causal_shift : p.cols - 1;  // last admissible key
-        C m = -INFINITY, S[NP];
-#pragma unroll
-        for (int k = 0; k < NP; ++k) S[k] = C(0);
-        for (int64_t c = threadIdx.x; c < p.cols && c <= limit; c += blockDim.x) {
-            C x[NP];
-            load_row_elem<NP, T, C>(p.x, p.np, xb + c, x);
-#pragma unroll
-            for (int k = 0; k < NP; ++k) x[k] *= sc;
-            lse_accumulate<NP, C>(m, S, x);
-        }
-        block_lse_combine<NP, C>(m, S, scratch);
         C lse[NP];
-        const bool empty = !(S[0] > C(0));
+        row_lse<T, NP, C>(p, xb, scratch, lse, sc, limit);
+        const bool empty = !(lse[0] > -INFINITY) || lse[0] != lse[0];
         if (empty) {
 #pragma unroll
             for (int k = 0; k < NP; ++k) lse[k] = C(0);
             lse[0] = INFINITY;  // a row without admissible keys: P = 0 (and 0 output)
-        } else {
-            lse_finish<NP, C>(m, S, lse);
         }
         if (threadIdx.x == 0) {
 #pragma unroll
             for (int k = 0; k < NP; ++k)
                 if (k < p.np) static_cast<C*>(p.stats)[row * p.np + k] = lse[k];
         }
-        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
-            C P[NP];
-            if (c <= limit && !empty) {
-                C x[NP];
-                load_row_elem<NP, T, C>(p.x, p.np, xb + c, x);
-                P[0] = x[0] * sc - lse[0];
+        for (int64_t c0 = static_cast<int64_t>(threadIdx.x) * ROW_VEC; c0 < p.cols;
+             c0 += static_cast<int64_t>(blockDim.x) * ROW_VEC) {
+            const int valid = vec_count(p.cols, c0);
+            C x[ROW_VEC][NP];
+            load_planes4<NP, T, C>(p.x, p.np, xb + c0, valid, p.vec != 0, x);
 #pragma unroll
-                for (int k = 1; k < NP; ++k) P[k] = x[k] * sc - lse[k];
-                s_exp<NP, C>(P, P);
-            } else {
+            for (int u = 0; u < ROW_VEC; ++u) {
+                if (c0 + u <= limit && !empty) {
+                    x[u][0] = x[u][0] * sc - lse[0];
 #pragma unroll
-                for (int k = 0; k < NP; ++k) P[k] = C(0);
+                    for (int k = 1; k < NP; ++k) x[u][k] = x[u][k] * sc - lse[k];
+                    s_exp<NP, C>(x[u], x[u]);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) x[u][k] = C(0);
+                }
             }
-#pragma unroll
-            for (int k = 0; k < NP; ++k)
-                if (k < p.np) static_cast<T*>(p.out[k])[yb + c] = from_c<T>(P[k]);
+            store_planes4<NP, T, C>(p.out, p.np, yb + c0, valid, p.vec != 0, x);
         }
     }
 }
@@ -285,16 +299,21 @@ __global__ void __launch_bounds__(256) attn_dscores_kernel(const SoftmaxParams p
         C ds[NP];
 #pragma unroll
         for (int k = 0; k < NP; ++k) ds[k] = k < p.np ? static_cast<const C*>(p.dsum)[row * p.np + k] : C(0);
-        for (int64_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
-            C P[NP], g[NP], r[NP];
-            load_row_elem<NP, T, C>(p.y, p.np, yb + c, P);
-            load_row_elem<NP, T, C>(p.g, p.np, gb + c, g);
+        for (int64_t c0 = static_cast<int64_t>(threadIdx.x) * ROW_VEC; c0 < p.cols;
+             c0 += static_cast<int64_t>(blockDim.x) * ROW_VEC) {
+            const int valid = vec_count(p.cols, c0);
+            C P[ROW_VEC][NP], g[ROW_VEC][NP], r[ROW_VEC][NP];
+            load_planes4<NP, T, C>(p.y, p.np, yb + c0, valid, p.vec != 0, P);
+            load_planes4<NP, T, C>(p.g, p.np, gb + c0, valid, p.vec != 0, g);
 #pragma unroll
-            for (int k = 0; k < NP; ++k) g[k] -= ds[k];
-            s_mul<NP, C>(P, g, r);
+            for (int u = 0; u < ROW_VEC; ++u) {
 #pragma unroll
-            for (int k = 0; k < NP; ++k)
-                if (k < p.np) static_cast<T*>(p.out[k])[ob + c] = from_c<T>(r[k] * sc);
+                for (int k = 0; k < NP; ++k) g[u][k] -= ds[k];
+                s_mul<NP, C>(P[u], g[u], r[u]);
+#pragma unroll
+                for (int k = 0; k < NP; ++k) r[u][k] *= sc;
+            }
+            store_planes4<NP, T, C>(p.out, p.np, ob + c0, valid, p.vec != 0, r);
         }
     }
 }
@@ -331,8 +350,23 @@ static void launch_rows_np(int which, const SoftmaxParams& p, cudaStream_t s) {
     }
 }
 
-static int dispatch_rows(int which, int dtype, const SoftmaxParams& p, void* stream, const char* what) {
+static int elem_bytes(int dtype) { return dtype == PK_F64 ? 8 : (dtype == PK_F32 ? 4 : 2); }
+
+static int dispatch_rows(int which, int dtype, SoftmaxParams& p, void* stream, const char* what) {
     if (p.rows == 0 || p.cols == 0) return PK_OK;
+    {
+        const int eb = elem_bytes(dtype);
+        bool ok = p.cols % ROW_VEC == 0;
+        const void* const* sets[4] = {p.x, p.y, p.g, reinterpret_cast<const void* const*>(p.out)};
+        const int64_t strides[4] = {p.x_rs, p.y_rs, p.g_rs, 0};
+        for (int i = 0; i < 4 && ok; ++i) {
+            if (!sets[i][0]) continue;
+            ok = row_vec_ok(sets[i], p.np, strides[i], eb);
+        }
+        // output planes share the row stride of their input role (x_rs or y_rs)
+        ok = ok && p.x_rs % ROW_VEC == 0 && p.y_rs % ROW_VEC == 0 && p.g_rs % ROW_VEC == 0;
+        p.vec = ok ? 1 : 0;
+    }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     void* tok;
     prof_begin(what, s, &tok);
