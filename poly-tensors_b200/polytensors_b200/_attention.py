@@ -79,14 +79,15 @@ def _block_heads(L, S, n_planes, esz, heads):
     return max(1, min(heads, _BLOCK_BYTES // max(per_head, 1)))
 
 
-def _probs(Sc, L, scale, causal):
-    """Scores -> probabilities in place; returns the per-row normaliser statistics."""
-    hb, _, S = Sc[0].shape
-    rows = hb * L
+def _probs(Sc, q_len, scale, causal, shift=0):
+    """Scores -> probabilities in place; returns the per-row normaliser statistics.  Row r of
+    each matrix is query shift + (r % q_len)."""
+    hb, Lq, S = Sc[0].shape
+    rows = hb * Lq
     stats = torch.empty(rows, len(Sc), dtype=K.compute_dtype(Sc[0].dtype), device=Sc[0].device)
     ps, keep = _lib.pointer_array(Sc)
-    status = _lib.load().pk_attn_probs(K.dtype_code(Sc[0].dtype), len(Sc) - 1, rows, S, L, ps, S, float(scale),
-                                       1 if causal else 0, 0, ps, S, stats.data_ptr(),
+    status = _lib.load().pk_attn_probs(K.dtype_code(Sc[0].dtype), len(Sc) - 1, rows, S, q_len, ps, S, float(scale),
+                                       1 if causal else 0, shift, ps, S, stats.data_ptr(),
                                        K._stream(Sc[0].device))
     _lib.check(status, "pk_attn_probs")
     return stats
@@ -114,6 +115,16 @@ def flash_forward(Q, Kp, V, causal, scale):
     return O
 
 
+def _query_tiles(L, S, causal):
+    """(start, stop, keys) per query tile: with a causal mask, query tile t only meets the keys up
+    to its last query, so tiling the queries skips most of the masked half of the scores."""
+    if not causal or L < 512:
+        return [(0, L, S)]
+    tiles = min(8, L // 256)
+    size = -(-L // tiles)
+    return [(q0, min(L, q0 + size), min(S, min(L, q0 + size))) for q0 in range(0, L, size)]
+
+
 def forward_planes(Q, Kp, V, causal, scale):
     """O planes (BH, L, Dv) for flattened (BH, T, D) planes."""
     if flash_eligible(Q, Kp, V):
@@ -124,12 +135,22 @@ def forward_planes(Q, Kp, V, causal, scale):
     outs = [torch.empty(BH, L, V[0].shape[2], dtype=Q[0].dtype, device=Q[0].device) for _ in Q]
     for h0 in range(0, BH, hb):
         h1 = min(BH, h0 + hb)
-        Sc = K.poly_matmul([q[h0:h1] for q in Q], [k[h0:h1].transpose(1, 2) for k in Kp])
-        _probs(Sc, L, scale, causal)
-        O = K.poly_matmul(Sc, [v[h0:h1] for v in V])
-        for dst, src in zip(outs, O):
-            dst[h0:h1].copy_(src)
+        for q0, q1, kend in _query_tiles(L, S, causal):
+            Sc = K.poly_matmul([q[h0:h1, q0:q1] for q in Q], [k[h0:h1, :kend].transpose(1, 2) for k in Kp])
+            _probs(Sc, q1 - q0, scale, causal, q0)
+            O = K.poly_matmul(Sc, [v[h0:h1, :kend] for v in V])
+            for dst, src in zip(outs, O):
+                dst[h0:h1, q0:q1].copy_(src)
     return outs
+
+
+def _accumulate(dst, src, first):
+    """dst (planes, a view) = src on the first contribution, dst + src afterwards."""
+    if first:
+        for d, s_ in zip(dst, src):
+            d.copy_(s_)
+    else:
+        K.series_map("add", len(dst) - 1, dst, src, p0=1.0, out=dst)
 
 
 def backward_planes(Q, Kp, V, O, dO, causal, scale, need):
@@ -141,33 +162,43 @@ def backward_planes(Q, Kp, V, O, dO, causal, scale, need):
     if prod[0].dtype in (torch.bfloat16, torch.float16):
         prod = [p.float() for p in prod]
     dsum = torch.stack(K.series_reduce(prod, BH * L, prod[0].shape[-1], 1), dim=-1)
-    dsum = dsum.to(K.compute_dtype(Q[0].dtype)).contiguous()
+    dsum = dsum.to(K.compute_dtype(Q[0].dtype)).contiguous().view(BH, L, D + 1)
     dQ = [torch.empty_like(q) for q in Q] if need[0] else None
     dK = [torch.empty_like(k) for k in Kp] if need[1] else None
     dV = [torch.empty_like(v) for v in V] if need[2] else None
     hb = _block_heads(L, S, len(Q), Q[0].element_size(), BH)
     code = K.dtype_code(Q[0].dtype)
+    tiles = _query_tiles(L, S, causal)
     for h0 in range(0, BH, hb):
         h1 = min(BH, h0 + hb)
-        sl = slice(h0, h1)
-        Pr = K.poly_matmul([q[sl] for q in Q], [k[sl].transpose(1, 2) for k in Kp])
-        _probs(Pr, L, scale, causal)
-        if dV is not None:
-            for dst, src in zip(dV, K.poly_matmul([p.transpose(1, 2) for p in Pr], [g[sl] for g in dO])):
-                dst[sl].copy_(src)
-        dP = K.poly_matmul([g[sl] for g in dO], [v[sl].transpose(1, 2) for v in V])
-        rows = (h1 - h0) * L
-        pp, k1 = _lib.pointer_array(Pr)
-        pd, k2 = _lib.pointer_array(dP)
-        status = _lib.load().pk_attn_dscores(code, D, rows, S, pp, S, pd, S, dsum[h0 * L:h1 * L].data_ptr(),
-                                             float(scale), pd, S, K._stream(Q[0].device))
-        _lib.check(status, "pk_attn_dscores")
-        if dQ is not None:
-            for dst, src in zip(dQ, K.poly_matmul(dP, [k[sl] for k in Kp])):
-                dst[sl].copy_(src)
+        hs = slice(h0, h1)
         if dK is not None:
-            for dst, src in zip(dK, K.poly_matmul([d.transpose(1, 2) for d in dP], [q[sl] for q in Q])):
-                dst[sl].copy_(src)
+            for t in dK:
+                t[hs].zero_()
+        if dV is not None:
+            for t in dV:
+                t[hs].zero_()
+        for q0, q1, kend in tiles:
+            qs, ks = slice(q0, q1), slice(0, kend)
+            Pr = K.poly_matmul([q[hs, qs] for q in Q], [k[hs, ks].transpose(1, 2) for k in Kp])
+            _probs(Pr, q1 - q0, scale, causal, q0)
+            if dV is not None:
+                part = K.poly_matmul([p.transpose(1, 2) for p in Pr], [g[hs, qs] for g in dO])
+                _accumulate([t[hs, ks] for t in dV], part, False)
+            dP = K.poly_matmul([g[hs, qs] for g in dO], [v[hs, ks].transpose(1, 2) for v in V])
+            rows = (h1 - h0) * (q1 - q0)
+            ds_rows = dsum[hs, qs].contiguous()
+            pp, k1 = _lib.pointer_array(Pr)
+            pd, k2 = _lib.pointer_array(dP)
+            status = _lib.load().pk_attn_dscores(code, D, rows, kend, pp, kend, pd, kend, ds_rows.data_ptr(),
+                                                 float(scale), pd, kend, K._stream(Q[0].device))
+            _lib.check(status, "pk_attn_dscores")
+            if dQ is not None:
+                for dst, src in zip(dQ, K.poly_matmul(dP, [k[hs, ks] for k in Kp])):
+                    dst[hs, qs].copy_(src)
+            if dK is not None:
+                part = K.poly_matmul([d.transpose(1, 2) for d in dP], [q[hs, qs] for q in Q])
+                _accumulate([t[hs, ks] for t in dK], part, False)
     return dQ, dK, dV
 
 

@@ -284,3 +284,24 @@ def test_flash_forward_bf16_against_oracle(n, shape, causal):
     with PolyTensor.plain_range():
         o = F.scaled_dot_product_attention(poly(Q), poly(Kp), poly(V), is_causal=causal)
     assert_close(coeffs(o), want, 3e-2, "through the API")
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, F32), (torch.float64, F64)])
+def test_causal_query_tiled_attention_against_oracle(dtype, tol):
+    """L >= 512 with a causal mask runs the head-blocked path in query tiles that only meet their
+    admissible key prefix (forward and backward)."""
+    from polytensors_b200 import PolyTensor
+
+    n, shape = 2, (1, 2, 640, 32)
+    Q, Kp, V, G = (series(shape, n, s, dtype) for s in (51, 52, 53, 54))
+    ref64 = [[p.double() for p in s] for s in (Q, Kp, V, G)]
+    fn = lambda q, k, v: ref.attention(q, k, v, is_causal=True)
+    want_o = fn(*ref64[:3])
+    want = ref.series_vjp(fn, ref64[:3], ref64[3])
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        q, k, v = (poly(s, requires_grad=True) for s in (Q, Kp, V))
+        o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+        o.backward(poly(G))
+    assert_close(coeffs(o), want_o, tol, "o")
+    for name, t, w in (("dq", q, want[0]), ("dk", k, want[1]), ("dv", v, want[2])):
+        assert_close(coeffs(t.grad), w, tol * (10 if dtype == torch.float64 else 1), name)
