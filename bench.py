@@ -317,7 +317,13 @@ def run_norm_ce(args, rank, world, device):
     mem_ms = sum(r["ms_per_launch"] * r["launches"] for r in rates.values())
     pk, source = peaks()
     value = mem_bytes / (mem_ms / 1e3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, dt, desc = cpu_norm_ce_rate(64, os.cpu_count() or 1)
+        cpu = {"value": rate, "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port", "sample": desc,
+               "ms_per_step_extrapolated": dt * 1e3 * 16384 / 64}
     return {
+        "cpu_baseline": cpu,
         "metric": "norm/CE kernels GB/s (configs[2]: RMSNorm+GELU+linear(32000)+CE fwd+bwd, degree 4, float32)",
         "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -331,6 +337,48 @@ def run_norm_ce(args, rank, world, device):
                      "frac": value / pk["hbm_gbs"], "traffic": None, "peak_source": f"hbm_gbs ({source})"},
         "clocks": clocks,
     }
+
+
+def cpu_norm_ce_rate(rows, threads):
+    """Reference algorithm (oracle restatement of the plain-range rules) for configs[2] on the host
+    CPU at `rows` rows: RMSNorm -> GELU -> linear(32000) -> CE forward and its series backward.
+    Returns (GB/s of the norm/CE algorithmic bytes scaled to the sample, seconds, description)."""
+    from oracle import polyref
+
+    torch.set_num_threads(threads)
+    n, H, V = 4, 4096, 32000
+    X = make_series((rows, H), n, 1, torch.float32)
+    g = torch.Generator().manual_seed(2)
+    W0 = [1 + 0.02 * torch.randn(H, generator=g)] + [torch.zeros(H) for _ in range(n)]
+    Wl = [0.02 * torch.randn(V, H, generator=g)] + [torch.zeros(V, H) for _ in range(n)]
+    target = torch.randint(0, V, (rows,), generator=g)
+
+    def loss_fn(Xs, ws, wl):
+        h = polyref.gelu(polyref.rms_norm(Xs, (H,), ws))
+        logits = polyref.cauchy(h, [w.t() for w in wl], lambda a, b: a @ b)
+        return polyref.cross_entropy(logits, target)
+
+    seed = [torch.tensor(1.0)] + [torch.tensor(0.0)] * n
+    t0 = time.perf_counter()
+    polyref.series_vjp(loss_fn, [X, W0, Wl], seed)
+    dt = time.perf_counter() - t0
+    P = n + 1
+    nbytes = (2 + 3) * P * rows * H * 4 + 3 * P * rows * V * 4
+    return nbytes / dt / 1e9, dt, f"{rows} of 16384 rows, fwd + series backward, float32, {dt:.1f} s"
+
+
+def cpu_attention_rate(L, threads):
+    """Reference SDPA decomposition (oracle) on a (1, 4, L, 128) head slice, causal, degree 3,
+    forward + series backward, float32.  Returns (coefficient TFLOP/s, description)."""
+    from oracle import polyref
+
+    torch.set_num_threads(threads)
+    n, shape = 3, (1, 4, L, 128)
+    Q, Kp, V, G = (make_series(shape, n, s, torch.float32) for s in (1, 2, 3, 4))
+    t0 = time.perf_counter()
+    polyref.series_vjp(lambda q, k, v: polyref.attention(q, k, v, is_causal=True), [Q, Kp, V], G)
+    dt = time.perf_counter() - t0
+    return attention_flops(1, 4, L, 128, n) / dt / 1e12, f"(1, 4, {L}, 128) head slice, fwd + backward, {dt:.1f} s"
 
 
 def attention_flops(B, H, L, D, n):
@@ -392,7 +440,12 @@ def run_attention(args, rank, world, device):
     fwd_flops = flops / 3
     pk, source = peaks()
     value = world * flops / (ms / 1e3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, desc = cpu_attention_rate(min(L, 1024), os.cpu_count() or 1)
+        cpu = {"value": rate, "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port", "sample": desc}
     return {
+        "cpu_baseline": cpu,
         "metric": f"poly-attention coeff TFLOP/s (configs[3]: causal, (8, 32, {L}, 128), degree 3, {args.dtype}, fwd+bwd)",
         "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.dtype,
