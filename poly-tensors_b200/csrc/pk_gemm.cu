@@ -127,7 +127,103 @@ __global__ void __launch_bounds__(256) stage_kernel(const StageParams p) {
     }
 }
 
+// float32 -> bf16 hi/lo staging, fast paths.  split4 writes the hi/lo pairs of four
+// consecutive k of one row (two 8-byte stores).
+__device__ __forceinline__ void split4_store(__nv_bfloat16* hi, __nv_bfloat16* lo, const float (&v)[4]) {
+    uint32_t h[2], l[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const __nv_bfloat16 h0 = __float2bfloat16_rn(v[2 * i]), h1 = __float2bfloat16_rn(v[2 * i + 1]);
+        const __nv_bfloat16 l0 = __float2bfloat16_rn(v[2 * i] - __bfloat162float(h0));
+        const __nv_bfloat16 l1 = __float2bfloat16_rn(v[2 * i + 1] - __bfloat162float(h1));
+        h[i] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
+        l[i] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
+    }
+    *reinterpret_cast<uint2*>(hi) = make_uint2(h[0], h[1]);
+    *reinterpret_cast<uint2*>(lo) = make_uint2(l[0], l[1]);
+}
+
+// k contiguous in the source (s_k == 1): grid.y walks (batch, plane, row), grid.x k in steps
+// of 4 per thread; 16-byte loads when the row start is 16-byte aligned.
+__global__ void __launch_bounds__(256) split_direct_kernel(const StageParams p, int64_t batch, int vec) {
+    const int64_t rows_total = batch * p.planes * p.rows;
+    const int64_t k = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (k >= p.Kp) return;
+    for (int64_t y = blockIdx.y; y < rows_total; y += gridDim.y) {
+        const int64_t r = y % p.rows;
+        const int pi = static_cast<int>((y / p.rows) % p.planes);
+        const int64_t b = y / (p.rows * p.planes);
+        const StagePlane pl = p.plane[pi];
+        const float* src = static_cast<const float*>(pl.src) + b * p.s_b + r * p.s_r;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (vec && k + 4 <= p.K) {
+            const float4 t = *reinterpret_cast<const float4*>(src + k);
+            v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (k + i < p.K) v[i] = src[k + i];
+        }
+        const int64_t sub0 = b * p.subs_per_batch + pl.dst_sub;
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.dst);
+        split4_store(dst + (sub0 * p.rows + r) * p.Kp + k, dst + ((sub0 + 1) * p.rows + r) * p.Kp + k, v);
+    }
+}
+
+// rows contiguous in the source (s_r == 1): a 64 x 64 tile is read along rows and written
+// along k through shared memory.  grid: x = k tiles, y = row tiles, z = batch * planes.
+__global__ void __launch_bounds__(256) split_transpose_kernel(const StageParams p) {
+    __shared__ float tile[64][65];
+    const int z = blockIdx.z;
+    const int pi = z % p.planes;
+    const int64_t b = z / p.planes;
+    const StagePlane pl = p.plane[pi];
+    const float* src = static_cast<const float*>(pl.src) + b * p.s_b;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 64, k0 = static_cast<int64_t>(blockIdx.x) * 64;
+    const int t = threadIdx.x;
+    {
+        const int tr = t & 63, tk = t >> 6;  // 64 rows x 4 k per pass, rows fastest (coalesced)
+        for (int kk = tk; kk < 64; kk += 4) {
+            const int64_t r = r0 + tr, k = k0 + kk;
+            tile[kk][tr] = (r < p.rows && k < p.K) ? src[r + k * p.s_k] : 0.f;
+        }
+    }
+    __syncthreads();
+    const int tk4 = (t & 15) * 4, tr = t >> 4;  // 16 rows x 16 four-k groups per pass
+    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.dst);
+    const int64_t sub0 = b * p.subs_per_batch + pl.dst_sub;
+    for (int rr = tr; rr < 64; rr += 16) {
+        const int64_t r = r0 + rr, k = k0 + tk4;
+        if (r >= p.rows || k >= p.Kp) continue;
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = tile[tk4 + i][rr];
+        split4_store(dst + (sub0 * p.rows + r) * p.Kp + k, dst + ((sub0 + 1) * p.rows + r) * p.Kp + k, v);
+    }
+}
+
 static int launch_stage(const StageParams& p, int64_t batch, bool has_kind[5], cudaStream_t stream) {
+    if (has_kind[STAGE_SPLIT_BF16] && !has_kind[STAGE_COPY_16] && !has_kind[STAGE_F64] &&
+        !has_kind[STAGE_C128_A] && !has_kind[STAGE_C128_B] && p.rows > 0 && p.Kp > 0 && batch > 0) {
+        if (p.s_k == 1) {
+            bool vec = p.s_r % 4 == 0 && p.s_b % 4 == 0;
+            for (int k = 0; k < p.planes; ++k)
+                if (reinterpret_cast<uintptr_t>(p.plane[k].src) % 16) vec = false;
+            const int64_t rows_total = batch * p.planes * p.rows;
+            dim3 grid(static_cast<unsigned>(ceil_div(p.Kp / 4, 256)),
+                      static_cast<unsigned>(std::min<int64_t>(rows_total, 65535)));
+            split_direct_kernel<<<grid, 256, 0, stream>>>(p, batch, vec ? 1 : 0);
+            PK_CHECK_LAUNCH("pk_poly_gemm: split kernel launch");
+            return PK_OK;
+        }
+        if (p.s_r == 1 && ceil_div(p.rows, 64) <= 65535 && batch * p.planes <= 65535) {
+            dim3 grid(static_cast<unsigned>(ceil_div(p.Kp, 64)), static_cast<unsigned>(ceil_div(p.rows, 64)),
+                      static_cast<unsigned>(batch * p.planes));
+            split_transpose_kernel<<<grid, 256, 0, stream>>>(p);
+            PK_CHECK_LAUNCH("pk_poly_gemm: split transpose kernel launch");
+            return PK_OK;
+        }
+    }
     if (p.rows == 0 || p.Kp == 0 || batch == 0) return PK_OK;
     const int64_t gx = ceil_div(p.Kp, 64), gy = ceil_div(p.rows, 32), gz = batch * p.planes;
     if (gy > 65535 || gz > 65535) return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: operand too large to stage");
