@@ -242,7 +242,8 @@ static int launch_stage(const StageParams& p, int64_t batch, bool has_kind[5], c
 
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 64;  // 64 bf16 = one 128-byte swizzle row
-constexpr int TC_THREADS = 192;  // warp 0: TMA, warp 1: MMA + TMEM owner, warps 2-5: epilogue
+constexpr int TC_EPI_WARPS = 8;  // two per TMEM lane quadrant, each draining half of the columns
+constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;  // warp 0: TMA, warp 1: MMA + TMEM owner, rest: epilogue
 
 struct TcParams {
     int planes, batch;
@@ -363,7 +364,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(&acc_full[s], 1);
-            mbar_init(&acc_empty[s], 128);
+            mbar_init(&acc_empty[s], 32 * TC_EPI_WARPS);
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
@@ -489,7 +490,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     } else {
         // ---------------- epilogue: TMEM -> registers -> global ----------------
+        // warp w drains lanes 32*(w%4).. (its TMEM lane quadrant) and column half (w-2)/4
         const uint32_t lane_base = 32u * (warp & 3);
+        const int half = (warp - 2) >> 2;
         uint32_t abuf = 0, aphase = 0;
         for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
             const TileCoord tc = decode_tile(p, t);
@@ -497,7 +500,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             tc_fence_after();
             const int row = tc.tm * TC_BM + lane_base + lane;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
+            for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(tmem_base + (lane_base << 16) + abuf * BN + c * 32, r);
                 tmem_ld_wait();
