@@ -443,11 +443,12 @@ def run_attention_fwd(args, rank, world, device):
 
 
 def run_attention(args, rank, world, device):
-    """causal series attention (8, 32, L, 128), degree 3, forward + backward."""
+    """causal series attention (8, 32, L, 128), degree 3, forward + backward
+    (--batch changes the batch for profiling runs)."""
     import torch.nn.functional as F
     from polytensors_b200 import PolyTensor
 
-    n, B, H, L, D = 3, 8, 32, args.seq, 128
+    n, B, H, L, D = 3, args.batch, 32, args.seq, 128
     dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
     q, k, v = (_series_poly((B, H, L, D), n, s, dtype, device, requires_grad=True) for s in (1, 2, 3))
     G = _series_poly((B, H, L, D), n, 4, dtype, device)
@@ -481,11 +482,11 @@ def run_attention(args, rank, world, device):
         cpu = {"value": rate, "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port", "sample": desc}
     return {
         "cpu_baseline": cpu,
-        "metric": f"poly-attention coeff TFLOP/s (configs[3]: causal, (8, 32, {L}, 128), degree 3, {args.dtype}, fwd+bwd)",
+        "metric": f"poly-attention coeff TFLOP/s (configs[3]: causal, ({B}, 32, {L}, 128), degree 3, {args.dtype}, fwd+bwd)",
         "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.dtype,
         "data": "synthetic: planes N(0,1)/k!, seeded",
-        "config": {"workload": f"attention B=8 H=32 L={L} D=128 degree 3 causal {args.dtype}",
+        "config": {"workload": f"attention B={B} H=32 L={L} D=128 degree 3 causal {args.dtype}",
                    "flops": "12*T*B*H*L(L+1)/2*D (causal pairs, no recompute)"},
         "roofline": {"bound": "tensor", "achieved": value / world, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": value / world / pk["bf16_tflops"], "traffic": None,
@@ -674,7 +675,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rows", type=int, default=16384, help="norm_ce: rows (batch*seq)")
     ap.add_argument("--seq", type=int, default=4096, help="attention: sequence length")
-    ap.add_argument("--batch", type=int, default=8, help="attention_fwd: batch")
+    ap.add_argument("--batch", type=int, default=8, help="attention / attention_fwd: batch")
     ap.add_argument("--dtype", default="f32", choices=["f32", "bf16"], help="attention: storage dtype")
     ap.add_argument("--layers", type=int, default=12, help="train: transformer layers")
     ap.add_argument("--micro", type=int, default=8, help="train: sequences per micro-batch")
