@@ -143,13 +143,15 @@ __device__ __forceinline__ void split4_store(__nv_bfloat16* hi, __nv_bfloat16* l
     *reinterpret_cast<uint2*>(lo) = make_uint2(l[0], l[1]);
 }
 
-// k contiguous in the source (s_k == 1): grid.y walks (batch, plane, row), grid.x k in steps
-// of 4 per thread; 16-byte loads when the row start is 16-byte aligned.
+// k contiguous in the source (s_k == 1): threads walk (batch, plane, row, k/4) flat, four k
+// per thread; 16-byte loads when row starts are 16-byte aligned.
 __global__ void __launch_bounds__(256) split_direct_kernel(const StageParams p, int64_t batch, int vec) {
-    const int64_t rows_total = batch * p.planes * p.rows;
-    const int64_t k = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
-    if (k >= p.Kp) return;
-    for (int64_t y = blockIdx.y; y < rows_total; y += gridDim.y) {
+    const int64_t kv = p.Kp / 4;
+    const int64_t total = batch * p.planes * p.rows * kv;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t k = (i % kv) * 4;
+        const int64_t y = i / kv;
         const int64_t r = y % p.rows;
         const int pi = static_cast<int>((y / p.rows) % p.planes);
         const int64_t b = y / (p.rows * p.planes);
@@ -161,8 +163,8 @@ __global__ void __launch_bounds__(256) split_direct_kernel(const StageParams p, 
             v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
         } else {
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                if (k + i < p.K) v[i] = src[k + i];
+            for (int j = 0; j < 4; ++j)
+                if (k + j < p.K) v[j] = src[k + j];
         }
         const int64_t sub0 = b * p.subs_per_batch + pl.dst_sub;
         __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.dst);
@@ -202,16 +204,94 @@ __global__ void __launch_bounds__(256) split_transpose_kernel(const StageParams 
     }
 }
 
+// 16-bit copy staging (bf16 / f16 planes), fast paths: k contiguous -> 8-byte copies of four
+// elements; rows contiguous -> 64 x 64 transpose through shared memory.
+__global__ void __launch_bounds__(256) copy16_direct_kernel(const StageParams p, int64_t batch, int vec) {
+    const int64_t kv = p.Kp / 4;
+    const int64_t total = batch * p.planes * p.rows * kv;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t k = (i % kv) * 4;
+        const int64_t y = i / kv;
+        const int64_t r = y % p.rows;
+        const int pi = static_cast<int>((y / p.rows) % p.planes);
+        const int64_t b = y / (p.rows * p.planes);
+        const StagePlane pl = p.plane[pi];
+        const uint16_t* src = static_cast<const uint16_t*>(pl.src) + b * p.s_b + r * p.s_r;
+        uint16_t v[4] = {0, 0, 0, 0};
+        if (vec && k + 4 <= p.K) {
+            const uint2 t = *reinterpret_cast<const uint2*>(src + k);
+            v[0] = t.x & 0xFFFFu; v[1] = t.x >> 16; v[2] = t.y & 0xFFFFu; v[3] = t.y >> 16;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (k + j < p.K) v[j] = src[k + j];
+        }
+        const int64_t sub0 = b * p.subs_per_batch + pl.dst_sub;
+        uint16_t* dst = static_cast<uint16_t*>(p.dst) + (sub0 * p.rows + r) * p.Kp + k;
+        *reinterpret_cast<uint2*>(dst) = make_uint2(static_cast<uint32_t>(v[0]) | (static_cast<uint32_t>(v[1]) << 16),
+                                                    static_cast<uint32_t>(v[2]) | (static_cast<uint32_t>(v[3]) << 16));
+    }
+}
+
+__global__ void __launch_bounds__(256) copy16_transpose_kernel(const StageParams p) {
+    __shared__ uint16_t tile[64][66];
+    const int z = blockIdx.z;
+    const int pi = z % p.planes;
+    const int64_t b = z / p.planes;
+    const StagePlane pl = p.plane[pi];
+    const uint16_t* src = static_cast<const uint16_t*>(pl.src) + b * p.s_b;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 64, k0 = static_cast<int64_t>(blockIdx.x) * 64;
+    const int t = threadIdx.x;
+    {
+        const int tr = t & 63, tk = t >> 6;
+        for (int kk = tk; kk < 64; kk += 4) {
+            const int64_t r = r0 + tr, k = k0 + kk;
+            tile[kk][tr] = (r < p.rows && k < p.K) ? src[r + k * p.s_k] : uint16_t(0);
+        }
+    }
+    __syncthreads();
+    const int tk4 = (t & 15) * 4, tr = t >> 4;
+    uint16_t* dst = static_cast<uint16_t*>(p.dst);
+    const int64_t sub0 = b * p.subs_per_batch + pl.dst_sub;
+    for (int rr = tr; rr < 64; rr += 16) {
+        const int64_t r = r0 + rr, k = k0 + tk4;
+        if (r >= p.rows || k >= p.Kp) continue;
+        *reinterpret_cast<uint2*>(dst + (sub0 * p.rows + r) * p.Kp + k) =
+            make_uint2(static_cast<uint32_t>(tile[tk4][rr]) | (static_cast<uint32_t>(tile[tk4 + 1][rr]) << 16),
+                       static_cast<uint32_t>(tile[tk4 + 2][rr]) | (static_cast<uint32_t>(tile[tk4 + 3][rr]) << 16));
+    }
+}
+
 static int launch_stage(const StageParams& p, int64_t batch, bool has_kind[5], cudaStream_t stream) {
+    if (has_kind[STAGE_COPY_16] && !has_kind[STAGE_SPLIT_BF16] && !has_kind[STAGE_F64] &&
+        !has_kind[STAGE_C128_A] && !has_kind[STAGE_C128_B] && p.rows > 0 && p.Kp > 0 && batch > 0) {
+        if (p.s_k == 1) {
+            bool vec = p.s_r % 4 == 0 && p.s_b % 4 == 0;
+            for (int k = 0; k < p.planes; ++k)
+                if (reinterpret_cast<uintptr_t>(p.plane[k].src) % 8) vec = false;
+            const int64_t total = batch * p.planes * p.rows * (p.Kp / 4);
+            const int grid = static_cast<int>(std::min<int64_t>(ceil_div(total, 256), static_cast<int64_t>(num_sms()) * 32));
+            copy16_direct_kernel<<<grid, 256, 0, stream>>>(p, batch, vec ? 1 : 0);
+            PK_CHECK_LAUNCH("pk_poly_gemm: copy kernel launch");
+            return PK_OK;
+        }
+        if (p.s_r == 1 && ceil_div(p.rows, 64) <= 65535 && batch * p.planes <= 65535) {
+            dim3 grid(static_cast<unsigned>(ceil_div(p.Kp, 64)), static_cast<unsigned>(ceil_div(p.rows, 64)),
+                      static_cast<unsigned>(batch * p.planes));
+            copy16_transpose_kernel<<<grid, 256, 0, stream>>>(p);
+            PK_CHECK_LAUNCH("pk_poly_gemm: copy transpose kernel launch");
+            return PK_OK;
+        }
+    }
     if (has_kind[STAGE_SPLIT_BF16] && !has_kind[STAGE_COPY_16] && !has_kind[STAGE_F64] &&
         !has_kind[STAGE_C128_A] && !has_kind[STAGE_C128_B] && p.rows > 0 && p.Kp > 0 && batch > 0) {
         if (p.s_k == 1) {
             bool vec = p.s_r % 4 == 0 && p.s_b % 4 == 0;
             for (int k = 0; k < p.planes; ++k)
                 if (reinterpret_cast<uintptr_t>(p.plane[k].src) % 16) vec = false;
-            const int64_t rows_total = batch * p.planes * p.rows;
-            dim3 grid(static_cast<unsigned>(ceil_div(p.Kp / 4, 256)),
-                      static_cast<unsigned>(std::min<int64_t>(rows_total, 65535)));
+            const int64_t total = batch * p.planes * p.rows * (p.Kp / 4);
+            const int grid = static_cast<int>(std::min<int64_t>(ceil_div(total, 256), static_cast<int64_t>(num_sms()) * 32));
             split_direct_kernel<<<grid, 256, 0, stream>>>(p, batch, vec ? 1 : 0);
             PK_CHECK_LAUNCH("pk_poly_gemm: split kernel launch");
             return PK_OK;
