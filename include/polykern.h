@@ -94,12 +94,24 @@ PK_API int pk_profile_query(const char* kernel, double* total_ms, int64_t* launc
  *                complex128 and lower planes are float64 (a real base with complex
  *                directions); pass degree+1 for "no complex plane".  Output plane k
  *                is complex128 iff some term A_i B_{k-i} has a complex factor.
- *   workspace:   device buffer of at least pk_poly_gemm_workspace_size(...) bytes,
- *                16-byte aligned.
+ *   workspace:   device buffer of at least pk_poly_gemm_workspace_query(...) bytes for
+ *                this call (pk_poly_gemm_workspace_size(...) bounds every call of the
+ *                shape); may be null when the query returns 0.  bf16 operands whose
+ *                planes are 16-byte aligned with k or rows contiguous (other strides
+ *                multiples of 8 elements, rows not overlapping) are read in place and
+ *                need no workspace; every other operand is staged through it.
  */
 PK_API size_t pk_poly_gemm_workspace_size(int dtype, int degree, int64_t batch,
                                    int64_t M, int64_t N, int64_t K,
                                    int a_complex_from, int b_complex_from);
+/* Workspace bytes the pk_poly_gemm call with these operands needs (*bytes; 0 = none).
+ * The reference has no workspace (its products are separate PyTorch GEMMs); this pairs
+ * with pk_poly_gemm, which replaces src/polytensors/_plain.py:118-128. */
+PK_API int pk_poly_gemm_workspace_query(int dtype, int degree, int64_t batch,
+                                        int64_t M, int64_t N, int64_t K,
+                                        const void* const* a_planes, int64_t a_bs, int64_t a_rs, int64_t a_cs,
+                                        const void* const* b_planes, int64_t b_bs, int64_t b_rs, int64_t b_cs,
+                                        int a_complex_from, int b_complex_from, size_t* bytes);
 PK_API int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K,
                  const void* const* a_planes, int64_t a_bs, int64_t a_rs, int64_t a_cs,
                  const void* const* b_planes, int64_t b_bs, int64_t b_rs, int64_t b_cs,
@@ -256,7 +268,7 @@ PK_API int pk_flash_attn_fwd(int dtype, int degree, int64_t bh, int64_t L, int64
  * device footprint after start-up, code with no allocator to link).  The scratch comes
  * from a fixed PK_NOALLOC_SCRATCH_BYTES array in the library's device memory, held on
  * every GPU that loads the library until the process exits.  Products needing more
- * scratch than that (pk_poly_gemm_workspace_size) fail with PK_ERR_UNSUPPORTED.  The
+ * scratch than that (pk_poly_gemm_workspace_query) fail with PK_ERR_UNSUPPORTED.  The
  * first call on a device looks up the array's address; make it before any stream
  * capture.  All calls share the array: calls that overlap on the GPU race, so order
  * them on one stream.  Allocates nothing.

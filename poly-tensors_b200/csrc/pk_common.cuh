@@ -252,6 +252,18 @@ __device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t smem_addr) {
     return d;
 }
 
+// The same layout with several 64-wide atoms along MN, `lbo` bytes apart (leading byte
+// offset = stride between MN atoms; stride byte offset = 1024 B between 8-row K groups).
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc_lbo(uint32_t smem_addr, uint32_t lbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>(1024u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(2u) << 61;
+    return d;
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }

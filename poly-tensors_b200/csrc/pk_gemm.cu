@@ -13,6 +13,7 @@
 //   float64 / complex128 : mma.sync m16n8k4 f64 (DMMA); a complex product is a sum of
 //                          real products over planar re / im / -im sub-planes.
 #include <algorithm>
+#include <cstring>
 #include <vector>
 
 #include "pk_common.cuh"
@@ -325,8 +326,24 @@ constexpr int TC_BK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int TC_EPI_WARPS = 8;  // two per TMEM lane quadrant, each draining half of the columns
 constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;  // warp 0: TMA, warp 1: MMA + TMEM owner, rest: epilogue
 
+// How the kernel reads an operand's planes (bf16 / f16 products; float32 products always
+// read the staged hi/lo workspace through one map).
+enum OperandMode {
+    OPM_STAGED = 0,   // K-major workspace sub-planes written by the staging kernels
+    OPM_KMAJOR = 1,   // the caller's planes, k contiguous: 64 x rows boxes
+    OPM_MNMAJOR = 2   // the caller's planes, rows contiguous: 64 (rows) x 64 (k) boxes
+};
+
+// One tensor map per operand plane (3-D: k or rows innermost, then the other, then batch).
+// float32 products use a[0] / b[0] only, over the whole staged workspace.
+struct TcMaps {
+    CUtensorMap a[PK_MAX_PLANES];
+    CUtensorMap b[PK_MAX_PLANES];
+};
+
 struct TcParams {
     int planes, batch;
+    int a_mn, b_mn;  // operand read MN-major (direct bf16 / f16 planes with rows contiguous)
     int M, N;
     int kblocks;
     int tiles_m, tiles_n, group_m;
@@ -418,8 +435,7 @@ __device__ __forceinline__ void store_row_chunk(const TcParams& p, int plane, in
 
 template <int BN, bool SPLIT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    tc_poly_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                        const TcParams p) {
+    tc_poly_gemm_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
     using Cfg = TcConfig<BN, SPLIT>;
     constexpr int STAGES = Cfg::STAGES;
     constexpr int NSUB = Cfg::NSUB;
@@ -449,8 +465,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
         fence_mbar_init();
-        tma_prefetch_desc(&map_a);
-        tma_prefetch_desc(&map_b);
+        const int nmaps = SPLIT ? 1 : p.planes;
+        for (int i = 0; i < nmaps; ++i) {
+            tma_prefetch_desc(&maps.a[i]);
+            tma_prefetch_desc(&maps.b[i]);
+        }
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -473,8 +492,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const TileCoord tc = decode_tile(p, t);
                 for (int i = 0; i <= tc.plane && ok; ++i) {
                     const int j = tc.plane - i;
-                    const int za = (tc.b * p.planes + i) * NSUB;
-                    const int zb = (tc.b * p.planes + j) * NSUB;
                     for (int kb = 0; kb < p.kblocks; ++kb) {
                         if (!mbar_wait_or_abort(&empty_bar[stage], phase ^ 1, abort_flag, p.status, 101)) {
                             ok = false;
@@ -482,13 +499,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         }
                         uint8_t* st = smem + stage * Cfg::STAGE_BYTES;
                         mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+                        if constexpr (SPLIT) {
+                            // staged workspace: z walks (batch, plane, hi/lo) sub-planes
+                            const int za = (tc.b * p.planes + i) * NSUB;
+                            const int zb = (tc.b * p.planes + j) * NSUB;
 #pragma unroll
-                        for (int h = 0; h < NSUB; ++h)
-                            tma_load_3d(st + h * Cfg::A_BYTES, &map_a, &full_bar[stage], kb * TC_BK, tc.tm * TC_BM, za + h);
+                            for (int h = 0; h < NSUB; ++h)
+                                tma_load_3d(st + h * Cfg::A_BYTES, &maps.a[0], &full_bar[stage], kb * TC_BK,
+                                            tc.tm * TC_BM, za + h);
 #pragma unroll
-                        for (int h = 0; h < NSUB; ++h)
-                            tma_load_3d(st + NSUB * Cfg::A_BYTES + h * Cfg::B_BYTES, &map_b, &full_bar[stage], kb * TC_BK,
-                                        tc.tn * BN, zb + h);
+                            for (int h = 0; h < NSUB; ++h)
+                                tma_load_3d(st + NSUB * Cfg::A_BYTES + h * Cfg::B_BYTES, &maps.b[0], &full_bar[stage],
+                                            kb * TC_BK, tc.tn * BN, zb + h);
+                        } else {
+                            // one map per plane, z = batch; MN-major tiles arrive as 64-row atoms
+                            if (p.a_mn) {
+#pragma unroll
+                                for (int h = 0; h < TC_BM / 64; ++h)
+                                    tma_load_3d(st + h * 8192, &maps.a[i], &full_bar[stage], tc.tm * TC_BM + h * 64,
+                                                kb * TC_BK, tc.b);
+                            } else {
+                                tma_load_3d(st, &maps.a[i], &full_bar[stage], kb * TC_BK, tc.tm * TC_BM, tc.b);
+                            }
+                            uint8_t* sb = st + Cfg::A_BYTES;
+                            if (p.b_mn) {
+#pragma unroll
+                                for (int h = 0; h < BN / 64; ++h)
+                                    tma_load_3d(sb + h * 8192, &maps.b[j], &full_bar[stage], tc.tn * BN + h * 64,
+                                                kb * TC_BK, tc.b);
+                            } else {
+                                tma_load_3d(sb, &maps.b[j], &full_bar[stage], kb * TC_BK, tc.tn * BN, tc.b);
+                            }
+                        }
                         issued_parity[stage] = static_cast<int>(phase);
                         if (++stage == STAGES) {
                             stage = 0;
@@ -512,7 +554,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc = f16_idesc(1u, TC_BM, BN);
+            // MN-major operands: transpose bits 15 (A) / 16 (B) of the instruction descriptor
+            const uint32_t idesc = f16_idesc(1u, TC_BM, BN) | (static_cast<uint32_t>(p.a_mn) << 15) |
+                                   (static_cast<uint32_t>(p.b_mn) << 16);
             uint32_t stage = 0, phase = 0;
             uint32_t abuf = 0, aphase = 0;
             bool ok = true;
@@ -537,10 +581,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const uint32_t b_hi = st + NSUB * Cfg::A_BYTES, b_lo = b_hi + Cfg::B_BYTES;
 #pragma unroll
                     for (int kk = 0; kk < TC_BK / 16; ++kk) {
-                        const uint32_t koff = kk * 32;  // 16 bf16 = 32 bytes along the swizzled row
-                        tc_mma_f16(d_tmem, sw128_kmajor_desc(a_hi + koff), sw128_kmajor_desc(b_hi + koff), idesc,
-                                   (it > 0 || kk > 0) ? 1u : 0u);
+                        // K-major: 16 bf16 = 32 bytes along the swizzled row; MN-major: 16 rows of
+                        // 128 bytes inside each 64-wide atom (atoms 8 KB apart)
+                        const uint64_t ad = p.a_mn ? sw128_mnmajor_desc_lbo(a_hi + kk * 2048, 8192)
+                                                   : sw128_kmajor_desc(a_hi + kk * 32);
+                        const uint64_t bd = p.b_mn ? sw128_mnmajor_desc_lbo(b_hi + kk * 2048, 8192)
+                                                   : sw128_kmajor_desc(b_hi + kk * 32);
+                        tc_mma_f16(d_tmem, ad, bd, idesc, (it > 0 || kk > 0) ? 1u : 0u);
                         if constexpr (SPLIT) {
+                            const uint32_t koff = kk * 32;
                             tc_mma_f16(d_tmem, sw128_kmajor_desc(a_hi + koff), sw128_kmajor_desc(b_lo + koff), idesc, 1u);
                             tc_mma_f16(d_tmem, sw128_kmajor_desc(a_lo + koff), sw128_kmajor_desc(b_hi + koff), idesc, 1u);
                         }
@@ -604,19 +653,55 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
-static int encode_operand_map(CUtensorMap* map, void* base, int64_t rows, int64_t Kp, int64_t depth, int box_rows) {
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(Kp), static_cast<cuuint64_t>(rows),
-                                static_cast<cuuint64_t>(depth)};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(Kp * 2), static_cast<cuuint64_t>(rows * Kp * 2)};
-    const cuuint32_t box[3] = {static_cast<cuuint32_t>(TC_BK), static_cast<cuuint32_t>(box_rows), 1u};
-    CUresult r = encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box,
+// 3-D bf16 tensor map with the 128-byte swizzle: dims {d0 (innermost), d1, d2}, byte strides
+// {s1, s2} of dims 1 and 2, box {64, box1, 1}.
+static int encode_map3(CUtensorMap* map, const void* base, int64_t d0, int64_t d1, int64_t d2, int64_t s1,
+                       int64_t s2, int box1) {
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1), static_cast<cuuint64_t>(d2)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(s1), static_cast<cuuint64_t>(s2)};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(TC_BK), static_cast<cuuint32_t>(box1), 1u};
+    CUresult r = encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
                               CU_TENSOR_MAP_SWIZZLE_128B);
     if (r != CUDA_SUCCESS) return fail(PK_ERR_CUDA, "pk_poly_gemm: cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
     return PK_OK;
 }
 
+// One operand of a tcgen05 product as the kernel reads it.
+struct TcOperand {
+    int mode;                      // OperandMode
+    int64_t rows;                  // M for A, N for B
+    int64_t K, Kp;
+    int64_t batch;
+    const void* const* planes;     // caller planes (direct modes)
+    int64_t s_b, s_rows, s_k;      // caller element strides (direct modes)
+    const char* ws;                // staged workspace base
+    const int* first;              // first staged sub-plane of each plane
+    int64_t subs;                  // staged sub-planes per batch entry
+};
+
+// Per-plane maps (bf16 / f16 products), or one map over the whole staged workspace (float32).
+static int encode_operand(CUtensorMap* maps, const TcOperand& o, int planes, bool split, int box_rows) {
+    if (split)
+        return encode_map3(&maps[0], o.ws, o.Kp, o.rows, o.batch * o.subs, o.Kp * 2, o.rows * o.Kp * 2, box_rows);
+    for (int p = 0; p < planes; ++p) {
+        int rc;
+        if (o.mode == OPM_KMAJOR) {
+            const int64_t sb = o.batch > 1 ? o.s_b * 2 : o.rows * o.s_rows * 2;
+            rc = encode_map3(&maps[p], o.planes[p], o.K, o.rows, o.batch, o.s_rows * 2, sb, box_rows);
+        } else if (o.mode == OPM_MNMAJOR) {
+            const int64_t sb = o.batch > 1 ? o.s_b * 2 : o.K * o.s_k * 2;
+            rc = encode_map3(&maps[p], o.planes[p], o.rows, o.K, o.batch, o.s_k * 2, sb, 64);
+        } else {
+            const char* base = o.ws + static_cast<int64_t>(o.first[p]) * o.rows * o.Kp * 2;
+            rc = encode_map3(&maps[p], base, o.Kp, o.rows, o.batch, o.Kp * 2, o.subs * o.rows * o.Kp * 2, box_rows);
+        }
+        if (rc) return rc;
+    }
+    return PK_OK;
+}
+
 template <int BN, bool SPLIT>
-static int launch_tc(TcParams& p, void* ws_a, void* ws_b, int64_t Kp, cudaStream_t stream) {
+static int launch_tc(TcParams& p, const TcOperand& a, const TcOperand& b, cudaStream_t stream) {
     using Cfg = TcConfig<BN, SPLIT>;
     static bool attr_set[64] = {false};
     int dev = 0;
@@ -627,12 +712,14 @@ static int launch_tc(TcParams& p, void* ws_a, void* ws_b, int64_t Kp, cudaStream
         if (e != cudaSuccess) return cuda_fail(e, "pk_poly_gemm: cudaFuncSetAttribute");
         attr_set[dev] = true;
     }
-    const int64_t depth = static_cast<int64_t>(p.batch) * p.planes * Cfg::NSUB;
-    CUtensorMap map_a, map_b;
-    int rc = encode_operand_map(&map_a, ws_a, p.M, Kp, depth, TC_BM);
+    TcMaps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    int rc = encode_operand(maps.a, a, p.planes, SPLIT, TC_BM);
     if (rc) return rc;
-    rc = encode_operand_map(&map_b, ws_b, p.N, Kp, depth, BN);
+    rc = encode_operand(maps.b, b, p.planes, SPLIT, BN);
     if (rc) return rc;
+    p.a_mn = (!SPLIT && a.mode == OPM_MNMAJOR) ? 1 : 0;
+    p.b_mn = (!SPLIT && b.mode == OPM_MNMAJOR) ? 1 : 0;
     p.tiles_m = static_cast<int>(ceil_div(p.M, TC_BM));
     p.tiles_n = static_cast<int>(ceil_div(p.N, BN));
     p.group_m = 8;
@@ -642,7 +729,7 @@ static int launch_tc(TcParams& p, void* ws_a, void* ws_b, int64_t Kp, cudaStream
     const int grid = static_cast<int>(std::min<int64_t>(total, num_sms()));
     void* tok;
     prof_begin("poly_gemm", stream, &tok);
-    tc_poly_gemm_kernel<BN, SPLIT><<<grid, TC_THREADS, Cfg::SMEM_BYTES, stream>>>(map_a, map_b, p);
+    tc_poly_gemm_kernel<BN, SPLIT><<<grid, TC_THREADS, Cfg::SMEM_BYTES, stream>>>(maps, p);
     prof_end("poly_gemm", stream, tok);
     PK_CHECK_LAUNCH("pk_poly_gemm: tcgen05 kernel launch");
     return PK_OK;
@@ -811,6 +898,7 @@ static int elem_size(int dtype) {
 }
 
 struct GemmPlan {
+    int a_mode = OPM_STAGED, b_mode = OPM_STAGED;
     int64_t Kp = 0;
     int64_t a_subs = 0, b_subs = 0;  // per batch entry
     size_t a_bytes = 0, b_bytes = 0, total = 0;
@@ -849,11 +937,60 @@ static GemmPlan plan_gemm(int dtype, int degree, int64_t batch, int64_t M, int64
     return g;
 }
 
+// Whether a bf16 operand's planes can be read in place by the tensor maps: 16-byte aligned
+// bases, one contiguous axis (k or rows) and the other strides multiples of 16 bytes that do
+// not make rows (or batch entries) overlap.  s_rows / s_k: element strides along the rows
+// (M or N) and along k.
+static int operand_mode(int dtype, const void* const* planes, int P, int64_t batch, int64_t rows, int64_t K,
+                        int64_t s_b, int64_t s_rows, int64_t s_k) {
+    if (dtype != PK_BF16) return OPM_STAGED;
+    for (int p = 0; p < P; ++p)
+        if (reinterpret_cast<uintptr_t>(planes[p]) % 16) return OPM_STAGED;
+    if (s_k == 1 && s_rows % 8 == 0 && s_rows >= K && (batch == 1 || (s_b % 8 == 0 && s_b >= rows * s_rows)))
+        return OPM_KMAJOR;
+    if (s_rows == 1 && s_k % 8 == 0 && s_k >= rows && (batch == 1 || (s_b % 8 == 0 && s_b >= K * s_k)))
+        return OPM_MNMAJOR;
+    return OPM_STAGED;
+}
+
+// The plan for one call: operands read in place need no workspace.
+static GemmPlan plan_call(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K, int acf, int bcf,
+                          const void* const* a_planes, int64_t a_bs, int64_t a_rs, int64_t a_cs,
+                          const void* const* b_planes, int64_t b_bs, int64_t b_rs, int64_t b_cs) {
+    GemmPlan g = plan_gemm(dtype, degree, batch, M, N, K, acf, bcf);
+    const int P = degree + 1;
+    g.a_mode = operand_mode(dtype, a_planes, P, batch, M, K, a_bs, a_rs, a_cs);
+    g.b_mode = operand_mode(dtype, b_planes, P, batch, N, K, b_bs, b_cs, b_rs);
+    if (g.a_mode != OPM_STAGED) g.a_bytes = 0;
+    if (g.b_mode != OPM_STAGED) g.b_bytes = 0;
+    g.total = (g.a_bytes + g.b_bytes) ? g.a_bytes + g.b_bytes + 1024 : 0;
+    return g;
+}
+
 }  // namespace pk
 
 using namespace pk;
 
 extern "C" {
+
+int pk_poly_gemm_workspace_query(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K,
+                                 const void* const* a_planes, int64_t a_bs, int64_t a_rs, int64_t a_cs,
+                                 const void* const* b_planes, int64_t b_bs, int64_t b_rs, int64_t b_cs,
+                                 int a_complex_from, int b_complex_from, size_t* bytes) {
+    if (!bytes) return fail(PK_ERR_ARG, "pk_poly_gemm_workspace_query: null result pointer");
+    *bytes = 0;
+    if (degree < 0 || degree >= PK_MAX_PLANES || batch < 0 || M < 0 || N < 0 || K < 0 || elem_size(dtype) == 0)
+        return fail(PK_ERR_ARG, "pk_poly_gemm_workspace_query: invalid dtype, degree or size");
+    if (batch == 0 || M == 0 || N == 0 || K == 0) return PK_OK;  // nothing is staged
+    if (!a_planes || !b_planes) return fail(PK_ERR_ARG, "pk_poly_gemm_workspace_query: null operand plane array");
+    for (int p = 0; p <= degree; ++p)
+        if (!a_planes[p] || !b_planes[p])
+            return fail(PK_ERR_ARG, "pk_poly_gemm_workspace_query: null operand plane pointer");
+    *bytes = plan_call(dtype, degree, batch, M, N, K, a_complex_from, b_complex_from, a_planes, a_bs, a_rs, a_cs,
+                       b_planes, b_bs, b_rs, b_cs)
+                 .total;
+    return PK_OK;
+}
 
 size_t pk_poly_gemm_workspace_size(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K,
                                    int a_complex_from, int b_complex_from) {
@@ -901,8 +1038,9 @@ int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int
     if (!a_planes || !b_planes) return fail(PK_ERR_ARG, "pk_poly_gemm: null operand plane array");
     for (int p = 0; p < P; ++p)
         if (!a_planes[p] || !b_planes[p]) return fail(PK_ERR_ARG, "pk_poly_gemm: null operand plane pointer");
-    const GemmPlan g = plan_gemm(dtype, degree, batch, M, N, K, a_complex_from, b_complex_from);
-    if (!workspace || workspace_bytes < g.total)
+    const GemmPlan g = plan_call(dtype, degree, batch, M, N, K, a_complex_from, b_complex_from, a_planes, a_bs, a_rs,
+                                 a_cs, b_planes, b_bs, b_rs, b_cs);
+    if (g.total > 0 && (!workspace || workspace_bytes < g.total))
         return fail(PK_ERR_WORKSPACE, "pk_poly_gemm: workspace of " + std::to_string(g.total) + " bytes required");
     char* ws = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(workspace) + 1023) & ~uintptr_t(1023));
     void* ws_a = ws;
@@ -930,9 +1068,9 @@ int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int
     sb.rows = N; sb.K = K; sb.Kp = g.Kp; sb.s_b = b_bs; sb.s_r = b_cs; sb.s_k = b_rs;
     sb.subs_per_batch = g.b_subs; sb.dst = ws_b;
     sa.elem_bytes = sb.elem_bytes = (dtype == PK_F64 || dtype == PK_C128) ? 8 : 2;
-    int rc = launch_stage(sa, batch, kinds_a, stream);
+    int rc = g.a_mode == OPM_STAGED ? launch_stage(sa, batch, kinds_a, stream) : PK_OK;
     if (rc) return rc;
-    rc = launch_stage(sb, batch, kinds_b, stream);
+    rc = g.b_mode == OPM_STAGED ? launch_stage(sb, batch, kinds_b, stream) : PK_OK;
     if (rc) return rc;
 
     if (dtype == PK_F32 || dtype == PK_BF16 || dtype == PK_F16) {
@@ -956,15 +1094,17 @@ int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int
         tp.status = device_status_ptr();
         const int64_t tiles256 = ceil_div(M, TC_BM) * ceil_div(N, 256) * batch * P;
         const bool wide = tiles256 >= 2 * num_sms();
+        const TcOperand oa{g.a_mode, M, K, g.Kp, batch, a_planes, a_bs, a_rs, a_cs,
+                           static_cast<const char*>(ws_a), g.a_first.data(), g.a_subs};
+        const TcOperand ob{g.b_mode, N, K, g.Kp, batch, b_planes, b_bs, b_cs, b_rs,
+                           static_cast<const char*>(ws_b), g.b_first.data(), g.b_subs};
         if (dtype == PK_F32) {
-            return wide ? launch_tc<256, true>(tp, ws_a, ws_b, g.Kp, stream)
-                        : launch_tc<128, true>(tp, ws_a, ws_b, g.Kp, stream);
+            return wide ? launch_tc<256, true>(tp, oa, ob, stream) : launch_tc<128, true>(tp, oa, ob, stream);
         }
         if (dtype == PK_F16) {
             return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: float16 planes are not implemented yet");
         }
-        return wide ? launch_tc<256, false>(tp, ws_a, ws_b, g.Kp, stream)
-                    : launch_tc<128, false>(tp, ws_a, ws_b, g.Kp, stream);
+        return wide ? launch_tc<256, false>(tp, oa, ob, stream) : launch_tc<128, false>(tp, oa, ob, stream);
     }
 
     // ---- DMMA path: build the per-output segment lists

@@ -12,7 +12,8 @@
 // Limits and behaviour
 //   - The array holds PK_NOALLOC_SCRATCH_BYTES (64 MiB).  Every GPU that loads the
 //     library keeps it reserved until the process exits.  A product whose workspace
-//     (pk_poly_gemm_workspace_size) is larger is rejected with PK_ERR_UNSUPPORTED.
+//     (pk_poly_gemm_workspace_query) is larger is rejected with PK_ERR_UNSUPPORTED;
+//     bf16 operands read in place need none.
 //   - The first call on a device looks up the array's device address for that device
 //     (cudaGetSymbolAddress with the device current).  Make that first call before any
 //     stream capture begins.
@@ -56,10 +57,10 @@ extern "C" int pk_poly_gemm_noalloc(int dtype, int degree, int64_t batch, int64_
                                     const void* const* b_planes, int64_t b_bs, int64_t b_rs, int64_t b_cs,
                                     void* const* c_planes, int64_t c_bs, int64_t c_rs, int a_complex_from,
                                     int b_complex_from, void* stream) {
-    const size_t need =
-        pk_poly_gemm_workspace_size(dtype, degree, batch, M, N, K, a_complex_from, b_complex_from);
-    if (need == 0)
-        return pk::fail(PK_ERR_ARG, "pk_poly_gemm_noalloc: invalid dtype, degree or size");
+    size_t need = 0;
+    const int qrc = pk_poly_gemm_workspace_query(dtype, degree, batch, M, N, K, a_planes, a_bs, a_rs, a_cs, b_planes,
+                                                 b_bs, b_rs, b_cs, a_complex_from, b_complex_from, &need);
+    if (qrc != PK_OK) return qrc;
     if (need > PK_NOALLOC_SCRATCH_BYTES)
         return pk::fail(PK_ERR_UNSUPPORTED,
                         "pk_poly_gemm_noalloc: this product needs " + std::to_string(need) +

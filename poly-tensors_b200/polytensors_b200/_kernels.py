@@ -6,6 +6,8 @@ CUDA stream.  Unsupported inputs raise ``NotImplementedError``; there is no CPU 
 eager-PyTorch fallback.
 """
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -99,14 +101,18 @@ def poly_matmul(a_planes, b_planes):
     c_bs, c_rs = (M * N, N)
     lib = _lib.load()
     degree = P - 1
-    ws_bytes = lib.pk_poly_gemm_workspace_size(code, degree, batch, M, N, K, acf, bcf)
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=a0.device)
     pa, ka = _lib.pointer_array(a_planes)
     pb, kb = _lib.pointer_array(b_planes)
     pc, kc = _lib.pointer_array(outs)
+    ws_bytes = ctypes.c_size_t(0)
+    _lib.check(lib.pk_poly_gemm_workspace_query(code, degree, batch, M, N, K, pa, a_bs, a_rs, a_cs,
+                                                pb, b_bs, b_rs, b_cs, acf, bcf, ctypes.byref(ws_bytes)),
+               "pk_poly_gemm_workspace_query")
+    ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device=a0.device) if ws_bytes.value else None
     status = lib.pk_poly_gemm(code, degree, batch, M, N, K,
                               pa, a_bs, a_rs, a_cs, pb, b_bs, b_rs, b_cs, pc, c_bs, c_rs,
-                              acf, bcf, ws.data_ptr(), ws.numel(), _stream(a0.device))
+                              acf, bcf, ws.data_ptr() if ws is not None else None,
+                              ws.numel() if ws is not None else 0, _stream(a0.device))
     _lib.check(status, "pk_poly_gemm")
     return outs
 

@@ -29,6 +29,10 @@ SIGNATURES = {
     "pk_profile_enable": (_i32, [_i32]),
     "pk_profile_query": (_i32, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
     "pk_poly_gemm_workspace_size": (_sz, [_i32, _i32, _i64, _i64, _i64, _i64, _i32, _i32]),
+    "pk_poly_gemm_workspace_query": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64,
+                                            _pp, _i64, _i64, _i64,
+                                            _pp, _i64, _i64, _i64,
+                                            _i32, _i32, ctypes.POINTER(ctypes.c_size_t)]),
     "pk_poly_gemm": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64,
                             _pp, _i64, _i64, _i64,
                             _pp, _i64, _i64, _i64,

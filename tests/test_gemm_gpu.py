@@ -94,6 +94,48 @@ def test_bf16_storage():
     check(A, B, TOL[torch.bfloat16])
 
 
+def _layout(planes, how):
+    """CUDA copies of (batch, R, K) planes laid out K-contiguous ("k"), rows-contiguous ("rows"),
+    or at a 2-byte offset that no tensor map can start from ("odd")."""
+    out = []
+    for p in planes:
+        if how == "k":
+            out.append(p.cuda().contiguous())
+        elif how == "rows":
+            out.append(p.transpose(-2, -1).contiguous().cuda().transpose(-2, -1))
+        else:
+            big = torch.zeros(*p.shape[:-1], p.shape[-1] + 1, dtype=p.dtype, device="cuda")
+            big[..., 1:] = p.cuda()
+            out.append(big[..., 1:])
+    return out
+
+
+@pytest.mark.parametrize("a_how", ["k", "rows", "odd"])
+@pytest.mark.parametrize("b_how", ["k", "rows", "odd"])
+def test_bf16_operands_read_in_place(a_how, b_how):
+    """bf16 planes are read where they lie (K-major or MN-major tensor maps, no staging) when
+    aligned, and staged otherwise; every combination, batched, with ragged M / N / K tails.
+    Tolerance 1e-2 of the plane max-norm: exact bf16 products, fp32 sums, bf16 output."""
+    from polytensors_b200 import _kernels, _lib
+
+    batch, M, N, K, n = 3, 200, 296, 136, 2
+    A = series((batch, M, K), n, 21, torch.bfloat16)
+    W = series((batch, N, K), n, 22, torch.bfloat16)         # B = W^T
+    a = _layout(A, a_how)
+    b = [w.transpose(-2, -1) for w in _layout(W, b_how)]   # "k": k contiguous in B
+    got = _kernels.poly_matmul(a, b)
+    check(A, [w.transpose(-2, -1) for w in W], 1e-2, got=got)
+    # the workspace query reports no scratch for the in-place operands
+    lib = _lib.load()
+    pa, ka = _lib.pointer_array(a)
+    pb, kb = _lib.pointer_array(b)
+    import ctypes
+    need = ctypes.c_size_t(1)
+    assert lib.pk_poly_gemm_workspace_query(_lib.PK_BF16, n, batch, M, N, K, pa, *a[0].stride(), pb,
+                                            *b[0].stride(), n + 1, n + 1, ctypes.byref(need)) == 0
+    assert (need.value == 0) == (a_how != "odd" and b_how != "odd")
+
+
 def test_empty_reduction_and_empty_output():
     from polytensors_b200 import _kernels
 

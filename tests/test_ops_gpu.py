@@ -286,7 +286,7 @@ def test_flash_forward_bf16_against_oracle(n, shape, causal):
     assert_close(coeffs(o), want, 3e-2, "through the API")
 
 
-@pytest.mark.parametrize("dtype,tol", [(torch.float32, F32), (torch.float64, F64)])
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, F32), (torch.float64, F64), (torch.bfloat16, 3e-2)])
 def test_causal_query_tiled_attention_against_oracle(dtype, tol):
     """L >= 512 with a causal mask runs the head-blocked path in query tiles that only meet their
     admissible key prefix (forward and backward)."""
