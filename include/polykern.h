@@ -260,7 +260,40 @@ PK_API int pk_attn_dscores(int dtype, int degree, int64_t rows, int64_t cols,
  */
 PK_API int pk_flash_attn_fwd(int dtype, int degree, int64_t bh, int64_t L, int64_t S, int64_t D,
                              const void* const* q, const void* const* k, const void* const* v,
-                             void* const* o, int causal, double scale, void* stream);
+                             void* const* o, int causal, double scale, void* stats, void* stream);
+/*   stats (optional, may be null): float32 [bh][L][degree+1], the softmax normaliser series of
+ *   every query row as pk_attn_probs writes it (lse_0, logz_1..n), for the backward. */
+
+/*
+ * Attention score products with the softmax in the epilogue, for the series attention
+ * backward (bfloat16 planes, degree <= 3).  Operands as in pk_poly_gemm (batch x M x K and
+ * batch x K x N, element strides), read in place: every plane 16-byte aligned with k or
+ * rows contiguous and the other strides multiples of 8 elements (PK_ERR_UNSUPPORTED
+ * otherwise).  Row values (stats, dsum): float32 [batch][M][degree+1], batch entries
+ * stats_bs / dsum_bs floats apart.  Query index of row r is r + causal_shift; with causal
+ * != 0, key j is admissible for it when j <= r + causal_shift.
+ *
+ * pk_attn_probs_gemm:   probs = exp-series(scale * Q K^T - stats) on admissible keys, 0 elsewhere
+ *                       (pk_poly_gemm followed by pk_attn_probs with the forward's stats).
+ * pk_attn_dscores_gemm: dscores = scale * probs (*) (dO V^T - dsum)
+ *                       (pk_poly_gemm followed by pk_attn_dscores).
+ * Together they replace the score and softmax-backward steps of the reference's attention
+ * backward (src/polytensors/_decompositions.py:28-43 through src/polytensors/_plain.py:342-347;
+ * degree-1 Triton form src/polytensors/_attention_kernels.py:84-201).
+ */
+PK_API int pk_attn_probs_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K,
+                              const void* const* q, int64_t q_bs, int64_t q_rs, int64_t q_cs,
+                              const void* const* kt, int64_t kt_bs, int64_t kt_rs, int64_t kt_cs,
+                              void* const* probs, int64_t p_bs, int64_t p_rs,
+                              const void* stats, int64_t stats_bs, double scale, int causal,
+                              int64_t causal_shift, void* stream);
+PK_API int pk_attn_dscores_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K,
+                                const void* const* dout, int64_t do_bs, int64_t do_rs, int64_t do_cs,
+                                const void* const* vt, int64_t vt_bs, int64_t vt_rs, int64_t vt_cs,
+                                const void* const* probs, int64_t p_bs, int64_t p_rs,
+                                const void* dsum, int64_t dsum_bs, double scale, int causal,
+                                int64_t causal_shift, void* const* dscores, int64_t ds_bs, int64_t ds_rs,
+                                void* stream);
 
 /*
  * pk_poly_gemm without a workspace argument, for callers that cannot allocate device

@@ -53,6 +53,7 @@ struct FlashParams {
     int n_slices, q_tiles, causal;
     float scale;
     void* o[FA_MAX_NP];
+    float* stats;  // optional: per query row (lse_0, logz_1..n) of the softmax series
     int* status;
 };
 
@@ -357,6 +358,27 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 #pragma unroll
                 for (int gg = 0; gg < 4; ++gg) lt[k] += red[(gg * 128 + row) * (NP + 1) + 1 + k];
             }
+            if (p.stats && slice == 0 && g == 0 && q < p.L) {
+                // the row's softmax normaliser as a series: lse_0 = m + log l_0 and the
+                // directions of log(l / l_0); a row without admissible keys gets lse_0 = +inf
+                float st[NP];
+                if (lt[0] > 0.f) {
+                    float u[NP];
+                    const float inv0 = 1.f / lt[0];
+                    u[0] = 1.f;
+#pragma unroll
+                    for (int k = 1; k < NP; ++k) u[k] = lt[k] * inv0;
+                    s_log1<NP, float>(u, st);
+                    st[0] = m_used + logf(lt[0]);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) st[k] = 0.f;
+                    st[0] = INFINITY;
+                }
+                float* dst = p.stats + (static_cast<int64_t>(bh) * p.L + q) * NP;
+#pragma unroll
+                for (int k = 0; k < NP; ++k) dst[k] = st[k];
+            }
             if (mbar_wait_or_abort(pv_done, (nblocks - 1) & 1, abort_flag, p.status, 408)) {
                 tc_fence_after();
                 const float inv = lt[0] > 0.f ? 1.f / lt[0] : 0.f;
@@ -439,7 +461,7 @@ using namespace pk;
 
 extern "C" int pk_flash_attn_fwd(int dtype, int degree, int64_t bh, int64_t L, int64_t S, int64_t D,
                                  const void* const* q, const void* const* k, const void* const* v, void* const* o,
-                                 int causal, double scale, void* stream) {
+                                 int causal, double scale, void* stats, void* stream) {
     if (dtype != PK_BF16) return fail(PK_ERR_UNSUPPORTED, "pk_flash_attn_fwd: bfloat16 planes only");
     if (degree < 0 || degree >= FA_MAX_NP) return fail(PK_ERR_UNSUPPORTED, "pk_flash_attn_fwd: degree must be <= 3");
     if (D != 64 && D != 128) return fail(PK_ERR_UNSUPPORTED, "pk_flash_attn_fwd: head dimension must be 64 or 128");
@@ -468,6 +490,7 @@ extern "C" int pk_flash_attn_fwd(int dtype, int degree, int64_t bh, int64_t L, i
     p.causal = causal ? 1 : 0;
     p.scale = static_cast<float>(scale);
     for (int a = 0; a < NP; ++a) p.o[a] = o[a];
+    p.stats = static_cast<float*>(stats);
     p.status = device_status_ptr();
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int dch = static_cast<int>(D / 64);

@@ -322,17 +322,8 @@ static int launch_stage(const StageParams& p, int64_t batch, bool has_kind[5], c
 // tcgen05 path
 
 constexpr int TC_BM = 128;
-constexpr int TC_BK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int TC_EPI_WARPS = 8;  // two per TMEM lane quadrant, each draining half of the columns
 constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;  // warp 0: TMA, warp 1: MMA + TMEM owner, rest: epilogue
-
-// How the kernel reads an operand's planes (bf16 / f16 products; float32 products always
-// read the staged hi/lo workspace through one map).
-enum OperandMode {
-    OPM_STAGED = 0,   // K-major workspace sub-planes written by the staging kernels
-    OPM_KMAJOR = 1,   // the caller's planes, k contiguous: 64 x rows boxes
-    OPM_MNMAJOR = 2   // the caller's planes, rows contiguous: 64 (rows) x 64 (k) boxes
-};
 
 // One tensor map per operand plane (3-D: k or rows innermost, then the other, then batch).
 // float32 products use a[0] / b[0] only, over the whole staged workspace.
@@ -653,53 +644,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
-// 3-D bf16 tensor map with the 128-byte swizzle: dims {d0 (innermost), d1, d2}, byte strides
-// {s1, s2} of dims 1 and 2, box {64, box1, 1}.
-static int encode_map3(CUtensorMap* map, const void* base, int64_t d0, int64_t d1, int64_t d2, int64_t s1,
-                       int64_t s2, int box1) {
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1), static_cast<cuuint64_t>(d2)};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(s1), static_cast<cuuint64_t>(s2)};
-    const cuuint32_t box[3] = {static_cast<cuuint32_t>(TC_BK), static_cast<cuuint32_t>(box1), 1u};
-    CUresult r = encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
-                              CU_TENSOR_MAP_SWIZZLE_128B);
-    if (r != CUDA_SUCCESS) return fail(PK_ERR_CUDA, "pk_poly_gemm: cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
-    return PK_OK;
-}
-
-// One operand of a tcgen05 product as the kernel reads it.
-struct TcOperand {
-    int mode;                      // OperandMode
-    int64_t rows;                  // M for A, N for B
-    int64_t K, Kp;
-    int64_t batch;
-    const void* const* planes;     // caller planes (direct modes)
-    int64_t s_b, s_rows, s_k;      // caller element strides (direct modes)
-    const char* ws;                // staged workspace base
-    const int* first;              // first staged sub-plane of each plane
-    int64_t subs;                  // staged sub-planes per batch entry
-};
-
-// Per-plane maps (bf16 / f16 products), or one map over the whole staged workspace (float32).
-static int encode_operand(CUtensorMap* maps, const TcOperand& o, int planes, bool split, int box_rows) {
-    if (split)
-        return encode_map3(&maps[0], o.ws, o.Kp, o.rows, o.batch * o.subs, o.Kp * 2, o.rows * o.Kp * 2, box_rows);
-    for (int p = 0; p < planes; ++p) {
-        int rc;
-        if (o.mode == OPM_KMAJOR) {
-            const int64_t sb = o.batch > 1 ? o.s_b * 2 : o.rows * o.s_rows * 2;
-            rc = encode_map3(&maps[p], o.planes[p], o.K, o.rows, o.batch, o.s_rows * 2, sb, box_rows);
-        } else if (o.mode == OPM_MNMAJOR) {
-            const int64_t sb = o.batch > 1 ? o.s_b * 2 : o.K * o.s_k * 2;
-            rc = encode_map3(&maps[p], o.planes[p], o.rows, o.K, o.batch, o.s_k * 2, sb, 64);
-        } else {
-            const char* base = o.ws + static_cast<int64_t>(o.first[p]) * o.rows * o.Kp * 2;
-            rc = encode_map3(&maps[p], base, o.Kp, o.rows, o.batch, o.Kp * 2, o.subs * o.rows * o.Kp * 2, box_rows);
-        }
-        if (rc) return rc;
-    }
-    return PK_OK;
-}
-
 template <int BN, bool SPLIT>
 static int launch_tc(TcParams& p, const TcOperand& a, const TcOperand& b, cudaStream_t stream) {
     using Cfg = TcConfig<BN, SPLIT>;
@@ -935,22 +879,6 @@ static GemmPlan plan_gemm(int dtype, int degree, int64_t batch, int64_t M, int64
     g.b_bytes = static_cast<size_t>(round_up(batch * g.b_subs * N * g.Kp * esz, 1024));
     g.total = g.a_bytes + g.b_bytes + 1024;  // +1024: alignment slack for the caller's pointer
     return g;
-}
-
-// Whether a bf16 operand's planes can be read in place by the tensor maps: 16-byte aligned
-// bases, one contiguous axis (k or rows) and the other strides multiples of 16 bytes that do
-// not make rows (or batch entries) overlap.  s_rows / s_k: element strides along the rows
-// (M or N) and along k.
-static int operand_mode(int dtype, const void* const* planes, int P, int64_t batch, int64_t rows, int64_t K,
-                        int64_t s_b, int64_t s_rows, int64_t s_k) {
-    if (dtype != PK_BF16) return OPM_STAGED;
-    for (int p = 0; p < P; ++p)
-        if (reinterpret_cast<uintptr_t>(planes[p]) % 16) return OPM_STAGED;
-    if (s_k == 1 && s_rows % 8 == 0 && s_rows >= K && (batch == 1 || (s_b % 8 == 0 && s_b >= rows * s_rows)))
-        return OPM_KMAJOR;
-    if (s_rows == 1 && s_k % 8 == 0 && s_k >= rows && (batch == 1 || (s_b % 8 == 0 && s_b >= K * s_k)))
-        return OPM_MNMAJOR;
-    return OPM_STAGED;
 }
 
 // The plan for one call: operands read in place need no workspace.

@@ -101,7 +101,9 @@ def flash_eligible(Q, Kp, V):
             and Kp[0].shape[-1] == D and V[0].shape[-1] == D)
 
 
-def flash_forward(Q, Kp, V, causal, scale):
+def flash_forward(Q, Kp, V, causal, scale, stats=None):
+    """O planes; ``stats`` (optional, float32 (BH, L, n+1)) receives each query row's softmax
+    normaliser series."""
     BH, L, D = Q[0].shape
     S = Kp[0].shape[1]
     O = [torch.empty_like(q) for q in Q]
@@ -110,9 +112,18 @@ def flash_forward(Q, Kp, V, causal, scale):
     pv, k3 = _lib.pointer_array(V)
     po, k4 = _lib.pointer_array(O)
     status = _lib.load().pk_flash_attn_fwd(_lib.PK_BF16, len(Q) - 1, BH, L, S, D, pq, pk_, pv, po,
-                                           1 if causal else 0, float(scale), K._stream(Q[0].device))
+                                           1 if causal else 0, float(scale),
+                                           stats.data_ptr() if stats is not None else None, K._stream(Q[0].device))
     _lib.check(status, "pk_flash_attn_fwd")
     return O
+
+
+def fused_backward_eligible(Q, Kp, V):
+    """Whether the backward builds probabilities and score gradients in the epilogue of their
+    products (pk_attn_probs_gemm / pk_attn_dscores_gemm): bfloat16 planes, degree <= 3, head
+    dimensions multiples of 8 (the flattened planes are contiguous, so every slice is aligned)."""
+    return (Q[0].dtype == torch.bfloat16 and len(Q) <= 4 and Q[0].shape[-1] % 8 == 0
+            and V[0].shape[-1] % 8 == 0)
 
 
 def _query_tiles(L, S, causal):
@@ -125,10 +136,11 @@ def _query_tiles(L, S, causal):
     return [(q0, min(L, q0 + size), min(S, min(L, q0 + size))) for q0 in range(0, L, size)]
 
 
-def forward_planes(Q, Kp, V, causal, scale):
-    """O planes (BH, L, Dv) for flattened (BH, T, D) planes."""
+def forward_planes(Q, Kp, V, causal, scale, stats=None):
+    """O planes (BH, L, Dv) for flattened (BH, T, D) planes; ``stats`` (optional, (BH, L, n+1) in
+    the compute dtype) receives each query row's softmax normaliser series."""
     if flash_eligible(Q, Kp, V):
-        return flash_forward(Q, Kp, V, causal, scale)
+        return flash_forward(Q, Kp, V, causal, scale, stats)
     BH, L, _ = Q[0].shape
     S = Kp[0].shape[1]
     hb = _block_heads(L, S, len(Q), Q[0].element_size(), BH)
@@ -137,11 +149,38 @@ def forward_planes(Q, Kp, V, causal, scale):
         h1 = min(BH, h0 + hb)
         for q0, q1, kend in _query_tiles(L, S, causal):
             Sc = K.poly_matmul([q[h0:h1, q0:q1] for q in Q], [k[h0:h1, :kend].transpose(1, 2) for k in Kp])
-            _probs(Sc, q1 - q0, scale, causal, q0)
+            st = _probs(Sc, q1 - q0, scale, causal, q0)
+            if stats is not None:
+                stats[h0:h1, q0:q1].copy_(st.view(h1 - h0, q1 - q0, -1))
             O = K.poly_matmul(Sc, [v[h0:h1, :kend] for v in V])
             for dst, src in zip(outs, O):
                 dst[h0:h1, q0:q1].copy_(src)
     return outs
+
+
+def _score_gemm(name, A, B, out, rows, scale, causal, shift, probs=None):
+    """pk_attn_probs_gemm / pk_attn_dscores_gemm on (hb, M, K) x (hb, K, N) bf16 plane views;
+    ``rows``: float32 (hb, M, n+1) view (statistics or dsum) with unit inner strides."""
+    hb, M, Kd = A[0].shape
+    N = B[0].shape[2]
+    pa, k1 = _lib.pointer_array(A)
+    pb, k2 = _lib.pointer_array(B)
+    po, k3 = _lib.pointer_array(out)
+    a_s, b_s, o_s = A[0].stride(), B[0].stride(), out[0].stride()
+    lib = _lib.load()
+    stream = K._stream(A[0].device)
+    if name == "probs":
+        status = lib.pk_attn_probs_gemm(_lib.PK_BF16, len(A) - 1, hb, M, N, Kd, pa, *a_s, pb, *b_s, po, o_s[0], o_s[1],
+                                        rows.data_ptr(), rows.stride(0), float(scale), 1 if causal else 0, shift,
+                                        stream)
+    else:
+        pp, k4 = _lib.pointer_array(probs)
+        p_s = probs[0].stride()
+        status = lib.pk_attn_dscores_gemm(_lib.PK_BF16, len(A) - 1, hb, M, N, Kd, pa, *a_s, pb, *b_s, pp, p_s[0],
+                                          p_s[1], rows.data_ptr(), rows.stride(0), float(scale),
+                                          1 if causal else 0, shift, po, o_s[0], o_s[1], stream)
+    _lib.check(status, f"pk_attn_{name}_gemm")
+    return out
 
 
 def _accumulate(dst, src, first):
@@ -153,7 +192,7 @@ def _accumulate(dst, src, first):
         K.series_map("add", len(dst) - 1, dst, src, p0=1.0, out=dst)
 
 
-def backward_planes(Q, Kp, V, O, dO, causal, scale, need):
+def backward_planes(Q, Kp, V, O, dO, causal, scale, need, stats=None):
     BH, L, _ = Q[0].shape
     S = Kp[0].shape[1]
     D = len(Q) - 1
@@ -169,6 +208,7 @@ def backward_planes(Q, Kp, V, O, dO, causal, scale, need):
     hb = _block_heads(L, S, len(Q), Q[0].element_size(), BH)
     code = K.dtype_code(Q[0].dtype)
     tiles = _query_tiles(L, S, causal)
+    fused = stats is not None and fused_backward_eligible(Q, Kp, V)
     for h0 in range(0, BH, hb):
         h1 = min(BH, h0 + hb)
         hs = slice(h0, h1)
@@ -180,6 +220,25 @@ def backward_planes(Q, Kp, V, O, dO, causal, scale, need):
                 t[hs].zero_()
         for q0, q1, kend in tiles:
             qs, ks = slice(q0, q1), slice(0, kend)
+            if fused:
+                hbn, Lq = h1 - h0, q1 - q0
+                Pr = [torch.empty(hbn, Lq, kend, dtype=Q[0].dtype, device=Q[0].device) for _ in Q]
+                _score_gemm("probs", [q[hs, qs] for q in Q], [k[hs, ks].transpose(1, 2) for k in Kp], Pr,
+                            stats[hs, qs], scale, causal, q0)
+                if dV is not None:
+                    part = K.poly_matmul([p.transpose(1, 2) for p in Pr], [g[hs, qs] for g in dO])
+                    _accumulate([t[hs, ks] for t in dV], part, False)
+                dS = [torch.empty_like(p) for p in Pr]
+                _score_gemm("dscores", [g[hs, qs] for g in dO], [v[hs, ks].transpose(1, 2) for v in V], dS,
+                            dsum[hs, qs], scale, causal, q0, probs=Pr)
+                del Pr
+                if dQ is not None:
+                    for dst, src in zip(dQ, K.poly_matmul(dS, [k[hs, ks] for k in Kp])):
+                        dst[hs, qs].copy_(src)
+                if dK is not None:
+                    part = K.poly_matmul([d.transpose(1, 2) for d in dS], [q[hs, qs] for q in Q])
+                    _accumulate([t[hs, ks] for t in dK], part, False)
+                continue
             Pr = K.poly_matmul([q[hs, qs] for q in Q], [k[hs, ks].transpose(1, 2) for k in Kp])
             _probs(Pr, q1 - q0, scale, causal, q0)
             if dV is not None:
@@ -212,8 +271,11 @@ class _SeriesAttention(torch.autograd.Function):
         Q = _flat(_planes(query, D), query.shape)
         Kp = _flat(_planes(key, D), key.shape)
         V = _flat(_planes(value, D), value.shape)
-        O = forward_planes(Q, Kp, V, causal, scale)
-        ctx.saved = (Q, Kp, V, O)
+        stats = None
+        if fused_backward_eligible(Q, Kp, V):
+            stats = torch.empty(*Q[0].shape[:2], len(Q), dtype=torch.float32, device=Q[0].device)
+        O = forward_planes(Q, Kp, V, causal, scale, stats)
+        ctx.saved = (Q, Kp, V, O, stats)
         ctx.meta = (causal, scale, D, query.shape, key.shape, value.shape)
         ctx.poly = tuple(isinstance(t, P) for t in (query, key, value))
         out_shape = (*query.shape[:-1], value.shape[-1])
@@ -223,11 +285,11 @@ class _SeriesAttention(torch.autograd.Function):
     @torch.autograd.function.once_differentiable
     def backward(ctx, grad):
         P = _poly_cls()
-        Q, Kp, V, O = ctx.saved
+        Q, Kp, V, O, stats = ctx.saved
         causal, scale, D, qs, ks, vs = ctx.meta
         dO = _flat(_planes(grad, D), (*qs[:-1], vs[-1]))
         need = tuple(p and n for p, n in zip(ctx.poly, ctx.needs_input_grad[:3]))
-        dQ, dK, dV = backward_planes(Q, Kp, V, O, dO, causal, scale, need)
+        dQ, dK, dV = backward_planes(Q, Kp, V, O, dO, causal, scale, need, stats)
         grads = []
         for g, shape in ((dQ, qs), (dK, ks), (dV, vs)):
             grads.append(P(tuple(t.view(shape) for t in g)) if g is not None else None)

@@ -58,7 +58,13 @@ SIGNATURES = {
     "pk_attn_dscores": (_i32, [_i32, _i32, _i64, _i64, _pp, _i64, _pp, _i64, _vp, ctypes.c_double, _pp, _i64,
                                _vp]),
     "pk_flash_attn_fwd": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64, _pp, _pp, _pp, _pp, _i32, ctypes.c_double,
-                                 _vp]),
+                                 _vp, _vp]),
+    "pk_attn_probs_gemm": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64, _pp, _i64, _i64, _i64,
+                                  _pp, _i64, _i64, _i64, _pp, _i64, _i64,
+                                  _vp, _i64, ctypes.c_double, _i32, _i64, _vp]),
+    "pk_attn_dscores_gemm": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64, _pp, _i64, _i64, _i64,
+                                    _pp, _i64, _i64, _i64, _pp, _i64, _i64,
+                                    _vp, _i64, ctypes.c_double, _i32, _i64, _pp, _i64, _i64, _vp]),
     "pk_poly_gemm_noalloc": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64,
                                     _pp, _i64, _i64, _i64,
                                     _pp, _i64, _i64, _i64,

@@ -305,3 +305,44 @@ def test_causal_query_tiled_attention_against_oracle(dtype, tol):
     assert_close(coeffs(o), want_o, tol, "o")
     for name, t, w in (("dq", q, want[0]), ("dk", k, want[1]), ("dv", v, want[2])):
         assert_close(coeffs(t.grad), w, tol * (10 if dtype == torch.float64 else 1), name)
+
+
+@pytest.mark.parametrize("n,shape,causal", [(3, (1, 2, 130, 64), False), (2, (2, 1, 200, 128), True),
+                                            (1, (1, 3, 96, 64), True), (0, (1, 2, 77, 64), False),
+                                            (3, (1, 1, 600, 64), True)])
+def test_bf16_backward_with_score_epilogues(n, shape, causal):
+    """bf16 backward through pk_attn_probs_gemm / pk_attn_dscores_gemm (probabilities rebuilt from
+    the forward's row statistics in the product's epilogue; score gradient likewise), against the
+    float64 oracle of the reference decomposition on the same bf16-rounded inputs; tolerance 3e-2
+    of the plane max-norm, as for the other bf16 attention paths."""
+    from polytensors_b200 import PolyTensor, _attention
+
+    Q, Kp, V, G = (series(shape, n, s, torch.bfloat16) for s in (61, 62, 63, 64))
+    flat = [_attention._flat([p.cuda() for p in X], shape) for X in (Q, Kp, V)]
+    assert _attention.fused_backward_eligible(*flat)
+    ref64 = [[p.double() for p in s] for s in (Q, Kp, V, G)]
+    fn = lambda q, k, v: ref.attention(q, k, v, is_causal=causal)
+    want_o = fn(*ref64[:3])
+    want = ref.series_vjp(fn, ref64[:3], ref64[3])
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        q, k, v = (poly(s, requires_grad=True) for s in (Q, Kp, V))
+        o = F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+        o.backward(poly(G))
+    assert_close(coeffs(o), want_o, 3e-2, "o")
+    for name, t, w in (("dq", q, want[0]), ("dk", k, want[1]), ("dv", v, want[2])):
+        assert_close(coeffs(t.grad), w, 3e-2, name)
+
+
+def test_flash_forward_row_statistics():
+    """pk_flash_attn_fwd's optional row statistics equal those of pk_attn_probs on the same scores."""
+    from polytensors_b200 import _attention, _kernels
+
+    n, shape = 3, (1, 2, 300, 128)
+    Q, Kp, V = (series(shape, n, s, torch.bfloat16) for s in (71, 72, 73))
+    flat = [_attention._flat([p.cuda() for p in X], shape) for X in (Q, Kp, V)]
+    BH, L = flat[0][0].shape[:2]
+    stats = torch.empty(BH, L, n + 1, dtype=torch.float32, device="cuda")
+    _attention.flash_forward(*flat, True, 1 / 128 ** 0.5, stats)
+    Sc = _kernels.poly_matmul([p.float() for p in flat[0]], [k.float().transpose(1, 2) for k in flat[1]])
+    want = _attention._probs(Sc, L, 1 / 128 ** 0.5, True).view(BH, L, n + 1)
+    torch.testing.assert_close(stats, want, rtol=2e-3, atol=2e-3)
