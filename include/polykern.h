@@ -118,6 +118,15 @@ PK_API int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t
                  void* const* c_planes, int64_t c_bs, int64_t c_rs,
                  int a_complex_from, int b_complex_from,
                  void* workspace, size_t workspace_bytes, void* stream);
+/* C_k += sum_{i+j=k} A_i B_j: pk_poly_gemm accumulating into the existing output planes
+ * (the beta = alpha = 1 case of addmm, src/polytensors/_range_ops.py:160-176).  Same
+ * arguments and workspace. */
+PK_API int pk_poly_gemm_accumulate(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K,
+                 const void* const* a_planes, int64_t a_bs, int64_t a_rs, int64_t a_cs,
+                 const void* const* b_planes, int64_t b_bs, int64_t b_rs, int64_t b_cs,
+                 void* const* c_planes, int64_t c_bs, int64_t c_rs,
+                 int a_complex_from, int b_complex_from,
+                 void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------
  * Elementwise series operations.  out = f(a) or f(a, b) for every element, all planes

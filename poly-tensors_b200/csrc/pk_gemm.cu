@@ -341,6 +341,7 @@ struct TcParams {
     int total_tiles;
     int out_kind;  // 0 = f32, 1 = bf16, 2 = f16
     int vec_ok;    // output rows 16-byte aligned: vectorised stores allowed
+    int accumulate;  // C += product (read-modify-write) instead of C = product
     int64_t c_bs, c_rs;
     void* c[PK_MAX_PLANES];
     int* status;
@@ -391,18 +392,49 @@ __device__ __forceinline__ void store_row_chunk(const TcParams& p, int plane, in
         float* dst = static_cast<float*>(p.c[plane]) + off;
         if (full) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                                  __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+            for (int j = 0; j < 32; j += 4) {
+                float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                       __uint_as_float(r[j + 3]));
+                if (p.accumulate) {
+                    const float4 o = *reinterpret_cast<const float4*>(dst + j);
+                    v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+                }
+                *reinterpret_cast<float4*>(dst + j) = v;
+            }
         } else {
-            for (int j = 0; j < 32 && col0 + j < p.N; ++j) dst[j] = __uint_as_float(r[j]);
+            for (int j = 0; j < 32 && col0 + j < p.N; ++j)
+                dst[j] = __uint_as_float(r[j]) + (p.accumulate ? dst[j] : 0.f);
         }
     } else {
         uint16_t* dst = static_cast<uint16_t*>(p.c[plane]) + off;
+        float prev[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) prev[j] = 0.f;
+        if (p.accumulate) {
+            if (full) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) {
+                    const uint4 o = *reinterpret_cast<const uint4*>(dst + j);
+                    const uint32_t w[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const uint16_t lo = static_cast<uint16_t>(w[t] & 0xFFFFu), hi = static_cast<uint16_t>(w[t] >> 16);
+                        prev[j + 2 * t] = p.out_kind == 1 ? __bfloat162float(__ushort_as_bfloat16(lo))
+                                                          : __half2float(__ushort_as_half(lo));
+                        prev[j + 2 * t + 1] = p.out_kind == 1 ? __bfloat162float(__ushort_as_bfloat16(hi))
+                                                              : __half2float(__ushort_as_half(hi));
+                    }
+                }
+            } else {
+                for (int j = 0; j < 32 && col0 + j < p.N; ++j)
+                    prev[j] = p.out_kind == 1 ? __bfloat162float(__ushort_as_bfloat16(dst[j]))
+                                              : __half2float(__ushort_as_half(dst[j]));
+            }
+        }
         uint32_t packed[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-            const float x0 = __uint_as_float(r[2 * j]), x1 = __uint_as_float(r[2 * j + 1]);
+            const float x0 = __uint_as_float(r[2 * j]) + prev[2 * j], x1 = __uint_as_float(r[2 * j + 1]) + prev[2 * j + 1];
             uint16_t h0, h1;
             if (p.out_kind == 1) {
                 h0 = __bfloat16_as_ushort(__float2bfloat16_rn(x0));
@@ -708,6 +740,7 @@ struct DmParams {
     uint8_t seg_a[DM_MAX_SEG];
     uint8_t seg_b[DM_MAX_SEG];
     int order[DM_MAX_OUT];  // output sub-planes, heaviest first
+    int accumulate;         // C += product
 };
 
 __device__ __forceinline__ void cp_async_16(void* smem, const void* gmem, bool valid) {
@@ -811,7 +844,8 @@ __global__ void __launch_bounds__(DM_THREADS, 1) dmma_poly_gemm_kernel(const DmP
                 const int col = n0 + wn * 32 + j * 8 + tg * 2 + (e & 1);
                 if (row < p.M && col < p.N) {
                     const int64_t idx = b * p.c_bs + static_cast<int64_t>(row) * p.c_rs + col;
-                    out.ptr[idx * out.mult + out.part] = acc[i][j][e];
+                    double* dst = out.ptr + idx * out.mult + out.part;
+                    *dst = acc[i][j][e] + (p.accumulate ? *dst : 0.0);
                 }
             }
         }
@@ -927,10 +961,14 @@ size_t pk_poly_gemm_workspace_size(int dtype, int degree, int64_t batch, int64_t
     return plan_gemm(dtype, degree, batch, M, N, K, a_complex_from, b_complex_from).total;
 }
 
-int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K, const void* const* a_planes,
-                 int64_t a_bs, int64_t a_rs, int64_t a_cs, const void* const* b_planes, int64_t b_bs, int64_t b_rs,
-                 int64_t b_cs, void* const* c_planes, int64_t c_bs, int64_t c_rs, int a_complex_from,
-                 int b_complex_from, void* workspace, size_t workspace_bytes, void* stream_ptr) {
+}  // extern "C"
+
+namespace pk {
+
+static int poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K, const void* const* a_planes,
+                     int64_t a_bs, int64_t a_rs, int64_t a_cs, const void* const* b_planes, int64_t b_bs, int64_t b_rs,
+                     int64_t b_cs, void* const* c_planes, int64_t c_bs, int64_t c_rs, int a_complex_from,
+                     int b_complex_from, void* workspace, size_t workspace_bytes, void* stream_ptr, int accumulate) {
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     if (degree < 0 || degree >= PK_MAX_PLANES)
         return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: degree must be in [0, " + std::to_string(PK_MAX_PLANES - 1) + "]");
@@ -953,6 +991,7 @@ int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int
         if (!c_planes[p]) return fail(PK_ERR_ARG, "pk_poly_gemm: null output plane pointer");
 
     if (K == 0) {  // empty reduction: the operands may have no storage at all
+        if (accumulate) return PK_OK;
         for (int p = 0; p < P; ++p) {
             const bool cplx = dtype == PK_C128 && (p >= a_complex_from || p >= b_complex_from);
             const int e = dtype == PK_C128 ? (cplx ? 16 : 8) : esz;
@@ -1019,6 +1058,7 @@ int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int
             if (reinterpret_cast<uintptr_t>(c_planes[p]) % 16 != 0) vec = false;
         }
         tp.vec_ok = vec ? 1 : 0;
+        tp.accumulate = accumulate;
         tp.status = device_status_ptr();
         const int64_t tiles256 = ceil_div(M, TC_BM) * ceil_div(N, 256) * batch * P;
         const bool wide = tiles256 >= 2 * num_sms();
@@ -1048,6 +1088,7 @@ int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int
     dp.ws_b = static_cast<const double*>(ws_b);
     dp.c_bs = c_bs;
     dp.c_rs = c_rs;
+    dp.accumulate = accumulate;
     int nseg = 0, nout = 0;
     for (int k = 0; k < P; ++k) {
         const bool out_complex = dtype == PK_C128 && (k >= a_complex_from || k >= b_complex_from);
@@ -1108,4 +1149,26 @@ int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int
     return PK_OK;
 }
 
+}  // namespace pk
+
+extern "C" {
+
+int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K, const void* const* a_planes,
+                 int64_t a_bs, int64_t a_rs, int64_t a_cs, const void* const* b_planes, int64_t b_bs, int64_t b_rs,
+                 int64_t b_cs, void* const* c_planes, int64_t c_bs, int64_t c_rs, int a_complex_from,
+                 int b_complex_from, void* workspace, size_t workspace_bytes, void* stream) {
+    return poly_gemm(dtype, degree, batch, M, N, K, a_planes, a_bs, a_rs, a_cs, b_planes, b_bs, b_rs, b_cs, c_planes,
+                     c_bs, c_rs, a_complex_from, b_complex_from, workspace, workspace_bytes, stream, 0);
+}
+
+int pk_poly_gemm_accumulate(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K,
+                            const void* const* a_planes, int64_t a_bs, int64_t a_rs, int64_t a_cs,
+                            const void* const* b_planes, int64_t b_bs, int64_t b_rs, int64_t b_cs,
+                            void* const* c_planes, int64_t c_bs, int64_t c_rs, int a_complex_from, int b_complex_from,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+    return poly_gemm(dtype, degree, batch, M, N, K, a_planes, a_bs, a_rs, a_cs, b_planes, b_bs, b_rs, b_cs, c_planes,
+                     c_bs, c_rs, a_complex_from, b_complex_from, workspace, workspace_bytes, stream, 1);
+}
+
 }  // extern "C"
+

@@ -183,15 +183,6 @@ def _score_gemm(name, A, B, out, rows, scale, causal, shift, probs=None):
     return out
 
 
-def _accumulate(dst, src, first):
-    """dst (planes, a view) = src on the first contribution, dst + src afterwards."""
-    if first:
-        for d, s_ in zip(dst, src):
-            d.copy_(s_)
-    else:
-        K.series_map("add", len(dst) - 1, dst, src, p0=1.0, out=dst)
-
-
 def backward_planes(Q, Kp, V, O, dO, causal, scale, need, stats=None):
     BH, L, _ = Q[0].shape
     S = Kp[0].shape[1]
@@ -221,43 +212,36 @@ def backward_planes(Q, Kp, V, O, dO, causal, scale, need, stats=None):
         for q0, q1, kend in tiles:
             qs, ks = slice(q0, q1), slice(0, kend)
             if fused:
+                # probabilities and score gradients straight from the products' epilogues
                 hbn, Lq = h1 - h0, q1 - q0
                 Pr = [torch.empty(hbn, Lq, kend, dtype=Q[0].dtype, device=Q[0].device) for _ in Q]
                 _score_gemm("probs", [q[hs, qs] for q in Q], [k[hs, ks].transpose(1, 2) for k in Kp], Pr,
                             stats[hs, qs], scale, causal, q0)
-                if dV is not None:
-                    part = K.poly_matmul([p.transpose(1, 2) for p in Pr], [g[hs, qs] for g in dO])
-                    _accumulate([t[hs, ks] for t in dV], part, False)
+            else:
+                Pr = K.poly_matmul([q[hs, qs] for q in Q], [k[hs, ks].transpose(1, 2) for k in Kp])
+                _probs(Pr, q1 - q0, scale, causal, q0)
+            if dV is not None:
+                K.poly_matmul([p.transpose(1, 2) for p in Pr], [g[hs, qs] for g in dO],
+                              out=[t[hs, ks] for t in dV], accumulate=True)
+            if fused:
                 dS = [torch.empty_like(p) for p in Pr]
                 _score_gemm("dscores", [g[hs, qs] for g in dO], [v[hs, ks].transpose(1, 2) for v in V], dS,
                             dsum[hs, qs], scale, causal, q0, probs=Pr)
-                del Pr
-                if dQ is not None:
-                    for dst, src in zip(dQ, K.poly_matmul(dS, [k[hs, ks] for k in Kp])):
-                        dst[hs, qs].copy_(src)
-                if dK is not None:
-                    part = K.poly_matmul([d.transpose(1, 2) for d in dS], [q[hs, qs] for q in Q])
-                    _accumulate([t[hs, ks] for t in dK], part, False)
-                continue
-            Pr = K.poly_matmul([q[hs, qs] for q in Q], [k[hs, ks].transpose(1, 2) for k in Kp])
-            _probs(Pr, q1 - q0, scale, causal, q0)
-            if dV is not None:
-                part = K.poly_matmul([p.transpose(1, 2) for p in Pr], [g[hs, qs] for g in dO])
-                _accumulate([t[hs, ks] for t in dV], part, False)
-            dP = K.poly_matmul([g[hs, qs] for g in dO], [v[hs, ks].transpose(1, 2) for v in V])
-            rows = (h1 - h0) * (q1 - q0)
-            ds_rows = dsum[hs, qs].contiguous()
-            pp, k1 = _lib.pointer_array(Pr)
-            pd, k2 = _lib.pointer_array(dP)
-            status = _lib.load().pk_attn_dscores(code, D, rows, kend, pp, kend, pd, kend, ds_rows.data_ptr(),
-                                                 float(scale), pd, kend, K._stream(Q[0].device))
-            _lib.check(status, "pk_attn_dscores")
+            else:
+                dS = K.poly_matmul([g[hs, qs] for g in dO], [v[hs, ks].transpose(1, 2) for v in V])
+                rows = (h1 - h0) * (q1 - q0)
+                ds_rows = dsum[hs, qs].contiguous()
+                pp, k1 = _lib.pointer_array(Pr)
+                pd, k2 = _lib.pointer_array(dS)
+                status = _lib.load().pk_attn_dscores(code, D, rows, kend, pp, kend, pd, kend, ds_rows.data_ptr(),
+                                                     float(scale), pd, kend, K._stream(Q[0].device))
+                _lib.check(status, "pk_attn_dscores")
+            del Pr
             if dQ is not None:
-                for dst, src in zip(dQ, K.poly_matmul(dP, [k[hs, ks] for k in Kp])):
-                    dst[hs, qs].copy_(src)
+                K.poly_matmul(dS, [k[hs, ks] for k in Kp], out=[t[hs, qs] for t in dQ])
             if dK is not None:
-                part = K.poly_matmul([d.transpose(1, 2) for d in dP], [q[hs, qs] for q in Q])
-                _accumulate([t[hs, ks] for t in dK], part, False)
+                K.poly_matmul([d.transpose(1, 2) for d in dS], [q[hs, qs] for q in Q],
+                              out=[t[hs, ks] for t in dK], accumulate=True)
     return dQ, dK, dV
 
 

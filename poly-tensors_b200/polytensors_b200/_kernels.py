@@ -61,11 +61,13 @@ def gemm_dtype(a_planes, b_planes):
     return _DTYPE_CODE[base], P, P, [base] * P
 
 
-def poly_matmul(a_planes, b_planes):
+def poly_matmul(a_planes, b_planes, out=None, accumulate=False):
     """C_k = sum_{i+j=k} A_i @ B_j for planes of shape (M, K) x (K, N) or (B, M, K) x (B, K, N).
 
     Mirrors plain_polynomial_product(matrix=True) (src/polytensors/_plain.py:118-128)
     including real-base / complex-direction promotion (src/polytensors/_plain.py:77-80).
+    ``out``: optional output planes (views with unit column stride) written in place;
+    ``accumulate``: add the product to ``out`` (C_k += ...) as addmm with beta = 1 does.
     """
     P = len(a_planes)
     if P != len(b_planes) or P == 0:
@@ -97,8 +99,20 @@ def poly_matmul(a_planes, b_planes):
     if b0.shape[-2] != K:
         raise ValueError(f"poly_matmul: inner dimensions differ ({K} vs {b0.shape[-2]})")
     shape = (batch, M, N) if batched else (M, N)
-    outs = [torch.empty(shape, dtype=dt, device=a0.device) for dt in out_dtypes]
-    c_bs, c_rs = (M * N, N)
+    if out is None:
+        if accumulate:
+            raise ValueError("poly_matmul: accumulate needs output planes")
+        outs = [torch.empty(shape, dtype=dt, device=a0.device) for dt in out_dtypes]
+        c_bs, c_rs = (M * N, N)
+    else:
+        outs = list(out)
+        if len(outs) != P or any(tuple(o.shape) != shape or o.dtype != dt or o.stride() != outs[0].stride()
+                                 for o, dt in zip(outs, out_dtypes)):
+            raise ValueError("poly_matmul: output planes must match the product's shape, dtypes and strides")
+        st = outs[0].stride()
+        if st[-1] != 1:
+            raise NotImplementedError("poly_matmul: output planes need unit column stride")
+        c_bs, c_rs = (st[0], st[1]) if batched else (0, st[0])
     lib = _lib.load()
     degree = P - 1
     pa, ka = _lib.pointer_array(a_planes)
@@ -109,11 +123,12 @@ def poly_matmul(a_planes, b_planes):
                                                 pb, b_bs, b_rs, b_cs, acf, bcf, ctypes.byref(ws_bytes)),
                "pk_poly_gemm_workspace_query")
     ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device=a0.device) if ws_bytes.value else None
-    status = lib.pk_poly_gemm(code, degree, batch, M, N, K,
+    fn = lib.pk_poly_gemm_accumulate if accumulate else lib.pk_poly_gemm
+    status = fn(code, degree, batch, M, N, K,
                               pa, a_bs, a_rs, a_cs, pb, b_bs, b_rs, b_cs, pc, c_bs, c_rs,
                               acf, bcf, ws.data_ptr() if ws is not None else None,
                               ws.numel() if ws is not None else 0, _stream(a0.device))
-    _lib.check(status, "pk_poly_gemm")
+    _lib.check(status, "pk_poly_gemm_accumulate" if accumulate else "pk_poly_gemm")
     return outs
 
 

@@ -136,6 +136,26 @@ def test_bf16_operands_read_in_place(a_how, b_how):
     assert (need.value == 0) == (a_how != "odd" and b_how != "odd")
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float64])
+def test_accumulate_into_strided_views(dtype):
+    """pk_poly_gemm_accumulate: C_k += sum A_i B_{k-i} into views of larger planes (addmm with
+    beta = 1), against the oracle product plus the prior contents."""
+    from polytensors_b200 import _kernels
+
+    n, batch, M, N, K = 2, 2, 136, 200, 72
+    A, B = series((batch, M, K), n, 31, dtype), series((batch, K, N), n, 32, dtype)
+    C0 = series((batch, M + 8, N + 16), n, 33, dtype)
+    big = cuda(C0)
+    views = [c[:, 8:, 16:] for c in big]
+    _kernels.poly_matmul(cuda(A), cuda(B), out=views, accumulate=True)
+    prod = ref.poly_matmul([a.double() for a in A], [b.double() for b in B])
+    want = [p + c[:, 8:, 16:].double() for p, c in zip(prod, C0)]
+    tol = {torch.float32: 1e-4, torch.bfloat16: 1e-2, torch.float64: 1e-10}[dtype]
+    assert max(ref.plane_errors(views, want)) <= tol
+    for c, c0 in zip(big, C0):   # untouched outside the views
+        assert torch.equal(c[:, :8].cpu(), c0[:, :8]) and torch.equal(c[:, :, :16].cpu(), c0[:, :, :16])
+
+
 def test_empty_reduction_and_empty_output():
     from polytensors_b200 import _kernels
 
