@@ -13,6 +13,7 @@
 #include <algorithm>
 
 #include "pk_common.cuh"
+#include "pk_rows.cuh"
 #include "pk_series.cuh"
 
 namespace pk {
@@ -32,6 +33,76 @@ struct MapParams {
     const void* a[PK_MAX_PLANES];
     const void* b[PK_MAX_PLANES];
 };
+
+// y = op(a, b) for one element's series (the operation table of pk_series_map).
+template <int NP, typename C>
+__device__ __forceinline__ void apply_op(const MapParams& p, const C (&a)[NP], const C (&b)[NP], C (&y)[NP]) {
+    switch (p.op) {
+        case PK_OP_COPY:
+#pragma unroll
+            for (int k = 0; k < NP; ++k) y[k] = a[k];
+            break;
+        case PK_OP_AFFINE:
+#pragma unroll
+            for (int k = 0; k < NP; ++k) y[k] = C(p.p0) * a[k];
+            y[0] += C(p.p1);
+            break;
+        case PK_OP_EXP: s_exp<NP, C>(a, y); break;
+        case PK_OP_LOG: s_log<NP, C>(a, y); break;
+        case PK_OP_SQRT: s_sqrt<NP, C>(a, y); break;
+        case PK_OP_RSQRT: s_rsqrt<NP, C>(a, y); break;
+        case PK_OP_RECIPROCAL: {
+            C one[NP];
+#pragma unroll
+            for (int k = 0; k < NP; ++k) one[k] = C(k == 0 ? 1 : 0);
+            s_div<NP, C>(one, a, y);
+            break;
+        }
+        case PK_OP_TANH: { C g[NP]; s_tanh<NP, C>(a, y, g); break; }
+        case PK_OP_SIGMOID: { C g[NP]; s_sigmoid<NP, C>(a, y, g); break; }
+        case PK_OP_GELU: { C d[NP]; s_gelu<NP, C>(a, y, d); break; }
+        case PK_OP_POWI: {
+            // repeated multiplication, as the reference's integer-power rule
+            // (src/polytensors/_dispatch.py:419-429); x^2 is one Cauchy product (_plain.py:291-293)
+            const int n = static_cast<int>(p.p0);
+#pragma unroll
+            for (int k = 0; k < NP; ++k) y[k] = C(k == 0 ? 1 : 0);
+            for (int r = 0; r < n; ++r) s_mul<NP, C>(y, a, y);
+            break;
+        }
+        case PK_OP_ADD:
+#pragma unroll
+            for (int k = 0; k < NP; ++k) y[k] = a[k] + C(p.p0) * b[k];
+            break;
+        case PK_OP_MUL: s_mul<NP, C>(a, b, y); break;
+        case PK_OP_DIV: s_div<NP, C>(a, b, y); break;
+        case PK_OP_GELU_BWD: {  // a = incoming gradient series, b = GELU input
+            C v[NP], d[NP];
+            s_gelu<NP, C>(b, v, d);
+            s_mul<NP, C>(a, d, y);
+            break;
+        }
+        case PK_OP_TANH_BWD: {  // a = gradient, b = tanh output: G (1 - Y^2)
+            C sq[NP];
+            s_mul<NP, C>(b, b, sq);
+#pragma unroll
+            for (int k = 0; k < NP; ++k) sq[k] = (k == 0 ? C(1) : C(0)) - sq[k];
+            s_mul<NP, C>(a, sq, y);
+            break;
+        }
+        case PK_OP_SIGMOID_BWD: {  // a = gradient, b = sigmoid output: G Y (1 - Y)
+            C om[NP], t[NP];
+#pragma unroll
+            for (int k = 0; k < NP; ++k) om[k] = (k == 0 ? C(1) : C(0)) - b[k];
+            s_mul<NP, C>(b, om, t);
+            s_mul<NP, C>(a, t, y);
+            break;
+        }
+        default:
+#pragma unroll
+            for (int k = 0; k < NP; ++k) y[k] = C(0);
+    }
+}
 
 template <typename T, int NP>
 __global__ void __launch_bounds__(256) series_map_kernel(const MapParams p) {
@@ -56,88 +127,54 @@ __global__ void __launch_bounds__(256) series_map_kernel(const MapParams p) {
             a[k] = (k < p.a_np && k < p.np) ? to_c<C>(static_cast<const T*>(p.a[k])[oa]) : C(0);
             b[k] = (p.b[0] != nullptr && k < p.b_np && k < p.np) ? to_c<C>(static_cast<const T*>(p.b[k])[ob]) : C(0);
         }
-        switch (p.op) {
-            case PK_OP_COPY:
-#pragma unroll
-                for (int k = 0; k < NP; ++k) y[k] = a[k];
-                break;
-            case PK_OP_AFFINE:
-#pragma unroll
-                for (int k = 0; k < NP; ++k) y[k] = C(p.p0) * a[k];
-                y[0] += C(p.p1);
-                break;
-            case PK_OP_EXP: s_exp<NP, C>(a, y); break;
-            case PK_OP_LOG: s_log<NP, C>(a, y); break;
-            case PK_OP_SQRT: s_sqrt<NP, C>(a, y); break;
-            case PK_OP_RSQRT: s_rsqrt<NP, C>(a, y); break;
-            case PK_OP_RECIPROCAL: {
-                C one[NP];
-#pragma unroll
-                for (int k = 0; k < NP; ++k) one[k] = C(k == 0 ? 1 : 0);
-                s_div<NP, C>(one, a, y);
-                break;
-            }
-            case PK_OP_TANH: { C g[NP]; s_tanh<NP, C>(a, y, g); break; }
-            case PK_OP_SIGMOID: { C g[NP]; s_sigmoid<NP, C>(a, y, g); break; }
-            case PK_OP_GELU: { C d[NP]; s_gelu<NP, C>(a, y, d); break; }
-            case PK_OP_POWI: {
-                // repeated multiplication, as the reference's integer-power rule
-                // (src/polytensors/_dispatch.py:419-429); x^2 is one Cauchy product (_plain.py:291-293)
-                const int n = static_cast<int>(p.p0);
-#pragma unroll
-                for (int k = 0; k < NP; ++k) y[k] = C(k == 0 ? 1 : 0);
-                for (int r = 0; r < n; ++r) s_mul<NP, C>(y, a, y);
-                break;
-            }
-            case PK_OP_ADD:
-#pragma unroll
-                for (int k = 0; k < NP; ++k) y[k] = a[k] + C(p.p0) * b[k];
-                break;
-            case PK_OP_MUL: s_mul<NP, C>(a, b, y); break;
-            case PK_OP_DIV: s_div<NP, C>(a, b, y); break;
-            case PK_OP_GELU_BWD: {  // a = incoming gradient series, b = GELU input
-                C v[NP], d[NP];
-                s_gelu<NP, C>(b, v, d);
-                s_mul<NP, C>(a, d, y);
-                break;
-            }
-            case PK_OP_TANH_BWD: {  // a = gradient, b = tanh output: G (1 - Y^2)
-                C sq[NP];
-                s_mul<NP, C>(b, b, sq);
-#pragma unroll
-                for (int k = 0; k < NP; ++k) sq[k] = (k == 0 ? C(1) : C(0)) - sq[k];
-                s_mul<NP, C>(a, sq, y);
-                break;
-            }
-            case PK_OP_SIGMOID_BWD: {  // a = gradient, b = sigmoid output: G Y (1 - Y)
-                C om[NP], t[NP];
-#pragma unroll
-                for (int k = 0; k < NP; ++k) om[k] = (k == 0 ? C(1) : C(0)) - b[k];
-                s_mul<NP, C>(b, om, t);
-                s_mul<NP, C>(a, t, y);
-                break;
-            }
-            default:
-#pragma unroll
-                for (int k = 0; k < NP; ++k) y[k] = C(0);
-        }
+        apply_op<NP, C>(p, a, b, y);
 #pragma unroll
         for (int k = 0; k < NP; ++k)
             if (k < p.np) static_cast<T*>(p.out[k])[oo] = from_c<T>(y[k]);
     }
 }
 
+// Dense operands with vector-aligned planes: four consecutive elements per thread and step,
+// one 8-32 byte access per plane (the last partial group element by element).
+template <typename T, int NP>
+__global__ void __launch_bounds__(256) series_map_vec_kernel(const MapParams p) {
+    using C = typename Compute<T>::type;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * ROW_VEC;
+    const int a_np = min(p.a_np, p.np);
+    const int b_np = p.b[0] != nullptr ? min(p.b_np, p.np) : 0;
+    for (int64_t off = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * ROW_VEC; off < p.numel;
+         off += stride) {
+        const int valid = vec_count(p.numel, off);
+        C a[ROW_VEC][NP], b[ROW_VEC][NP], y[ROW_VEC][NP];
+        load_planes4<NP, T, C>(p.a, a_np, off, valid, true, a);
+        load_planes4<NP, T, C>(p.b, b_np, off, valid, true, b);
+#pragma unroll
+        for (int u = 0; u < ROW_VEC; ++u) apply_op<NP, C>(p, a[u], b[u], y[u]);
+        store_planes4<NP, T, C>(p.out, p.np, off, valid, true, y);
+    }
+}
+
+template <typename T, int NP>
+static void launch_map_np(const MapParams& p, int grid, bool vec, cudaStream_t s) {
+    if (vec) {
+        const int g = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, ceil_div(p.numel, 256 * ROW_VEC))));
+        series_map_vec_kernel<T, NP><<<g, 256, 0, s>>>(p);
+    } else {
+        series_map_kernel<T, NP><<<grid, 256, 0, s>>>(p);
+    }
+}
+
 template <typename T>
-static void launch_map_t(const MapParams& p, int grid, cudaStream_t s) {
+static void launch_map_t(const MapParams& p, int grid, bool vec, cudaStream_t s) {
     switch (p.np) {
-        case 1: series_map_kernel<T, 1><<<grid, 256, 0, s>>>(p); break;
-        case 2: series_map_kernel<T, 2><<<grid, 256, 0, s>>>(p); break;
-        case 3: series_map_kernel<T, 3><<<grid, 256, 0, s>>>(p); break;
-        case 4: series_map_kernel<T, 4><<<grid, 256, 0, s>>>(p); break;
-        case 5: series_map_kernel<T, 5><<<grid, 256, 0, s>>>(p); break;
-        case 6: series_map_kernel<T, 6><<<grid, 256, 0, s>>>(p); break;
-        case 7: case 8: case 9: series_map_kernel<T, 9><<<grid, 256, 0, s>>>(p); break;
-        default: series_map_kernel<T, 16><<<grid, 256, 0, s>>>(p); break;
+        case 1: launch_map_np<T, 1>(p, grid, vec, s); break;
+        case 2: launch_map_np<T, 2>(p, grid, vec, s); break;
+        case 3: launch_map_np<T, 3>(p, grid, vec, s); break;
+        case 4: launch_map_np<T, 4>(p, grid, vec, s); break;
+        case 5: launch_map_np<T, 5>(p, grid, vec, s); break;
+        case 6: launch_map_np<T, 6>(p, grid, vec, s); break;
+        case 7: case 8: case 9: launch_map_np<T, 9>(p, grid, vec, s); break;
+        default: launch_map_np<T, 16>(p, grid, vec, s); break;
     }
 }
 
@@ -353,14 +390,20 @@ int pk_series_map(int op, int dtype, int degree, int ndim, const int64_t* shape,
     p.contig = dense(ndim, shape, out_strides) && dense(ndim, shape, a_strides) &&
                (!binary || dense(ndim, shape, b_strides));
     const int grid = grid_for(p.numel);
+    bool vec = p.contig != 0;
+    if (vec) {
+        const int esz = dtype == PK_F64 ? 8 : (dtype == PK_F32 ? 4 : 2);
+        vec = row_vec_ok(p.out, np, 0, esz) && row_vec_ok(p.a, std::min(a_planes, np), 0, esz) &&
+              (!binary || row_vec_ok(p.b, std::min(b_planes, np), 0, esz));
+    }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     void* tok;
     prof_begin("series_map", s, &tok);
     switch (dtype) {
-        case PK_F32: launch_map_t<float>(p, grid, s); break;
-        case PK_F64: launch_map_t<double>(p, grid, s); break;
-        case PK_BF16: launch_map_t<__nv_bfloat16>(p, grid, s); break;
-        case PK_F16: launch_map_t<__half>(p, grid, s); break;
+        case PK_F32: launch_map_t<float>(p, grid, vec, s); break;
+        case PK_F64: launch_map_t<double>(p, grid, vec, s); break;
+        case PK_BF16: launch_map_t<__nv_bfloat16>(p, grid, vec, s); break;
+        case PK_F16: launch_map_t<__half>(p, grid, vec, s); break;
         default: return fail(PK_ERR_UNSUPPORTED, "pk_series_map: unsupported dtype");
     }
     prof_end("series_map", s, tok);

@@ -11,6 +11,8 @@
 //   dx = r (*) gy - (r (*) r (*) r (*) d / cols) (*) x,   dw = sum_rows G (*) (x (*) r).
 #include <algorithm>
 
+#include <cooperative_groups.h>
+
 #include "pk_rows.cuh"
 
 namespace pk {
@@ -107,6 +109,64 @@ __global__ void __launch_bounds__(512) rmsnorm_fwd_kernel(const NormParams p) {
     }
 }
 
+// The same forward with the row held in registers: thread t owns columns (s * blockDim + t) * 4
+// .. +3 for s < STEPS, issues every load of its share of the row at once, and writes y from the
+// registers after the row's reduction, so x is read from HBM exactly once and never re-read.
+template <typename T, int NP, int STEPS>
+__global__ void __launch_bounds__(512, 1) rmsnorm_fwd_reg_kernel(const NormParams p) {
+    using C = typename Compute<T>::type;
+    __shared__ C scratch[16 * NP];
+    const int64_t span = static_cast<int64_t>(blockDim.x) * ROW_VEC;
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        const int64_t xb = row * p.x_rs;
+        C x[STEPS][ROW_VEC][NP];
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+            const int64_t c0 = s * span + static_cast<int64_t>(threadIdx.x) * ROW_VEC;
+            load_planes4<NP, T, C>(p.x, p.np, xb + c0, max(0, vec_count(p.cols, c0)), p.vec != 0, x[s]);
+        }
+        C acc[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) acc[k] = C(0);
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+#pragma unroll
+            for (int u = 0; u < ROW_VEC; ++u) {
+                C sq[NP];
+                s_mul<NP, C>(x[s][u], x[s][u], sq);
+#pragma unroll
+                for (int k = 0; k < NP; ++k) acc[k] += sq[k];
+            }
+        }
+        block_sum<NP, C>(acc, scratch);
+        C m[NP], r[NP];
+        const C inv_cols = C(1) / C(p.cols);
+#pragma unroll
+        for (int k = 0; k < NP; ++k) m[k] = acc[k] * inv_cols;
+        m[0] += C(p.eps);
+        s_rsqrt<NP, C>(m, r);
+        if (p.rstd && threadIdx.x < p.np) {
+#pragma unroll
+            for (int k = 0; k < NP; ++k)
+                if (k == static_cast<int>(threadIdx.x)) static_cast<C*>(p.rstd)[row * p.np + k] = r[k];
+        }
+        const int64_t yb = row * p.y_rs;
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+            const int64_t c0 = s * span + static_cast<int64_t>(threadIdx.x) * ROW_VEC;
+            const int valid = max(0, vec_count(p.cols, c0));
+            C w[ROW_VEC][NP], t[ROW_VEC][NP];
+            if (p.w_np) load_weight4<NP, T, C>(p, c0, valid, w);
+#pragma unroll
+            for (int u = 0; u < ROW_VEC; ++u) {
+                s_mul<NP, C>(x[s][u], r, t[u]);
+                if (p.w_np) s_mul<NP, C>(t[u], w[u], t[u]);
+            }
+            store_planes4<NP, T, C>(p.y, p.np, yb + c0, valid, p.vec != 0, t);
+        }
+    }
+}
+
 // Each CTA walks rows blockIdx.x, blockIdx.x + gridDim.x, ... and keeps its weight-gradient
 // partial sums for the columns it owns in shared memory (np x cols values).
 template <typename T, int NP>
@@ -178,8 +238,10 @@ __global__ void __launch_bounds__(512) rmsnorm_bwd_kernel(const NormParams p) {
                     C xr[NP], gx[NP];
                     s_mul<NP, C>(x[u], r, xr);
                     s_mul<NP, C>(g[u], xr, gx);
+                    // vector layout: [k][u][cols/4], consecutive threads on consecutive words
+                    const int64_t slot = p.vec ? u * (p.cols / ROW_VEC) + c0 / ROW_VEC : c0 + u;
 #pragma unroll
-                    for (int k = 0; k < NP; ++k) dwp[k * p.cols + c0 + u] += gx[k];
+                    for (int k = 0; k < NP; ++k) dwp[k * p.cols + slot] += gx[k];
                 }
             }
             store_planes4<NP, T, C>(p.y, p.np, yb + c0, valid, p.vec != 0, out);
@@ -188,25 +250,188 @@ __global__ void __launch_bounds__(512) rmsnorm_bwd_kernel(const NormParams p) {
     if (want_dw) {
         __syncthreads();
         C* out = static_cast<C*>(p.dw_part) + static_cast<int64_t>(blockIdx.x) * p.np * p.cols;
-        for (int64_t i = threadIdx.x; i < static_cast<int64_t>(p.np) * p.cols; i += blockDim.x) out[i] = dwp[i];
+        const int64_t q = p.cols / ROW_VEC;
+        for (int64_t i = threadIdx.x; i < static_cast<int64_t>(p.np) * p.cols; i += blockDim.x) {
+            const int64_t k = i / p.cols, c = i % p.cols;
+            out[i] = dwp[k * p.cols + (p.vec ? (c % ROW_VEC) * q + c / ROW_VEC : c)];
+        }
     }
 }
 
-// dw[k][c] = sum_b part[b][k][c]
-template <typename T, int NP>
-__global__ void rmsnorm_dw_reduce_kernel(const NormParams p, int parts, void* const* dw_planes_unused) {
+// The backward with each row split over a cluster of two CTAs: CTA rank h owns columns
+// [h * cols/2, (h+1) * cols/2), holds its x and g in registers (thread t: columns
+// h * cols/2 + (s * blockDim + t) * 4 .. +3, s < STEPS), so both passes read registers and x, g
+// come from HBM once.  The row sum d = sum gy (*) x is combined through distributed shared memory
+// (both CTAs add rank 0's partial to rank 1's, in that order, so they agree bit for bit); the
+// per-row slots are double-buffered so one cluster barrier per row suffices.  Two CTAs fit per
+// SM, so one row's loads overlap another row's arithmetic.  Weight-gradient partials accumulate
+// in shared memory per cluster ([k][u][half/4] layout), written to dw_part[cluster][k][cols].
+template <typename T, int NP, int STEPS>
+__global__ void __launch_bounds__(256, 2) rmsnorm_bwd_cluster_kernel(const NormParams p) {
     using C = typename Compute<T>::type;
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    __shared__ C scratch[16 * NP];
+    __shared__ C dslot[2][NP];
+    extern __shared__ __align__(16) unsigned char dyn[];
+    C* dwp = reinterpret_cast<C*>(dyn);
+    const int h = static_cast<int>(cluster.block_rank());
+    const int64_t half = p.cols / 2, q = half / ROW_VEC;
+    const int64_t cbase = h * half;
+    const int64_t n_clusters = gridDim.x / 2, cid = blockIdx.x / 2;
+    const bool want_dw = p.dw_part != nullptr;
+    if (want_dw)
+        for (int64_t i = threadIdx.x; i < static_cast<int64_t>(NP) * half; i += blockDim.x) dwp[i] = C(0);
+    const C* peer_slot = cluster.map_shared_rank(&dslot[0][0], h ^ 1);
+    const C inv_cols = C(1) / C(p.cols);
+    const int64_t span = static_cast<int64_t>(blockDim.x) * ROW_VEC;
+    int par = 0;
+    for (int64_t row = cid; row < p.rows; row += n_clusters, par ^= 1) {
+        const int64_t xb = row * p.x_rs + cbase, gb = row * p.g_rs + cbase;
+        C x[STEPS][ROW_VEC][NP], g[STEPS][ROW_VEC][NP];
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+            const int64_t c0 = s * span + static_cast<int64_t>(threadIdx.x) * ROW_VEC;
+            const int valid = max(0, vec_count(half, c0));
+            load_planes4<NP, T, C>(p.x, p.np, xb + c0, valid, true, x[s]);
+            load_planes4<NP, T, C>(p.g, p.np, gb + c0, valid, true, g[s]);
+        }
+        C r[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) r[k] = k < p.np ? static_cast<const C*>(p.rstd)[row * p.np + k] : C(0);
+        C d[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) d[k] = C(0);
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+            const int64_t c0 = s * span + static_cast<int64_t>(threadIdx.x) * ROW_VEC;
+            const int valid = max(0, vec_count(half, c0));
+            C w[ROW_VEC][NP];
+            if (p.w_np) load_weight4<NP, T, C>(p, cbase + c0, valid, w);
+#pragma unroll
+            for (int u = 0; u < ROW_VEC; ++u) {
+                if (want_dw && u < valid) {
+                    // weight gradient G (*) (x (*) r), from the incoming g before it becomes gy
+                    C xr[NP], gx[NP];
+                    s_mul<NP, C>(x[s][u], r, xr);
+                    s_mul<NP, C>(g[s][u], xr, gx);
+                    const int64_t slot = u * q + c0 / ROW_VEC;
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) dwp[k * half + slot] += gx[k];
+                }
+                C t[NP];
+                if (p.w_np) s_mul<NP, C>(g[s][u], w[u], g[s][u]);
+                s_mul<NP, C>(g[s][u], x[s][u], t);
+#pragma unroll
+                for (int k = 0; k < NP; ++k) d[k] += t[k];
+            }
+        }
+        block_sum<NP, C>(d, scratch);
+        if (threadIdx.x == 0) {
+#pragma unroll
+            for (int k = 0; k < NP; ++k) dslot[par][k] = d[k];
+        }
+        cluster.sync();
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+            const C mine = dslot[par][k], other = peer_slot[par * NP + k];
+            d[k] = h == 0 ? mine + other : other + mine;
+        }
+        C r2[NP], r3[NP], coef[NP];
+        s_mul<NP, C>(r, r, r2);
+        s_mul<NP, C>(r2, r, r3);
+        s_mul<NP, C>(r3, d, coef);
+#pragma unroll
+        for (int k = 0; k < NP; ++k) coef[k] *= inv_cols;
+        const int64_t yb = row * p.y_rs + cbase;
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+            const int64_t c0 = s * span + static_cast<int64_t>(threadIdx.x) * ROW_VEC;
+            C out[ROW_VEC][NP];
+#pragma unroll
+            for (int u = 0; u < ROW_VEC; ++u) {
+                C a[NP], b[NP];
+                s_mul<NP, C>(r, g[s][u], a);
+                s_mul<NP, C>(coef, x[s][u], b);
+#pragma unroll
+                for (int k = 0; k < NP; ++k) out[u][k] = a[k] - b[k];
+            }
+            store_planes4<NP, T, C>(p.y, p.np, yb + c0, max(0, vec_count(half, c0)), true, out);
+        }
+    }
+    if (want_dw) {
+        __syncthreads();
+        C* out = static_cast<C*>(p.dw_part) + cid * p.np * p.cols + cbase;
+        for (int64_t i = threadIdx.x; i < static_cast<int64_t>(p.np) * half; i += blockDim.x) {
+            const int64_t k = i / half, c = i % half;
+            out[k * p.cols + c] = dwp[k * half + (c % ROW_VEC) * q + c / ROW_VEC];
+        }
+    }
+    cluster.sync();  // the peer may still read this CTA's row slots
+}
+
+// dw[k][c] = sum_b part[b][k][c].  A CTA covers 32 consecutive values with 8 lanes of partials
+// each (warp j sums partials j, j+8, ...; coalesced 128-byte rows), then combines the 8 lanes.
+template <typename T, int NP>
+__global__ void __launch_bounds__(256) rmsnorm_dw_reduce_kernel(const NormParams p, int parts) {
+    using C = typename Compute<T>::type;
+    __shared__ C lanes[8][33];
     const int64_t total = static_cast<int64_t>(p.np) * p.cols;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        C s = C(0);
-        for (int b = 0; b < parts; ++b) s += static_cast<const C*>(p.dw_part)[static_cast<int64_t>(b) * total + i];
+    const int col = threadIdx.x & 31, lane = threadIdx.x >> 5;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * 32 + col;
+    C s = C(0);
+    if (i < total) {
+        const C* src = static_cast<const C*>(p.dw_part) + i;
+#pragma unroll 4
+        for (int b = lane; b < parts; b += 8) s += src[static_cast<int64_t>(b) * total];
+    }
+    lanes[lane][col] = s;
+    __syncthreads();
+    if (lane == 0 && i < total) {
+        C t = C(0);
+#pragma unroll
+        for (int l = 0; l < 8; ++l) t += lanes[l][col];
         const int k = static_cast<int>(i / p.cols);
-        static_cast<T*>(const_cast<void*>(p.g[k]))[i % p.cols] = from_c<T>(s);
+        static_cast<T*>(const_cast<void*>(p.g[k]))[i % p.cols] = from_c<T>(t);
     }
 }
 
 static int norm_threads(int64_t cols) { return cols >= 2048 ? 512 : (cols >= 512 ? 256 : 128); }
+
+// Launch the register-resident forward when a row fits: STEPS vectors of 4 columns per thread,
+// at most 512 threads, float compute, degree <= 5.  Returns false when it does not apply.
+template <typename T, int NP>
+static bool reg_row_forward(const NormParams& p, cudaStream_t s) {
+    using C = typename Compute<T>::type;
+    if constexpr (sizeof(C) != 4 || NP > 6) {
+        return false;
+    } else {
+        const int64_t quads = ceil_div(p.cols, ROW_VEC);
+        int steps = 0;
+        int64_t threads = 0;
+        for (int st : {1, 2, 4}) {
+            threads = round_up(ceil_div(quads, st), 32);
+            if (threads <= 256 || (st == 4 && threads <= 512)) {
+                steps = st;
+                break;
+            }
+        }
+        if (steps == 0) return false;
+        int per_sm = 0;
+        const void* fn = steps == 1 ? reinterpret_cast<const void*>(rmsnorm_fwd_reg_kernel<T, NP, 1>)
+                         : steps == 2 ? reinterpret_cast<const void*>(rmsnorm_fwd_reg_kernel<T, NP, 2>)
+                                      : reinterpret_cast<const void*>(rmsnorm_fwd_reg_kernel<T, NP, 4>);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, static_cast<int>(threads), 0) != cudaSuccess ||
+            per_sm < 1)
+            return false;
+        const int grid = static_cast<int>(std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * per_sm));
+        const int th = static_cast<int>(threads);
+        if (steps == 1) rmsnorm_fwd_reg_kernel<T, NP, 1><<<grid, th, 0, s>>>(p);
+        else if (steps == 2) rmsnorm_fwd_reg_kernel<T, NP, 2><<<grid, th, 0, s>>>(p);
+        else rmsnorm_fwd_reg_kernel<T, NP, 4><<<grid, th, 0, s>>>(p);
+        return true;
+    }
+}
 
 template <typename T, int NP>
 static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, size_t ws_bytes, cudaStream_t s) {
@@ -221,10 +446,12 @@ static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, siz
     }
     const int threads = norm_threads(p.cols);
     if (!backward) {
-        const int grid = static_cast<int>(std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * 8));
         void* tok;
         prof_begin("rmsnorm_fwd", s, &tok);
-        rmsnorm_fwd_kernel<T, NP><<<grid, threads, 0, s>>>(p);
+        if (!reg_row_forward<T, NP>(p, s)) {
+            const int grid = static_cast<int>(std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * 8));
+            rmsnorm_fwd_kernel<T, NP><<<grid, threads, 0, s>>>(p);
+        }
         prof_end("rmsnorm_fwd", s, tok);
         PK_CHECK_LAUNCH("pk_rmsnorm_fwd");
         return PK_OK;
@@ -236,8 +463,76 @@ static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, siz
                                              static_cast<int>(smem));
         if (e != cudaSuccess) return cuda_fail(e, "pk_rmsnorm_bwd: cudaFuncSetAttribute");
     }
-    int per_sm = 4;
-    if (smem > 0) per_sm = static_cast<int>(std::max<size_t>(1, std::min<size_t>(4, (220 * 1024) / (smem + 4096))));
+    // rows split over 2-CTA clusters with x and g in registers (vector-aligned planes, float compute)
+    if constexpr (sizeof(C) == 4 && NP <= 5) {
+        int steps = 0;
+        int64_t cthreads = 0;
+        if (p.vec && p.cols % (2 * ROW_VEC) == 0 && p.cols >= 512) {
+            const int64_t quads = p.cols / 2 / ROW_VEC;
+            for (int st : {1, 2}) {
+                cthreads = round_up(ceil_div(quads, st), 32);
+                if (cthreads <= 256) {
+                    steps = st;
+                    break;
+                }
+            }
+        }
+        if (steps) {
+            const size_t csmem = dw ? static_cast<size_t>(NP) * (p.cols / 2) * sizeof(C) : 0;
+            auto kern = steps == 1 ? rmsnorm_bwd_cluster_kernel<T, NP, 1> : rmsnorm_bwd_cluster_kernel<T, NP, 2>;
+            if (csmem > 48 * 1024) {
+                cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     static_cast<int>(csmem));
+                if (e != cudaSuccess) return cuda_fail(e, "pk_rmsnorm_bwd: cudaFuncSetAttribute");
+            }
+            int per_sm = 0;
+            cudaError_t e =
+                cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, static_cast<int>(cthreads), csmem);
+            if (e != cudaSuccess) return cuda_fail(e, "pk_rmsnorm_bwd: occupancy query");
+            per_sm = std::max(1, std::min(per_sm, 4));
+            const int64_t clusters = std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * per_sm / 2);
+            if (dw) {
+                const size_t need = static_cast<size_t>(clusters) * p.np * p.cols * sizeof(C);
+                if (!ws || ws_bytes < need) return fail(PK_ERR_WORKSPACE, "pk_rmsnorm_bwd: workspace too small");
+                p.dw_part = ws;
+            }
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters));
+            cfg.blockDim = dim3(static_cast<unsigned>(cthreads));
+            cfg.dynamicSmemBytes = csmem;
+            cfg.stream = s;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 2;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            void* tok;
+            prof_begin("rmsnorm_bwd", s, &tok);
+            e = cudaLaunchKernelEx(&cfg, kern, p);
+            if (e != cudaSuccess) return cuda_fail(e, "pk_rmsnorm_bwd: cluster launch");
+            PK_CHECK_LAUNCH("pk_rmsnorm_bwd");
+            if (dw) {
+                NormParams q = p;
+                for (int k = 0; k < p.np; ++k) q.g[k] = dw[k];
+                const int64_t total = static_cast<int64_t>(p.np) * p.cols;
+                rmsnorm_dw_reduce_kernel<T, NP><<<static_cast<int>(ceil_div(total, 32)), 256, 0, s>>>(
+                    q, static_cast<int>(clusters));
+                PK_CHECK_LAUNCH("pk_rmsnorm_bwd: weight reduction");
+            }
+            prof_end("rmsnorm_bwd", s, tok);
+            return PK_OK;
+        }
+    }
+    // as many CTAs as fit on the SMs at once (registers and the weight-gradient buffer decide)
+    const int bthreads = std::min(threads, 256);
+    int per_sm = 0;
+    {
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rmsnorm_bwd_kernel<T, NP>, bthreads, smem);
+        if (e != cudaSuccess) return cuda_fail(e, "pk_rmsnorm_bwd: occupancy query");
+        per_sm = std::max(1, std::min(per_sm, 4));
+    }
     int grid = static_cast<int>(std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * per_sm));
     if (dw) {
         const size_t need = static_cast<size_t>(grid) * p.np * p.cols * sizeof(C);
@@ -246,17 +541,16 @@ static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, siz
     }
     void* tok;
     prof_begin("rmsnorm_bwd", s, &tok);
-    rmsnorm_bwd_kernel<T, NP><<<grid, threads, smem, s>>>(p);
-    prof_end("rmsnorm_bwd", s, tok);
+    rmsnorm_bwd_kernel<T, NP><<<grid, bthreads, smem, s>>>(p);
     PK_CHECK_LAUNCH("pk_rmsnorm_bwd");
     if (dw) {
         NormParams q = p;
         for (int k = 0; k < p.np; ++k) q.g[k] = dw[k];
         const int64_t total = static_cast<int64_t>(p.np) * p.cols;
-        const int g2 = static_cast<int>(std::min<int64_t>(ceil_div(total, 256), 4096));
-        rmsnorm_dw_reduce_kernel<T, NP><<<g2, 256, 0, s>>>(q, grid, nullptr);
+        rmsnorm_dw_reduce_kernel<T, NP><<<static_cast<int>(ceil_div(total, 32)), 256, 0, s>>>(q, grid);
         PK_CHECK_LAUNCH("pk_rmsnorm_bwd: weight reduction");
     }
+    prof_end("rmsnorm_bwd", s, tok);
     return PK_OK;
 }
 
