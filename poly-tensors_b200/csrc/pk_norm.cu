@@ -258,15 +258,15 @@ __global__ void __launch_bounds__(512) rmsnorm_bwd_kernel(const NormParams p) {
     }
 }
 
-// The backward with each row split over a cluster of two CTAs: CTA rank h owns columns
-// [h * cols/2, (h+1) * cols/2), holds its x and g in registers (thread t: columns
-// h * cols/2 + (s * blockDim + t) * 4 .. +3, s < STEPS), so both passes read registers and x, g
+// The backward with each row split over a cluster of CL CTAs: CTA rank h owns columns
+// [h * cols/CL, (h+1) * cols/CL), holds its x and g in registers (thread t: columns
+// h * cols/CL + (s * blockDim + t) * 4 .. +3, s < STEPS), so both passes read registers and x, g
 // come from HBM once.  The row sum d = sum gy (*) x is combined through distributed shared memory
-// (both CTAs add rank 0's partial to rank 1's, in that order, so they agree bit for bit); the
-// per-row slots are double-buffered so one cluster barrier per row suffices.  Two CTAs fit per
-// SM, so one row's loads overlap another row's arithmetic.  Weight-gradient partials accumulate
-// in shared memory per cluster ([k][u][half/4] layout), written to dw_part[cluster][k][cols].
-template <typename T, int NP, int STEPS>
+// (every CTA adds the CL partials in rank order, so they agree bit for bit); the per-row slots are
+// double-buffered so one cluster barrier per row suffices.  Several CTAs fit per SM, so one row's
+// loads overlap another row's arithmetic.  Weight-gradient partials accumulate in shared memory
+// per cluster ([k][u][part/4] layout), written to dw_part[cluster][k][cols].
+template <typename T, int NP, int STEPS, int CL>
 __global__ void __launch_bounds__(256, 2) rmsnorm_bwd_cluster_kernel(const NormParams p) {
     using C = typename Compute<T>::type;
     namespace cg = cooperative_groups;
@@ -276,13 +276,15 @@ __global__ void __launch_bounds__(256, 2) rmsnorm_bwd_cluster_kernel(const NormP
     extern __shared__ __align__(16) unsigned char dyn[];
     C* dwp = reinterpret_cast<C*>(dyn);
     const int h = static_cast<int>(cluster.block_rank());
-    const int64_t half = p.cols / 2, q = half / ROW_VEC;
+    const int64_t half = p.cols / CL, q = half / ROW_VEC;  // "half": this CTA's share of the row
     const int64_t cbase = h * half;
-    const int64_t n_clusters = gridDim.x / 2, cid = blockIdx.x / 2;
+    const int64_t n_clusters = gridDim.x / CL, cid = blockIdx.x / CL;
     const bool want_dw = p.dw_part != nullptr;
     if (want_dw)
         for (int64_t i = threadIdx.x; i < static_cast<int64_t>(NP) * half; i += blockDim.x) dwp[i] = C(0);
-    const C* peer_slot = cluster.map_shared_rank(&dslot[0][0], h ^ 1);
+    const C* slots[CL];
+#pragma unroll
+    for (int j = 0; j < CL; ++j) slots[j] = cluster.map_shared_rank(&dslot[0][0], j);
     const C inv_cols = C(1) / C(p.cols);
     const int64_t span = static_cast<int64_t>(blockDim.x) * ROW_VEC;
     int par = 0;
@@ -310,20 +312,27 @@ __global__ void __launch_bounds__(256, 2) rmsnorm_bwd_cluster_kernel(const NormP
             if (p.w_np) load_weight4<NP, T, C>(p, cbase + c0, valid, w);
 #pragma unroll
             for (int u = 0; u < ROW_VEC; ++u) {
+                // gx = g (*) x serves both the weight gradient (gx (*) r) and the row sum
+                // (gy (*) x = w (*) gx); g then becomes gy = g (*) w for the second pass
+                C gx[NP];
+                s_mul<NP, C>(g[s][u], x[s][u], gx);
                 if (want_dw && u < valid) {
-                    // weight gradient G (*) (x (*) r), from the incoming g before it becomes gy
-                    C xr[NP], gx[NP];
-                    s_mul<NP, C>(x[s][u], r, xr);
-                    s_mul<NP, C>(g[s][u], xr, gx);
+                    C gxr[NP];
+                    s_mul<NP, C>(gx, r, gxr);
                     const int64_t slot = u * q + c0 / ROW_VEC;
 #pragma unroll
-                    for (int k = 0; k < NP; ++k) dwp[k * half + slot] += gx[k];
+                    for (int k = 0; k < NP; ++k) dwp[k * half + slot] += gxr[k];
                 }
-                C t[NP];
-                if (p.w_np) s_mul<NP, C>(g[s][u], w[u], g[s][u]);
-                s_mul<NP, C>(g[s][u], x[s][u], t);
+                if (p.w_np) {
+                    C t[NP];
+                    s_mul<NP, C>(w[u], gx, t);
+                    s_mul<NP, C>(g[s][u], w[u], g[s][u]);
 #pragma unroll
-                for (int k = 0; k < NP; ++k) d[k] += t[k];
+                    for (int k = 0; k < NP; ++k) d[k] += t[k];
+                } else {
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) d[k] += gx[k];
+                }
             }
         }
         block_sum<NP, C>(d, scratch);
@@ -334,8 +343,10 @@ __global__ void __launch_bounds__(256, 2) rmsnorm_bwd_cluster_kernel(const NormP
         cluster.sync();
 #pragma unroll
         for (int k = 0; k < NP; ++k) {
-            const C mine = dslot[par][k], other = peer_slot[par * NP + k];
-            d[k] = h == 0 ? mine + other : other + mine;
+            C t = slots[0][par * NP + k];
+#pragma unroll
+            for (int j = 1; j < CL; ++j) t += slots[j][par * NP + k];
+            d[k] = t;
         }
         C r2[NP], r3[NP], coef[NP];
         s_mul<NP, C>(r, r, r2);
@@ -465,10 +476,13 @@ static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, siz
     }
     // rows split over 2-CTA clusters with x and g in registers (vector-aligned planes, float compute)
     if constexpr (sizeof(C) == 4 && NP <= 5) {
+        // pairs of CTAs (a 4-CTA split measured slower: its per-row cluster barrier costs more
+        // than the extra occupancy gains); each CTA's half row fits 256 threads x STEPS x 4 columns
+        constexpr int cl = 2;
         int steps = 0;
         int64_t cthreads = 0;
-        if (p.vec && p.cols % (2 * ROW_VEC) == 0 && p.cols >= 512) {
-            const int64_t quads = p.cols / 2 / ROW_VEC;
+        if (p.vec && p.cols >= 512 && p.cols % (cl * ROW_VEC) == 0) {
+            const int64_t quads = p.cols / cl / ROW_VEC;
             for (int st : {1, 2}) {
                 cthreads = round_up(ceil_div(quads, st), 32);
                 if (cthreads <= 256) {
@@ -478,8 +492,8 @@ static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, siz
             }
         }
         if (steps) {
-            const size_t csmem = dw ? static_cast<size_t>(NP) * (p.cols / 2) * sizeof(C) : 0;
-            auto kern = steps == 1 ? rmsnorm_bwd_cluster_kernel<T, NP, 1> : rmsnorm_bwd_cluster_kernel<T, NP, 2>;
+            const size_t csmem = dw ? static_cast<size_t>(NP) * (p.cols / cl) * sizeof(C) : 0;
+            auto kern = steps == 1 ? rmsnorm_bwd_cluster_kernel<T, NP, 1, cl> : rmsnorm_bwd_cluster_kernel<T, NP, 2, cl>;
             if (csmem > 48 * 1024) {
                 cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                      static_cast<int>(csmem));
@@ -490,20 +504,20 @@ static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, siz
                 cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, static_cast<int>(cthreads), csmem);
             if (e != cudaSuccess) return cuda_fail(e, "pk_rmsnorm_bwd: occupancy query");
             per_sm = std::max(1, std::min(per_sm, 4));
-            const int64_t clusters = std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * per_sm / 2);
+            const int64_t clusters = std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * per_sm / cl);
             if (dw) {
                 const size_t need = static_cast<size_t>(clusters) * p.np * p.cols * sizeof(C);
                 if (!ws || ws_bytes < need) return fail(PK_ERR_WORKSPACE, "pk_rmsnorm_bwd: workspace too small");
                 p.dw_part = ws;
             }
             cudaLaunchConfig_t cfg{};
-            cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters));
+            cfg.gridDim = dim3(static_cast<unsigned>(cl * clusters));
             cfg.blockDim = dim3(static_cast<unsigned>(cthreads));
             cfg.dynamicSmemBytes = csmem;
             cfg.stream = s;
             cudaLaunchAttribute attr[1];
             attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = 2;
+            attr[0].val.clusterDim.x = static_cast<unsigned>(cl);
             attr[0].val.clusterDim.y = 1;
             attr[0].val.clusterDim.z = 1;
             cfg.attrs = attr;
