@@ -472,6 +472,19 @@ def run_attention(args, rank, world, device):
     _lib.profile_enable(False)
     kms, klaunch = _lib.profile_query("flash_attn_fwd")
     ms, clocks = _timed(step, args.steps, args.warmup, device, world)
+    # per-kernel device time of one fwd+bwd step (separate, untimed pass with the event hooks on)
+    names = ("flash_attn_fwd", "attn_probs_gemm", "attn_dscores_gemm", "poly_gemm", "attn_probs", "attn_dscores",
+             "series_map")
+    for nm in names:
+        _lib.profile_query(nm)
+    _lib.profile_enable(True)
+    _timed(step, 2, 0, device, world)
+    _lib.profile_enable(False)
+    kernels = {}
+    for nm in names:
+        kt, kl = _lib.profile_query(nm)
+        if kl:
+            kernels[nm] = {"ms_per_step": kt / 2, "launches_per_step": kl // 2}
     flops = attention_flops(B, H, L, D, n)
     fwd_flops = flops / 3
     pk, source = peaks()
@@ -491,6 +504,7 @@ def run_attention(args, rank, world, device):
         "roofline": {"bound": "tensor", "achieved": value / world, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": value / world / pk["bf16_tflops"], "traffic": None,
                      "peak_source": f"bf16_tflops ({source})"},
+        "kernels": kernels,
         "forward": {"ms": fwd_ms, "TFLOP/s": fwd_flops / (fwd_ms / 1e3) / 1e12,
                     "fused_kernel_ms": kms / klaunch if klaunch else None,
                     "fused_kernel_TFLOP/s": fwd_flops / (kms / klaunch / 1e3) / 1e12 if klaunch else None},

@@ -14,10 +14,13 @@
 // apply the series function on the way out.  The score planes are written once, as P or dS,
 // and never re-read for the softmax.
 //
-// Per 64-wide k block the TMA warp loads A_i and B_i (i = 0..n) once into n+1 ring stages and the
-// MMA warp issues all (n+1)(n+2)/2 products A_i B_j (i + j <= n) from them, so each operand tile is
-// read once per k block instead of once per product.  With a causal mask, tiles whose keys all
-// lie after their last query are neither loaded nor multiplied: the epilogue writes their zeros.
+// A work unit is 128 rows of A (queries) against a run of up to AG_CHUNK 64-column tiles of B
+// (keys): the unit's A planes (all n+1 planes, the whole reduction, k <= 128) are loaded once into
+// shared memory and stay resident while B streams through a ring of per-plane 64 x 64 k-blocks,
+// so A crosses L2 once per unit instead of once per tile.  Per k block the MMA warp issues all
+// (n+1)(n+2)/2 products A_i B_j (i + j <= n) from the resident A and n+1 ring stages.  Units are
+// ordered so CTAs running together share a B chunk in L2.  With a causal mask, tiles whose keys
+// all lie after their last query are neither loaded nor multiplied: the epilogue writes zeros.
 #include <algorithm>
 #include <cstring>
 
@@ -29,13 +32,15 @@ namespace pk {
 
 constexpr int AG_BM = 128;
 constexpr int AG_BN = 64;
-constexpr int AG_EPI_WARPS = 8;                    // two per TMEM lane quadrant, 32 columns each
+constexpr int AG_EPI_WARPS = 16;                   // four per TMEM lane quadrant, 16 columns each
 constexpr int AG_THREADS = 64 + 32 * AG_EPI_WARPS;  // warp 0: TMA, warp 1: MMA + TMEM owner
-constexpr int AG_A_BYTES = AG_BM * TC_BK * 2;
-constexpr int AG_B_BYTES = AG_BN * TC_BK * 2;
-constexpr int AG_STAGE_BYTES = AG_A_BYTES + AG_B_BYTES;  // one plane's A and B k-block
-constexpr int AG_STAGES = 8;
-constexpr int AG_SMEM_BYTES = AG_STAGES * AG_STAGE_BYTES + 1024 + 256;
+constexpr int AG_A_BYTES = AG_BM * TC_BK * 2;     // one plane's 128 x 64 A k-block
+constexpr int AG_B_BYTES = AG_BN * TC_BK * 2;     // one plane's 64 x 64 B k-block (a ring stage)
+constexpr int AG_MAX_K = 128;                     // reduction held resident (head dimension)
+constexpr int AG_MAX_STAGES = 24;
+constexpr int AG_SMEM_BUDGET = 220 * 1024;        // resident A + B ring
+constexpr int AG_SMEM_BYTES = AG_SMEM_BUDGET + 1024 + 512;
+constexpr int AG_CHUNK = 8;                       // B tiles per work unit
 constexpr int AG_MAX_NP = 4;
 
 enum { AG_PROBS = 0, AG_DSCORES = 1 };
@@ -47,7 +52,9 @@ struct AgMaps {
 
 struct AgParams {
     int batch, M, N;
-    int kblocks, tiles_m, tiles_n, group_m, total_tiles;
+    int kblocks, tiles_m, tiles_n, n_chunks, total_units;
+    int nstages;       // B ring stages
+    int a_bytes;       // resident A bytes (NP * kblocks * AG_A_BYTES)
     int a_mn, b_mn;
     int causal;
     int64_t shift;     // query index of row r is r + shift
@@ -66,16 +73,21 @@ struct AgTile {
     int b, tm, tn;
 };
 
-__device__ __forceinline__ AgTile ag_decode(const AgParams& p, int t) {
-    AgTile c;
-    const int per_b = p.tiles_m * p.tiles_n;
-    c.b = t / per_b;
-    const int r = t % per_b;
-    const int span = p.group_m * p.tiles_n;
-    const int first_m = (r / span) * p.group_m;
-    const int gsize = min(p.tiles_m - first_m, p.group_m);
-    c.tm = first_m + (r % span) % gsize;
-    c.tn = (r % span) / gsize;
+// Unit u -> (batch entry, B chunk, row tile) with the row tile fastest: CTAs that run together
+// work on the same B chunk.  Tiles of the unit: tn in [tn0, tn1).
+struct AgUnit {
+    int b, tm, tn0, tn1;
+};
+
+__device__ __forceinline__ AgUnit ag_unit(const AgParams& p, int u) {
+    AgUnit c;
+    const int per_b = p.n_chunks * p.tiles_m;
+    c.b = u / per_b;
+    const int r = u % per_b;
+    const int chunk = r / p.tiles_m;
+    c.tm = r % p.tiles_m;
+    c.tn0 = chunk * AG_CHUNK;
+    c.tn1 = min(p.tiles_n, c.tn0 + AG_CHUNK);
     return c;
 }
 
@@ -86,34 +98,22 @@ __device__ __forceinline__ bool ag_masked(const AgParams& p, const AgTile& c) {
     return static_cast<int64_t>(c.tn) * AG_BN > last_row + p.shift;
 }
 
-__device__ __forceinline__ void ag_load16(const __nv_bfloat16* src, bool vec, int valid, float (&v)[16]) {
-    if (vec && valid == 16) {
-        const uint4 a = reinterpret_cast<const uint4*>(src)[0];
-        const uint4 b = reinterpret_cast<const uint4*>(src)[1];
-        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+// exp of a series with the constant term through the fast exponential intrinsic (the
+// probabilities are stored as bfloat16, far coarser than its error); directions by the ODE
+// recurrence k y_k = sum_{i=1..k} i x_i y_{k-i}.
+template <int NP>
+__device__ __forceinline__ void s_exp_fast(float (&x)[NP]) {
+    float r[NP];
+    r[0] = __expf(x[0]);
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            v[2 * t] = __uint_as_float(w[t] << 16);
-            v[2 * t + 1] = __uint_as_float(w[t] & 0xFFFF0000u);
-        }
-    } else {
+    for (int k = 1; k < NP; ++k) {
+        float acc = 0.f;
 #pragma unroll
-        for (int t = 0; t < 16; ++t) v[t] = t < valid ? __bfloat162float(src[t]) : 0.f;
+        for (int i = 1; i <= k; ++i) acc += float(i) * x[i] * r[k - i];
+        r[k] = acc * inv_int<float>(k);
     }
-}
-
-__device__ __forceinline__ void ag_store16(__nv_bfloat16* dst, bool vec, int valid, const float (&v)[16]) {
-    if (vec && valid == 16) {
-        uint32_t w[8];
 #pragma unroll
-        for (int t = 0; t < 8; ++t)
-            w[t] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * t]))) |
-                   (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v[2 * t + 1]))) << 16);
-        reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    } else {
-        for (int t = 0; t < valid; ++t) dst[t] = __float2bfloat16_rn(v[t]);
-    }
+    for (int k = 0; k < NP; ++k) x[k] = r[k];
 }
 
 template <int NP, int MODE>
@@ -122,19 +122,24 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
     constexpr int TMEM_COLS = 2 * NP * AG_BN <= 128 ? 128 : (2 * NP * AG_BN <= 256 ? 256 : 512);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + AG_STAGES * AG_STAGE_BYTES);
-    uint64_t* empty_bar = full_bar + AG_STAGES;
-    uint64_t* acc_full = empty_bar + AG_STAGES;
+    uint8_t* a_res = smem;                // [plane][kblock] 16 KB boxes
+    uint8_t* ring = smem + p.a_bytes;     // B stages, 8 KB each
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + AG_SMEM_BUDGET);
+    uint64_t* empty_bar = full_bar + AG_MAX_STAGES;
+    uint64_t* acc_full = empty_bar + AG_MAX_STAGES;
     uint64_t* acc_empty = acc_full + 2;
-    uint64_t* drain_bar = acc_empty + 2;
+    uint64_t* a_full = acc_empty + 2;
+    uint64_t* a_empty = a_full + 1;
+    uint64_t* drain_bar = a_empty + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const int nst = p.nstages;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < AG_STAGES; ++s) {
+        for (int s = 0; s < nst; ++s) {
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
@@ -142,6 +147,8 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
             mbar_init(&acc_full[s], 1);
             mbar_init(&acc_empty[s], 32 * AG_EPI_WARPS);
         }
+        mbar_init(a_full, 1);
+        mbar_init(a_empty, 1);
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -160,113 +167,153 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        // ---------------- TMA producer: plane i of k block kb into one ring stage ----------------
+        // ---------------- TMA producer: a unit's A planes once, then its B k-blocks ----------------
         if (lane == 0) {
-            uint32_t stage = 0, phase = 0;
-            int issued_parity[AG_STAGES];
-#pragma unroll
-            for (int s = 0; s < AG_STAGES; ++s) issued_parity[s] = -1;
+            uint32_t stage = 0, phase = 0, a_phase = 0;
+            int issued_parity[AG_MAX_STAGES];
+            for (int s = 0; s < nst; ++s) issued_parity[s] = -1;
+            int a_issued = -1;
             bool ok = true;
-            for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-                const AgTile tc = ag_decode(p, t);
-                if (ag_masked(p, tc)) continue;
-                for (int kb = 0; kb < p.kblocks && ok; ++kb) {
-                    for (int i = 0; i < NP; ++i) {
-                        if (!mbar_wait_or_abort(&empty_bar[stage], phase ^ 1, abort_flag, p.status, 121)) {
-                            ok = false;
-                            break;
-                        }
-                        uint8_t* st = smem + stage * AG_STAGE_BYTES;
-                        mbar_arrive_expect_tx(&full_bar[stage], AG_STAGE_BYTES);
+            for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+                const AgUnit un = ag_unit(p, u);
+                if (ag_masked(p, AgTile{un.b, un.tm, un.tn0})) continue;  // every tile of the unit masked
+                if (!mbar_wait_or_abort(a_empty, a_phase ^ 1, abort_flag, p.status, 125)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(a_full, static_cast<uint32_t>(p.a_bytes));
+                for (int i = 0; i < NP; ++i) {
+                    for (int kb = 0; kb < p.kblocks; ++kb) {
+                        uint8_t* dst = a_res + (i * p.kblocks + kb) * AG_A_BYTES;
                         if (p.a_mn) {
 #pragma unroll
                             for (int h = 0; h < AG_BM / 64; ++h)
-                                tma_load_3d(st + h * 8192, &maps.a[i], &full_bar[stage], tc.tm * AG_BM + h * 64,
-                                            kb * TC_BK, tc.b);
+                                tma_load_3d(dst + h * 8192, &maps.a[i], a_full, un.tm * AG_BM + h * 64, kb * TC_BK, un.b);
                         } else {
-                            tma_load_3d(st, &maps.a[i], &full_bar[stage], kb * TC_BK, tc.tm * AG_BM, tc.b);
+                            tma_load_3d(dst, &maps.a[i], a_full, kb * TC_BK, un.tm * AG_BM, un.b);
                         }
-                        if (p.b_mn)
-                            tma_load_3d(st + AG_A_BYTES, &maps.b[i], &full_bar[stage], tc.tn * AG_BN, kb * TC_BK, tc.b);
-                        else
-                            tma_load_3d(st + AG_A_BYTES, &maps.b[i], &full_bar[stage], kb * TC_BK, tc.tn * AG_BN, tc.b);
-                        issued_parity[stage] = static_cast<int>(phase);
-                        if (++stage == AG_STAGES) {
-                            stage = 0;
-                            phase ^= 1;
+                    }
+                }
+                a_issued = static_cast<int>(a_phase);
+                a_phase ^= 1;
+                for (int tn = un.tn0; tn < un.tn1 && ok; ++tn) {
+                    if (ag_masked(p, AgTile{un.b, un.tm, tn})) break;  // later tiles are masked too
+                    for (int kb = 0; kb < p.kblocks && ok; ++kb) {
+                        for (int i = 0; i < NP; ++i) {
+                            if (!mbar_wait_or_abort(&empty_bar[stage], phase ^ 1, abort_flag, p.status, 121)) {
+                                ok = false;
+                                break;
+                            }
+                            uint8_t* st = ring + stage * AG_B_BYTES;
+                            mbar_arrive_expect_tx(&full_bar[stage], AG_B_BYTES);
+                            if (p.b_mn)
+                                tma_load_3d(st, &maps.b[i], &full_bar[stage], tn * AG_BN, kb * TC_BK, un.b);
+                            else
+                                tma_load_3d(st, &maps.b[i], &full_bar[stage], kb * TC_BK, tn * AG_BN, un.b);
+                            issued_parity[stage] = static_cast<int>(phase);
+                            if (++stage == static_cast<uint32_t>(nst)) {
+                                stage = 0;
+                                phase ^= 1;
+                            }
                         }
                     }
                 }
             }
             if (!ok) {
-                for (int s = 0; s < AG_STAGES; ++s) {
+                // let copies in flight land before the CTA (and its shared memory) exits (bounded)
+                for (int s = 0; s < nst; ++s) {
                     if (issued_parity[s] < 0) continue;
                     const uint64_t t0 = pk_globaltimer();
                     while (!mbar_try_wait(&full_bar[s], static_cast<uint32_t>(issued_parity[s])) &&
                            pk_globaltimer() - t0 < 1000000000ull) {
                     }
                 }
+                if (a_issued >= 0) {
+                    const uint64_t t0 = pk_globaltimer();
+                    while (!mbar_try_wait(a_full, static_cast<uint32_t>(a_issued)) &&
+                           pk_globaltimer() - t0 < 1000000000ull) {
+                    }
+                }
             }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer: all products of a k block from its NP resident stages ----------------
+        // ---------------- MMA issuer ----------------
         if (lane == 0) {
             const uint32_t idesc = f16_idesc(1u, AG_BM, AG_BN) | (static_cast<uint32_t>(p.a_mn) << 15) |
                                    (static_cast<uint32_t>(p.b_mn) << 16);
-            uint32_t stage = 0, phase = 0;
+            uint32_t stage = 0, phase = 0, a_par = 0;
             uint32_t abuf = 0, aphase = 0;
             bool ok = true, issued = false;
-            for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-                const AgTile tc = ag_decode(p, t);
-                if (ag_masked(p, tc)) continue;
-                if (!mbar_wait_or_abort(&acc_empty[abuf], aphase ^ 1, abort_flag, p.status, 122)) {
+            for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+                const AgUnit un = ag_unit(p, u);
+                if (ag_masked(p, AgTile{un.b, un.tm, un.tn0})) continue;
+                if (!mbar_wait_or_abort(a_full, a_par, abort_flag, p.status, 126)) {
                     ok = false;
                     break;
                 }
+                a_par ^= 1;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + abuf * (NP * AG_BN);
-                for (int kb = 0; kb < p.kblocks && ok; ++kb) {
-                    uint32_t st[NP];
-#pragma unroll
-                    for (int i = 0; i < NP; ++i) {
-                        if (!mbar_wait_or_abort(&full_bar[stage], phase, abort_flag, p.status, 123)) {
-                            ok = false;
-                            break;
-                        }
-                        st[i] = stage;
-                        if (++stage == AG_STAGES) {
-                            stage = 0;
-                            phase ^= 1;
-                        }
+                for (int tn = un.tn0; tn < un.tn1 && ok; ++tn) {
+                    if (ag_masked(p, AgTile{un.b, un.tm, tn})) break;
+                    if (!mbar_wait_or_abort(&acc_empty[abuf], aphase ^ 1, abort_flag, p.status, 122)) {
+                        ok = false;
+                        break;
                     }
-                    if (!ok) break;
                     tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + abuf * (NP * AG_BN);
+                    for (int kb = 0; kb < p.kblocks && ok; ++kb) {
+                        uint32_t st[NP];
 #pragma unroll
-                    for (int k = 0; k < NP; ++k) {
-#pragma unroll
-                        for (int i = 0; i <= k; ++i) {
-                            const uint32_t a_s = smem_u32(smem + st[i] * AG_STAGE_BYTES);
-                            const uint32_t b_s = smem_u32(smem + st[k - i] * AG_STAGE_BYTES) + AG_A_BYTES;
-#pragma unroll
-                            for (int kk = 0; kk < TC_BK / 16; ++kk) {
-                                const uint64_t ad = p.a_mn ? sw128_mnmajor_desc_lbo(a_s + kk * 2048, 8192)
-                                                           : sw128_kmajor_desc(a_s + kk * 32);
-                                const uint64_t bd = p.b_mn ? sw128_mnmajor_desc_lbo(b_s + kk * 2048, 8192)
-                                                           : sw128_kmajor_desc(b_s + kk * 32);
-                                tc_mma_f16(d_tmem + k * AG_BN, ad, bd, idesc, (kb > 0 || i > 0 || kk > 0) ? 1u : 0u);
+                        for (int i = 0; i < NP; ++i) {
+                            if (!mbar_wait_or_abort(&full_bar[stage], phase, abort_flag, p.status, 123)) {
+                                ok = false;
+                                break;
+                            }
+                            st[i] = stage;
+                            if (++stage == static_cast<uint32_t>(nst)) {
+                                stage = 0;
+                                phase ^= 1;
                             }
                         }
-                    }
-                    issued = true;
+                        if (!ok) break;
+                        tc_fence_after();
+                        // descriptors built once per k block; each 16-wide k step advances the
+                        // start address field by a constant (32 B K-major, 2048 B MN-major)
+                        uint64_t ad[NP], bd[NP];
 #pragma unroll
-                    for (int i = 0; i < NP; ++i) tc_commit(&empty_bar[st[i]]);
+                        for (int i = 0; i < NP; ++i) {
+                            const uint32_t a_s = smem_u32(a_res + (i * p.kblocks + kb) * AG_A_BYTES);
+                            const uint32_t b_s = smem_u32(ring + st[i] * AG_B_BYTES);
+                            ad[i] = p.a_mn ? sw128_mnmajor_desc_lbo(a_s, 8192) : sw128_kmajor_desc(a_s);
+                            bd[i] = p.b_mn ? sw128_mnmajor_desc_lbo(b_s, 8192) : sw128_kmajor_desc(b_s);
+                        }
+                        const uint64_t a_step = p.a_mn ? 2048 >> 4 : 32 >> 4;
+                        const uint64_t b_step = p.b_mn ? 2048 >> 4 : 32 >> 4;
+                        // consecutive MMAs go to different accumulators (k varies fastest), so no
+                        // MMA waits on the previous one's accumulation
+#pragma unroll
+                        for (int kk = 0; kk < TC_BK / 16; ++kk) {
+#pragma unroll
+                            for (int i = 0; i < NP; ++i) {
+#pragma unroll
+                                for (int k = i; k < NP; ++k)
+                                    tc_mma_f16(d_tmem + k * AG_BN, ad[i] + kk * a_step, bd[k - i] + kk * b_step, idesc,
+                                               (kb > 0 || i > 0 || kk > 0) ? 1u : 0u);
+                            }
+                        }
+                        issued = true;
+#pragma unroll
+                        for (int i = 0; i < NP; ++i) tc_commit(&empty_bar[st[i]]);
+                    }
+                    if (!ok) break;
+                    tc_commit(&acc_full[abuf]);
+                    if (++abuf == 2) {
+                        abuf = 0;
+                        aphase ^= 1;
+                    }
                 }
                 if (!ok) break;
-                tc_commit(&acc_full[abuf]);
-                if (++abuf == 2) {
-                    abuf = 0;
-                    aphase ^= 1;
-                }
+                tc_commit(a_empty);  // the unit's A may be overwritten once its products retire
             }
             if (!ok && issued) {
                 tc_commit(drain_bar);
@@ -277,94 +324,124 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
         }
     } else {
         // ---------------- epilogue: series softmax / score gradient, TMEM -> global ----------------
-        // warp w drains TMEM lanes 32*(w%4).. (its lane quadrant) and columns 32*((w-2)/4)..+31
+        // warp w drains TMEM lanes 32*(w%4).. (its lane quadrant) and columns 16*((w-2)/4)..+15,
+        // eight columns at a time, each element's n+1 coefficients transformed in place
         const uint32_t lane_base = 32u * (warp & 3);
-        const int half = (warp - 2) >> 2;
+        const int grp = (warp - 2) >> 2;
         const bool vec = p.vec_ok != 0;
         const float sc = p.scale;
         uint32_t abuf = 0, aphase = 0;
-        for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
-            const AgTile tc = ag_decode(p, t);
+        bool eok = true;
+        for (int u = blockIdx.x; u < p.total_units && eok; u += gridDim.x) {
+          const AgUnit un = ag_unit(p, u);
+          for (int tn = un.tn0; tn < un.tn1; ++tn) {
+            const AgTile tc{un.b, un.tm, tn};
             const int r = tc.tm * AG_BM + static_cast<int>(lane_base) + lane;
-            const int col0 = tc.tn * AG_BN + half * 32;
             const bool masked_tile = ag_masked(p, tc);
-            if (!masked_tile) {
-                if (!mbar_wait_or_abort(&acc_full[abuf], aphase, abort_flag, p.status, 124)) break;
-                tc_fence_after();
-            }
             const bool row_ok = r < p.M;
             float rv[NP];
 #pragma unroll
             for (int k = 0; k < NP; ++k) rv[k] = row_ok ? p.rowv[tc.b * p.rowv_bs + static_cast<int64_t>(r) * NP + k] : 0.f;
             const int64_t last_key = p.causal ? static_cast<int64_t>(r) + p.shift : static_cast<int64_t>(p.N) - 1;
-#pragma unroll 1
+            const bool live = MODE == AG_PROBS ? rv[0] < INFINITY : true;
+            // tile entirely inside the matrix and below the causal diagonal: no per-element tests
+            const bool interior = (tc.tn + 1) * AG_BN <= p.N &&
+                                  (!p.causal || static_cast<int64_t>(tc.tn + 1) * AG_BN - 1 <=
+                                                    static_cast<int64_t>(tc.tm) * AG_BM + p.shift);
+            const int cbase = tc.tn * AG_BN + grp * 16;
+            // score gradient: this thread's 16 probabilities of every plane, requested before the
+            // accumulator wait so that their latency overlaps it (bf16 pairs, zero outside the matrix)
+            uint32_t pw[NP][8];
+            if constexpr (MODE == AG_DSCORES) {
+                const int valid16 = row_ok ? max(0, min(16, p.N - cbase)) : 0;
+#pragma unroll
+                for (int k = 0; k < NP; ++k) {
+                    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(p.pr[k]) + tc.b * p.p_bs +
+                                               static_cast<int64_t>(r) * p.p_rs + cbase;
+                    if (masked_tile) {
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) pw[k][t] = 0u;
+                    } else if (vec && valid16 == 16) {
+                        const uint4 w0 = reinterpret_cast<const uint4*>(src)[0];
+                        const uint4 w1 = reinterpret_cast<const uint4*>(src)[1];
+                        pw[k][0] = w0.x; pw[k][1] = w0.y; pw[k][2] = w0.z; pw[k][3] = w0.w;
+                        pw[k][4] = w1.x; pw[k][5] = w1.y; pw[k][6] = w1.z; pw[k][7] = w1.w;
+                    } else {
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) {
+                            const uint32_t lo = 2 * t < valid16 ? __bfloat16_as_ushort(src[2 * t]) : 0u;
+                            const uint32_t hi = 2 * t + 1 < valid16 ? __bfloat16_as_ushort(src[2 * t + 1]) : 0u;
+                            pw[k][t] = lo | (hi << 16);
+                        }
+                    }
+                }
+            }
+            if (!masked_tile) {
+                if (!mbar_wait_or_abort(&acc_full[abuf], aphase, abort_flag, p.status, 124)) {
+                    eok = false;
+                    break;
+                }
+                tc_fence_after();
+            }
+#pragma unroll
             for (int c = 0; c < 2; ++c) {
-                const int cb = col0 + c * 16;
-                float y[NP][16];
+                const int cb = cbase + c * 8;
+                const int valid = row_ok ? max(0, min(8, p.N - cb)) : 0;
+                float y[NP][8];
                 if (!masked_tile) {
-                    uint32_t x[NP][16];
+                    uint32_t x[NP][8];
 #pragma unroll
                     for (int k = 0; k < NP; ++k)
-                        tmem_ld_32x32b_x16(tmem_base + (lane_base << 16) + abuf * (NP * AG_BN) + k * AG_BN + half * 32 +
-                                               c * 16,
-                                           x[k]);
+                        tmem_ld_32x32b_x8(tmem_base + (lane_base << 16) + abuf * (NP * AG_BN) + k * AG_BN + grp * 16 +
+                                              c * 8,
+                                          x[k]);
                     tmem_ld_wait();
-                    if constexpr (MODE == AG_PROBS) {
-                        const bool live = rv[0] < INFINITY;
 #pragma unroll
-                        for (int u = 0; u < 16; ++u) {
-                            float s[NP];
+                    for (int e = 0; e < 8; ++e) {
+                        float v[NP];
+                        if constexpr (MODE == AG_PROBS) {
 #pragma unroll
-                            for (int k = 0; k < NP; ++k) s[k] = sc * __uint_as_float(x[k][u]) - rv[k];
-                            if (live && cb + u <= last_key) {
-                                s_exp<NP, float>(s, s);
+                            for (int k = 0; k < NP; ++k) v[k] = sc * __uint_as_float(x[k][e]) - rv[k];
+                            if (interior ? live : (live && cb + e <= last_key)) {
+                                s_exp_fast<NP>(v);
                             } else {
 #pragma unroll
-                                for (int k = 0; k < NP; ++k) s[k] = 0.f;
+                                for (int k = 0; k < NP; ++k) v[k] = 0.f;
                             }
-#pragma unroll
-                            for (int k = 0; k < NP; ++k) y[k][u] = s[k];
-                        }
-                    } else {
-                        const int valid = row_ok ? max(0, min(16, p.N - cb)) : 0;
-                        float P[NP][16];
-#pragma unroll
-                        for (int k = 0; k < NP; ++k) {
-                            if (valid > 0) {
-                                ag_load16(static_cast<const __nv_bfloat16*>(p.pr[k]) + tc.b * p.p_bs +
-                                              static_cast<int64_t>(r) * p.p_rs + cb,
-                                          vec, valid, P[k]);
-                            } else {
-#pragma unroll
-                                for (int u = 0; u < 16; ++u) P[k][u] = 0.f;
-                            }
-                        }
-#pragma unroll
-                        for (int u = 0; u < 16; ++u) {
-                            float g[NP], pu[NP], d[NP];
+                        } else {
+                            float g[NP], pe[NP];
 #pragma unroll
                             for (int k = 0; k < NP; ++k) {
-                                g[k] = __uint_as_float(x[k][u]) - rv[k];
-                                pu[k] = P[k][u];
+                                g[k] = __uint_as_float(x[k][e]) - rv[k];
+                                const uint32_t wbits = pw[k][c * 4 + e / 2];
+                                pe[k] = __uint_as_float((e & 1) ? (wbits & 0xFFFF0000u) : (wbits << 16));
                             }
-                            s_mul<NP, float>(pu, g, d);
+                            s_mul<NP, float>(pe, g, v);
 #pragma unroll
-                            for (int k = 0; k < NP; ++k) y[k][u] = sc * d[k];
+                            for (int k = 0; k < NP; ++k) v[k] *= sc;
                         }
+#pragma unroll
+                        for (int k = 0; k < NP; ++k) y[k][e] = v[k];
                     }
                 } else {
 #pragma unroll
                     for (int k = 0; k < NP; ++k)
 #pragma unroll
-                        for (int u = 0; u < 16; ++u) y[k][u] = 0.f;
+                        for (int e = 0; e < 8; ++e) y[k][e] = 0.f;
                 }
-                if (row_ok && cb < p.N) {
-                    const int valid = min(16, p.N - cb);
+                if (valid > 0) {
 #pragma unroll
-                    for (int k = 0; k < NP; ++k)
-                        ag_store16(static_cast<__nv_bfloat16*>(p.c[k]) + tc.b * p.c_bs + static_cast<int64_t>(r) * p.c_rs +
-                                       cb,
-                                   vec, valid, y[k]);
+                    for (int k = 0; k < NP; ++k) {
+                        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c[k]) + tc.b * p.c_bs +
+                                             static_cast<int64_t>(r) * p.c_rs + cb;
+                        if (vec && valid == 8) {
+                            *reinterpret_cast<uint4*>(dst) =
+                                make_uint4(bf16x2_bits(y[k][0], y[k][1]), bf16x2_bits(y[k][2], y[k][3]),
+                                           bf16x2_bits(y[k][4], y[k][5]), bf16x2_bits(y[k][6], y[k][7]));
+                        } else {
+                            for (int t = 0; t < valid; ++t) dst[t] = __float2bfloat16_rn(y[k][t]);
+                        }
+                    }
                 }
             }
             if (!masked_tile) {
@@ -375,6 +452,7 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
                     aphase ^= 1;
                 }
             }
+          }
         }
     }
 
@@ -398,7 +476,7 @@ static int launch_ag(const AgMaps& maps, AgParams& p, cudaStream_t stream) {
         if (e != cudaSuccess) return cuda_fail(e, "pk_attn_score_gemm: cudaFuncSetAttribute");
         attr_set[dev] = true;
     }
-    const int grid = static_cast<int>(std::min<int64_t>(p.total_tiles, num_sms()));
+    const int grid = static_cast<int>(std::min<int64_t>(p.total_units, num_sms()));
     void* tok;
     prof_begin(MODE == AG_PROBS ? "attn_probs_gemm" : "attn_dscores_gemm", stream, &tok);
     attn_score_gemm_kernel<NP, MODE><<<grid, AG_THREADS, AG_SMEM_BYTES, stream>>>(maps, p);
@@ -421,6 +499,7 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
         return fail(PK_ERR_UNSUPPORTED, w + ": dimension exceeds 2^31-1");
     if (batch == 0 || M == 0 || N == 0) return PK_OK;
     if (K == 0) return fail(PK_ERR_UNSUPPORTED, w + ": empty reduction");
+    if (K > AG_MAX_K) return fail(PK_ERR_UNSUPPORTED, w + ": reduction (head dimension) above 128");
     const int P = degree + 1;
     if (!a_planes || !b_planes || !c_planes || !rowv) return fail(PK_ERR_ARG, w + ": null plane array or row values");
     for (int k = 0; k < P; ++k)
@@ -452,10 +531,14 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
     p.kblocks = static_cast<int>(ceil_div(K, TC_BK));
     p.tiles_m = static_cast<int>(ceil_div(M, AG_BM));
     p.tiles_n = static_cast<int>(ceil_div(N, AG_BN));
-    p.group_m = 8;
-    const int64_t total = static_cast<int64_t>(p.tiles_m) * p.tiles_n * batch;
+    p.n_chunks = static_cast<int>(ceil_div(p.tiles_n, AG_CHUNK));
+    const int64_t total = static_cast<int64_t>(p.tiles_m) * p.n_chunks * batch;
     if (total > 0x7fffffff) return fail(PK_ERR_UNSUPPORTED, w + ": too many tiles");
-    p.total_tiles = static_cast<int>(total);
+    p.total_units = static_cast<int>(total);
+    p.a_bytes = P * p.kblocks * AG_A_BYTES;
+    p.nstages = std::min(AG_MAX_STAGES, (AG_SMEM_BUDGET - p.a_bytes) / AG_B_BYTES);
+    if (p.nstages < 2 * P)
+        return fail(PK_ERR_UNSUPPORTED, w + ": reduction too long for the resident operand");
     p.a_mn = am == OPM_MNMAJOR;
     p.b_mn = bm == OPM_MNMAJOR;
     p.causal = causal ? 1 : 0;

@@ -177,6 +177,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             uint32_t stage = 0, phase = 0;
             bool ok = mbar_wait_or_abort(q_full, 0, abort_flag, p.status, 402);
             bool issued = false;
+            // Shared-memory descriptors are built once; a tile or 16-wide k step further on only
+            // advances the start-address field (bytes >> 4), so the single issuing thread spends
+            // a couple of integer adds per MMA instead of rebuilding two descriptors.
+            const uint64_t q_desc = sw128_kmajor_desc(smem_u32(sq));
+            const uint64_t ring_kdesc = sw128_kmajor_desc(smem_u32(ring));
+            const uint64_t ring_vdesc = sw128_mnmajor_desc(smem_u32(ring));
             for (int j = 0; j < nblocks && ok; ++j) {
                 if (j > 0 && !mbar_wait_or_abort(pv_done, (j - 1) & 1, abort_flag, p.status, 403)) {
                     ok = false;
@@ -191,13 +197,14 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t kt = smem_u32(ring + stage * FA_TILE);
-                        for (int a = 0; a + b < NP; ++a) {
-                            const uint32_t qtile = smem_u32(sq + (a * DCH + c) * FA_QTILE);
+                        const uint64_t kd = ring_kdesc + (stage * FA_TILE >> 4);
+#pragma unroll
+                        for (int a = 0; a < NP; ++a) {
+                            if (a + b >= NP) break;
+                            const uint64_t qd = q_desc + ((a * DCH + c) * FA_QTILE >> 4);
 #pragma unroll
                             for (int kk = 0; kk < 4; ++kk)
-                                tc_mma_f16(tmem + (a + b) * FA_BN, sw128_kmajor_desc(qtile + kk * 32),
-                                           sw128_kmajor_desc(kt + kk * 32), idesc_qk,
+                                tc_mma_f16(tmem + (a + b) * FA_BN, qd + kk * 2, kd + kk * 2, idesc_qk,
                                            (b == 0 && c == 0 && kk == 0) ? 0u : 1u);
                         }
                         issued = true;
@@ -223,13 +230,14 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t vt = smem_u32(ring + stage * FA_TILE);
-                    for (int a = 0; a + b < NP; ++a) {
+                    const uint64_t vd = ring_vdesc + (stage * FA_TILE >> 4);
+#pragma unroll
+                    for (int a = 0; a < NP; ++a) {
+                        if (a + b >= NP) break;
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)
                             tc_mma_f16_ts(tmem + Cfg::O_BASE + (a + b) * FA_DS, tmem + a * FA_BN + kk * 16,
-                                          sw128_mnmajor_desc(vt + kk * 2048), idesc_pv,
-                                          (j == 0 && b == 0 && kk == 0) ? 0u : 1u);
+                                          vd + kk * (2048 >> 4), idesc_pv, (j == 0 && b == 0 && kk == 0) ? 0u : 1u);
                     }
                     tc_commit(&empty[stage]);
                     if (++stage == FA_STAGES) {

@@ -602,19 +602,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const uint32_t st = smem_u32(smem + stage * Cfg::STAGE_BYTES);
                     const uint32_t a_hi = st, a_lo = st + Cfg::A_BYTES;
                     const uint32_t b_hi = st + NSUB * Cfg::A_BYTES, b_lo = b_hi + Cfg::B_BYTES;
+                    // descriptors built once per stage; a 16-wide k step advances the start address
+                    // field: 32 bytes along a K-major swizzled row, 16 rows (2048 bytes) MN-major
+                    const uint64_t ahd = p.a_mn ? sw128_mnmajor_desc_lbo(a_hi, 8192) : sw128_kmajor_desc(a_hi);
+                    const uint64_t bhd = p.b_mn ? sw128_mnmajor_desc_lbo(b_hi, 8192) : sw128_kmajor_desc(b_hi);
+                    const uint64_t a_step = p.a_mn ? (2048 >> 4) : (32 >> 4);
+                    const uint64_t b_step = p.b_mn ? (2048 >> 4) : (32 >> 4);
 #pragma unroll
                     for (int kk = 0; kk < TC_BK / 16; ++kk) {
-                        // K-major: 16 bf16 = 32 bytes along the swizzled row; MN-major: 16 rows of
-                        // 128 bytes inside each 64-wide atom (atoms 8 KB apart)
-                        const uint64_t ad = p.a_mn ? sw128_mnmajor_desc_lbo(a_hi + kk * 2048, 8192)
-                                                   : sw128_kmajor_desc(a_hi + kk * 32);
-                        const uint64_t bd = p.b_mn ? sw128_mnmajor_desc_lbo(b_hi + kk * 2048, 8192)
-                                                   : sw128_kmajor_desc(b_hi + kk * 32);
-                        tc_mma_f16(d_tmem, ad, bd, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+                        tc_mma_f16(d_tmem, ahd + kk * a_step, bhd + kk * b_step, idesc, (it > 0 || kk > 0) ? 1u : 0u);
                         if constexpr (SPLIT) {
-                            const uint32_t koff = kk * 32;
-                            tc_mma_f16(d_tmem, sw128_kmajor_desc(a_hi + koff), sw128_kmajor_desc(b_lo + koff), idesc, 1u);
-                            tc_mma_f16(d_tmem, sw128_kmajor_desc(a_lo + koff), sw128_kmajor_desc(b_hi + koff), idesc, 1u);
+                            tc_mma_f16(d_tmem, ahd + kk * 2, sw128_kmajor_desc(b_lo) + kk * 2, idesc, 1u);
+                            tc_mma_f16(d_tmem, sw128_kmajor_desc(a_lo) + kk * 2, bhd + kk * 2, idesc, 1u);
                         }
                     }
                     issued = true;

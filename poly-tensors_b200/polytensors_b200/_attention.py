@@ -121,9 +121,10 @@ def flash_forward(Q, Kp, V, causal, scale, stats=None):
 def fused_backward_eligible(Q, Kp, V):
     """Whether the backward builds probabilities and score gradients in the epilogue of their
     products (pk_attn_probs_gemm / pk_attn_dscores_gemm): bfloat16 planes, degree <= 3, head
-    dimensions multiples of 8 (the flattened planes are contiguous, so every slice is aligned)."""
+    dimensions multiples of 8 up to 128 (the flattened planes are contiguous, so every slice is
+    aligned)."""
     return (Q[0].dtype == torch.bfloat16 and len(Q) <= 4 and Q[0].shape[-1] % 8 == 0
-            and V[0].shape[-1] % 8 == 0)
+            and V[0].shape[-1] % 8 == 0 and Q[0].shape[-1] <= 128 and V[0].shape[-1] <= 128)
 
 
 def _query_tiles(L, S, causal):
