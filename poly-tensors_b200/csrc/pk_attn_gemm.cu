@@ -38,7 +38,9 @@ constexpr int AG_A_BYTES = AG_BM * TC_BK * 2;     // one plane's 128 x 64 A k-bl
 constexpr int AG_B_BYTES = AG_BN * TC_BK * 2;     // one plane's 64 x 64 B k-block (a ring stage)
 constexpr int AG_MAX_K = 128;                     // reduction held resident (head dimension)
 constexpr int AG_MAX_STAGES = 24;
-constexpr int AG_SMEM_BUDGET = 220 * 1024;        // resident A + B ring
+constexpr int AG_STAGE_OUT = 32 * AG_BN * 2;      // one lane quadrant's 32 x 64 block of one plane, bf16
+constexpr int AG_OUT_BYTES = 4 * 2 * AG_STAGE_OUT; // 4 quadrants x 2 buffers (output staging for TMA stores)
+constexpr int AG_SMEM_BUDGET = 220 * 1024;        // resident A + B ring + output staging
 constexpr int AG_SMEM_BYTES = AG_SMEM_BUDGET + 1024 + 512;
 constexpr int AG_CHUNK = 8;                       // B tiles per work unit
 constexpr int AG_MAX_NP = 4;
@@ -48,6 +50,7 @@ enum { AG_PROBS = 0, AG_DSCORES = 1 };
 struct AgMaps {
     CUtensorMap a[AG_MAX_NP];
     CUtensorMap b[AG_MAX_NP];
+    CUtensorMap c[AG_MAX_NP];  // output planes, boxes of 64 columns x 32 rows (TMA stores)
 };
 
 struct AgParams {
@@ -60,6 +63,7 @@ struct AgParams {
     int64_t shift;     // query index of row r is r + shift
     float scale;
     int vec_ok;        // 16-byte vector access to the output (and probability) planes
+    int tma_store;     // output planes written by TMA stores from shared-memory staging
     int64_t c_bs, c_rs;
     void* c[AG_MAX_NP];
     int64_t p_bs, p_rs;              // AG_DSCORES: probability planes
@@ -124,6 +128,7 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* a_res = smem;                // [plane][kblock] 16 KB boxes
     uint8_t* ring = smem + p.a_bytes;     // B stages, 8 KB each
+    uint8_t* out_stage = smem + AG_SMEM_BUDGET - AG_OUT_BYTES;  // [quadrant][buffer] 4 KB blocks
     uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + AG_SMEM_BUDGET);
     uint64_t* empty_bar = full_bar + AG_MAX_STAGES;
     uint64_t* acc_full = empty_bar + AG_MAX_STAGES;
@@ -155,6 +160,7 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
         for (int i = 0; i < NP; ++i) {
             tma_prefetch_desc(&maps.a[i]);
             tma_prefetch_desc(&maps.b[i]);
+            if (p.tma_store) tma_prefetch_desc(&maps.c[i]);
         }
     }
     if (warp == 1) {
@@ -331,13 +337,14 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
         const bool vec = p.vec_ok != 0;
         const float sc = p.scale;
         uint32_t abuf = 0, aphase = 0;
-        bool eok = true;
-        for (int u = blockIdx.x; u < p.total_units && eok; u += gridDim.x) {
+        // A wait that fails (timeout or abort) turns its tile into zeros; every warp still runs the
+        // same tile sequence, so the quadrants' named barriers always match.
+        for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
           const AgUnit un = ag_unit(p, u);
           for (int tn = un.tn0; tn < un.tn1; ++tn) {
             const AgTile tc{un.b, un.tm, tn};
             const int r = tc.tm * AG_BM + static_cast<int>(lane_base) + lane;
-            const bool masked_tile = ag_masked(p, tc);
+            bool masked_tile = ag_masked(p, tc);
             const bool row_ok = r < p.M;
             float rv[NP];
 #pragma unroll
@@ -377,17 +384,14 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
                 }
             }
             if (!masked_tile) {
-                if (!mbar_wait_or_abort(&acc_full[abuf], aphase, abort_flag, p.status, 124)) {
-                    eok = false;
-                    break;
-                }
-                tc_fence_after();
+                if (mbar_wait_or_abort(&acc_full[abuf], aphase, abort_flag, p.status, 124)) tc_fence_after();
+                else masked_tile = true;  // no accumulator to read: write zeros
             }
+            // this thread's 16 columns of every plane as bf16 pairs: ypk[k][0..7]
+            uint32_t ypk[NP][8];
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 const int cb = cbase + c * 8;
-                const int valid = row_ok ? max(0, min(8, p.N - cb)) : 0;
-                float y[NP][8];
                 if (!masked_tile) {
                     uint32_t x[NP][8];
 #pragma unroll
@@ -396,64 +400,107 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
                                               c * 8,
                                           x[k]);
                     tmem_ld_wait();
+                    if (c == 1) {
+                        // the accumulator is in registers: release it to the next tile's products
+                        tc_fence_before();
+                        mbar_arrive(&acc_empty[abuf]);
+                        if (++abuf == 2) {
+                            abuf = 0;
+                            aphase ^= 1;
+                        }
+                    }
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        float v[NP];
-                        if constexpr (MODE == AG_PROBS) {
+                    for (int e = 0; e < 8; e += 2) {
+                        float v2[2][NP];
 #pragma unroll
-                            for (int k = 0; k < NP; ++k) v[k] = sc * __uint_as_float(x[k][e]) - rv[k];
-                            if (interior ? live : (live && cb + e <= last_key)) {
-                                s_exp_fast<NP>(v);
+                        for (int h = 0; h < 2; ++h) {
+                            float* v = v2[h];
+                            const int ee = e + h;
+                            if constexpr (MODE == AG_PROBS) {
+#pragma unroll
+                                for (int k = 0; k < NP; ++k) v[k] = sc * __uint_as_float(x[k][ee]) - rv[k];
+                                if (interior ? live : (live && cb + ee <= last_key)) {
+                                    s_exp_fast<NP>(v2[h]);
+                                } else {
+#pragma unroll
+                                    for (int k = 0; k < NP; ++k) v[k] = 0.f;
+                                }
                             } else {
+                                float g[NP], pe[NP], d[NP];
 #pragma unroll
-                                for (int k = 0; k < NP; ++k) v[k] = 0.f;
+                                for (int k = 0; k < NP; ++k) {
+                                    g[k] = __uint_as_float(x[k][ee]) - rv[k];
+                                    const uint32_t wbits = pw[k][c * 4 + ee / 2];
+                                    pe[k] = __uint_as_float((ee & 1) ? (wbits & 0xFFFF0000u) : (wbits << 16));
+                                }
+                                s_mul<NP, float>(pe, g, d);
+#pragma unroll
+                                for (int k = 0; k < NP; ++k) v[k] = sc * d[k];
                             }
-                        } else {
-                            float g[NP], pe[NP];
-#pragma unroll
-                            for (int k = 0; k < NP; ++k) {
-                                g[k] = __uint_as_float(x[k][e]) - rv[k];
-                                const uint32_t wbits = pw[k][c * 4 + e / 2];
-                                pe[k] = __uint_as_float((e & 1) ? (wbits & 0xFFFF0000u) : (wbits << 16));
-                            }
-                            s_mul<NP, float>(pe, g, v);
-#pragma unroll
-                            for (int k = 0; k < NP; ++k) v[k] *= sc;
                         }
 #pragma unroll
-                        for (int k = 0; k < NP; ++k) y[k][e] = v[k];
+                        for (int k = 0; k < NP; ++k) ypk[k][c * 4 + e / 2] = bf16x2_bits(v2[0][k], v2[1][k]);
                     }
                 } else {
 #pragma unroll
                     for (int k = 0; k < NP; ++k)
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) y[k][e] = 0.f;
+                        for (int t = 0; t < 4; ++t) ypk[k][c * 4 + t] = 0u;
                 }
-                if (valid > 0) {
+            }
+            if (p.tma_store) {
+                // Per plane: the quadrant's four warps write their 32 rows x 16 columns into the
+                // quadrant's staging block (128-byte swizzle: 16-byte chunk j of row t sits at chunk
+                // j ^ (t & 7)), then one thread stores the 32 x 64 block with TMA.  Two blocks per
+                // quadrant alternate; a block is rewritten only after its previous store has read it.
+                const int q = warp & 3;
+                const bool elected = grp == 0 && lane == 0;
+#pragma unroll
+                for (int k = 0; k < NP; ++k) {
+                    uint8_t* blk = out_stage + (q * 2 + (k & 1)) * AG_STAGE_OUT;
+                    if (elected) {
+                        if (k == 0) bulk_wait_group_read<0>();
+                        else bulk_wait_group_read<1>();
+                    }
+                    named_barrier_sync(1 + q, 128);
+                    uint8_t* row = blk + lane * 128;
+                    const int j0 = grp * 2;
+                    *reinterpret_cast<uint4*>(row + (((j0 + 0) ^ (lane & 7)) << 4)) =
+                        make_uint4(ypk[k][0], ypk[k][1], ypk[k][2], ypk[k][3]);
+                    *reinterpret_cast<uint4*>(row + (((j0 + 1) ^ (lane & 7)) << 4)) =
+                        make_uint4(ypk[k][4], ypk[k][5], ypk[k][6], ypk[k][7]);
+                    fence_proxy_async();
+                    named_barrier_sync(1 + q, 128);
+                    if (elected) {
+                        tma_store_3d(&maps.c[k], blk, tc.tn * AG_BN, tc.tm * AG_BM + q * 32, tc.b);
+                        bulk_commit_group();
+                    }
+                }
+            } else if (row_ok) {
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const int cb = cbase + c * 8;
+                    const int valid = max(0, min(8, p.N - cb));
+                    if (valid <= 0) continue;
 #pragma unroll
                     for (int k = 0; k < NP; ++k) {
                         __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c[k]) + tc.b * p.c_bs +
                                              static_cast<int64_t>(r) * p.c_rs + cb;
                         if (vec && valid == 8) {
                             *reinterpret_cast<uint4*>(dst) =
-                                make_uint4(bf16x2_bits(y[k][0], y[k][1]), bf16x2_bits(y[k][2], y[k][3]),
-                                           bf16x2_bits(y[k][4], y[k][5]), bf16x2_bits(y[k][6], y[k][7]));
+                                make_uint4(ypk[k][c * 4], ypk[k][c * 4 + 1], ypk[k][c * 4 + 2], ypk[k][c * 4 + 3]);
                         } else {
-                            for (int t = 0; t < valid; ++t) dst[t] = __float2bfloat16_rn(y[k][t]);
+                            for (int t = 0; t < valid; ++t)
+                                dst[t] = __ushort_as_bfloat16(
+                                    static_cast<unsigned short>((ypk[k][c * 4 + t / 2] >> (16 * (t & 1))) & 0xFFFFu));
                         }
                     }
                 }
             }
-            if (!masked_tile) {
-                tc_fence_before();
-                mbar_arrive(&acc_empty[abuf]);
-                if (++abuf == 2) {
-                    abuf = 0;
-                    aphase ^= 1;
-                }
-            }
           }
         }
+        if (p.tma_store && grp == 0 && lane == 0)
+            bulk_wait_group_all();  // this quadrant's stores have completed before the CTA exits
     }
 
     tc_fence_before();
@@ -536,8 +583,8 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
     if (total > 0x7fffffff) return fail(PK_ERR_UNSUPPORTED, w + ": too many tiles");
     p.total_units = static_cast<int>(total);
     p.a_bytes = P * p.kblocks * AG_A_BYTES;
-    p.nstages = std::min(AG_MAX_STAGES, (AG_SMEM_BUDGET - p.a_bytes) / AG_B_BYTES);
-    if (p.nstages < 2 * P)
+    p.nstages = std::min(AG_MAX_STAGES, (AG_SMEM_BUDGET - AG_OUT_BYTES - p.a_bytes) / AG_B_BYTES);
+    if (p.nstages < P + 2)
         return fail(PK_ERR_UNSUPPORTED, w + ": reduction too long for the resident operand");
     p.a_mn = am == OPM_MNMAJOR;
     p.b_mn = bm == OPM_MNMAJOR;
@@ -549,9 +596,12 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
     p.p_bs = p_bs;
     p.p_rs = p_rs;
     bool vec = c_rs % 8 == 0 && (batch == 1 || c_bs % 8 == 0);
+    // TMA stores of the output planes: 16-byte aligned bases and row / batch strides, rows and
+    // batch entries not overlapping
+    bool tstore = vec && c_rs >= N && (batch == 1 || c_bs >= M * c_rs);
     for (int k = 0; k < P; ++k) {
         p.c[k] = c_planes[k];
-        if (reinterpret_cast<uintptr_t>(c_planes[k]) % 16) vec = false;
+        if (reinterpret_cast<uintptr_t>(c_planes[k]) % 16) vec = tstore = false;
         if (mode == AG_DSCORES) {
             p.pr[k] = probs[k];
             if (reinterpret_cast<uintptr_t>(probs[k]) % 16) vec = false;
@@ -559,6 +609,12 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
     }
     if (mode == AG_DSCORES && (p_rs % 8 != 0 || (batch > 1 && p_bs % 8 != 0))) vec = false;
     p.vec_ok = vec ? 1 : 0;
+    if (tstore) {
+        const int64_t sb = batch > 1 ? c_bs * 2 : M * c_rs * 2;
+        for (int k = 0; k < P && tstore; ++k)
+            if (encode_map3(&maps.c[k], c_planes[k], N, M, batch, c_rs * 2, sb, 32) != PK_OK) tstore = false;
+    }
+    p.tma_store = tstore ? 1 : 0;
     p.rowv = static_cast<const float*>(rowv);
     p.rowv_bs = rowv_bs;
     p.status = device_status_ptr();
