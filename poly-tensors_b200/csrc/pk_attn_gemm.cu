@@ -564,8 +564,8 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
 
     AgMaps maps;
     std::memset(&maps, 0, sizeof(maps));
-    const TcOperand oa{am, M, K, K, batch, a_planes, a_bs, a_rs, a_cs, nullptr, nullptr, 0};
-    const TcOperand ob{bm, N, K, K, batch, b_planes, b_bs, b_cs, b_rs, nullptr, nullptr, 0};
+    const TcOperand oa{am, M, K, K, batch, a_planes, a_bs, a_rs, a_cs, nullptr, nullptr, 0, false};
+    const TcOperand ob{bm, N, K, K, batch, b_planes, b_bs, b_cs, b_rs, nullptr, nullptr, 0, false};
     int rc = encode_operand(maps.a, oa, P, false, AG_BM);
     if (rc) return rc;
     rc = encode_operand(maps.b, ob, P, false, AG_BN);

@@ -335,6 +335,7 @@ struct TcMaps {
 struct TcParams {
     int planes, batch;
     int a_mn, b_mn;  // operand read MN-major (direct bf16 / f16 planes with rows contiguous)
+    int in_fmt;      // MMA input format: 1 = bf16 (also the float32 hi/lo split), 0 = f16
     int M, N;
     int kblocks;
     int tiles_m, tiles_n, group_m;
@@ -578,8 +579,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             // MN-major operands: transpose bits 15 (A) / 16 (B) of the instruction descriptor
-            const uint32_t idesc = f16_idesc(1u, TC_BM, BN) | (static_cast<uint32_t>(p.a_mn) << 15) |
-                                   (static_cast<uint32_t>(p.b_mn) << 16);
+            const uint32_t idesc = f16_idesc(static_cast<uint32_t>(p.in_fmt), TC_BM, BN) |
+                                   (static_cast<uint32_t>(p.a_mn) << 15) | (static_cast<uint32_t>(p.b_mn) << 16);
             uint32_t stage = 0, phase = 0;
             uint32_t abuf = 0, aphase = 0;
             bool ok = true;
@@ -1061,15 +1062,14 @@ static int poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N,
         tp.status = device_status_ptr();
         const int64_t tiles256 = ceil_div(M, TC_BM) * ceil_div(N, 256) * batch * P;
         const bool wide = tiles256 >= 2 * num_sms();
+        const bool f16 = dtype == PK_F16;
         const TcOperand oa{g.a_mode, M, K, g.Kp, batch, a_planes, a_bs, a_rs, a_cs,
-                           static_cast<const char*>(ws_a), g.a_first.data(), g.a_subs};
+                           static_cast<const char*>(ws_a), g.a_first.data(), g.a_subs, f16};
         const TcOperand ob{g.b_mode, N, K, g.Kp, batch, b_planes, b_bs, b_cs, b_rs,
-                           static_cast<const char*>(ws_b), g.b_first.data(), g.b_subs};
+                           static_cast<const char*>(ws_b), g.b_first.data(), g.b_subs, f16};
+        tp.in_fmt = f16 ? 0 : 1;
         if (dtype == PK_F32) {
             return wide ? launch_tc<256, true>(tp, oa, ob, stream) : launch_tc<128, true>(tp, oa, ob, stream);
-        }
-        if (dtype == PK_F16) {
-            return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: float16 planes are not implemented yet");
         }
         return wide ? launch_tc<256, false>(tp, oa, ob, stream) : launch_tc<128, false>(tp, oa, ob, stream);
     }

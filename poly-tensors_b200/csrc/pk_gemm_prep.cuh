@@ -62,7 +62,7 @@ enum OperandMode {
 // (M or N) and along k.
 inline int operand_mode(int dtype, const void* const* planes, int P, int64_t batch, int64_t rows, int64_t K,
                         int64_t s_b, int64_t s_rows, int64_t s_k) {
-    if (dtype != PK_BF16) return OPM_STAGED;
+    if (dtype != PK_BF16 && dtype != PK_F16) return OPM_STAGED;
     for (int p = 0; p < P; ++p)
         if (reinterpret_cast<uintptr_t>(planes[p]) % 16) return OPM_STAGED;
     if (s_k == 1 && s_rows % 8 == 0 && s_rows >= K && (batch == 1 || (s_b % 8 == 0 && s_b >= rows * s_rows)))
@@ -72,15 +72,15 @@ inline int operand_mode(int dtype, const void* const* planes, int P, int64_t bat
     return OPM_STAGED;
 }
 
-// 3-D bf16 tensor map with the 128-byte swizzle: dims {d0 (innermost), d1, d2}, byte strides
-// {s1, s2} of dims 1 and 2, box {64, box1, 1}.
+// 3-D 16-bit (bf16, or f16 with f16 = true) tensor map with the 128-byte swizzle: dims
+// {d0 (innermost), d1, d2}, byte strides {s1, s2} of dims 1 and 2, box {64, box1, 1}.
 inline int encode_map3(CUtensorMap* map, const void* base, int64_t d0, int64_t d1, int64_t d2, int64_t s1,
-                       int64_t s2, int box1) {
+                       int64_t s2, int box1, bool f16 = false) {
     const cuuint64_t dims[3] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1), static_cast<cuuint64_t>(d2)};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(s1), static_cast<cuuint64_t>(s2)};
     const cuuint32_t box[3] = {static_cast<cuuint32_t>(TC_BK), static_cast<cuuint32_t>(box1), 1u};
-    CUresult r = encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
-                              CU_TENSOR_MAP_SWIZZLE_128B);
+    CUresult r = encode_tiled(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                              const_cast<void*>(base), dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (r != CUDA_SUCCESS) return fail(PK_ERR_CUDA, "pk_poly_gemm: cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
     return PK_OK;
 }
@@ -96,6 +96,7 @@ struct TcOperand {
     const char* ws;                // staged workspace base
     const int* first;              // first staged sub-plane of each plane
     int64_t subs;                  // staged sub-planes per batch entry
+    bool f16;                      // float16 planes (bfloat16 otherwise)
 };
 
 // Per-plane maps (bf16 / f16 products), or one map over the whole staged workspace (float32).
@@ -106,13 +107,14 @@ inline int encode_operand(CUtensorMap* maps, const TcOperand& o, int planes, boo
         int rc;
         if (o.mode == OPM_KMAJOR) {
             const int64_t sb = o.batch > 1 ? o.s_b * 2 : o.rows * o.s_rows * 2;
-            rc = encode_map3(&maps[p], o.planes[p], o.K, o.rows, o.batch, o.s_rows * 2, sb, box_rows);
+            rc = encode_map3(&maps[p], o.planes[p], o.K, o.rows, o.batch, o.s_rows * 2, sb, box_rows, o.f16);
         } else if (o.mode == OPM_MNMAJOR) {
             const int64_t sb = o.batch > 1 ? o.s_b * 2 : o.K * o.s_k * 2;
-            rc = encode_map3(&maps[p], o.planes[p], o.rows, o.K, o.batch, o.s_k * 2, sb, 64);
+            rc = encode_map3(&maps[p], o.planes[p], o.rows, o.K, o.batch, o.s_k * 2, sb, 64, o.f16);
         } else {
             const char* base = o.ws + static_cast<int64_t>(o.first[p]) * o.rows * o.Kp * 2;
-            rc = encode_map3(&maps[p], base, o.Kp, o.rows, o.batch, o.Kp * 2, o.subs * o.rows * o.Kp * 2, box_rows);
+            rc = encode_map3(&maps[p], base, o.Kp, o.rows, o.batch, o.Kp * 2, o.subs * o.rows * o.Kp * 2, box_rows,
+                             o.f16);
         }
         if (rc) return rc;
     }

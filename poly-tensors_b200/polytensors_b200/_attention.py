@@ -61,7 +61,7 @@ def eligible(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False, 
         return False
     planes = [c for t in tensors for c in _planes(t, degree)]
     dtype = planes[0].dtype
-    if dtype not in (torch.float32, torch.float64, torch.bfloat16):
+    if dtype not in (torch.float32, torch.float64, torch.bfloat16, torch.float16):
         return False
     if any(c.dtype != dtype or not c.is_cuda for c in planes):
         return False

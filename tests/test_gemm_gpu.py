@@ -110,17 +110,18 @@ def _layout(planes, how):
     return out
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("a_how", ["k", "rows", "odd"])
 @pytest.mark.parametrize("b_how", ["k", "rows", "odd"])
-def test_bf16_operands_read_in_place(a_how, b_how):
-    """bf16 planes are read where they lie (K-major or MN-major tensor maps, no staging) when
+def test_16bit_operands_read_in_place(a_how, b_how, dtype):
+    """bf16 / f16 planes are read where they lie (K-major or MN-major tensor maps, no staging) when
     aligned, and staged otherwise; every combination, batched, with ragged M / N / K tails.
-    Tolerance 1e-2 of the plane max-norm: exact bf16 products, fp32 sums, bf16 output."""
+    Tolerance 1e-2 of the plane max-norm: exact 16-bit products, fp32 sums, 16-bit output."""
     from polytensors_b200 import _kernels, _lib
 
     batch, M, N, K, n = 3, 200, 296, 136, 2
-    A = series((batch, M, K), n, 21, torch.bfloat16)
-    W = series((batch, N, K), n, 22, torch.bfloat16)         # B = W^T
+    A = series((batch, M, K), n, 21, dtype)
+    W = series((batch, N, K), n, 22, dtype)         # B = W^T
     a = _layout(A, a_how)
     b = [w.transpose(-2, -1) for w in _layout(W, b_how)]   # "k": k contiguous in B
     got = _kernels.poly_matmul(a, b)
@@ -131,7 +132,8 @@ def test_bf16_operands_read_in_place(a_how, b_how):
     pb, kb = _lib.pointer_array(b)
     import ctypes
     need = ctypes.c_size_t(1)
-    assert lib.pk_poly_gemm_workspace_query(_lib.PK_BF16, n, batch, M, N, K, pa, *a[0].stride(), pb,
+    code = _lib.PK_BF16 if dtype == torch.bfloat16 else _lib.PK_F16
+    assert lib.pk_poly_gemm_workspace_query(code, n, batch, M, N, K, pa, *a[0].stride(), pb,
                                             *b[0].stride(), n + 1, n + 1, ctypes.byref(need)) == 0
     assert (need.value == 0) == (a_how != "odd" and b_how != "odd")
 
