@@ -118,6 +118,21 @@ PK_API int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t
                  void* const* c_planes, int64_t c_bs, int64_t c_rs,
                  int a_complex_from, int b_complex_from,
                  void* workspace, size_t workspace_bytes, void* stream);
+/* pk_poly_gemm (accumulate = 0) or pk_poly_gemm_accumulate (accumulate != 0) for operands
+ * whose A planes are zero outside a band, as the causal attention products are:
+ *   band 1: A[b][m][k] may be nonzero only for k >= m + band_offset,
+ *   band 2: A[b][m][k] may be nonzero only for k <= m + band_offset,
+ *   band 0: no band (plain product).
+ * k blocks outside the band of a whole row tile are skipped (the caller guarantees the skipped
+ * entries are zero; the product may still read some of them).  Replaces the same products as
+ * pk_poly_gemm; the reference evaluates them over the full (masked) score matrices
+ * (src/polytensors/_decompositions.py:28-43). */
+PK_API int pk_poly_gemm_banded(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K,
+                 const void* const* a_planes, int64_t a_bs, int64_t a_rs, int64_t a_cs,
+                 const void* const* b_planes, int64_t b_bs, int64_t b_rs, int64_t b_cs,
+                 void* const* c_planes, int64_t c_bs, int64_t c_rs,
+                 int a_complex_from, int b_complex_from, int accumulate, int band, int64_t band_offset,
+                 void* workspace, size_t workspace_bytes, void* stream);
 /* C_k += sum_{i+j=k} A_i B_j: pk_poly_gemm accumulating into the existing output planes
  * (the beta = alpha = 1 case of addmm, src/polytensors/_range_ops.py:160-176).  Same
  * arguments and workspace. */

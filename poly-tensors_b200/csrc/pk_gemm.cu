@@ -343,6 +343,9 @@ struct TcParams {
     int out_kind;  // 0 = f32, 1 = bf16, 2 = f16
     int vec_ok;    // output rows 16-byte aligned: vectorised stores allowed
     int accumulate;  // C += product (read-modify-write) instead of C = product
+    int band;        // 0: every k; 1: only k >= m + band_off contributes; 2: only k <= m + band_off
+    int64_t band_off;
+    int K;           // reduction length (banded k ranges)
     int64_t c_bs, c_rs;
     void* c[PK_MAX_PLANES];
     int* status;
@@ -369,6 +372,27 @@ __device__ __forceinline__ TileCoord decode_tile(const TcParams& p, int t) {
     c.tm = first_m + (r % span) % gsize;
     c.tn = (r % span) / gsize;
     return c;
+}
+
+// The k blocks a row tile needs.  A banded product (a causal attention product) only has
+// nonzeros for k >= m + off (band 1) or k <= m + off (band 2) in row m; k blocks entirely
+// outside the band of every row of the tile are neither loaded nor multiplied.
+__device__ __forceinline__ void tile_kblocks(const TcParams& p, int tm, int& kb0, int& kb1) {
+    kb0 = 0;
+    kb1 = p.kblocks;
+    if (p.band == 0) return;
+    const int64_t m0 = static_cast<int64_t>(tm) * TC_BM;
+    const int64_t m1 = (m0 + TC_BM - 1 < p.M - 1) ? m0 + TC_BM - 1 : static_cast<int64_t>(p.M) - 1;
+    if (p.band == 1) {
+        const int64_t lo = m0 + p.band_off;
+        const int64_t b = lo <= 0 ? 0 : lo / TC_BK;
+        kb0 = static_cast<int>(b < p.kblocks ? b : p.kblocks);
+    } else {
+        int64_t hi = m1 + p.band_off;
+        if (hi > static_cast<int64_t>(p.K) - 1) hi = static_cast<int64_t>(p.K) - 1;
+        const int64_t b = hi < 0 ? 0 : hi / TC_BK + 1;
+        kb1 = static_cast<int>(b < p.kblocks ? b : p.kblocks);
+    }
 }
 
 template <int BN, bool SPLIT>
@@ -514,9 +538,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             bool ok = true;
             for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
                 const TileCoord tc = decode_tile(p, t);
+                int kb0, kb1;
+                tile_kblocks(p, tc.tm, kb0, kb1);
                 for (int i = 0; i <= tc.plane && ok; ++i) {
                     const int j = tc.plane - i;
-                    for (int kb = 0; kb < p.kblocks; ++kb) {
+                    for (int kb = kb0; kb < kb1; ++kb) {
                         if (!mbar_wait_or_abort(&empty_bar[stage], phase ^ 1, abort_flag, p.status, 101)) {
                             ok = false;
                             break;
@@ -587,13 +613,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             bool issued = false;
             for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
                 const TileCoord tc = decode_tile(p, t);
+                int kb0, kb1;
+                tile_kblocks(p, tc.tm, kb0, kb1);
+                if (kb1 <= kb0) continue;  // no k block in the band: the epilogue writes the zeros
                 if (!mbar_wait_or_abort(&acc_empty[abuf], aphase ^ 1, abort_flag, p.status, 102)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + abuf * BN;
-                const int iters = (tc.plane + 1) * p.kblocks;
+                const int iters = (tc.plane + 1) * (kb1 - kb0);
                 for (int it = 0; it < iters; ++it) {
                     if (!mbar_wait_or_abort(&full_bar[stage], phase, abort_flag, p.status, 103)) {
                         ok = false;
@@ -648,9 +677,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         uint32_t abuf = 0, aphase = 0;
         for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
             const TileCoord tc = decode_tile(p, t);
+            const int row = tc.tm * TC_BM + lane_base + lane;
+            int kb0, kb1;
+            tile_kblocks(p, tc.tm, kb0, kb1);
+            if (kb1 <= kb0) {
+                // empty band: the product is zero (nothing to add when accumulating)
+                if (!p.accumulate) {
+                    uint32_t z[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) z[j] = 0u;
+                    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c)
+                        store_row_chunk(p, tc.plane, tc.b, row, tc.tn * BN + c * 32, z);
+                }
+                continue;
+            }
             if (!mbar_wait_or_abort(&acc_full[abuf], aphase, abort_flag, p.status, 104)) break;
             tc_fence_after();
-            const int row = tc.tm * TC_BM + lane_base + lane;
 #pragma unroll 1
             for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
                 uint32_t r[32];
@@ -968,7 +1010,8 @@ namespace pk {
 static int poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K, const void* const* a_planes,
                      int64_t a_bs, int64_t a_rs, int64_t a_cs, const void* const* b_planes, int64_t b_bs, int64_t b_rs,
                      int64_t b_cs, void* const* c_planes, int64_t c_bs, int64_t c_rs, int a_complex_from,
-                     int b_complex_from, void* workspace, size_t workspace_bytes, void* stream_ptr, int accumulate) {
+                     int b_complex_from, void* workspace, size_t workspace_bytes, void* stream_ptr, int accumulate,
+                     int band = 0, int64_t band_off = 0) {
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     if (degree < 0 || degree >= PK_MAX_PLANES)
         return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: degree must be in [0, " + std::to_string(PK_MAX_PLANES - 1) + "]");
@@ -1059,9 +1102,14 @@ static int poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N,
         }
         tp.vec_ok = vec ? 1 : 0;
         tp.accumulate = accumulate;
+        tp.band = band;
+        tp.band_off = band_off;
+        tp.K = static_cast<int>(K);
         tp.status = device_status_ptr();
         const int64_t tiles256 = ceil_div(M, TC_BM) * ceil_div(N, 256) * batch * P;
-        const bool wide = tiles256 >= 2 * num_sms();
+        // 256-column tiles when N fills them (a 128-wide N would leave half of every MMA on the
+        // zero fill past N) and there are at least two such tiles per SM
+        const bool wide = tiles256 >= 2 * num_sms() && N > 192;
         const bool f16 = dtype == PK_F16;
         const TcOperand oa{g.a_mode, M, K, g.Kp, batch, a_planes, a_bs, a_rs, a_cs,
                            static_cast<const char*>(ws_a), g.a_first.data(), g.a_subs, f16};
@@ -1158,6 +1206,18 @@ int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int
                  int b_complex_from, void* workspace, size_t workspace_bytes, void* stream) {
     return poly_gemm(dtype, degree, batch, M, N, K, a_planes, a_bs, a_rs, a_cs, b_planes, b_bs, b_rs, b_cs, c_planes,
                      c_bs, c_rs, a_complex_from, b_complex_from, workspace, workspace_bytes, stream, 0);
+}
+
+int pk_poly_gemm_banded(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K,
+                        const void* const* a_planes, int64_t a_bs, int64_t a_rs, int64_t a_cs,
+                        const void* const* b_planes, int64_t b_bs, int64_t b_rs, int64_t b_cs,
+                        void* const* c_planes, int64_t c_bs, int64_t c_rs, int a_complex_from, int b_complex_from,
+                        int accumulate, int band, int64_t band_offset, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+    if (band < 0 || band > 2) return fail(PK_ERR_ARG, "pk_poly_gemm_banded: band must be 0, 1 or 2");
+    return poly_gemm(dtype, degree, batch, M, N, K, a_planes, a_bs, a_rs, a_cs, b_planes, b_bs, b_rs, b_cs, c_planes,
+                     c_bs, c_rs, a_complex_from, b_complex_from, workspace, workspace_bytes, stream, accumulate ? 1 : 0,
+                     band, band_offset);
 }
 
 int pk_poly_gemm_accumulate(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K,

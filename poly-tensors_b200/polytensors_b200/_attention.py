@@ -27,6 +27,9 @@ from . import _state
 
 # Bytes of score planes (scores/probabilities and their gradient) alive per head block.
 _BLOCK_BYTES = 4 << 30
+# The bf16 backward keeps the probability and score-gradient planes of ALL queries of a head
+# block (no query tiling; the causal products skip the masked half instead), so it gets more.
+_FUSED_BLOCK_BYTES = 16 << 30
 
 
 def _poly_cls():
@@ -184,6 +187,35 @@ def _score_gemm(name, A, B, out, rows, scale, causal, shift, probs=None):
     return out
 
 
+def _fused_backward(Q, Kp, V, dO, dsum, stats, causal, scale, dQ, dK, dV):
+    """bf16 backward over all queries of a head block at a time: probabilities and score gradients
+    from the score-epilogue products, then the three gradient products, banded under a causal
+    mask (dV = P^T dO and dK = dS^T Q need keys <= queries, k >= m; dQ = dS K needs k <= m), so
+    the masked half of the score planes is neither multiplied nor re-read."""
+    BH, L, _ = Q[0].shape
+    S = Kp[0].shape[1]
+    NP = len(Q)
+    per_head = 2 * NP * L * S * Q[0].element_size()
+    hb = max(1, min(BH, _FUSED_BLOCK_BYTES // max(per_head, 1)))
+    lower, upper = (1, 2) if causal else (0, 0)
+    for h0 in range(0, BH, hb):
+        hs = slice(h0, min(BH, h0 + hb))
+        hbn = hs.stop - hs.start
+        Pr = [torch.empty(hbn, L, S, dtype=Q[0].dtype, device=Q[0].device) for _ in Q]
+        _score_gemm("probs", [q[hs] for q in Q], [k[hs].transpose(1, 2) for k in Kp], Pr, stats[hs], scale,
+                    causal, 0)
+        if dV is not None:
+            K.poly_matmul([p.transpose(1, 2) for p in Pr], [g[hs] for g in dO], out=[t[hs] for t in dV], band=lower)
+        dS = [torch.empty_like(p) for p in Pr]
+        _score_gemm("dscores", [g[hs] for g in dO], [v[hs].transpose(1, 2) for v in V], dS, dsum[hs], scale,
+                    causal, 0, probs=Pr)
+        del Pr
+        if dQ is not None:
+            K.poly_matmul(dS, [k[hs] for k in Kp], out=[t[hs] for t in dQ], band=upper)
+        if dK is not None:
+            K.poly_matmul([d.transpose(1, 2) for d in dS], [q[hs] for q in Q], out=[t[hs] for t in dK], band=lower)
+
+
 def backward_planes(Q, Kp, V, O, dO, causal, scale, need, stats=None):
     BH, L, _ = Q[0].shape
     S = Kp[0].shape[1]
@@ -201,6 +233,9 @@ def backward_planes(Q, Kp, V, O, dO, causal, scale, need, stats=None):
     code = K.dtype_code(Q[0].dtype)
     tiles = _query_tiles(L, S, causal)
     fused = stats is not None and fused_backward_eligible(Q, Kp, V)
+    if fused:
+        _fused_backward(Q, Kp, V, dO, dsum, stats, causal, scale, dQ, dK, dV)
+        return dQ, dK, dV
     for h0 in range(0, BH, hb):
         h1 = min(BH, h0 + hb)
         hs = slice(h0, h1)
@@ -212,31 +247,19 @@ def backward_planes(Q, Kp, V, O, dO, causal, scale, need, stats=None):
                 t[hs].zero_()
         for q0, q1, kend in tiles:
             qs, ks = slice(q0, q1), slice(0, kend)
-            if fused:
-                # probabilities and score gradients straight from the products' epilogues
-                hbn, Lq = h1 - h0, q1 - q0
-                Pr = [torch.empty(hbn, Lq, kend, dtype=Q[0].dtype, device=Q[0].device) for _ in Q]
-                _score_gemm("probs", [q[hs, qs] for q in Q], [k[hs, ks].transpose(1, 2) for k in Kp], Pr,
-                            stats[hs, qs], scale, causal, q0)
-            else:
-                Pr = K.poly_matmul([q[hs, qs] for q in Q], [k[hs, ks].transpose(1, 2) for k in Kp])
-                _probs(Pr, q1 - q0, scale, causal, q0)
+            Pr = K.poly_matmul([q[hs, qs] for q in Q], [k[hs, ks].transpose(1, 2) for k in Kp])
+            _probs(Pr, q1 - q0, scale, causal, q0)
             if dV is not None:
                 K.poly_matmul([p.transpose(1, 2) for p in Pr], [g[hs, qs] for g in dO],
                               out=[t[hs, ks] for t in dV], accumulate=True)
-            if fused:
-                dS = [torch.empty_like(p) for p in Pr]
-                _score_gemm("dscores", [g[hs, qs] for g in dO], [v[hs, ks].transpose(1, 2) for v in V], dS,
-                            dsum[hs, qs], scale, causal, q0, probs=Pr)
-            else:
-                dS = K.poly_matmul([g[hs, qs] for g in dO], [v[hs, ks].transpose(1, 2) for v in V])
-                rows = (h1 - h0) * (q1 - q0)
-                ds_rows = dsum[hs, qs].contiguous()
-                pp, k1 = _lib.pointer_array(Pr)
-                pd, k2 = _lib.pointer_array(dS)
-                status = _lib.load().pk_attn_dscores(code, D, rows, kend, pp, kend, pd, kend, ds_rows.data_ptr(),
-                                                     float(scale), pd, kend, K._stream(Q[0].device))
-                _lib.check(status, "pk_attn_dscores")
+            dS = K.poly_matmul([g[hs, qs] for g in dO], [v[hs, ks].transpose(1, 2) for v in V])
+            rows = (h1 - h0) * (q1 - q0)
+            ds_rows = dsum[hs, qs].contiguous()
+            pp, k1 = _lib.pointer_array(Pr)
+            pd, k2 = _lib.pointer_array(dS)
+            status = _lib.load().pk_attn_dscores(code, D, rows, kend, pp, kend, pd, kend, ds_rows.data_ptr(),
+                                                 float(scale), pd, kend, K._stream(Q[0].device))
+            _lib.check(status, "pk_attn_dscores")
             del Pr
             if dQ is not None:
                 K.poly_matmul(dS, [k[hs, ks] for k in Kp], out=[t[hs, qs] for t in dQ])

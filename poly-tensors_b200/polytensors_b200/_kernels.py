@@ -61,13 +61,15 @@ def gemm_dtype(a_planes, b_planes):
     return _DTYPE_CODE[base], P, P, [base] * P
 
 
-def poly_matmul(a_planes, b_planes, out=None, accumulate=False):
+def poly_matmul(a_planes, b_planes, out=None, accumulate=False, band=0, band_offset=0):
     """C_k = sum_{i+j=k} A_i @ B_j for planes of shape (M, K) x (K, N) or (B, M, K) x (B, K, N).
 
     Mirrors plain_polynomial_product(matrix=True) (src/polytensors/_plain.py:118-128)
     including real-base / complex-direction promotion (src/polytensors/_plain.py:77-80).
     ``out``: optional output planes (views with unit column stride) written in place;
     ``accumulate``: add the product to ``out`` (C_k += ...) as addmm with beta = 1 does.
+    ``band``/``band_offset``: A is zero outside a band (1: k >= m + offset, 2: k <= m + offset), as
+    in causal attention; k blocks outside it are skipped (pk_poly_gemm_banded).
     """
     P = len(a_planes)
     if P != len(b_planes) or P == 0:
@@ -123,11 +125,16 @@ def poly_matmul(a_planes, b_planes, out=None, accumulate=False):
                                                 pb, b_bs, b_rs, b_cs, acf, bcf, ctypes.byref(ws_bytes)),
                "pk_poly_gemm_workspace_query")
     ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device=a0.device) if ws_bytes.value else None
+    ws_ptr, ws_n = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
+    if band:
+        status = lib.pk_poly_gemm_banded(code, degree, batch, M, N, K, pa, a_bs, a_rs, a_cs, pb, b_bs, b_rs, b_cs,
+                                         pc, c_bs, c_rs, acf, bcf, 1 if accumulate else 0, int(band),
+                                         int(band_offset), ws_ptr, ws_n, _stream(a0.device))
+        _lib.check(status, "pk_poly_gemm_banded")
+        return outs
     fn = lib.pk_poly_gemm_accumulate if accumulate else lib.pk_poly_gemm
-    status = fn(code, degree, batch, M, N, K,
-                              pa, a_bs, a_rs, a_cs, pb, b_bs, b_rs, b_cs, pc, c_bs, c_rs,
-                              acf, bcf, ws.data_ptr() if ws is not None else None,
-                              ws.numel() if ws is not None else 0, _stream(a0.device))
+    status = fn(code, degree, batch, M, N, K, pa, a_bs, a_rs, a_cs, pb, b_bs, b_rs, b_cs, pc, c_bs, c_rs,
+                acf, bcf, ws_ptr, ws_n, _stream(a0.device))
     _lib.check(status, "pk_poly_gemm_accumulate" if accumulate else "pk_poly_gemm")
     return outs
 

@@ -38,6 +38,11 @@ SIGNATURES = {
                             _pp, _i64, _i64, _i64,
                             _pp, _i64, _i64,
                             _i32, _i32, _vp, _sz, _vp]),
+    "pk_poly_gemm_banded": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64,
+                                   _pp, _i64, _i64, _i64,
+                                   _pp, _i64, _i64, _i64,
+                                   _pp, _i64, _i64,
+                                   _i32, _i32, _i32, _i32, _i64, _vp, _sz, _vp]),
     "pk_poly_gemm_accumulate": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64,
                                        _pp, _i64, _i64, _i64,
                                        _pp, _i64, _i64, _i64,

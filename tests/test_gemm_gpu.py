@@ -158,6 +158,29 @@ def test_accumulate_into_strided_views(dtype):
         assert torch.equal(c[:, :8].cpu(), c0[:, :8]) and torch.equal(c[:, :, :16].cpu(), c0[:, :, :16])
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float64])
+@pytest.mark.parametrize("band,offset", [(1, 0), (2, 0), (1, 200), (2, -150), (1, -64)])
+def test_banded_product(dtype, band, offset):
+    """pk_poly_gemm_banded: A zero outside the band (1: k >= m + offset, 2: k <= m + offset) gives
+    the plain product; row tiles whose band holds no k block write zeros (or add nothing)."""
+    from polytensors_b200 import _kernels
+
+    batch, M, N, K, n = 2, 300, 136, 260, 2
+    A, B = series((batch, M, K), n, 41, dtype), series((batch, K, N), n, 42, dtype)
+    m = torch.arange(M).view(M, 1)
+    k = torch.arange(K).view(1, K)
+    keep = (k >= m + offset) if band == 1 else (k <= m + offset)
+    A = [a * keep.to(a.dtype) for a in A]
+    tol = {torch.bfloat16: 1e-2, torch.float32: 1e-4, torch.float64: 1e-10}[dtype]
+    got = _kernels.poly_matmul(cuda(A), cuda(B), band=band, band_offset=offset)
+    check(A, B, tol, got=got)
+    C0 = series((batch, M, N), n, 43, dtype)
+    out = cuda(C0)
+    _kernels.poly_matmul(cuda(A), cuda(B), out=out, accumulate=True, band=band, band_offset=offset)
+    want = [w + c.double() for w, c in zip(ref.poly_matmul([a.double() for a in A], [b.double() for b in B]), C0)]
+    assert max(ref.plane_errors(out, want)) <= tol
+
+
 def test_empty_reduction_and_empty_output():
     from polytensors_b200 import _kernels
 
