@@ -754,6 +754,286 @@ static int launch_tc(TcParams& p, const TcOperand& a, const TcOperand& b, cudaSt
 }
 
 // =====================================================================================
+// All-planes tcgen05 product (bf16 / f16 planes, degree <= 3)
+//
+// For output tile (b, tm, tn) the accumulators of EVERY output plane live in tensor memory
+// (plane k at column k * AP_BN).  Per 64-wide k block the TMA warp loads each plane's A and B
+// k-block once (n+1 ring stages) and the MMA warp issues all (n+1)(n+2)/2 products A_i B_j from
+// them; the per-plane kernel above instead loads the operands of each product separately
+// (sum_k (k+1) operand pairs per k block against n+1 here: 10 against 4 at degree 3), which makes
+// narrow products (N = 128, e.g. attention head dimensions) L2-bandwidth bound.  The accumulator
+// set (NP x 128 <= 512 columns) is single-buffered: the epilogue drains it and releases it before
+// the next tile's products start, a small share of a tile when the reduction is long.
+
+constexpr int AP_BN = 128;
+constexpr int AP_A_BYTES = TC_BM * TC_BK * 2;
+constexpr int AP_STAGE_BYTES = AP_A_BYTES + AP_BN * TC_BK * 2;  // one plane's A and B k-block
+constexpr int AP_STAGES = 6;
+constexpr int AP_SMEM_BYTES = AP_STAGES * AP_STAGE_BYTES + 1024 + 256;
+
+__device__ __forceinline__ TileCoord ap_decode(const TcParams& p, int t) {
+    // batch entry, then groups of group_m row tiles (CTAs running together share B tiles in L2)
+    TileCoord c;
+    const int per_b = p.tiles_m * p.tiles_n;
+    c.plane = 0;
+    c.b = t / per_b;
+    const int r = t % per_b;
+    const int span = p.group_m * p.tiles_n;
+    const int first_m = (r / span) * p.group_m;
+    const int gsize = min(p.tiles_m - first_m, p.group_m);
+    c.tm = first_m + (r % span) % gsize;
+    c.tn = (r % span) / gsize;
+    return c;
+}
+
+template <int NP>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_allplanes_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
+    constexpr int TMEM_COLS = NP * AP_BN <= 128 ? 128 : (NP * AP_BN <= 256 ? 256 : 512);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + AP_STAGES * AP_STAGE_BYTES);
+    uint64_t* empty_bar = full_bar + AP_STAGES;
+    uint64_t* acc_full = empty_bar + AP_STAGES;
+    uint64_t* acc_empty = acc_full + 1;
+    uint64_t* drain_bar = acc_empty + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < AP_STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 32 * TC_EPI_WARPS);
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        for (int i = 0; i < NP; ++i) {
+            tma_prefetch_desc(&maps.a[i]);
+            tma_prefetch_desc(&maps.b[i]);
+        }
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer: plane i's A and B k-block into one ring stage ----------------
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0;
+            int issued_parity[AP_STAGES];
+#pragma unroll
+            for (int s = 0; s < AP_STAGES; ++s) issued_parity[s] = -1;
+            bool ok = true;
+            for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+                const TileCoord tc = ap_decode(p, t);
+                int kb0, kb1;
+                tile_kblocks(p, tc.tm, kb0, kb1);
+                for (int kb = kb0; kb < kb1 && ok; ++kb) {
+                    for (int i = 0; i < NP; ++i) {
+                        if (!mbar_wait_or_abort(&empty_bar[stage], phase ^ 1, abort_flag, p.status, 111)) {
+                            ok = false;
+                            break;
+                        }
+                        uint8_t* st = smem + stage * AP_STAGE_BYTES;
+                        mbar_arrive_expect_tx(&full_bar[stage], AP_STAGE_BYTES);
+                        if (p.a_mn) {
+#pragma unroll
+                            for (int h = 0; h < TC_BM / 64; ++h)
+                                tma_load_3d(st + h * 8192, &maps.a[i], &full_bar[stage], tc.tm * TC_BM + h * 64,
+                                            kb * TC_BK, tc.b);
+                        } else {
+                            tma_load_3d(st, &maps.a[i], &full_bar[stage], kb * TC_BK, tc.tm * TC_BM, tc.b);
+                        }
+                        uint8_t* sb = st + AP_A_BYTES;
+                        if (p.b_mn) {
+#pragma unroll
+                            for (int h = 0; h < AP_BN / 64; ++h)
+                                tma_load_3d(sb + h * 8192, &maps.b[i], &full_bar[stage], tc.tn * AP_BN + h * 64,
+                                            kb * TC_BK, tc.b);
+                        } else {
+                            tma_load_3d(sb, &maps.b[i], &full_bar[stage], kb * TC_BK, tc.tn * AP_BN, tc.b);
+                        }
+                        issued_parity[stage] = static_cast<int>(phase);
+                        if (++stage == AP_STAGES) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                }
+            }
+            if (!ok) {
+                for (int s = 0; s < AP_STAGES; ++s) {
+                    if (issued_parity[s] < 0) continue;
+                    const uint64_t t0 = pk_globaltimer();
+                    while (!mbar_try_wait(&full_bar[s], static_cast<uint32_t>(issued_parity[s])) &&
+                           pk_globaltimer() - t0 < 1000000000ull) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer: all products of a k block from its NP resident stages ----------------
+        if (lane == 0) {
+            const uint32_t idesc = f16_idesc(static_cast<uint32_t>(p.in_fmt), TC_BM, AP_BN) |
+                                   (static_cast<uint32_t>(p.a_mn) << 15) | (static_cast<uint32_t>(p.b_mn) << 16);
+            const uint64_t a_step = p.a_mn ? (2048 >> 4) : (32 >> 4);
+            const uint64_t b_step = p.b_mn ? (2048 >> 4) : (32 >> 4);
+            uint32_t stage = 0, phase = 0, aphase = 0;
+            bool ok = true, issued = false;
+            for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+                const TileCoord tc = ap_decode(p, t);
+                int kb0, kb1;
+                tile_kblocks(p, tc.tm, kb0, kb1);
+                if (kb1 <= kb0) continue;  // empty band: the epilogue writes the zeros
+                if (!mbar_wait_or_abort(acc_empty, aphase ^ 1, abort_flag, p.status, 112)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int kb = kb0; kb < kb1 && ok; ++kb) {
+                    uint32_t st[NP];
+#pragma unroll
+                    for (int i = 0; i < NP; ++i) {
+                        if (!mbar_wait_or_abort(&full_bar[stage], phase, abort_flag, p.status, 113)) {
+                            ok = false;
+                            break;
+                        }
+                        st[i] = stage;
+                        if (++stage == AP_STAGES) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                    if (!ok) break;
+                    tc_fence_after();
+                    uint64_t ad[NP], bd[NP];
+#pragma unroll
+                    for (int i = 0; i < NP; ++i) {
+                        const uint32_t a_s = smem_u32(smem + st[i] * AP_STAGE_BYTES);
+                        const uint32_t b_s = a_s + AP_A_BYTES;
+                        ad[i] = p.a_mn ? sw128_mnmajor_desc_lbo(a_s, 8192) : sw128_kmajor_desc(a_s);
+                        bd[i] = p.b_mn ? sw128_mnmajor_desc_lbo(b_s, 8192) : sw128_kmajor_desc(b_s);
+                    }
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) {
+#pragma unroll
+                        for (int i = 0; i <= k; ++i) {
+#pragma unroll
+                            for (int kk = 0; kk < TC_BK / 16; ++kk)
+                                tc_mma_f16(tmem_base + k * AP_BN, ad[i] + kk * a_step, bd[k - i] + kk * b_step, idesc,
+                                           (kb > kb0 || i > 0 || kk > 0) ? 1u : 0u);
+                        }
+                    }
+                    issued = true;
+#pragma unroll
+                    for (int i = 0; i < NP; ++i) tc_commit(&empty_bar[st[i]]);
+                }
+                if (!ok) break;
+                tc_commit(acc_full);
+                aphase ^= 1;
+            }
+            if (!ok && issued) {
+                tc_commit(drain_bar);
+                const uint64_t t0 = pk_globaltimer();
+                while (!mbar_try_wait(drain_bar, 0) && pk_globaltimer() - t0 < 1000000000ull) {
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue: every plane of the tile, TMEM -> registers -> global ----------------
+        // warp w drains lanes 32*(w%4).. (its TMEM lane quadrant) and column half (w-2)/4 of each plane
+        const uint32_t lane_base = 32u * (warp & 3);
+        const int half = (warp - 2) >> 2;
+        uint32_t aphase = 0;
+        for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+            const TileCoord tc = ap_decode(p, t);
+            const int row = tc.tm * TC_BM + lane_base + lane;
+            int kb0, kb1;
+            tile_kblocks(p, tc.tm, kb0, kb1);
+            if (kb1 <= kb0) {
+                if (!p.accumulate) {
+                    uint32_t z[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) z[j] = 0u;
+                    for (int k = 0; k < NP; ++k)
+                        for (int c = half * (AP_BN / 64); c < (half + 1) * (AP_BN / 64); ++c)
+                            store_row_chunk(p, k, tc.b, row, tc.tn * AP_BN + c * 32, z);
+                }
+                continue;
+            }
+            if (!mbar_wait_or_abort(acc_full, aphase, abort_flag, p.status, 114)) break;
+            tc_fence_after();
+#pragma unroll 1
+            for (int k = 0; k < NP; ++k) {
+#pragma unroll 1
+                for (int c = half * (AP_BN / 64); c < (half + 1) * (AP_BN / 64); ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(tmem_base + (lane_base << 16) + k * AP_BN + c * 32, r);
+                    tmem_ld_wait();
+                    store_row_chunk(p, k, tc.b, row, tc.tn * AP_BN + c * 32, r);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(acc_empty);
+            aphase ^= 1;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+template <int NP>
+static int launch_allplanes(TcParams& p, const TcOperand& a, const TcOperand& b, cudaStream_t stream) {
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(tc_allplanes_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             AP_SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_fail(e, "pk_poly_gemm: cudaFuncSetAttribute");
+        attr_set[dev] = true;
+    }
+    TcMaps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    int rc = encode_operand(maps.a, a, p.planes, false, TC_BM);
+    if (rc) return rc;
+    rc = encode_operand(maps.b, b, p.planes, false, AP_BN);
+    if (rc) return rc;
+    p.a_mn = a.mode == OPM_MNMAJOR ? 1 : 0;
+    p.b_mn = b.mode == OPM_MNMAJOR ? 1 : 0;
+    p.tiles_m = static_cast<int>(ceil_div(p.M, TC_BM));
+    p.tiles_n = static_cast<int>(ceil_div(p.N, AP_BN));
+    p.group_m = 8;
+    const int64_t total = static_cast<int64_t>(p.tiles_m) * p.tiles_n * p.batch;
+    if (total > 0x7fffffff) return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: too many tiles");
+    p.total_tiles = static_cast<int>(total);
+    const int grid = static_cast<int>(std::min<int64_t>(total, num_sms()));
+    void* tok;
+    prof_begin("poly_gemm", stream, &tok);
+    tc_allplanes_kernel<NP><<<grid, TC_THREADS, AP_SMEM_BYTES, stream>>>(maps, p);
+    prof_end("poly_gemm", stream, tok);
+    PK_CHECK_LAUNCH("pk_poly_gemm: tcgen05 all-planes kernel launch");
+    return PK_OK;
+}
+
+// =====================================================================================
 // DMMA path (float64, complex128)
 
 constexpr int DM_BM = 128, DM_BN = 128, DM_BK = 16, DM_LD = 20, DM_STAGES = 3;
@@ -1118,6 +1398,16 @@ static int poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N,
         tp.in_fmt = f16 ? 0 : 1;
         if (dtype == PK_F32) {
             return wide ? launch_tc<256, true>(tp, oa, ob, stream) : launch_tc<128, true>(tp, oa, ob, stream);
+        }
+        // degree <= 3 with enough output tiles: every plane of a tile at once (operands loaded once
+        // per k block for all products)
+        const int64_t ap_tiles = ceil_div(M, TC_BM) * ceil_div(N, AP_BN) * batch;
+        if (P >= 2 && P <= 4 && ap_tiles >= num_sms()) {
+            switch (P) {
+                case 2: return launch_allplanes<2>(tp, oa, ob, stream);
+                case 3: return launch_allplanes<3>(tp, oa, ob, stream);
+                default: return launch_allplanes<4>(tp, oa, ob, stream);
+            }
         }
         return wide ? launch_tc<256, false>(tp, oa, ob, stream) : launch_tc<128, false>(tp, oa, ob, stream);
     }

@@ -181,6 +181,33 @@ def test_banded_product(dtype, band, offset):
     assert max(ref.plane_errors(out, want)) <= tol
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n", [1, 2, 3])
+@pytest.mark.parametrize("layout", ["k", "rows"])
+def test_all_planes_product(dtype, n, layout):
+    """Degree <= 3 bf16 / f16 products with at least one 128 x 128 output tile per SM run the
+    all-planes kernel (every output plane of a tile in tensor memory): plain, banded and
+    accumulating, ragged M / N / K, K-major or MN-major operands."""
+    from polytensors_b200 import _kernels
+
+    batch, M, N, K = 10, 2000, 200, 200
+    A = series((batch, M, K), n, 51, dtype)
+    B = series((batch, K, N), n, 52, dtype)
+    a = cuda(A) if layout == "k" else [x.transpose(1, 2).contiguous().cuda().transpose(1, 2) for x in A]
+    b = cuda(B) if layout == "rows" else [x.transpose(1, 2).contiguous().cuda().transpose(1, 2) for x in B]
+    check(A, B, 1e-2, got=_kernels.poly_matmul(a, b))
+    # banded (k >= m - 1500: the first row tiles keep every k, later ones skip k blocks)
+    keep = (torch.arange(K).view(1, K) >= torch.arange(M).view(M, 1) - 1500)
+    Ab = [x * keep.to(x.dtype) for x in A]
+    ab = cuda(Ab) if layout == "k" else [x.transpose(1, 2).contiguous().cuda().transpose(1, 2) for x in Ab]
+    check(Ab, B, 1e-2, got=_kernels.poly_matmul(ab, b, band=1, band_offset=-1500))
+    C0 = series((batch, M, N), n, 53, dtype)
+    out = cuda(C0)
+    _kernels.poly_matmul(a, b, out=out, accumulate=True)
+    want = [w + c.double() for w, c in zip(ref.poly_matmul([x.double() for x in A], [y.double() for y in B]), C0)]
+    assert max(ref.plane_errors(out, want)) <= 1e-2
+
+
 def test_empty_reduction_and_empty_output():
     from polytensors_b200 import _kernels
 
