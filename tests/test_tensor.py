@@ -147,3 +147,36 @@ def test_coefficient_autograd_mode_raises_explicitly():
     with PolyTensor.coefficient_autograd():
         with pytest.raises(NotImplementedError, match="coefficient_autograd"):
             x.t()
+
+
+def test_checkpoint_round_trip_stacked_planes(tmp_path):
+    """polytensors_b200.checkpoint: PolyTensors (one dtype, and a real base with complex directions),
+    parameters, plain tensors and nested containers survive save/load bit for bit; the stored form
+    of a PolyTensor is one (n+1, *shape) plane stack."""
+    from polytensors_b200 import PolyTensor, checkpoint
+
+    g = torch.Generator().manual_seed(5)
+    a = PolyTensor(tuple(torch.randn(3, 4, generator=g) for _ in range(4)), requires_grad=True)
+    base = torch.randn(2, 3, generator=g, dtype=torch.float64)
+    dirs = tuple(torch.complex(torch.randn(2, 3, generator=g, dtype=torch.float64),
+                               torch.randn(2, 3, generator=g, dtype=torch.float64)) for _ in range(2))
+    b = PolyTensor((base,) + dirs)
+    w = torch.nn.Parameter(PolyTensor((torch.ones(5), torch.zeros(5)), degree=3))
+    state = {"a": a, "nested": [b, (torch.arange(3), "tag", 7)], "w": w}
+    path = tmp_path / "ckpt.pt"
+    checkpoint.save(state, path)
+    raw = checkpoint.load(path, stacked=True)
+    assert raw["a"]["planes"].shape == (4, 3, 4) and raw["a"]["degree"] == 3
+    assert raw["nested"][0]["directions"].shape == (2, 2, 3) and raw["nested"][0]["base"].dtype == torch.float64
+    got = checkpoint.load(path)
+    assert isinstance(got["a"], PolyTensor) and got["a"].requires_grad
+    for x, y in zip(got["a"].coeffs, a.coeffs):
+        assert torch.equal(x, y.detach())
+    for x, y in zip(got["nested"][0].coeffs, b.coeffs):
+        assert x.dtype == y.dtype and torch.equal(x, y)
+    assert got["nested"][1][1] == "tag" and got["nested"][1][2] == 7 and torch.equal(got["nested"][1][0], torch.arange(3))
+    assert got["w"].degree == 3 and torch.equal(got["w"].coeffs[0], torch.ones(5))
+    bad = tmp_path / "other.pt"
+    torch.save({"x": 1}, bad)
+    with pytest.raises(ValueError):
+        checkpoint.load(bad)
