@@ -33,7 +33,7 @@ import torch  # noqa: E402
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 # Measured DRAM traffic per product launch (ncu, B200) for the configurations it was captured on.
-_GEMM_TRAFFIC = {(8192, 4, "float32"): 68569692160 + 1340765696}
+_GEMM_TRAFFIC = {(8192, 4, "float32"): 56470521088 + 1338964736}
 
 WORKLOADS = {
     "poly_matmul": dict(M=8192, N=8192, K=8192, degree=4, dtype="float32"),
