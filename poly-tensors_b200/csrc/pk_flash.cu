@@ -85,7 +85,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     uint64_t* p_ready = s_full + 1;
     uint64_t* pv_done = p_ready + 1;
     uint64_t* drain = pv_done + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* s0_full = drain + 1;   // score plane 0 final (its only product Q_0 K_0 is done)
+    uint64_t* p0_ready = s0_full + 1;  // probability plane 0 written (and O rescaled)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p0_ready + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     float* red = reinterpret_cast<float*>(tmem_slot + 4);  // [4 key groups][128 rows][NP + 1]
 
@@ -107,6 +109,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         mbar_init(p_ready, 32 * FA_SOFTMAX_WARPS);
         mbar_init(pv_done, 1);
         mbar_init(drain, 1);
+        mbar_init(s0_full, 1);
+        mbar_init(p0_ready, 32 * FA_SOFTMAX_WARPS);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -214,38 +218,57 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                             phase ^= 1;
                         }
                     }
+                    // S_0 = Q_0 K_0^T is complete once the K_0 chunks are multiplied: the softmax
+                    // warps start on plane 0 while the remaining products run
+                    if (b == 0 && ok) tc_commit(s0_full);
                 }
                 if (!ok) break;
                 tc_commit(s_full);
-                if (!mbar_wait_or_abort(p_ready, j & 1, abort_flag, p.status, 405)) {
+                // O~_k += sum_{a+b=k} E_a V_b, E_a in TMEM: the bf16 pairs of keys 16kk..16kk+15 sit in
+                // columns 16kk..16kk+7 of S_a (written by the warp that owned those scores).  The E_0
+                // products run first (as soon as plane 0 is written), the V_b stages are kept until
+                // the higher planes' products have been issued too.
+                if (!mbar_wait_or_abort(p0_ready, j & 1, abort_flag, p.status, 409)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                // O~_k += sum_{a+b=k} E_a V_b, E_a in TMEM: the bf16 pairs of keys 16kk..16kk+15 sit in
-                // columns 16kk..16kk+7 of S_a (written by the warp that owned those scores)
+                uint32_t vstage[NP];
                 for (int b = 0; b < NP && ok; ++b) {
                     if (!mbar_wait_or_abort(&full[stage], phase, abort_flag, p.status, 406)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
+                    vstage[b] = stage;
                     const uint64_t vd = ring_vdesc + (stage * FA_TILE >> 4);
 #pragma unroll
-                    for (int a = 0; a < NP; ++a) {
-                        if (a + b >= NP) break;
-#pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            tc_mma_f16_ts(tmem + Cfg::O_BASE + (a + b) * FA_DS, tmem + a * FA_BN + kk * 16,
-                                          vd + kk * (2048 >> 4), idesc_pv, (j == 0 && b == 0 && kk == 0) ? 0u : 1u);
-                    }
-                    tc_commit(&empty[stage]);
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc_mma_f16_ts(tmem + Cfg::O_BASE + b * FA_DS, tmem + kk * 16, vd + kk * (2048 >> 4), idesc_pv,
+                                      (j == 0 && kk == 0) ? 0u : 1u);
                     if (++stage == FA_STAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
                 if (!ok) break;
+                if (!mbar_wait_or_abort(p_ready, j & 1, abort_flag, p.status, 405)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int b = 0; b < NP; ++b) {
+                    const uint64_t vd = ring_vdesc + (vstage[b] * FA_TILE >> 4);
+#pragma unroll
+                    for (int a = 1; a < NP; ++a) {
+                        if (a + b >= NP) break;
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            tc_mma_f16_ts(tmem + Cfg::O_BASE + (a + b) * FA_DS, tmem + a * FA_BN + kk * 16,
+                                          vd + kk * (2048 >> 4), idesc_pv, 1u);
+                    }
+                    tc_commit(&empty[vstage[b]]);
+                }
                 tc_commit(pv_done);
             }
             if (!ok && issued) {
@@ -273,21 +296,22 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         auto quad_sync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(1 + quad), "r"(128) : "memory"); };
         bool ok = true;
         for (int j = 0; j < nblocks; ++j) {
-            if (!mbar_wait_or_abort(s_full, j & 1, abort_flag, p.status, 407)) {
+            // ---- phase 1: plane 0 (final once Q_0 K_0 is multiplied): row maxima, the rescale of
+            // O~ when the maximum moved, E_0 = exp(scale * S_0 - m) and its bf16 pairs over S_0
+            if (!mbar_wait_or_abort(s0_full, j & 1, abort_flag, p.status, 407)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             const int key0 = j * FA_BN + g * 16;
             const int last_key = p.causal ? min(q, p.S - 1) : p.S - 1;
-            uint32_t r[NP][16];
-#pragma unroll
-            for (int k = 0; k < NP; ++k) tmem_ld_32x32b_x16(trow + k * FA_BN + g * 16, r[k]);
+            uint32_t r0[16];
+            tmem_ld_32x32b_x16(trow + g * 16, r0);
             tmem_ld_wait();
             float pmax = -INFINITY;
 #pragma unroll
             for (int t = 0; t < 16; ++t)
-                if (key0 + t <= last_key) pmax = fmaxf(pmax, sc * __uint_as_float(r[0][t]));
+                if (key0 + t <= last_key) pmax = fmaxf(pmax, sc * __uint_as_float(r0[t]));
             red[(g * 128 + row) * (NP + 1)] = pmax;
             quad_sync();
             float bmax = -INFINITY;
@@ -305,37 +329,19 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                 }
                 m_used = bmax;
             }
-            // E = exp(scale * S - m) as a series for this warp's 16 keys; bf16 pairs written over
-            // the first 8 of its own 16 score columns in every plane
-            uint32_t packed[NP][8];
+            float w[16];  // E_0 of this warp's 16 keys
+            {
+                uint32_t packed0[8];
 #pragma unroll
-            for (int t = 0; t < 16; t += 2) {
-                float e2[2][NP];
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    float x[NP], e[NP];
-#pragma unroll
-                    for (int k = 0; k < NP; ++k) x[k] = sc * __uint_as_float(r[k][t + u]);
-                    if (key0 + t + u <= last_key && m_used > -INFINITY) {
-                        s_exp_dir<NP, float>(x, e);
-                        const float w = __expf(x[0] - m_used);
-#pragma unroll
-                        for (int k = 0; k < NP; ++k) e[k] *= w;
-                    } else {
-#pragma unroll
-                        for (int k = 0; k < NP; ++k) e[k] = 0.f;
-                    }
-#pragma unroll
-                    for (int k = 0; k < NP; ++k) {
-                        l[k] += e[k];
-                        e2[u][k] = e[k];
-                    }
+                for (int t = 0; t < 16; ++t) {
+                    const bool live = key0 + t <= last_key && m_used > -INFINITY;
+                    w[t] = live ? __expf(sc * __uint_as_float(r0[t]) - m_used) : 0.f;
+                    l[0] += w[t];
                 }
 #pragma unroll
-                for (int k = 0; k < NP; ++k) packed[k][t / 2] = pack_bf16x2(e2[0][k], e2[1][k]);
+                for (int t = 0; t < 8; ++t) packed0[t] = pack_bf16x2(w[2 * t], w[2 * t + 1]);
+                tmem_st_32x32b_x8(trow + g * 16, packed0);
             }
-#pragma unroll
-            for (int k = 0; k < NP; ++k) tmem_st_32x32b_x8(trow + k * FA_BN + g * 16, packed[k]);
             // rescale this warp's 16 columns of every O~ plane where the row maximum moved
             if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
@@ -351,6 +357,44 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             }
             tmem_st_wait();
             tc_fence_before();
+            mbar_arrive(p0_ready);
+            // ---- phase 2: planes 1..n once all products are in: E_k = E_0 e_k with e the
+            // exponential series of the directions (k e_k = sum_i i x_i e_{k-i}), bf16 over S_k
+            if constexpr (NP > 1) {
+                if (!mbar_wait_or_abort(s_full, j & 1, abort_flag, p.status, 410)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                uint32_t r[NP][16];
+#pragma unroll
+                for (int k = 1; k < NP; ++k) tmem_ld_32x32b_x16(trow + k * FA_BN + g * 16, r[k]);
+                tmem_ld_wait();
+                uint32_t packed[NP][8];
+#pragma unroll
+                for (int t = 0; t < 16; t += 2) {
+                    float e2[2][NP];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        float x[NP], e[NP];
+                        x[0] = 0.f;
+#pragma unroll
+                        for (int k = 1; k < NP; ++k) x[k] = sc * __uint_as_float(r[k][t + u]);
+                        s_exp_dir<NP, float>(x, e);
+#pragma unroll
+                        for (int k = 1; k < NP; ++k) {
+                            e2[u][k] = w[t + u] * e[k];
+                            l[k] += e2[u][k];
+                        }
+                    }
+#pragma unroll
+                    for (int k = 1; k < NP; ++k) packed[k][t / 2] = pack_bf16x2(e2[0][k], e2[1][k]);
+                }
+#pragma unroll
+                for (int k = 1; k < NP; ++k) tmem_st_32x32b_x8(trow + k * FA_BN + g * 16, packed[k]);
+                tmem_st_wait();
+                tc_fence_before();
+            }
             mbar_arrive(p_ready);
         }
         // epilogue: combine the four normaliser partials of each row, O = O~ (/) l for this
