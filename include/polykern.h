@@ -122,9 +122,11 @@ PK_API int pk_poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t
  * whose A planes are zero outside a band, as the causal attention products are:
  *   band 1: A[b][m][k] may be nonzero only for k >= m + band_offset,
  *   band 2: A[b][m][k] may be nonzero only for k <= m + band_offset,
+ *   band 3: only the outputs C[b][m][n] with n <= m + band_offset are wanted (causal scores);
+ *           the others are unspecified (zero where a whole output tile lies beyond the band),
  *   band 0: no band (plain product).
- * k blocks outside the band of a whole row tile are skipped (the caller guarantees the skipped
- * entries are zero; the product may still read some of them).  Replaces the same products as
+ * For bands 1 and 2, k blocks outside the band of a whole row tile are skipped (the caller
+ * guarantees the skipped entries are zero; the product may still read some of them).  Replaces the same products as
  * pk_poly_gemm; the reference evaluates them over the full (masked) score matrices
  * (src/polytensors/_decompositions.py:28-43). */
 PK_API int pk_poly_gemm_banded(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K,

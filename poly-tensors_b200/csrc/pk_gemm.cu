@@ -343,7 +343,8 @@ struct TcParams {
     int out_kind;  // 0 = f32, 1 = bf16, 2 = f16
     int vec_ok;    // output rows 16-byte aligned: vectorised stores allowed
     int accumulate;  // C += product (read-modify-write) instead of C = product
-    int band;        // 0: every k; 1: only k >= m + band_off contributes; 2: only k <= m + band_off
+    int band;        // 0: every k; 1: only k >= m + band_off contributes; 2: only k <= m + band_off;
+                     // 3: only outputs n <= m + band_off are needed (causal scores)
     int64_t band_off;
     int K;           // reduction length (banded k ranges)
     int64_t c_bs, c_rs;
@@ -374,15 +375,21 @@ __device__ __forceinline__ TileCoord decode_tile(const TcParams& p, int t) {
     return c;
 }
 
-// The k blocks a row tile needs.  A banded product (a causal attention product) only has
+// The k blocks an output tile needs.  A banded product (a causal attention product) only has
 // nonzeros for k >= m + off (band 1) or k <= m + off (band 2) in row m; k blocks entirely
-// outside the band of every row of the tile are neither loaded nor multiplied.
-__device__ __forceinline__ void tile_kblocks(const TcParams& p, int tm, int& kb0, int& kb1) {
+// outside the band of every row of the tile are neither loaded nor multiplied.  Band 3 asks only
+// for the outputs n <= m + off: tiles whose columns all lie beyond that get an empty range (their
+// outputs are written as zeros, or left as they are when accumulating).
+__device__ __forceinline__ void tile_kblocks(const TcParams& p, int tm, int tn, int bn, int& kb0, int& kb1) {
     kb0 = 0;
     kb1 = p.kblocks;
     if (p.band == 0) return;
     const int64_t m0 = static_cast<int64_t>(tm) * TC_BM;
     const int64_t m1 = (m0 + TC_BM - 1 < p.M - 1) ? m0 + TC_BM - 1 : static_cast<int64_t>(p.M) - 1;
+    if (p.band == 3) {
+        if (static_cast<int64_t>(tn) * bn > m1 + p.band_off) kb1 = 0;
+        return;
+    }
     if (p.band == 1) {
         const int64_t lo = m0 + p.band_off;
         const int64_t b = lo <= 0 ? 0 : lo / TC_BK;
@@ -539,7 +546,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
                 const TileCoord tc = decode_tile(p, t);
                 int kb0, kb1;
-                tile_kblocks(p, tc.tm, kb0, kb1);
+                tile_kblocks(p, tc.tm, tc.tn, BN, kb0, kb1);
                 for (int i = 0; i <= tc.plane && ok; ++i) {
                     const int j = tc.plane - i;
                     for (int kb = kb0; kb < kb1; ++kb) {
@@ -614,7 +621,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
                 const TileCoord tc = decode_tile(p, t);
                 int kb0, kb1;
-                tile_kblocks(p, tc.tm, kb0, kb1);
+                tile_kblocks(p, tc.tm, tc.tn, BN, kb0, kb1);
                 if (kb1 <= kb0) continue;  // no k block in the band: the epilogue writes the zeros
                 if (!mbar_wait_or_abort(&acc_empty[abuf], aphase ^ 1, abort_flag, p.status, 102)) {
                     ok = false;
@@ -679,7 +686,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const TileCoord tc = decode_tile(p, t);
             const int row = tc.tm * TC_BM + lane_base + lane;
             int kb0, kb1;
-            tile_kblocks(p, tc.tm, kb0, kb1);
+            tile_kblocks(p, tc.tm, tc.tn, BN, kb0, kb1);
             if (kb1 <= kb0) {
                 // empty band: the product is zero (nothing to add when accumulating)
                 if (!p.accumulate) {
@@ -840,7 +847,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
                 const TileCoord tc = ap_decode(p, t);
                 int kb0, kb1;
-                tile_kblocks(p, tc.tm, kb0, kb1);
+                tile_kblocks(p, tc.tm, tc.tn, AP_BN, kb0, kb1);
                 for (int kb = kb0; kb < kb1 && ok; ++kb) {
                     for (int i = 0; i < NP; ++i) {
                         if (!mbar_wait_or_abort(&empty_bar[stage], phase ^ 1, abort_flag, p.status, 111)) {
@@ -896,7 +903,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
                 const TileCoord tc = ap_decode(p, t);
                 int kb0, kb1;
-                tile_kblocks(p, tc.tm, kb0, kb1);
+                tile_kblocks(p, tc.tm, tc.tn, AP_BN, kb0, kb1);
                 if (kb1 <= kb0) continue;  // empty band: the epilogue writes the zeros
                 if (!mbar_wait_or_abort(acc_empty, aphase ^ 1, abort_flag, p.status, 112)) {
                     ok = false;
@@ -962,7 +969,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const TileCoord tc = ap_decode(p, t);
             const int row = tc.tm * TC_BM + lane_base + lane;
             int kb0, kb1;
-            tile_kblocks(p, tc.tm, kb0, kb1);
+            tile_kblocks(p, tc.tm, tc.tn, AP_BN, kb0, kb1);
             if (kb1 <= kb0) {
                 if (!p.accumulate) {
                     uint32_t z[32];
@@ -1506,7 +1513,7 @@ int pk_poly_gemm_banded(int dtype, int degree, int64_t batch, int64_t M, int64_t
                         void* const* c_planes, int64_t c_bs, int64_t c_rs, int a_complex_from, int b_complex_from,
                         int accumulate, int band, int64_t band_offset, void* workspace, size_t workspace_bytes,
                         void* stream) {
-    if (band < 0 || band > 2) return fail(PK_ERR_ARG, "pk_poly_gemm_banded: band must be 0, 1 or 2");
+    if (band < 0 || band > 3) return fail(PK_ERR_ARG, "pk_poly_gemm_banded: band must be 0, 1, 2 or 3");
     return poly_gemm(dtype, degree, batch, M, N, K, a_planes, a_bs, a_rs, a_cs, b_planes, b_bs, b_rs, b_cs, c_planes,
                      c_bs, c_rs, a_complex_from, b_complex_from, workspace, workspace_bytes, stream, accumulate ? 1 : 0,
                      band, band_offset);

@@ -14,7 +14,11 @@ and the backward (the series form of the reference's bmm / softmax backward rule
     dQ = dS K,    dK = dS^T Q.
 
 P is recomputed in backward from the saved inputs; only the per-row normaliser series
-(n+1 values per query row) is kept from the forward.
+(n+1 values per query row) is kept from the forward.  bfloat16 planes (degree <= 3) use the
+single-kernel forward (pk_flash_attn_fwd) and a backward over all queries of a block of heads
+with the softmax in the score products' epilogue (pk_attn_probs_gemm / pk_attn_dscores_gemm)
+and banded gradient products (pk_poly_gemm_banded).  Other dtypes tile the queries under a causal
+mask, so that their row-wise softmax passes and operand staging skip the masked half.
 """
 
 import math

@@ -69,7 +69,8 @@ def poly_matmul(a_planes, b_planes, out=None, accumulate=False, band=0, band_off
     ``out``: optional output planes (views with unit column stride) written in place;
     ``accumulate``: add the product to ``out`` (C_k += ...) as addmm with beta = 1 does.
     ``band``/``band_offset``: A is zero outside a band (1: k >= m + offset, 2: k <= m + offset), as
-    in causal attention; k blocks outside it are skipped (pk_poly_gemm_banded).
+    in causal attention, and k blocks outside it are skipped; or (3) only the outputs with
+    n <= m + offset are wanted, the rest being unspecified (pk_poly_gemm_banded).
     """
     P = len(a_planes)
     if P != len(b_planes) or P == 0:

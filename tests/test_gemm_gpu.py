@@ -208,6 +208,23 @@ def test_all_planes_product(dtype, n, layout):
     assert max(ref.plane_errors(out, want)) <= 1e-2
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("offset", [0, -200, 100])
+def test_causal_output_band(dtype, offset):
+    """Band 3: the outputs with n <= m + offset equal the plain product (others unspecified); the
+    all-planes kernel (bf16 / f16 with enough tiles) and the per-plane kernel (float32)."""
+    from polytensors_b200 import _kernels
+
+    batch, M, N, K, n = 10, 1100, 900, 72, 2
+    A, B = series((batch, M, K), n, 61, dtype), series((batch, K, N), n, 62, dtype)
+    got = _kernels.poly_matmul(cuda(A), cuda(B), band=3, band_offset=offset)
+    want = ref.poly_matmul([a.double() for a in A], [b.double() for b in B])
+    keep = (torch.arange(N).view(1, N) <= torch.arange(M).view(M, 1) + offset)
+    tol = {torch.bfloat16: 1e-2, torch.float16: 1e-2, torch.float32: 1e-4}[dtype]
+    errs = ref.plane_errors([g.cpu().double() * keep for g in got], [w * keep for w in want])
+    assert max(errs) <= tol, errs
+
+
 def test_empty_reduction_and_empty_output():
     from polytensors_b200 import _kernels
 
