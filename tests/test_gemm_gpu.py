@@ -225,6 +225,23 @@ def test_causal_output_band(dtype, offset):
     assert max(errs) <= tol, errs
 
 
+@pytest.mark.parametrize("a_how", ["k", "rows", "odd"])
+@pytest.mark.parametrize("b_how", ["k", "rows"])
+def test_f32_operand_layouts(a_how, b_how):
+    """float32 planes K-major, MN-major or at an odd offset are staged into bf16 hi/lo (direct or
+    transposing staging kernels, the generic one for odd strides).  Batched, ragged tails, K not a
+    multiple of 64, tolerance 1e-4."""
+    from polytensors_b200 import _kernels
+
+    batch, M, N, K, n = 3, 200, 296, 136, 3
+    A = series((batch, M, K), n, 71)
+    W = series((batch, N, K), n, 72)
+    a = _layout(A, a_how)
+    b = [w.transpose(-2, -1) for w in _layout(W, b_how)]
+    got = _kernels.poly_matmul(a, b)
+    check(A, [w.transpose(-2, -1) for w in W], TOL[torch.float32], got=got)
+
+
 def test_empty_reduction_and_empty_output():
     from polytensors_b200 import _kernels
 

@@ -9,6 +9,7 @@ holds the first call's contents.  Tolerance: per-plane max |diff| / max |ref| <=
 for float32 and 1e-10 for float64 (the kernels are the same, so the results agree far
 more closely)."""
 
+import ctypes
 import math
 
 import pytest
@@ -75,9 +76,16 @@ def test_noalloc_rejects_products_beyond_its_scratch():
     degree, M = 4, 8192
     need = lib.pk_poly_gemm_workspace_size(0, degree, 1, M, M, M, degree + 1, degree + 1)
     assert need > (64 << 20)
+    # A row stride of M + 1 floats (not a multiple of 4) makes both operands go through the
+    # workspace staging, so the call needs more scratch than the array holds and is rejected
+    # before anything is launched (the 1-element planes are never read).
     dummy = [torch.empty(1, device="cuda") for _ in range(degree + 1)]
     pa, ka = _lib.pointer_array(dummy)
-    status = lib.pk_poly_gemm_noalloc(0, degree, 1, M, M, M, pa, 0, M, 1, pa, 0, M, 1, pa, 0, M,
+    size = ctypes.c_size_t(0)
+    assert lib.pk_poly_gemm_workspace_query(0, degree, 1, M, M, M, pa, 0, M + 1, 1, pa, 0, M + 1, 1,
+                                            degree + 1, degree + 1, ctypes.byref(size)) == 0
+    assert size.value > (64 << 20)
+    status = lib.pk_poly_gemm_noalloc(0, degree, 1, M, M, M, pa, 0, M + 1, 1, pa, 0, M + 1, 1, pa, 0, M,
                                       degree + 1, degree + 1, torch.cuda.current_stream().cuda_stream)
     assert status == -2
     assert "scratch" in _lib.last_error()
