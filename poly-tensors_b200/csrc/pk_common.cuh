@@ -162,6 +162,44 @@ __device__ __forceinline__ void bulk_wait_group_read() {
 }
 // Wait until every committed bulk group of this thread has completed.
 __device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Per-thread asynchronous global -> shared copies (cp.async), completion tracked per thread by
+// commit groups: after cp_async_wait<N>() at most N of this thread's latest groups are pending.
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Shared-memory address (shared::cluster window) of the variable at `p` in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t cluster_map_u32(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+// Store one float into another CTA's shared memory; the store completes 4 transaction bytes on
+// that CTA's mbarrier (both addresses from cluster_map_u32), which orders it for the CTA's waiters.
+__device__ __forceinline__ void st_async_f32(uint32_t remote, float v, uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(remote), "f"(v),
+                 "r"(remote_bar)
+                 : "memory");
+}
+// Bulk prefetch of [gmem, gmem + bytes) from global memory into L2; nothing tracks its completion.
+// The range is widened to 16-byte boundaries, which stay inside the 16-byte blocks holding its
+// first and last bytes (so inside the same mapped allocation).
+__device__ __forceinline__ void prefetch_l2(const void* gmem, size_t bytes) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(gmem) & ~uintptr_t(15);
+    const uintptr_t e = (reinterpret_cast<uintptr_t>(gmem) + bytes + 15) & ~uintptr_t(15);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(static_cast<uint32_t>(e - a)) : "memory");
+}
+// One aligned 8- or 16-byte vector (the 16-byte form bypasses L1).
+template <int BYTES>
+__device__ __forceinline__ void cp_async_vec(void* smem, const void* gmem) {
+    static_assert(BYTES == 8 || BYTES == 16, "cp_async_vec: 8 or 16 bytes");
+    if constexpr (BYTES == 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }

@@ -20,6 +20,11 @@
 //                                                  MN-major straight from the caller's planes
 //   O     = O~ (/) l                               series division in the epilogue
 //
+// Both contractions issue one MMA per left plane: Q_a (or E_a) meets K_0 .. K_{n-a} (V_0 ..
+// V_{n-a}), whose products land in the adjacent TMEM planes a .. n, and those right planes sit in
+// consecutive ring stages, so the n+1-a products are one MMA of N = 64 (n+1-a) columns (n+1 MMAs
+// per 16-wide k step instead of (n+1)(n+2)/2, each Q plane read from shared memory once).
+//
 // The running maximum m is only raised (and O~, l rescaled) when a block's maximum exceeds it
 // by more than FA_TAU, so most blocks skip the TMEM read-modify-write of O~; a stale m only
 // scales E by at most e^FA_TAU, which fp32 accumulation absorbs.
@@ -144,7 +149,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                     uint8_t* dst = ring + stage * FA_TILE;
                     mbar_arrive_expect_tx(&full[stage], FA_TILE);
                     if (t < NP * DCH) {
-                        const int b = t / DCH, c = t % DCH;
+                        // head-dimension chunk major, plane minor: a chunk's K planes fill
+                        // consecutive stages (one wide MMA reads them together)
+                        const int c = t / NP, b = t % NP;
                         tma_load_3d(dst, &maps.k[b], &full[stage], c * 64, j * FA_BN, bh);
                     } else {
                         const int b = t - NP * DCH;
@@ -176,8 +183,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc_qk = f16_idesc(1u, FA_BM, FA_BN);
-            constexpr uint32_t idesc_pv = f16_idesc(1u, FA_BM, FA_DS) | (1u << 16);  // B (V) MN-major
+            // instruction descriptors without the N field; N = 64 m sets (8 m) << 17
+            constexpr uint32_t idesc_qk0 = f16_idesc(1u, FA_BM, 0);
+            constexpr uint32_t idesc_pv0 = f16_idesc(1u, FA_BM, 0) | (1u << 16);  // B (V) MN-major
+            auto n_field = [](int m) { return static_cast<uint32_t>(FA_BN / 8 * m) << 17; };
             uint32_t stage = 0, phase = 0;
             bool ok = mbar_wait_or_abort(q_full, 0, abort_flag, p.status, 402);
             bool issued = false;
@@ -186,7 +195,16 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             // a couple of integer adds per MMA instead of rebuilding two descriptors.
             const uint64_t q_desc = sw128_kmajor_desc(smem_u32(sq));
             const uint64_t ring_kdesc = sw128_kmajor_desc(smem_u32(ring));
-            const uint64_t ring_vdesc = sw128_mnmajor_desc(smem_u32(ring));
+            const uint64_t ring_vdesc = sw128_mnmajor_desc_lbo(smem_u32(ring), FA_TILE);
+            // The products of one left plane with the right planes b0 .. b1-1 go to the adjacent
+            // accumulator planes a+b0 .. a+b1-1 and read consecutive ring stages, so they are ONE
+            // MMA of N = 64 (b1 - b0) columns (K-major: 8-row groups 1024 B apart run on into the
+            // next stage; MN-major V: 64-column atoms FA_TILE apart), split in two where the
+            // stages wrap around the ring's end (`wrap` = planes before it).
+            auto segments = [](int b0, int b1, int wrap, auto&& issue) {
+                if (b0 < wrap) issue(b0, min(b1, wrap));
+                if (b1 > wrap) issue(max(b0, wrap), b1);
+            };
             for (int j = 0; j < nblocks && ok; ++j) {
                 if (j > 0 && !mbar_wait_or_abort(pv_done, (j - 1) & 1, abort_flag, p.status, 403)) {
                     ok = false;
@@ -194,33 +212,46 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                 }
                 tc_fence_after();
                 // S_k = sum_{a+b=k} Q_a K_b^T over the head dimension (DCH chunks of 64)
-                for (int b = 0; b < NP && ok; ++b) {
-                    for (int c = 0; c < DCH; ++c) {
+                for (int c = 0; c < DCH && ok; ++c) {
+                    uint32_t kst[NP];
+                    for (int b = 0; b < NP; ++b) {
                         if (!mbar_wait_or_abort(&full[stage], phase, abort_flag, p.status, 404)) {
                             ok = false;
                             break;
                         }
-                        tc_fence_after();
-                        const uint64_t kd = ring_kdesc + (stage * FA_TILE >> 4);
-#pragma unroll
-                        for (int a = 0; a < NP; ++a) {
-                            if (a + b >= NP) break;
-                            const uint64_t qd = q_desc + ((a * DCH + c) * FA_QTILE >> 4);
-#pragma unroll
-                            for (int kk = 0; kk < 4; ++kk)
-                                tc_mma_f16(tmem + (a + b) * FA_BN, qd + kk * 2, kd + kk * 2, idesc_qk,
-                                           (b == 0 && c == 0 && kk == 0) ? 0u : 1u);
-                        }
-                        issued = true;
-                        tc_commit(&empty[stage]);
+                        kst[b] = stage;
                         if (++stage == FA_STAGES) {
                             stage = 0;
                             phase ^= 1;
                         }
                     }
-                    // S_0 = Q_0 K_0^T is complete once the K_0 chunks are multiplied: the softmax
-                    // warps start on plane 0 while the remaining products run
-                    if (b == 0 && ok) tc_commit(s0_full);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const int wrap = min(NP, FA_STAGES - static_cast<int>(kst[0]));
+                    auto qk = [&](int a, int b0, int b1) {
+                        const uint64_t qd = q_desc + ((a * DCH + c) * FA_QTILE >> 4);
+                        segments(b0, b1, wrap, [&](int s0, int s1) {
+                            const uint64_t kd = ring_kdesc + (kst[s0] * FA_TILE >> 4);
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk)
+                                tc_mma_f16(tmem + (a + s0) * FA_BN, qd + kk * 2, kd + kk * 2,
+                                           idesc_qk0 | n_field(s1 - s0), (c == 0 && a == 0 && kk == 0) ? 0u : 1u);
+                        });
+                    };
+                    if (c + 1 < DCH) {
+                        qk(0, 0, NP);
+                    } else {
+                        // S_0 = Q_0 K_0^T is complete once the last chunk's Q_0 K_0 product is
+                        // issued: the softmax warps start on plane 0 while the other products run
+                        qk(0, 0, 1);
+                        tc_commit(s0_full);
+                        qk(0, 1, NP);
+                    }
+#pragma unroll
+                    for (int a = 1; a < NP; ++a) qk(a, 0, NP - a);
+                    issued = true;
+#pragma unroll
+                    for (int b = 0; b < NP; ++b) tc_commit(&empty[kst[b]]);
                 }
                 if (!ok) break;
                 tc_commit(s_full);
@@ -232,43 +263,41 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                     ok = false;
                     break;
                 }
-                tc_fence_after();
-                uint32_t vstage[NP];
+                uint32_t vst[NP];
                 for (int b = 0; b < NP && ok; ++b) {
                     if (!mbar_wait_or_abort(&full[stage], phase, abort_flag, p.status, 406)) {
                         ok = false;
                         break;
                     }
-                    tc_fence_after();
-                    vstage[b] = stage;
-                    const uint64_t vd = ring_vdesc + (stage * FA_TILE >> 4);
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        tc_mma_f16_ts(tmem + Cfg::O_BASE + b * FA_DS, tmem + kk * 16, vd + kk * (2048 >> 4), idesc_pv,
-                                      (j == 0 && kk == 0) ? 0u : 1u);
+                    vst[b] = stage;
                     if (++stage == FA_STAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
                 if (!ok) break;
+                tc_fence_after();
+                const int vwrap = min(NP, FA_STAGES - static_cast<int>(vst[0]));
+                auto pv = [&](int a) {
+                    segments(0, NP - a, vwrap, [&](int s0, int s1) {
+                        const uint64_t vd = ring_vdesc + (vst[s0] * FA_TILE >> 4);
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            tc_mma_f16_ts(tmem + Cfg::O_BASE + (a + s0) * FA_DS, tmem + a * FA_BN + kk * 16,
+                                          vd + kk * (2048 >> 4), idesc_pv0 | n_field(s1 - s0),
+                                          (j == 0 && a == 0 && kk == 0) ? 0u : 1u);
+                    });
+                };
+                pv(0);
                 if (!mbar_wait_or_abort(p_ready, j & 1, abort_flag, p.status, 405)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                for (int b = 0; b < NP; ++b) {
-                    const uint64_t vd = ring_vdesc + (vstage[b] * FA_TILE >> 4);
 #pragma unroll
-                    for (int a = 1; a < NP; ++a) {
-                        if (a + b >= NP) break;
+                for (int a = 1; a < NP; ++a) pv(a);
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            tc_mma_f16_ts(tmem + Cfg::O_BASE + (a + b) * FA_DS, tmem + a * FA_BN + kk * 16,
-                                          vd + kk * (2048 >> 4), idesc_pv, 1u);
-                    }
-                    tc_commit(&empty[vstage[b]]);
-                }
+                for (int b = 0; b < NP; ++b) tc_commit(&empty[vst[b]]);
                 tc_commit(pv_done);
             }
             if (!ok && issued) {

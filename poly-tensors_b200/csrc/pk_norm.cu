@@ -30,6 +30,7 @@ struct NormParams {
     void* dw_part;            // backward: [gridDim.x][np][cols] partial weight gradients (compute type)
     void* rstd;               // [rows][np] rsqrt series per row (compute type)
     int vec;                  // planes and row strides allow ROW_VEC-element vector access
+    int* status;              // device status word for waits that time out
 };
 
 template <int NP, typename T, typename C>
@@ -165,6 +166,114 @@ __global__ void __launch_bounds__(512, 1) rmsnorm_fwd_reg_kernel(const NormParam
             store_planes4<NP, T, C>(p.y, p.np, yb + c0, valid, p.vec != 0, t);
         }
     }
+}
+
+// Rows beyond the next one that the streaming kernels prefetch into L2.
+constexpr int NORM_L2_AHEAD = 2;
+
+// The forward with the next row streaming in while this one is computed: thread t owns the column
+// quads q = s * blockDim + t (s < STEPS) and copies its quads of the NEXT row's x planes into the
+// second of two shared-memory stages with cp.async before it works on the current row, so HBM
+// reads continue through the row reduction and the stores.  A thread reads back only what it
+// copied, so the stages need no block barrier; the weight series of its columns stays in registers.
+template <typename T, int NP, int STEPS>
+__global__ void __launch_bounds__(512, 1) rmsnorm_fwd_stream_kernel(const NormParams p) {
+    using C = float;
+    __shared__ C scratch[16 * NP];
+    extern __shared__ __align__(16) unsigned char dyn[];
+    T* const stages = reinterpret_cast<T*>(dyn);  // [2][NP][cols]
+    constexpr int VB = ROW_VEC * static_cast<int>(sizeof(T));
+    const int64_t quads = p.cols / ROW_VEC, stage_elems = NP * p.cols;
+    const C inv_cols = C(1) / C(p.cols);
+    C w[STEPS][ROW_VEC][NP];
+#pragma unroll
+    for (int s = 0; s < STEPS; ++s) {
+        const int64_t q = static_cast<int64_t>(s) * blockDim.x + threadIdx.x;
+        load_weight4<NP, T, C>(p, q * ROW_VEC, q < quads ? ROW_VEC : 0, w[s]);
+    }
+    auto issue = [&](int64_t row, int stage) {
+        T* st = stages + stage * stage_elems;
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+            const int64_t q = static_cast<int64_t>(s) * blockDim.x + threadIdx.x;
+            if (q < quads) {
+#pragma unroll
+                for (int k = 0; k < NP; ++k)
+                    cp_async_vec<VB>(st + k * p.cols + q * ROW_VEC,
+                                     static_cast<const T*>(p.x[k]) + row * p.x_rs + q * ROW_VEC);
+            }
+        }
+        cp_async_commit();
+    };
+    // rows further ahead go to L2 only (one bulk prefetch per plane), so more of HBM's latency is
+    // covered than two shared-memory stages allow
+    auto prefetch = [&](int64_t row) {
+        if (row < p.rows && threadIdx.x < NP)
+            prefetch_l2(static_cast<const T*>(p.x[threadIdx.x]) + row * p.x_rs, static_cast<size_t>(p.cols) * sizeof(T));
+    };
+    int64_t row = blockIdx.x;
+    if (row < p.rows) issue(row, 0);
+#pragma unroll
+    for (int a = 1; a <= NORM_L2_AHEAD; ++a) prefetch(row + static_cast<int64_t>(a) * gridDim.x);
+    for (int64_t i = 0; row < p.rows; ++i, row += gridDim.x) {
+        const int stage = static_cast<int>(i & 1);
+        const int64_t nrow = row + gridDim.x;
+        prefetch(row + static_cast<int64_t>(NORM_L2_AHEAD + 1) * gridDim.x);
+        if (nrow < p.rows) issue(nrow, stage ^ 1);
+        else cp_async_commit();  // an empty group keeps the wait count below uniform
+        cp_async_wait<1>();      // this thread's copies of `row` have landed
+        const T* const xs = stages + stage * stage_elems;
+        C acc[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) acc[k] = C(0);
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+            const int64_t q = static_cast<int64_t>(s) * blockDim.x + threadIdx.x;
+            if (q >= quads) continue;
+            C xv[NP][ROW_VEC];
+#pragma unroll
+            for (int k = 0; k < NP; ++k) load_vec4<T>(xs + k * p.cols + q * ROW_VEC, xv[k]);
+#pragma unroll
+            for (int u = 0; u < ROW_VEC; ++u) {
+                C x[NP], sq[NP];
+#pragma unroll
+                for (int k = 0; k < NP; ++k) x[k] = xv[k][u];
+                s_mul<NP, C>(x, x, sq);
+#pragma unroll
+                for (int k = 0; k < NP; ++k) acc[k] += sq[k];
+            }
+        }
+        block_sum<NP, C>(acc, scratch);
+        C m[NP], r[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) m[k] = acc[k] * inv_cols;
+        m[0] += C(p.eps);
+        s_rsqrt<NP, C>(m, r);
+        if (p.rstd && threadIdx.x < NP) {
+#pragma unroll
+            for (int k = 0; k < NP; ++k)
+                if (k == static_cast<int>(threadIdx.x)) static_cast<C*>(p.rstd)[row * NP + k] = r[k];
+        }
+        const int64_t yb = row * p.y_rs;
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+            const int64_t q = static_cast<int64_t>(s) * blockDim.x + threadIdx.x;
+            if (q >= quads) continue;
+            C xv[NP][ROW_VEC], out[ROW_VEC][NP];
+#pragma unroll
+            for (int k = 0; k < NP; ++k) load_vec4<T>(xs + k * p.cols + q * ROW_VEC, xv[k]);
+#pragma unroll
+            for (int u = 0; u < ROW_VEC; ++u) {
+                C x[NP];
+#pragma unroll
+                for (int k = 0; k < NP; ++k) x[k] = xv[k][u];
+                s_mul<NP, C>(x, r, out[u]);
+                if (p.w_np) s_mul<NP, C>(out[u], w[s][u], out[u]);
+            }
+            store_planes4<NP, T, C>(p.y, NP, yb + q * ROW_VEC, ROW_VEC, true, out);
+        }
+    }
+    cp_async_wait<0>();
 }
 
 // Each CTA walks rows blockIdx.x, blockIdx.x + gridDim.x, ... and keeps its weight-gradient
@@ -381,6 +490,231 @@ __global__ void __launch_bounds__(256, 2) rmsnorm_bwd_cluster_kernel(const NormP
     cluster.sync();  // the peer may still read this CTA's row slots
 }
 
+// The cluster backward with the next row streaming in while this one is computed.  CTA rank h
+// of a CL-CTA cluster owns columns [h * cols/CL, (h+1) * cols/CL); thread t owns the column
+// quads q = s * blockDim + t (s < STEPS) of every row.  Each thread copies its own quads of the
+// NEXT row's x and g planes into a second shared-memory stage with cp.async while it computes
+// the current row from the first (rows further ahead are bulk-prefetched into L2), so HBM reads
+// never wait for the arithmetic, the row exchange or the stores; since a thread reads back only
+// what it copied, the stages need no block barrier.  The weight series and the weight-gradient
+// partial sums of the thread's columns stay in registers for the whole launch.  For float planes
+// the first pass leaves a = r (*) g (*) w in the g stage, so the second pass is dx = a - coef (*) x.
+// The CTAs of a cluster exchange their row partials of d by pushing them into each other's shared
+// memory (st.async completing bytes on the receiver's mbarrier, one barrier and slot set per row
+// parity), so no cluster-wide barrier (and no release of the previous row's stores) sits in the
+// row loop.
+template <typename T, int NP, int STEPS, int CL>
+__global__ void __launch_bounds__(512, 1) rmsnorm_bwd_stream_kernel(const NormParams p) {
+    using C = float;
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    __shared__ C scratch[16 * NP];
+    __shared__ C xslot[2][CL][NP];  // [row parity][sender rank][k]
+    __shared__ __align__(8) uint64_t xbar[2];
+    extern __shared__ __align__(16) unsigned char dyn[];
+    T* const stages = reinterpret_cast<T*>(dyn);  // [2][x planes, g planes][NP][half]
+    constexpr int VB = ROW_VEC * static_cast<int>(sizeof(T));
+    const int h = static_cast<int>(cluster.block_rank());
+    const int64_t half = p.cols / CL, quads = half / ROW_VEC, cbase = h * half;
+    const int64_t stage_elems = 2 * NP * half;
+    const int64_t n_clusters = gridDim.x / CL, cid = blockIdx.x / CL;
+    const bool want_dw = p.dw_part != nullptr;
+    if (threadIdx.x == 0) {
+        mbar_init(&xbar[0], 1);
+        mbar_init(&xbar[1], 1);
+        fence_mbar_init();
+    }
+    cluster.sync();  // every CTA's barriers are initialised before any peer signals them
+    const C inv_cols = C(1) / C(p.cols);
+
+    C w[STEPS][ROW_VEC][NP], dwa[STEPS][ROW_VEC][NP];
+#pragma unroll
+    for (int s = 0; s < STEPS; ++s) {
+        const int64_t q = static_cast<int64_t>(s) * blockDim.x + threadIdx.x;
+        load_weight4<NP, T, C>(p, cbase + q * ROW_VEC, q < quads ? ROW_VEC : 0, w[s]);
+#pragma unroll
+        for (int u = 0; u < ROW_VEC; ++u) {
+#pragma unroll
+            for (int k = 0; k < NP; ++k) dwa[s][u][k] = C(0);
+        }
+    }
+    auto issue = [&](int64_t row, int stage) {
+        T* st = stages + stage * stage_elems;
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+            const int64_t q = static_cast<int64_t>(s) * blockDim.x + threadIdx.x;
+            if (q < quads) {
+                const int64_t off = cbase + q * ROW_VEC;
+#pragma unroll
+                for (int k = 0; k < NP; ++k) {
+                    cp_async_vec<VB>(st + k * half + q * ROW_VEC, static_cast<const T*>(p.x[k]) + row * p.x_rs + off);
+                    cp_async_vec<VB>(st + (NP + k) * half + q * ROW_VEC,
+                                     static_cast<const T*>(p.g[k]) + row * p.g_rs + off);
+                }
+            }
+        }
+        cp_async_commit();
+    };
+    // rows further ahead go to L2 only (one bulk prefetch per plane segment), so more of HBM's
+    // latency is covered than two shared-memory stages allow
+    auto prefetch = [&](int64_t row) {
+        if (row < p.rows && threadIdx.x < 2 * NP) {
+            const int k = threadIdx.x % NP;
+            const T* base = threadIdx.x < NP ? static_cast<const T*>(p.x[k]) + row * p.x_rs
+                                             : static_cast<const T*>(p.g[k]) + row * p.g_rs;
+            prefetch_l2(base + cbase, static_cast<size_t>(half) * sizeof(T));
+        }
+    };
+    auto load_r = [&](int64_t row, C (&r)[NP]) {
+#pragma unroll
+        for (int k = 0; k < NP; ++k) r[k] = static_cast<const C*>(p.rstd)[row * NP + k];
+    };
+
+    int64_t row = cid;
+    C rn[NP];
+    if (row < p.rows) {
+        issue(row, 0);
+        load_r(row, rn);
+    }
+#pragma unroll
+    for (int a = 1; a <= NORM_L2_AHEAD; ++a) prefetch(row + a * n_clusters);
+    int par = 0;
+    for (int64_t i = 0; row < p.rows; ++i, row += n_clusters, par ^= 1) {
+        const int stage = static_cast<int>(i & 1);
+        const int64_t nrow = row + n_clusters;
+        prefetch(row + (NORM_L2_AHEAD + 1) * n_clusters);
+        if (nrow < p.rows) issue(nrow, stage ^ 1);
+        else cp_async_commit();  // an empty group keeps the wait count below uniform
+        C r[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) r[k] = rn[k];
+        if (nrow < p.rows) load_r(nrow, rn);
+        cp_async_wait<1>();  // this thread's copies of `row` have landed
+        T* const xs = stages + stage * stage_elems;
+        T* const gs = xs + NP * half;
+
+        C d[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) d[k] = C(0);
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+            const int64_t q = static_cast<int64_t>(s) * blockDim.x + threadIdx.x;
+            if (q >= quads) continue;
+            C xv[NP][ROW_VEC], gv[NP][ROW_VEC];
+#pragma unroll
+            for (int k = 0; k < NP; ++k) {
+                load_vec4<T>(xs + k * half + q * ROW_VEC, xv[k]);
+                load_vec4<T>(gs + k * half + q * ROW_VEC, gv[k]);
+            }
+#pragma unroll
+            for (int u = 0; u < ROW_VEC; ++u) {
+                C x[NP], g[NP], gx[NP], t[NP];
+#pragma unroll
+                for (int k = 0; k < NP; ++k) {
+                    x[k] = xv[k][u];
+                    g[k] = gv[k][u];
+                }
+                // gx = g (*) x feeds the weight gradient (gx (*) r) and the row sum
+                // (gy (*) x = w (*) gx) with gy = g (*) w
+                s_mul<NP, C>(g, x, gx);
+                if (want_dw) {
+                    s_mul<NP, C>(gx, r, t);
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) dwa[s][u][k] += t[k];
+                }
+                s_mul<NP, C>(w[s][u], gx, t);
+#pragma unroll
+                for (int k = 0; k < NP; ++k) d[k] += t[k];
+                if constexpr (sizeof(T) == 4) {
+                    s_mul<NP, C>(g, w[s][u], t);
+                    s_mul<NP, C>(r, t, t);
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) gv[k][u] = t[k];  // g of element u is no longer needed
+                }
+            }
+            if constexpr (sizeof(T) == 4) {
+#pragma unroll
+                for (int k = 0; k < NP; ++k) store_vec4<T>(gs + k * half + q * ROW_VEC, gv[k]);
+            }
+        }
+        block_sum<NP, C>(d, scratch);
+        if (threadIdx.x == 0) {
+            mbar_arrive_expect_tx(&xbar[par], (CL - 1) * NP * static_cast<uint32_t>(sizeof(C)));
+#pragma unroll
+            for (int j = 0; j < CL; ++j) {
+                if (j == h) continue;
+                const uint32_t slot = cluster_map_u32(&xslot[par][h][0], j), bar = cluster_map_u32(&xbar[par], j);
+#pragma unroll
+                for (int k = 0; k < NP; ++k) st_async_f32(slot + 4 * k, d[k], bar);
+            }
+        }
+        // barrier xbar[par] serves every second row: its (i / 2)-th phase is this row's
+        const bool ok = mbar_wait_bounded(&xbar[par], static_cast<uint32_t>(i >> 1) & 1u, p.status, 501);
+        if (__syncthreads_or(!ok)) break;  // the whole CTA leaves together (the peer's wait ends too)
+        // the partials in rank order, so every CTA of the cluster forms the same sum
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+            C t = h == 0 ? d[k] : xslot[par][0][k];
+#pragma unroll
+            for (int j = 1; j < CL; ++j) t += j == h ? d[k] : xslot[par][j][k];
+            d[k] = t;
+        }
+        C coef[NP];
+        s_mul<NP, C>(r, r, coef);
+        s_mul<NP, C>(coef, r, coef);
+        s_mul<NP, C>(coef, d, coef);
+#pragma unroll
+        for (int k = 0; k < NP; ++k) coef[k] *= inv_cols;
+        const int64_t yb = row * p.y_rs + cbase;
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+            const int64_t q = static_cast<int64_t>(s) * blockDim.x + threadIdx.x;
+            if (q >= quads) continue;
+            C xv[NP][ROW_VEC], av[NP][ROW_VEC];
+#pragma unroll
+            for (int k = 0; k < NP; ++k) {
+                load_vec4<T>(xs + k * half + q * ROW_VEC, xv[k]);
+                load_vec4<T>(gs + k * half + q * ROW_VEC, av[k]);
+            }
+            C out[ROW_VEC][NP];
+#pragma unroll
+            for (int u = 0; u < ROW_VEC; ++u) {
+                C x[NP], a[NP], b[NP];
+#pragma unroll
+                for (int k = 0; k < NP; ++k) {
+                    x[k] = xv[k][u];
+                    a[k] = av[k][u];
+                }
+                if constexpr (sizeof(T) != 4) {
+                    s_mul<NP, C>(a, w[s][u], a);  // the stage holds g: a = r (*) g (*) w
+                    s_mul<NP, C>(r, a, a);
+                }
+                s_mul<NP, C>(coef, x, b);
+#pragma unroll
+                for (int k = 0; k < NP; ++k) out[u][k] = a[k] - b[k];
+            }
+            store_planes4<NP, T, C>(p.y, NP, yb + q * ROW_VEC, ROW_VEC, true, out);
+        }
+    }
+    cp_async_wait<0>();
+    if (want_dw) {
+        C* out = static_cast<C*>(p.dw_part) + cid * NP * p.cols + cbase;
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+            const int64_t q = static_cast<int64_t>(s) * blockDim.x + threadIdx.x;
+            if (q >= quads) continue;
+#pragma unroll
+            for (int k = 0; k < NP; ++k) {
+                C v[ROW_VEC];
+#pragma unroll
+                for (int u = 0; u < ROW_VEC; ++u) v[u] = dwa[s][u][k];
+                store_vec4<C>(out + k * p.cols + q * ROW_VEC, v);
+            }
+        }
+    }
+    cluster.sync();  // no CTA leaves while a peer may still write into its shared memory
+}
+
 // dw[k][c] = sum_b part[b][k][c].  A CTA covers 32 consecutive values with 8 lanes of partials
 // each (warp j sums partials j, j+8, ...; coalesced 128-byte rows), then combines the 8 lanes.
 template <typename T, int NP>
@@ -411,6 +745,97 @@ static int norm_threads(int64_t cols) { return cols >= 2048 ? 512 : (cols >= 512
 
 // Launch the register-resident forward when a row fits: STEPS vectors of 4 columns per thread,
 // at most 512 threads, float compute, degree <= 5.  Returns false when it does not apply.
+// Weight-gradient partials [parts][np][cols] -> dw planes.
+template <typename T, int NP>
+static int reduce_dw(const NormParams& p, void* const* dw, int parts, cudaStream_t s) {
+    NormParams q = p;
+    for (int k = 0; k < p.np; ++k) q.g[k] = dw[k];
+    const int64_t total = static_cast<int64_t>(p.np) * p.cols;
+    rmsnorm_dw_reduce_kernel<T, NP><<<static_cast<int>(ceil_div(total, 32)), 256, 0, s>>>(q, parts);
+    PK_CHECK_LAUNCH("pk_rmsnorm_bwd: weight reduction");
+    return PK_OK;
+}
+
+// The streaming backward (rmsnorm_bwd_stream_kernel) for rows that split into CL-CTA clusters of
+// at most 512 threads x 4 columns with two stages of x and g in shared memory.  Returns 1 when the
+// shape does not suit it (the caller uses another kernel), else a status.
+template <typename T, int NP, int CL>
+static int bwd_stream(NormParams& p, void* const* dw, void* ws, size_t ws_bytes, cudaStream_t s) {
+    if (p.np != NP || !p.vec || p.cols % (CL * ROW_VEC)) return 1;
+    const int64_t half = p.cols / CL, quads = half / ROW_VEC;
+    const size_t smem = 2 * 2 * static_cast<size_t>(NP) * half * sizeof(T);
+    if (quads < 64 || quads > 512 || smem > 200 * 1024) return 1;
+    const int threads = static_cast<int>(round_up(quads, 32));
+    auto kern = rmsnorm_bwd_stream_kernel<T, NP, 1, CL>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_fail(e, "pk_rmsnorm_bwd: cudaFuncSetAttribute");
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(CL);
+    cfg.blockDim = dim3(static_cast<unsigned>(threads));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CL;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // only as many clusters as can be resident at once: rows are dealt out statically, so a
+    // cluster that waited for a free slot would finish its rows after all the others
+    int resident = 0;
+    e = cudaOccupancyMaxActiveClusters(&resident, kern, &cfg);
+    if (e != cudaSuccess) return cuda_fail(e, "pk_rmsnorm_bwd: cluster occupancy query");
+    if (resident < 1) return 1;
+    const int64_t clusters =
+        std::min<int64_t>({p.rows, static_cast<int64_t>(resident), static_cast<int64_t>(num_sms()) * 4 / CL});
+    if (dw) {
+        const size_t need = static_cast<size_t>(clusters) * p.np * p.cols * sizeof(float);
+        if (!ws || ws_bytes < need) return fail(PK_ERR_WORKSPACE, "pk_rmsnorm_bwd: workspace too small");
+        p.dw_part = ws;
+    }
+    cfg.gridDim = dim3(static_cast<unsigned>(CL * clusters));
+    void* tok;
+    prof_begin("rmsnorm_bwd", s, &tok);
+    e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess) return cuda_fail(e, "pk_rmsnorm_bwd: cluster launch");
+    PK_CHECK_LAUNCH("pk_rmsnorm_bwd");
+    if (dw) {
+        const int st = reduce_dw<T, NP>(p, dw, static_cast<int>(clusters), s);
+        if (st != PK_OK) return st;
+    }
+    prof_end("rmsnorm_bwd", s, tok);
+    return PK_OK;
+}
+
+// Launch the streaming forward when two stages of a row fit in shared memory and the row fits
+// 512 threads x STEPS x 4 columns (vector-aligned planes, float compute, degree <= 5).  Returns
+// false when it does not apply.
+template <typename T, int NP>
+static bool stream_row_forward(const NormParams& p, cudaStream_t s) {
+    using C = typename Compute<T>::type;
+    if constexpr (sizeof(C) != 4 || NP > 6) {
+        return false;
+    } else {
+        if (p.np != NP || !p.vec || p.cols % ROW_VEC) return false;
+        const int64_t quads = p.cols / ROW_VEC;
+        const int steps = quads <= 512 ? 1 : (quads <= 1024 ? 2 : 0);
+        const size_t smem = 2 * static_cast<size_t>(NP) * p.cols * sizeof(T);
+        if (!steps || quads < 64 || smem > 200 * 1024) return false;
+        const int threads = static_cast<int>(round_up(ceil_div(quads, steps), 32));
+        auto kern = steps == 1 ? rmsnorm_fwd_stream_kernel<T, NP, 1> : rmsnorm_fwd_stream_kernel<T, NP, 2>;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+            cudaSuccess)
+            return false;
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
+            return false;
+        const int grid = static_cast<int>(std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * per_sm));
+        kern<<<grid, threads, smem, s>>>(p);
+        return true;
+    }
+}
+
 template <typename T, int NP>
 static bool reg_row_forward(const NormParams& p, cudaStream_t s) {
     using C = typename Compute<T>::type;
@@ -459,13 +884,21 @@ static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, siz
     if (!backward) {
         void* tok;
         prof_begin("rmsnorm_fwd", s, &tok);
-        if (!reg_row_forward<T, NP>(p, s)) {
+        if (!stream_row_forward<T, NP>(p, s) && !reg_row_forward<T, NP>(p, s)) {
             const int grid = static_cast<int>(std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * 8));
             rmsnorm_fwd_kernel<T, NP><<<grid, threads, 0, s>>>(p);
         }
         prof_end("rmsnorm_fwd", s, tok);
         PK_CHECK_LAUNCH("pk_rmsnorm_fwd");
         return PK_OK;
+    }
+    if constexpr (sizeof(C) == 4 && NP <= 6) {
+        // next rows streamed into shared memory: half rows over 2-CTA clusters, quarter rows
+        // over 4-CTA clusters for rows too long for a pair (a 4-CTA split of 4096-column rows
+        // measured slower: 3.4 against 4.0 TB/s)
+        int st = bwd_stream<T, NP, 2>(p, dw, ws, ws_bytes, s);
+        if (st == 1) st = bwd_stream<T, NP, 4>(p, dw, ws, ws_bytes, s);
+        if (st != 1) return st;
     }
     const size_t smem = dw ? static_cast<size_t>(NP) * p.cols * sizeof(C) : 0;
     if (smem > 200 * 1024) return fail(PK_ERR_UNSUPPORTED, "pk_rmsnorm_bwd: row too long for the weight-gradient buffer");
@@ -643,6 +1076,7 @@ int pk_rmsnorm_bwd(int dtype, int degree, int64_t rows, int64_t cols, const void
     p.w_np = w ? w_planes : 0;
     if (w && w_planes != 1 && w_planes != p.np) return fail(PK_ERR_ARG, "pk_rmsnorm_bwd: w_planes must be 1 or degree+1");
     p.rstd = const_cast<void*>(rstd);
+    p.status = device_status_ptr();
     for (int k = 0; k < p.np; ++k) {
         p.x[k] = x[k];
         p.g[k] = g[k];

@@ -21,11 +21,20 @@ __device__ __forceinline__ void block_sum(A (&v)[NP], A* scratch) {
         for (int k = 0; k < NP; ++k) scratch[warp * NP + k] = v[k];
     }
     __syncthreads();
+    // every warp reduces the per-warp partials itself: with P = nw rounded up to a power of two,
+    // lane j holds warp (j mod P)'s partial (zero past nw) and a butterfly over offsets < P gives
+    // every lane the total; all warps run the same butterfly, so all threads agree bit for bit
+    int pw = 1;
+    while (pw < nw) pw <<= 1;
+    const int src = lane & (pw - 1);
 #pragma unroll
-    for (int k = 0; k < NP; ++k) {
-        A s = A(0);
-        for (int w = 0; w < nw; ++w) s += scratch[w * NP + k];
-        v[k] = s;
+    for (int k = 0; k < NP; ++k) v[k] = src < nw ? scratch[src * NP + k] : A(0);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        if (off < pw) {
+#pragma unroll
+            for (int k = 0; k < NP; ++k) v[k] += __shfl_xor_sync(0xffffffffu, v[k], off);
+        }
     }
 }
 

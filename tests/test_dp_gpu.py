@@ -65,7 +65,9 @@ def _worker(rank, world, port, queue):
                     loss.backward()
                     allreduce_gradients(list(P.values()))
                     opt.step()
-        final = {k: [c.detach().cpu() for c in p.coeffs] for k, p in P.items()}
+        # numpy arrays travel by value; a tensor would travel through shared memory that this
+        # process removes when it exits, possibly before the parent has received it
+        final = {k: [c.detach().cpu().numpy() for c in p.coeffs] for k, p in P.items()}
         queue.put((rank, final))
     finally:
         dist.destroy_process_group()
@@ -83,7 +85,8 @@ def test_two_rank_training_matches_reference(golden):
     procs = [ctx.Process(target=_worker, args=(r, world, port, queue)) for r in range(world)]
     for p in procs:
         p.start()
-    results = dict(queue.get(timeout=600) for _ in range(world))
+    results = {r: {k: [torch.from_numpy(c) for c in v] for k, v in final.items()}
+               for r, final in (queue.get(timeout=600) for _ in range(world))}
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0

@@ -122,6 +122,45 @@ def test_rmsnorm_f32_config_width():
     assert_close(coeffs(w.grad), want_dw, F32, "dw")
 
 
+@pytest.mark.parametrize("dtype,n,cols,weight", [
+    (torch.float32, 4, 4096, "series"), (torch.float32, 5, 2048, "plain"), (torch.float32, 3, 8192, "none"),
+    (torch.bfloat16, 4, 4096, "series"), (torch.float16, 2, 1024, "plain")])
+def test_rmsnorm_backward_many_rows(dtype, n, cols, weight):
+    """More rows than clusters fit on the GPU at once (each cluster streams a run of rows), rows
+    strided inside a wider buffer, a weight series with non-zero directions, a plain weight, none."""
+    from polytensors_b200 import PolyTensor
+
+    rows, tol = 1000, {torch.float32: F32, torch.bfloat16: 2e-2, torch.float16: 2e-3}[dtype]
+    X = series((rows, cols + 64), n, 21, dtype)
+    G = series((rows, cols), n, 22, dtype)
+    gw = torch.Generator().manual_seed(23)
+    W = [(1 + 0.1 * torch.randn(cols, generator=gw, dtype=torch.float64)).to(dtype)]
+    W += [(0.1 * torch.randn(cols, generator=gw, dtype=torch.float64) / (k + 1)).to(dtype) if weight == "series"
+          else torch.zeros(cols, dtype=dtype) for k in range(n)]
+    d64 = lambda s: [p.double() for p in s]
+    X64 = [p[:, :cols].double() for p in X]
+    eps = torch.finfo(dtype).eps  # F.rms_norm's default for these planes
+    fn = ((lambda x, w: ref.rms_norm(x, (cols,), w, eps)) if weight != "none"
+          else (lambda x: ref.rms_norm(x, (cols,), None, eps)))
+    ins = [X64] + ([d64(W)] if weight != "none" else [])
+    want_y = fn(*ins)
+    want_g = ref.series_vjp(fn, ins, d64(G))
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        x = PolyTensor(tuple(p.cuda()[:, :cols] for p in X), requires_grad=True)
+        if weight == "series":
+            w = poly(W, requires_grad=True)
+        elif weight == "plain":
+            w = W[0].cuda()
+        else:
+            w = None
+        y = F.rms_norm(x, (cols,), w)
+        y.backward(poly(G))
+    assert_close(coeffs(y), want_y, tol, "y")
+    assert_close(coeffs(x.grad), want_g[0], tol, "dx")
+    if weight == "series":
+        assert_close(coeffs(w.grad), want_g[1], tol, "dw")
+
+
 def test_gelu_golden(golden):
     from polytensors_b200 import PolyTensor
 

@@ -38,7 +38,9 @@ def _average_worker(rank, world, port, queue):
             p.grad = PolyTensor(tuple(torch.full(shape, float(rank * 10 + i * 100 + k)) for k in range(4)))
             params.append(p)
         allreduce_gradients(params, bucket_bytes=64)   # several buckets
-        got = [[c.clone() for c in p.grad.coeffs] for p in params]
+        # plain lists: a tensor sent through the queue lives in shared memory that this process
+        # removes when it exits, possibly before the parent has received it
+        got = [[c.tolist() for c in p.grad.coeffs] for p in params]
         queue.put((rank, got))
     finally:
         dist.destroy_process_group()
@@ -58,7 +60,7 @@ def test_allreduce_averages_every_plane():
     for rank in range(world):
         for i, planes in enumerate(results[rank]):
             for k, c in enumerate(planes):
-                assert torch.all(c == (0 + 10) / 2 + i * 100 + k)
+                assert torch.all(torch.tensor(c) == (0 + 10) / 2 + i * 100 + k)
 
 
 def _failing_worker(rank, world, port, queue):
