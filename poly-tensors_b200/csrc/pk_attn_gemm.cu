@@ -341,14 +341,15 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
         // same tile sequence, so the quadrants' named barriers always match.
         for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
           const AgUnit un = ag_unit(p, u);
+          // the unit's rows are this thread's rows in every tile: their statistics are read once
+          const int r = un.tm * AG_BM + static_cast<int>(lane_base) + lane;
+          const bool row_ok = r < p.M;
+          float rv[NP];
+#pragma unroll
+          for (int k = 0; k < NP; ++k) rv[k] = row_ok ? p.rowv[un.b * p.rowv_bs + static_cast<int64_t>(r) * NP + k] : 0.f;
           for (int tn = un.tn0; tn < un.tn1; ++tn) {
             const AgTile tc{un.b, un.tm, tn};
-            const int r = tc.tm * AG_BM + static_cast<int>(lane_base) + lane;
             bool masked_tile = ag_masked(p, tc);
-            const bool row_ok = r < p.M;
-            float rv[NP];
-#pragma unroll
-            for (int k = 0; k < NP; ++k) rv[k] = row_ok ? p.rowv[tc.b * p.rowv_bs + static_cast<int64_t>(r) * NP + k] : 0.f;
             const int64_t last_key = p.causal ? static_cast<int64_t>(r) + p.shift : static_cast<int64_t>(p.N) - 1;
             const bool live = MODE == AG_PROBS ? rv[0] < INFINITY : true;
             // tile entirely inside the matrix and below the causal diagonal: no per-element tests
@@ -360,6 +361,15 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
             // accumulator wait so that their latency overlaps it (bf16 pairs, zero outside the matrix)
             uint32_t pw[NP][8];
             if constexpr (MODE == AG_DSCORES) {
+                // the unit's next tile: its probability rows (64 columns = one 128-byte line per
+                // row and plane) go to L2 now, a whole tile ahead of their loads
+                const int ncol = (tn + 1) * AG_BN;
+                if (grp == 0 && row_ok && tn + 1 < un.tn1 && ncol < p.N && !ag_masked(p, AgTile{un.b, un.tm, tn + 1})) {
+#pragma unroll
+                    for (int k = 0; k < NP; ++k)
+                        prefetch_l2_line(static_cast<const __nv_bfloat16*>(p.pr[k]) + tc.b * p.p_bs +
+                                         static_cast<int64_t>(r) * p.p_rs + ncol);
+                }
                 const int valid16 = row_ok ? max(0, min(16, p.N - cbase)) : 0;
 #pragma unroll
                 for (int k = 0; k < NP; ++k) {

@@ -191,6 +191,10 @@ __device__ __forceinline__ void prefetch_l2(const void* gmem, size_t bytes) {
     const uintptr_t e = (reinterpret_cast<uintptr_t>(gmem) + bytes + 15) & ~uintptr_t(15);
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(static_cast<uint32_t>(e - a)) : "memory");
 }
+// Prefetch the cache line holding `gmem` into L2 (`gmem` must lie inside an allocation).
+__device__ __forceinline__ void prefetch_l2_line(const void* gmem) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(gmem) : "memory");
+}
 // One aligned 8- or 16-byte vector (the 16-byte form bypasses L1).
 template <int BYTES>
 __device__ __forceinline__ void cp_async_vec(void* smem, const void* gmem) {
