@@ -23,6 +23,7 @@
 // all lie after their last query are neither loaded nor multiplied: the epilogue writes zeros.
 #include <algorithm>
 #include <cstring>
+#include <vector>
 
 #include "pk_common.cuh"
 #include "pk_gemm_prep.cuh"
@@ -44,6 +45,7 @@ constexpr int AG_SMEM_BUDGET = 220 * 1024;        // resident A + B ring + outpu
 constexpr int AG_SMEM_BYTES = AG_SMEM_BUDGET + 1024 + 512;
 constexpr int AG_CHUNK = 8;                       // B tiles per work unit
 constexpr int AG_MAX_NP = 4;
+constexpr int AG_MAX_SHAPES = 4096;               // unit shapes (chunk, row tile) the cost order holds
 
 enum { AG_PROBS = 0, AG_DSCORES = 1 };
 
@@ -71,29 +73,51 @@ struct AgParams {
     const float* rowv;               // AG_PROBS: (lse_0, logz_1..n); AG_DSCORES: dsum; per row
     int64_t rowv_bs;                 // floats between batch entries (rows are NP floats apart)
     int* status;
+    // Unit schedule.  n_groups == 0: natural order (batch entry, B chunk, row tile).  Otherwise the
+    // unit shapes (B chunk, row tile) in classes of equal live-tile count, heaviest class first:
+    // class g holds shapes order[grp_first[g] .. grp_first[g+1]) for every batch entry, ranks
+    // grp_cum[g] .. grp_cum[g+1] (batch entry outer, row tile fastest within a chunk).
+    int n_groups;
+    int grp_first[AG_CHUNK + 2];
+    int grp_cum[AG_CHUNK + 2];
+    uint16_t order[AG_MAX_SHAPES];   // chunk * tiles_m + row tile
 };
 
 struct AgTile {
     int b, tm, tn;
 };
 
-// Unit u -> (batch entry, B chunk, row tile) with the row tile fastest: CTAs that run together
-// work on the same B chunk.  Tiles of the unit: tn in [tn0, tn1).
+// Unit of schedule rank u -> (batch entry, B chunk, row tile), the row tile fastest within a
+// class so that CTAs running together work on the same B chunk.  Tiles of the unit: tn in
+// [tn0, tn1).
 struct AgUnit {
     int b, tm, tn0, tn1;
 };
 
 __device__ __forceinline__ AgUnit ag_unit(const AgParams& p, int u) {
     AgUnit c;
-    const int per_b = p.n_chunks * p.tiles_m;
-    c.b = u / per_b;
-    const int r = u % per_b;
-    const int chunk = r / p.tiles_m;
-    c.tm = r % p.tiles_m;
+    int chunk;
+    if (p.n_groups == 0) {
+        const int per_b = p.n_chunks * p.tiles_m;
+        c.b = u / per_b;
+        const int r = u % per_b;
+        chunk = r / p.tiles_m;
+        c.tm = r % p.tiles_m;
+    } else {
+        int g = 0;
+        while (g + 1 < p.n_groups && u >= p.grp_cum[g + 1]) ++g;
+        const int local = u - p.grp_cum[g];
+        const int gsize = p.grp_first[g + 1] - p.grp_first[g];
+        c.b = local / gsize;
+        const int code = p.order[p.grp_first[g] + local % gsize];
+        chunk = code / p.tiles_m;
+        c.tm = code % p.tiles_m;
+    }
     c.tn0 = chunk * AG_CHUNK;
     c.tn1 = min(p.tiles_n, c.tn0 + AG_CHUNK);
     return c;
 }
+
 
 // Every key of the tile lies after the last query of its rows: all probabilities are zero.
 __device__ __forceinline__ bool ag_masked(const AgParams& p, const AgTile& c) {
@@ -122,7 +146,7 @@ __device__ __forceinline__ void s_exp_fast(float (&x)[NP]) {
 
 template <int NP, int MODE>
 __global__ void __launch_bounds__(AG_THREADS, 1)
-    attn_score_gemm_kernel(const __grid_constant__ AgMaps maps, const AgParams p) {
+    attn_score_gemm_kernel(const __grid_constant__ AgMaps maps, const __grid_constant__ AgParams p) {
     constexpr int TMEM_COLS = 2 * NP * AG_BN <= 128 ? 128 : (2 * NP * AG_BN <= 256 ? 256 : 512);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -180,7 +204,7 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
             for (int s = 0; s < nst; ++s) issued_parity[s] = -1;
             int a_issued = -1;
             bool ok = true;
-            for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+            for (int rk = 0, u = snake_rank(0); u < p.total_units && ok; u = snake_rank(++rk)) {
                 const AgUnit un = ag_unit(p, u);
                 if (ag_masked(p, AgTile{un.b, un.tm, un.tn0})) continue;  // every tile of the unit masked
                 if (!mbar_wait_or_abort(a_empty, a_phase ^ 1, abort_flag, p.status, 125)) {
@@ -250,7 +274,7 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
             uint32_t stage = 0, phase = 0, a_par = 0;
             uint32_t abuf = 0, aphase = 0;
             bool ok = true, issued = false;
-            for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+            for (int rk = 0, u = snake_rank(0); u < p.total_units && ok; u = snake_rank(++rk)) {
                 const AgUnit un = ag_unit(p, u);
                 if (ag_masked(p, AgTile{un.b, un.tm, un.tn0})) continue;
                 if (!mbar_wait_or_abort(a_full, a_par, abort_flag, p.status, 126)) {
@@ -339,7 +363,7 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
         uint32_t abuf = 0, aphase = 0;
         // A wait that fails (timeout or abort) turns its tile into zeros; every warp still runs the
         // same tile sequence, so the quadrants' named barriers always match.
-        for (int u = blockIdx.x; u < p.total_units; u += gridDim.x) {
+        for (int rk = 0, u = snake_rank(0); u < p.total_units; u = snake_rank(++rk)) {
           const AgUnit un = ag_unit(p, u);
           // the unit's rows are this thread's rows in every tile: their statistics are read once
           const int r = un.tm * AG_BM + static_cast<int>(lane_base) + lane;
@@ -628,6 +652,37 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
     p.rowv = static_cast<const float*>(rowv);
     p.rowv_bs = rowv_bs;
     p.status = device_status_ptr();
+    // Schedule: unit shapes by live (unmasked) tile count, heaviest first, so that the rounds of
+    // the snake deal comparable units together (causal masking makes a static round-robin over
+    // the natural order leave some SMs with far more tiles than others).  Fully masked units stay
+    // in the schedule as the last class: their epilogue writes the zero tiles.
+    p.n_groups = 0;
+    if (static_cast<int64_t>(p.tiles_m) * p.n_chunks <= AG_MAX_SHAPES) {
+        std::vector<int> by_cost[AG_CHUNK + 1];
+        for (int ch = 0; ch < p.n_chunks; ++ch) {
+            for (int tm = 0; tm < p.tiles_m; ++tm) {
+                const int tn0 = ch * AG_CHUNK, tn1 = std::min(p.tiles_n, tn0 + AG_CHUNK);
+                const int64_t last_row = std::min<int64_t>(static_cast<int64_t>(tm) * AG_BM + AG_BM - 1, M - 1);
+                int cost = 0;
+                for (int tn = tn0; tn < tn1; ++tn)
+                    if (!p.causal || static_cast<int64_t>(tn) * AG_BN <= last_row + p.shift) ++cost;
+                by_cost[cost].push_back(ch * p.tiles_m + tm);
+            }
+        }
+        int s = 0, g = 0;
+        int64_t rank = 0;
+        for (int cost = AG_CHUNK; cost >= 0; --cost) {
+            if (by_cost[cost].empty()) continue;
+            p.grp_first[g] = s;
+            p.grp_cum[g] = static_cast<int>(rank);
+            for (int code : by_cost[cost]) p.order[s++] = static_cast<uint16_t>(code);
+            rank += static_cast<int64_t>(by_cost[cost].size()) * batch;
+            ++g;
+        }
+        p.grp_first[g] = s;
+        p.grp_cum[g] = static_cast<int>(rank);
+        p.n_groups = g;
+    }
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     switch (P * 2 + mode) {
         case 2: return launch_ag<1, AG_PROBS>(maps, p, stream);

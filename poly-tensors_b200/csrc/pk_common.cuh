@@ -191,6 +191,13 @@ __device__ __forceinline__ void prefetch_l2(const void* gmem, size_t bytes) {
     const uintptr_t e = (reinterpret_cast<uintptr_t>(gmem) + bytes + 15) & ~uintptr_t(15);
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(static_cast<uint32_t>(e - a)) : "memory");
 }
+// A persistent CTA's k-th work rank: rounds of gridDim.x ranks dealt out in alternating
+// directions, so a CTA that drew a heavy item in one round draws a lighter one in the next when
+// items come heaviest first (ranks increase with k; each round's ranks go to distinct CTAs).
+__device__ __forceinline__ int snake_rank(int k) {
+    const int g = static_cast<int>(gridDim.x), i = static_cast<int>(blockIdx.x);
+    return k * g + ((k & 1) ? g - 1 - i : i);
+}
 // Prefetch the cache line holding `gmem` into L2 (`gmem` must lie inside an allocation).
 __device__ __forceinline__ void prefetch_l2_line(const void* gmem) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(gmem) : "memory");

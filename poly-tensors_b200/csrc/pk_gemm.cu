@@ -781,10 +781,21 @@ constexpr int AP_STAGES = 6;
 constexpr int AP_SMEM_BYTES = AP_STAGES * AP_STAGE_BYTES + 1024 + 256;
 
 __device__ __forceinline__ TileCoord ap_decode(const TcParams& p, int t) {
-    // batch entry, then groups of group_m row tiles (CTAs running together share B tiles in L2)
     TileCoord c;
-    const int per_b = p.tiles_m * p.tiles_n;
     c.plane = 0;
+    if (p.band == 1 || p.band == 2) {
+        // banded product: a row tile's k-block count falls (band 1) or rises (band 2) with its
+        // index, so row tiles in decreasing cost order, then batch entries, then column tiles
+        // (dealt out with snake_rank, the CTAs' loads stay balanced)
+        const int per_m = p.batch * p.tiles_n;
+        const int i = t / per_m, rem = t % per_m;
+        c.tm = p.band == 1 ? i : p.tiles_m - 1 - i;
+        c.b = rem / p.tiles_n;
+        c.tn = rem % p.tiles_n;
+        return c;
+    }
+    // batch entry, then groups of group_m row tiles (CTAs running together share B tiles in L2)
+    const int per_b = p.tiles_m * p.tiles_n;
     c.b = t / per_b;
     const int r = t % per_b;
     const int span = p.group_m * p.tiles_n;
@@ -844,7 +855,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
             for (int s = 0; s < AP_STAGES; ++s) issued_parity[s] = -1;
             bool ok = true;
-            for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+            for (int rk = 0, t = snake_rank(0); t < p.total_tiles && ok; t = snake_rank(++rk)) {
                 const TileCoord tc = ap_decode(p, t);
                 int kb0, kb1;
                 tile_kblocks(p, tc.tm, tc.tn, AP_BN, kb0, kb1);
@@ -900,7 +911,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint64_t b_step = p.b_mn ? (2048 >> 4) : (32 >> 4);
             uint32_t stage = 0, phase = 0, aphase = 0;
             bool ok = true, issued = false;
-            for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+            for (int rk = 0, t = snake_rank(0); t < p.total_tiles && ok; t = snake_rank(++rk)) {
                 const TileCoord tc = ap_decode(p, t);
                 int kb0, kb1;
                 tile_kblocks(p, tc.tm, tc.tn, AP_BN, kb0, kb1);
@@ -965,7 +976,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const uint32_t lane_base = 32u * (warp & 3);
         const int half = (warp - 2) >> 2;
         uint32_t aphase = 0;
-        for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+        for (int rk = 0, t = snake_rank(0); t < p.total_tiles; t = snake_rank(++rk)) {
             const TileCoord tc = ap_decode(p, t);
             const int row = tc.tm * TC_BM + lane_base + lane;
             int kb0, kb1;
