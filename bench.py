@@ -593,6 +593,24 @@ def run_train(args, rank, world, device):
                 opt.step()
 
     ms, clocks = _timed(step, args.steps, args.warmup, device, world)
+    # device time per kernel family over one more step, with the library's launch timing on
+    # (outside the timed region: the per-launch events would perturb it)
+    from polytensors_b200 import _lib
+
+    names = ("poly_gemm", "flash_attn_fwd", "attn_probs_gemm", "attn_dscores_gemm", "attn_probs", "attn_dscores",
+             "rmsnorm_fwd", "rmsnorm_bwd", "series_map", "softmax_fwd", "softmax_bwd", "cross_entropy_fwd",
+             "cross_entropy_bwd")
+    for nm in names:
+        _lib.profile_query(nm)
+    _lib.profile_enable(True)
+    step()
+    torch.cuda.synchronize(device)
+    _lib.profile_enable(False)
+    breakdown = {}
+    for nm in names:
+        kt, kl = _lib.profile_query(nm)
+        if kl:
+            breakdown[nm] = {"ms_per_step": kt, "launches_per_step": kl}
     tokens = world * n_micro * micro * seq
     tps = tokens / (ms / 1e3)
     return {
@@ -605,6 +623,7 @@ def run_train(args, rank, world, device):
                    "micro_batch": micro, "micro_batches_timed_per_rank": n_micro},
         "steps_per_s": tps / (global_batch * seq) if n_micro * micro == per_rank else None,
         "extrapolated_steps_per_s": tps / (global_batch * seq),
+        "kernels": breakdown,
         "clocks": clocks,
     }
 

@@ -144,47 +144,72 @@ __device__ __forceinline__ void split4_store(__nv_bfloat16* hi, __nv_bfloat16* l
     *reinterpret_cast<uint2*>(lo) = make_uint2(l[0], l[1]);
 }
 
-// k contiguous in the source (s_k == 1): threads walk (batch, plane, row, k/4) flat, four k
-// per thread; 16-byte loads when row starts are 16-byte aligned.
-__global__ void __launch_bounds__(256) split_direct_kernel(const StageParams p, int64_t batch, int vec) {
+// k contiguous in the source (s_k == 1): each source row (batch entry, plane, row) is a "line"
+// of K floats.  A line gets `lpl` lanes (the power of two >= its 4-float groups, at most 32; a
+// warp takes 32 / lpl lines at once), its indices are decoded once, and the lanes stride over its
+// groups of four k: 16-byte loads when rows are 16-byte aligned, 8-byte hi and lo stores.
+__global__ void __launch_bounds__(256) split_direct_kernel(const __grid_constant__ StageParams p, int64_t batch,
+                                                           int vec, int lpl) {
     const int64_t kv = p.Kp / 4;
-    const int64_t total = batch * p.planes * p.rows * kv;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t k = (i % kv) * 4;
-        const int64_t y = i / kv;
+    const int64_t lines = batch * p.planes * p.rows;
+    const int lane = threadIdx.x & 31;
+    const int per_warp = 32 / lpl, sub = lane / lpl, j0 = lane % lpl;
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.dst);
+    for (int64_t y = warp * per_warp + sub; y < lines; y += nwarps * per_warp) {
         const int64_t r = y % p.rows;
-        const int pi = static_cast<int>((y / p.rows) % p.planes);
-        const int64_t b = y / (p.rows * p.planes);
-        const StagePlane pl = p.plane[pi];
+        const int64_t bp = y / p.rows;
+        const int pi = static_cast<int>(bp % p.planes);
+        const int64_t b = bp / p.planes;
+        const StagePlane& pl = p.plane[pi];
         const float* src = static_cast<const float*>(pl.src) + b * p.s_b + r * p.s_r;
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        if (vec && k + 4 <= p.K) {
-            const float4 t = *reinterpret_cast<const float4*>(src + k);
-            v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-        } else {
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                if (k + j < p.K) v[j] = src[k + j];
-        }
         const int64_t sub0 = b * p.subs_per_batch + pl.dst_sub;
-        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.dst);
-        split4_store(dst + (sub0 * p.rows + r) * p.Kp + k, dst + ((sub0 + 1) * p.rows + r) * p.Kp + k, v);
+        __nv_bfloat16* hi = dst + (sub0 * p.rows + r) * p.Kp;
+        __nv_bfloat16* lo = dst + ((sub0 + 1) * p.rows + r) * p.Kp;
+#pragma unroll 4
+        for (int64_t jj = j0; jj < kv; jj += lpl) {
+            const int64_t k = jj * 4;
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            if (vec && k + 4 <= p.K) {
+                const float4 t = *reinterpret_cast<const float4*>(src + k);
+                v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    if (k + i < p.K) v[i] = src[k + i];
+            }
+            split4_store(hi + k, lo + k, v);
+        }
     }
 }
 
 // rows contiguous in the source (s_r == 1): a 64 x 64 tile is read along rows and written
-// along k through shared memory.  grid: x = k tiles, y = row tiles, z = batch * planes.
-__global__ void __launch_bounds__(256) split_transpose_kernel(const StageParams p) {
+// along k through shared memory.  grid: x = k tiles, y = row tiles, z = batch * planes.  With
+// `vec` (16-byte aligned planes, s_k and s_b multiples of 4) a thread reads four rows of one k
+// with one 16-byte load.
+__global__ void __launch_bounds__(256) split_transpose_kernel(const __grid_constant__ StageParams p, int vec) {
     __shared__ float tile[64][65];
     const int z = blockIdx.z;
     const int pi = z % p.planes;
     const int64_t b = z / p.planes;
-    const StagePlane pl = p.plane[pi];
+    const StagePlane& pl = p.plane[pi];
     const float* src = static_cast<const float*>(pl.src) + b * p.s_b;
     const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 64, k0 = static_cast<int64_t>(blockIdx.x) * 64;
     const int t = threadIdx.x;
-    {
+    if (vec && r0 + 64 <= p.rows) {
+        const int tr = (t & 15) * 4, tk = t >> 4;  // 16 groups of four rows x 16 k per pass
+#pragma unroll
+        for (int kk = tk; kk < 64; kk += 16) {
+            const int64_t k = k0 + kk;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k < p.K) v = *reinterpret_cast<const float4*>(src + r0 + tr + k * p.s_k);
+            tile[kk][tr] = v.x;
+            tile[kk][tr + 1] = v.y;
+            tile[kk][tr + 2] = v.z;
+            tile[kk][tr + 3] = v.w;
+        }
+    } else {
         const int tr = t & 63, tk = t >> 6;  // 64 rows x 4 k per pass, rows fastest (coalesced)
         for (int kk = tk; kk < 64; kk += 4) {
             const int64_t r = r0 + tr, k = k0 + kk;
@@ -291,16 +316,23 @@ static int launch_stage(const StageParams& p, int64_t batch, bool has_kind[5], c
             bool vec = p.s_r % 4 == 0 && p.s_b % 4 == 0;
             for (int k = 0; k < p.planes; ++k)
                 if (reinterpret_cast<uintptr_t>(p.plane[k].src) % 16) vec = false;
-            const int64_t total = batch * p.planes * p.rows * (p.Kp / 4);
-            const int grid = static_cast<int>(std::min<int64_t>(ceil_div(total, 256), static_cast<int64_t>(num_sms()) * 32));
-            split_direct_kernel<<<grid, 256, 0, stream>>>(p, batch, vec ? 1 : 0);
+            const int64_t kv = p.Kp / 4;
+            int lpl = 1;
+            while (lpl < 32 && lpl < kv) lpl <<= 1;
+            const int64_t lines = batch * p.planes * p.rows;
+            const int64_t warps = ceil_div(lines, 32 / lpl);
+            const int grid = static_cast<int>(std::min<int64_t>(ceil_div(warps, 8), static_cast<int64_t>(num_sms()) * 16));
+            split_direct_kernel<<<grid, 256, 0, stream>>>(p, batch, vec ? 1 : 0, lpl);
             PK_CHECK_LAUNCH("pk_poly_gemm: split kernel launch");
             return PK_OK;
         }
         if (p.s_r == 1 && ceil_div(p.rows, 64) <= 65535 && batch * p.planes <= 65535) {
             dim3 grid(static_cast<unsigned>(ceil_div(p.Kp, 64)), static_cast<unsigned>(ceil_div(p.rows, 64)),
                       static_cast<unsigned>(batch * p.planes));
-            split_transpose_kernel<<<grid, 256, 0, stream>>>(p);
+            bool vec = p.s_k % 4 == 0 && p.s_b % 4 == 0;
+            for (int k = 0; k < p.planes; ++k)
+                if (reinterpret_cast<uintptr_t>(p.plane[k].src) % 16) vec = false;
+            split_transpose_kernel<<<grid, 256, 0, stream>>>(p, vec ? 1 : 0);
             PK_CHECK_LAUNCH("pk_poly_gemm: split transpose kernel launch");
             return PK_OK;
         }
