@@ -444,7 +444,7 @@ struct TcConfig {
     static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
     static_assert(STAGES >= 2, "need at least two pipeline stages");
-    static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+    static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
 };
 
 __device__ __forceinline__ void store_row_chunk(const TcParams& p, int plane, int b, int row, int col0,
@@ -1443,7 +1443,11 @@ static int poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N,
         const TcOperand ob{g.b_mode, N, K, g.Kp, batch, b_planes, b_bs, b_cs, b_rs,
                            static_cast<const char*>(ws_b), g.b_first.data(), g.b_subs, f16};
         tp.in_fmt = f16 ? 0 : 1;
+        // N <= 64 (e.g. attention head dimensions): 64-column tiles; a 128-column tile would spend
+        // half of every MMA on the zero fill beyond N
+        const bool narrow = N <= 64;
         if (dtype == PK_F32) {
+            if (narrow) return launch_tc<64, true>(tp, oa, ob, stream);
             return wide ? launch_tc<256, true>(tp, oa, ob, stream) : launch_tc<128, true>(tp, oa, ob, stream);
         }
         // degree <= 3 with enough output tiles: every plane of a tile at once (operands loaded once
@@ -1456,6 +1460,7 @@ static int poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N,
                 default: return launch_allplanes<4>(tp, oa, ob, stream);
             }
         }
+        if (narrow) return launch_tc<64, false>(tp, oa, ob, stream);
         return wide ? launch_tc<256, false>(tp, oa, ob, stream) : launch_tc<128, false>(tp, oa, ob, stream);
     }
 

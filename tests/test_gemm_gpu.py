@@ -181,6 +181,30 @@ def test_banded_product(dtype, band, offset):
     assert max(ref.plane_errors(out, want)) <= tol
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("N", [1, 17, 64])
+@pytest.mark.parametrize("n", [1, 3])
+def test_narrow_products(dtype, N, n):
+    """N <= 64 runs in 64-column tiles: plain, B read transposed, batched, banded, accumulated."""
+    from polytensors_b200 import _kernels
+
+    tol = {torch.bfloat16: 1e-2, torch.float32: 1e-4}[dtype]
+    batch, M, K = 2, 300, 260
+    A, B = series((batch, M, K), n, 51, dtype), series((batch, K, N), n, 52, dtype)
+    check(A, B, tol)
+    Bt = [b.transpose(1, 2).contiguous() for b in B]  # rows of B contiguous in memory
+    got = _kernels.poly_matmul(cuda(A), [b.cuda().transpose(1, 2) for b in Bt])
+    check(A, B, tol, got=got)
+    keep = torch.arange(K).view(1, K) >= torch.arange(M).view(M, 1) - 40
+    Ab = [a * keep.to(a.dtype) for a in A]
+    check(Ab, B, tol, got=_kernels.poly_matmul(cuda(Ab), cuda(B), band=1, band_offset=-40))
+    C0 = series((batch, M, N), n, 53, dtype)
+    out = cuda(C0)
+    _kernels.poly_matmul(cuda(A), cuda(B), out=out, accumulate=True)
+    want = [w + c.double() for w, c in zip(ref.poly_matmul([a.double() for a in A], [b.double() for b in B]), C0)]
+    assert max(ref.plane_errors(out, want)) <= tol
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("n", [1, 2, 3])
 @pytest.mark.parametrize("layout", ["k", "rows"])
