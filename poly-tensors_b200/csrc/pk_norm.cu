@@ -504,7 +504,7 @@ __global__ void __launch_bounds__(256, 2) rmsnorm_bwd_cluster_kernel(const NormP
 // parity), so no cluster-wide barrier (and no release of the previous row's stores) sits in the
 // row loop.
 template <typename T, int NP, int STEPS, int CL>
-__global__ void __launch_bounds__(512, 1) rmsnorm_bwd_stream_kernel(const NormParams p) {
+__global__ void __launch_bounds__(STEPS == 1 ? 512 : 256, 1) rmsnorm_bwd_stream_kernel(const NormParams p) {
     using C = float;
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
@@ -765,8 +765,11 @@ static int bwd_stream(NormParams& p, void* const* dw, void* ws, size_t ws_bytes,
     const int64_t half = p.cols / CL, quads = half / ROW_VEC;
     const size_t smem = 2 * 2 * static_cast<size_t>(NP) * half * sizeof(T);
     if (quads < 64 || quads > 512 || smem > 200 * 1024) return 1;
-    const int threads = static_cast<int>(round_up(quads, 32));
-    auto kern = rmsnorm_bwd_stream_kernel<T, NP, 1, CL>;
+    // two column quads per thread once a half row has 256 of them: the per-row work (block
+    // reduction, exchange, rsqrt-series coefficients) is shared by twice the elements
+    const int steps = quads >= 256 ? 2 : 1;
+    const int threads = static_cast<int>(round_up(ceil_div(quads, steps), 32));
+    auto kern = steps == 2 ? rmsnorm_bwd_stream_kernel<T, NP, 2, CL> : rmsnorm_bwd_stream_kernel<T, NP, 1, CL>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_fail(e, "pk_rmsnorm_bwd: cudaFuncSetAttribute");
     cudaLaunchConfig_t cfg{};
