@@ -297,7 +297,10 @@ PK_API int pk_flash_attn_fwd(int dtype, int degree, int64_t bh, int64_t L, int64
  * rows contiguous and the other strides multiples of 8 elements (PK_ERR_UNSUPPORTED
  * otherwise).  Row values (stats, dsum): float32 [batch][M][degree+1], batch entries
  * stats_bs / dsum_bs floats apart.  Query index of row r is r + causal_shift; with causal
- * != 0, key j is admissible for it when j <= r + causal_shift.
+ * != 0, key j is admissible for it when j <= r + causal_shift.  causal == 1 writes the zeros
+ * of every inadmissible entry; causal == 2 writes them only within 192 keys of the admissible
+ * region (the most that band-limited consumers such as pk_poly_gemm_banded read there) and
+ * leaves 64-key tiles lying wholly further out unwritten.
  *
  * pk_attn_probs_gemm:   probs = exp-series(scale * Q K^T - stats) on admissible keys, 0 elsewhere
  *                       (pk_poly_gemm followed by pk_attn_probs with the forward's stats).

@@ -46,6 +46,7 @@ constexpr int AG_SMEM_BYTES = AG_SMEM_BUDGET + 1024 + 512;
 constexpr int AG_CHUNK = 8;                       // B tiles per work unit
 constexpr int AG_MAX_NP = 4;
 constexpr int AG_MAX_SHAPES = 4096;               // unit shapes (chunk, row tile) the cost order holds
+constexpr int64_t AG_FAR_KEYS = 192;              // causal == 2: zero tiles written up to this far out
 
 enum { AG_PROBS = 0, AG_DSCORES = 1 };
 
@@ -62,6 +63,7 @@ struct AgParams {
     int a_bytes;       // resident A bytes (NP * kblocks * AG_A_BYTES)
     int a_mn, b_mn;
     int causal;
+    int skip_far;      // masked tiles starting more than AG_FAR_KEYS keys past their rows are not written
     int64_t shift;     // query index of row r is r + shift
     float scale;
     int vec_ok;        // 16-byte vector access to the output (and probability) planes
@@ -374,6 +376,12 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
           for (int tn = un.tn0; tn < un.tn1; ++tn) {
             const AgTile tc{un.b, un.tm, tn};
             bool masked_tile = ag_masked(p, tc);
+            if (masked_tile && p.skip_far) {
+                // far above the diagonal: no consumer reads these zeros (the decision depends on
+                // the tile only, so every warp of the CTA skips the same tiles)
+                const int64_t last_row = min(tc.tm * AG_BM + AG_BM - 1, p.M - 1);
+                if (static_cast<int64_t>(tc.tn) * AG_BN > last_row + p.shift + AG_FAR_KEYS) continue;
+            }
             const int64_t last_key = p.causal ? static_cast<int64_t>(r) + p.shift : static_cast<int64_t>(p.N) - 1;
             const bool live = MODE == AG_PROBS ? rv[0] < INFINITY : true;
             // tile entirely inside the matrix and below the causal diagonal: no per-element tests
@@ -623,6 +631,7 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
     p.a_mn = am == OPM_MNMAJOR;
     p.b_mn = bm == OPM_MNMAJOR;
     p.causal = causal ? 1 : 0;
+    p.skip_far = causal == 2 ? 1 : 0;
     p.shift = causal_shift;
     p.scale = static_cast<float>(scale);
     p.c_bs = c_bs;

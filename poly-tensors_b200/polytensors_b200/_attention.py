@@ -168,7 +168,9 @@ def forward_planes(Q, Kp, V, causal, scale, stats=None):
 
 def _score_gemm(name, A, B, out, rows, scale, causal, shift, probs=None):
     """pk_attn_probs_gemm / pk_attn_dscores_gemm on (hb, M, K) x (hb, K, N) bf16 plane views;
-    ``rows``: float32 (hb, M, n+1) view (statistics or dsum) with unit inner strides."""
+    ``rows``: float32 (hb, M, n+1) view (statistics or dsum) with unit inner strides.  ``causal``:
+    False, True, or 2 (causal; tiles lying wholly more than 192 keys past the admissible region are
+    left unwritten, for consumers that only read near it)."""
     hb, M, Kd = A[0].shape
     N = B[0].shape[2]
     pa, k1 = _lib.pointer_array(A)
@@ -179,14 +181,14 @@ def _score_gemm(name, A, B, out, rows, scale, causal, shift, probs=None):
     stream = K._stream(A[0].device)
     if name == "probs":
         status = lib.pk_attn_probs_gemm(_lib.PK_BF16, len(A) - 1, hb, M, N, Kd, pa, *a_s, pb, *b_s, po, o_s[0], o_s[1],
-                                        rows.data_ptr(), rows.stride(0), float(scale), 1 if causal else 0, shift,
+                                        rows.data_ptr(), rows.stride(0), float(scale), int(causal), shift,
                                         stream)
     else:
         pp, k4 = _lib.pointer_array(probs)
         p_s = probs[0].stride()
         status = lib.pk_attn_dscores_gemm(_lib.PK_BF16, len(A) - 1, hb, M, N, Kd, pa, *a_s, pb, *b_s, pp, p_s[0],
                                           p_s[1], rows.data_ptr(), rows.stride(0), float(scale),
-                                          1 if causal else 0, shift, po, o_s[0], o_s[1], stream)
+                                          int(causal), shift, po, o_s[0], o_s[1], stream)
     _lib.check(status, f"pk_attn_{name}_gemm")
     return out
 
@@ -202,17 +204,20 @@ def _fused_backward(Q, Kp, V, dO, dsum, stats, causal, scale, dQ, dK, dV):
     per_head = 2 * NP * L * S * Q[0].element_size()
     hb = max(1, min(BH, _FUSED_BLOCK_BYTES // max(per_head, 1)))
     lower, upper = (1, 2) if causal else (0, 0)
+    # the banded products read the score planes only near the diagonal (k-block rounding), so the
+    # score kernels leave the zeros of tiles far above it unwritten
+    mode = 2 if causal else 0
     for h0 in range(0, BH, hb):
         hs = slice(h0, min(BH, h0 + hb))
         hbn = hs.stop - hs.start
         Pr = [torch.empty(hbn, L, S, dtype=Q[0].dtype, device=Q[0].device) for _ in Q]
         _score_gemm("probs", [q[hs] for q in Q], [k[hs].transpose(1, 2) for k in Kp], Pr, stats[hs], scale,
-                    causal, 0)
+                    mode, 0)
         if dV is not None:
             K.poly_matmul([p.transpose(1, 2) for p in Pr], [g[hs] for g in dO], out=[t[hs] for t in dV], band=lower)
         dS = [torch.empty_like(p) for p in Pr]
         _score_gemm("dscores", [g[hs] for g in dO], [v[hs].transpose(1, 2) for v in V], dS, dsum[hs], scale,
-                    causal, 0, probs=Pr)
+                    mode, 0, probs=Pr)
         del Pr
         if dQ is not None:
             K.poly_matmul(dS, [k[hs] for k in Kp], out=[t[hs] for t in dQ], band=upper)

@@ -372,6 +372,71 @@ def test_bf16_backward_with_score_epilogues(n, shape, causal):
         assert_close(coeffs(t.grad), w, 3e-2, name)
 
 
+def test_far_masked_score_tiles_left_unwritten():
+    """causal == 2: the score kernels leave the 64-key tiles lying wholly more than 192 keys past the
+    causal boundary of their 128-row tile unwritten, and write every other entry exactly as
+    causal == 1 does (zeros included)."""
+    from polytensors_b200 import _attention
+
+    n, shape, scale = 3, (1, 2, 1000, 64), 1 / 64 ** 0.5
+    Q, Kp = (series(shape, n, s, torch.bfloat16) for s in (81, 82))
+    flat = [_attention._flat([p.cuda() for p in X], shape) for X in (Q, Kp)]
+    BH, L = flat[0][0].shape[:2]
+    V = [torch.zeros_like(q) for q in flat[0]]
+    stats = torch.empty(BH, L, n + 1, dtype=torch.float32, device="cuda")
+    _attention.flash_forward(flat[0], flat[1], V, True, scale, stats)
+    outs = {}
+    for mode in (1, 2):
+        P = [torch.full((BH, L, L), float("nan"), dtype=torch.bfloat16, device="cuda") for _ in range(n + 1)]
+        _attention._score_gemm("probs", flat[0], [k.transpose(1, 2) for k in flat[1]], P, stats, scale, mode, 0)
+        outs[mode] = P
+    rows = torch.arange(L, device="cuda")
+    last_row = torch.clamp(rows // 128 * 128 + 127, max=L - 1)
+    far = (rows // 64 * 64)[None, :] > last_row[:, None] + 192
+    assert far.any()
+    for a, b in zip(outs[1], outs[2]):
+        assert not torch.isnan(a).any()
+        assert torch.isnan(b[:, far]).all()
+        assert torch.equal(b[:, ~far], a[:, ~far])
+
+
+@pytest.mark.parametrize("shape", [(1, 2, 1000, 64), (2, 2, 700, 128)])
+def test_attention_backward_reads_only_written_memory(shape, monkeypatch):
+    """Every buffer the attention code allocates starts as NaN, so a read of anything left
+    unwritten (the far score tiles above all) would reach the gradients."""
+    from polytensors_b200 import PolyTensor, _attention
+
+    real = _attention.torch
+
+    class Poisoned:
+        def __getattr__(self, name):
+            return getattr(real, name)
+
+        @staticmethod
+        def empty(*args, **kw):
+            t = real.empty(*args, **kw)
+            return t.fill_(float("nan")) if t.is_floating_point() else t
+
+        @staticmethod
+        def empty_like(x, *args, **kw):
+            t = real.empty_like(x, *args, **kw)
+            return t.fill_(float("nan")) if t.is_floating_point() else t
+
+    monkeypatch.setattr(_attention, "torch", Poisoned())
+    n = 3
+    Q, Kp, V, G = (series(shape, n, s, torch.bfloat16) for s in (91, 92, 93, 94))
+    ref64 = [[p.double() for p in s] for s in (Q, Kp, V, G)]
+    fn = lambda q, k, v: ref.attention(q, k, v, is_causal=True)
+    want = ref.series_vjp(fn, ref64[:3], ref64[3])
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        q, k, v = (poly(s, requires_grad=True) for s in (Q, Kp, V))
+        o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+        o.backward(poly(G))
+    for name, t, w in (("dq", q, want[0]), ("dk", k, want[1]), ("dv", v, want[2])):
+        assert all(torch.isfinite(c).all() for c in coeffs(t.grad)), name
+        assert_close(coeffs(t.grad), w, 3e-2, name)
+
+
 def test_flash_forward_row_statistics():
     """pk_flash_attn_fwd's optional row statistics equal those of pk_attn_probs on the same scores."""
     from polytensors_b200 import _attention, _kernels
