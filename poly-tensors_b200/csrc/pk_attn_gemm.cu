@@ -39,8 +39,8 @@ constexpr int AG_A_BYTES = AG_BM * TC_BK * 2;     // one plane's 128 x 64 A k-bl
 constexpr int AG_B_BYTES = AG_BN * TC_BK * 2;     // one plane's 64 x 64 B k-block (a ring stage)
 constexpr int AG_MAX_K = 128;                     // reduction held resident (head dimension)
 constexpr int AG_MAX_STAGES = 24;
-constexpr int AG_STAGE_OUT = 32 * AG_BN * 2;      // one lane quadrant's 32 x 64 block of one plane, bf16
-constexpr int AG_OUT_BYTES = 4 * 2 * AG_STAGE_OUT; // 4 quadrants x 2 buffers (output staging for TMA stores)
+constexpr int AG_WARP_OUT = 32 * 16 * 2;          // one epilogue warp's 32 rows x 16 columns of one plane, bf16
+constexpr int AG_OUT_BYTES = AG_EPI_WARPS * 2 * AG_WARP_OUT;  // 2 buffers per epilogue warp (TMA-store staging)
 constexpr int AG_SMEM_BUDGET = 220 * 1024;        // resident A + B ring + output staging
 constexpr int AG_SMEM_BYTES = AG_SMEM_BUDGET + 1024 + 512;
 constexpr int AG_CHUNK = 8;                       // B tiles per work unit
@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* a_res = smem;                // [plane][kblock] 16 KB boxes
     uint8_t* ring = smem + p.a_bytes;     // B stages, 8 KB each
-    uint8_t* out_stage = smem + AG_SMEM_BUDGET - AG_OUT_BYTES;  // [quadrant][buffer] 4 KB blocks
+    uint8_t* out_stage = smem + AG_SMEM_BUDGET - AG_OUT_BYTES;  // [epilogue warp][buffer] 1 KB blocks
     uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + AG_SMEM_BUDGET);
     uint64_t* empty_bar = full_bar + AG_MAX_STAGES;
     uint64_t* acc_full = empty_bar + AG_MAX_STAGES;
@@ -491,30 +491,26 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
                 }
             }
             if (p.tma_store) {
-                // Per plane: the quadrant's four warps write their 32 rows x 16 columns into the
-                // quadrant's staging block (128-byte swizzle: 16-byte chunk j of row t sits at chunk
-                // j ^ (t & 7)), then one thread stores the 32 x 64 block with TMA.  Two blocks per
-                // quadrant alternate; a block is rewritten only after its previous store has read it.
-                const int q = warp & 3;
-                const bool elected = grp == 0 && lane == 0;
+                // Per plane: the warp writes its 32 rows x 16 columns into its own staging block
+                // (row t at 32 t bytes) and its lane 0 stores the block with TMA, so no other warp
+                // takes part and the only synchronisation is within the warp.  Two blocks per warp
+                // alternate; a block is rewritten only after its previous store has read it.
+                const int q = warp & 3, ew = warp - 2;
 #pragma unroll
                 for (int k = 0; k < NP; ++k) {
-                    uint8_t* blk = out_stage + (q * 2 + (k & 1)) * AG_STAGE_OUT;
-                    if (elected) {
+                    uint8_t* blk = out_stage + (ew * 2 + (k & 1)) * AG_WARP_OUT;
+                    if (lane == 0) {
                         if (k == 0) bulk_wait_group_read<0>();
                         else bulk_wait_group_read<1>();
                     }
-                    named_barrier_sync(1 + q, 128);
-                    uint8_t* row = blk + lane * 128;
-                    const int j0 = grp * 2;
-                    *reinterpret_cast<uint4*>(row + (((j0 + 0) ^ (lane & 7)) << 4)) =
-                        make_uint4(ypk[k][0], ypk[k][1], ypk[k][2], ypk[k][3]);
-                    *reinterpret_cast<uint4*>(row + (((j0 + 1) ^ (lane & 7)) << 4)) =
-                        make_uint4(ypk[k][4], ypk[k][5], ypk[k][6], ypk[k][7]);
+                    __syncwarp();
+                    uint8_t* row = blk + lane * 32;
+                    *reinterpret_cast<uint4*>(row) = make_uint4(ypk[k][0], ypk[k][1], ypk[k][2], ypk[k][3]);
+                    *reinterpret_cast<uint4*>(row + 16) = make_uint4(ypk[k][4], ypk[k][5], ypk[k][6], ypk[k][7]);
                     fence_proxy_async();
-                    named_barrier_sync(1 + q, 128);
-                    if (elected) {
-                        tma_store_3d(&maps.c[k], blk, tc.tn * AG_BN, tc.tm * AG_BM + q * 32, tc.b);
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_3d(&maps.c[k], blk, tc.tn * AG_BN + grp * 16, tc.tm * AG_BM + q * 32, tc.b);
                         bulk_commit_group();
                     }
                 }
@@ -541,8 +537,8 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
             }
           }
         }
-        if (p.tma_store && grp == 0 && lane == 0)
-            bulk_wait_group_all();  // this quadrant's stores have completed before the CTA exits
+        if (p.tma_store && lane == 0)
+            bulk_wait_group_all();  // this warp's stores have completed before the CTA exits
     }
 
     tc_fence_before();
@@ -572,6 +568,19 @@ static int launch_ag(const AgMaps& maps, AgParams& p, cudaStream_t stream) {
     prof_end(MODE == AG_PROBS ? "attn_probs_gemm" : "attn_dscores_gemm", stream, tok);
     PK_CHECK_LAUNCH("pk_attn_score_gemm: kernel launch");
     return PK_OK;
+}
+
+// Output plane map for the epilogue's TMA stores: boxes of 16 columns (32 bytes) x 32 rows, no
+// swizzle (one epilogue warp's block of one plane).
+static int encode_out_map(CUtensorMap* map, const void* base, int64_t cols, int64_t rows, int64_t batch,
+                          int64_t row_bytes, int64_t batch_bytes) {
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                                static_cast<cuuint64_t>(batch)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(batch_bytes)};
+    const cuuint32_t box[3] = {16u, 32u, 1u};
+    CUresult r = encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                              CU_TENSOR_MAP_SWIZZLE_NONE);
+    return r == CUDA_SUCCESS ? PK_OK : fail(PK_ERR_CUDA, "pk_attn_score_gemm: cuTensorMapEncodeTiled failed");
 }
 
 static int attn_score_gemm(int mode, const char* what, int dtype, int degree, int64_t batch, int64_t M, int64_t N,
@@ -655,7 +664,7 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
     if (tstore) {
         const int64_t sb = batch > 1 ? c_bs * 2 : M * c_rs * 2;
         for (int k = 0; k < P && tstore; ++k)
-            if (encode_map3(&maps.c[k], c_planes[k], N, M, batch, c_rs * 2, sb, 32) != PK_OK) tstore = false;
+            if (encode_out_map(&maps.c[k], c_planes[k], N, M, batch, c_rs * 2, sb) != PK_OK) tstore = false;
     }
     p.tma_store = tstore ? 1 : 0;
     p.rowv = static_cast<const float*>(rowv);
