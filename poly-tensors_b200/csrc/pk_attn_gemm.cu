@@ -53,7 +53,7 @@ enum { AG_PROBS = 0, AG_DSCORES = 1 };
 struct AgMaps {
     CUtensorMap a[AG_MAX_NP];
     CUtensorMap b[AG_MAX_NP];
-    CUtensorMap c[AG_MAX_NP];  // output planes, boxes of 64 columns x 32 rows (TMA stores)
+    CUtensorMap c[AG_MAX_NP];  // output planes, boxes of 16 columns x 32 rows (per-warp TMA stores)
 };
 
 struct AgParams {
