@@ -2,15 +2,19 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl reference]
 
-Default workload (configs[1] of the baseline): the polynomial matrix product
-C_k = sum_{i+j=k} A_i B_j of float32 PolyTensors, M = N = K = 8192, degree 4, planes
-N(0,1)/k!.  A "step" is one product over one pair of resident operands; the metric is
-coefficient TFLOP/s = 2*M*N*K*(n+1)(n+2)/2 per step (algorithmic work, the split-bf16
-tensor-core passes are not counted).  With N > 1 (torchrun) every rank multiplies its own
-operands (replicas, weak scaling) and the value is total work / max-over-ranks time.
+Default workload: configs[4], one SGD step of the 12-layer d768 transformer with PolyTensor
+parameters (degree 3, float32) over the global batch of 64 x 1024 tokens.  With N > 1
+(torchrun, one rank per GPU) the batch is sharded over the ranks and the gradient series are
+averaged by one bucketed NCCL all-reduce per step (strong scaling); value = tokens/s of the
+whole job, max-over-ranks device time.  The line also carries, under ``poly_matmul``, the
+configs[1] float32 polynomial matrix product (M = N = K = 8192, degree 4; replicas on every
+rank) with its own roofline, e2e, row-sampled parity and CPU baseline; and under ``parity`` the
+training forward + backward checked against the oracle on a bounded full-width sample.
 
-``--impl reference`` times the reference algorithm on the host CPU instead (the oracle
-restatement of src/polytensors/_plain.py:118-128, all host threads, a bounded row sample).
+``--impl reference`` times the reference's CPU path on the host cores instead (the oracle
+restatement of the reference's plain-range rules, all host threads, bounded samples).  Other
+``--workload`` values (poly_matmul, norm_ce, attention, poly_matmul_sweep, ...) are per-op
+measurements of configs[1-3].
 """
 
 import argparse
@@ -32,7 +36,8 @@ import torch  # noqa: E402
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
-# Measured DRAM traffic per product launch (ncu, B200) for the configurations it was captured on.
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one product launch, from the ncu
+# capture summarised in profiles/tc_poly_gemm_f32_n4_2048_and_8192.md, per configuration.
 _GEMM_TRAFFIC = {(8192, 4, "float32"): 56470521088 + 1338964736}
 
 WORKLOADS = {
@@ -146,7 +151,23 @@ def cpu_matmul_rate(cfg, threads, target_s=12.0):
     return rate, f"{rows} of {M} rows of A, full B ({cfg['dtype']}, degree {n}), {dt:.1f} s"
 
 
-def run_matmul(args, cfg, rank, world, device):
+def matmul_parity(A_host, B_host, C, rows=64, seed=99):
+    """Row-sampled parity of one full-size product: rows of A times the whole of B through the
+    float64 oracle on the CPU, against the same rows of the GPU product."""
+    from oracle import polyref
+
+    M = A_host[0].shape[0]
+    idx = torch.randperm(M, generator=torch.Generator().manual_seed(seed))[:rows].sort().values
+    want = polyref.poly_matmul([a[idx].double() for a in A_host], [b.double() for b in B_host])
+    got = [c[idx.to(c.device)].cpu() for c in C]
+    errs = polyref.plane_errors(got, want)
+    return {"max_plane_err": max(errs), "per_plane": errs, "tol": 1e-4 if A_host[0].dtype == torch.float32 else 1e-10,
+            "metric": "per coefficient plane max|gpu - oracle| / max|oracle|",
+            "against": "oracle restatement of plain_polynomial_product, float64, CPU",
+            "sample": f"{rows} random rows of A times the full B (seeded)"}
+
+
+def run_matmul(args, cfg, rank, world, device, parity=False):
     from polytensors_b200 import _kernels, _lib
 
     dtype = getattr(torch, cfg["dtype"])
@@ -166,10 +187,13 @@ def run_matmul(args, cfg, rank, world, device):
         return _kernels.poly_matmul(A, B)
 
     for _ in range(args.warmup):
-        step()
+        C = step()
     torch.cuda.synchronize(device)
+    parity_result = matmul_parity(A_host, B_host, C) if parity else None
+    del C
     barrier(world)
     _lib.profile_query("poly_gemm")
+    _lib.launch_count(reset=True)
     _lib.profile_enable(True)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(device.index) as clocks:
@@ -182,6 +206,7 @@ def run_matmul(args, cfg, rank, world, device):
         torch.cuda.synchronize(device)
         barrier(world)
     _lib.profile_enable(False)
+    gpu_launches = _lib.launch_count()
     ms = start.elapsed_time(end) / args.steps
     kernel_ms, launches = _lib.profile_query("poly_gemm")
     ms_max = max_over_ranks(ms, world, device)
@@ -256,9 +281,8 @@ def run_matmul(args, cfg, rank, world, device):
         "vs_baseline": None,
         "dtype": "f32 (bf16x3 split on tcgen05, fp32 accumulate)" if dtype == torch.float32 else cfg["dtype"],
         "data": "synthetic: planes N(0,1)/k!, seeded",
-        "config": {"workload": f"poly_matmul M=N=K={M} degree {n} {cfg['dtype']}", "M": M, "N": N, "K": K,
-                   "degree": n, "dtype": cfg["dtype"], "parallelism": f"replicas x{world}",
-                   "l2": "inputs larger than L2 (no flush)"},
+        "config": matmul_config(cfg),
+        "parallelism": f"replicas x{world}",
         "e2e": {"value": world * flops / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes, "ms_per_step": e2e_ms,
                 "wall_ms_per_step": e2e_wall,
@@ -273,7 +297,8 @@ def run_matmul(args, cfg, rank, world, device):
                      "note": "algorithmic flops; the float32 path issues 3 bf16 MMAs per product, "
                              "so its tensor-pipe ceiling is peak/3" if dtype == torch.float32 else
                              "float64 runs on DMMA; bf16 peak shown for reference"},
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": gpu_launches,
+        "parity": parity_result,
         "kernel_ms_per_launch": kernel_ms / launches if launches else None,
         "clocks": clocks.summary(),
     }
@@ -518,28 +543,46 @@ def run_attention(args, rank, world, device):
     }
 
 
+def transformer_init(layers=12, d=768, heads=12, mlp=3072, vocab=32000, degree=3, seed=0, higher_seed=None):
+    """Parameter series of the configs[4] transformer on the CPU: name -> list of degree+1 planes.
+    Weights N(0, 0.02), norm weights 1; higher coefficients zero (the config), or with
+    ``higher_seed`` N(0, 0.02)/k! (the parity sample, so that every coefficient plane of the
+    forward and backward is exercised)."""
+    g = torch.Generator().manual_seed(seed)
+    gh = torch.Generator().manual_seed(higher_seed) if higher_seed is not None else None
+
+    def series(*shape, ones=False):
+        base = torch.ones(*shape) if ones else 0.02 * torch.randn(*shape, generator=g)
+        if gh is None:
+            return [base] + [torch.zeros(*shape) for _ in range(degree)]
+        return [base] + [0.02 * torch.randn(*shape, generator=gh) / math.factorial(k) for k in range(1, degree + 1)]
+
+    p = {"emb": series(vocab, d)}
+    for l in range(layers):
+        p[f"n1.{l}"], p[f"n2.{l}"] = series(d, ones=True), series(d, ones=True)
+        for nm in ("wq", "wk", "wv", "wo"):
+            p[f"{nm}.{l}"] = series(d, d)
+        p[f"w1.{l}"], p[f"w2.{l}"] = series(mlp, d), series(d, mlp)
+    p["nf"] = series(d, ones=True)
+    p["head"] = series(vocab, d)
+    return p
+
+
 class TinyGPT:
     """decoder-only transformer with PolyTensor parameters (degree 3, float32):
-    embedding, 12 x [RMSNorm, q/k/v/o linears, causal SDPA, RMSNorm, GELU MLP], RMSNorm, untied head."""
+    embedding, L x [RMSNorm, q/k/v/o linears, causal SDPA, RMSNorm, GELU MLP], RMSNorm, untied head."""
 
-    def __init__(self, device, layers=12, d=768, heads=12, mlp=3072, vocab=32000, degree=3, seed=0):
+    def __init__(self, device, init, layers=12, d=768, heads=12, vocab=32000, degree=3):
         from polytensors_b200 import PolyTensor
 
-        g = torch.Generator().manual_seed(seed)
         self.layers, self.d, self.heads, self.vocab, self.degree = layers, d, heads, vocab, degree
-
-        def param(*shape, ones=False):
-            base = torch.ones(*shape) if ones else 0.02 * torch.randn(*shape, generator=g)
-            return torch.nn.Parameter(PolyTensor((base.to(device),), degree=degree))
-
-        self.p = {"emb": param(vocab, d)}
-        for l in range(layers):
-            self.p[f"n1.{l}"], self.p[f"n2.{l}"] = param(d, ones=True), param(d, ones=True)
-            for nm in ("wq", "wk", "wv", "wo"):
-                self.p[f"{nm}.{l}"] = param(d, d)
-            self.p[f"w1.{l}"], self.p[f"w2.{l}"] = param(mlp, d), param(d, mlp)
-        self.p["nf"] = param(d, ones=True)
-        self.p["head"] = param(vocab, d)
+        self.p = {}
+        for name, planes in init.items():
+            if all(not bool(c.any()) for c in planes[1:]):
+                poly = PolyTensor((planes[0].to(device),), degree=degree)
+            else:
+                poly = PolyTensor(tuple(c.to(device) for c in planes))
+            self.p[name] = torch.nn.Parameter(poly)
 
     def parameters(self):
         return list(self.p.values())
@@ -561,71 +604,279 @@ class TinyGPT:
         return F.cross_entropy(logits.reshape(-1, self.vocab), tgt.reshape(-1)) * (1 - lam * Z)
 
 
-def run_train(args, rank, world, device):
-    """global batch 64 x seq 1024 sharded over the ranks, micro-batches of args.micro
-    sequences per rank with gradient accumulation, one bucketed NCCL all-reduce of the gradient
-    series, SGD(lr=0.1, foreach=False).  A timed step is the whole global batch (unless
-    --micro-batches bounds it); reports tokens/s and steps/s."""
+def oracle_train_sample(init, ids, layers, dtype, threads, d=768, heads=12, vocab=32000, lam=0.5):
+    """The reference algorithm for one configs[4] forward + backward on the host CPU: the oracle
+    restatement of the plain-range rules (embedding, RMSNorm, series linear, causal SDPA, GELU,
+    cross entropy, the (1 - lam Z) factor) with the swapped-cotangent series backward.
+    Returns (seconds, loss series, {name: gradient series})."""
+    from oracle import polyref as R
+
+    torch.set_num_threads(threads)
+    names = list(init)
+    inp, tgt = ids[:, :-1], ids[:, 1:]
+    n = len(init[names[0]]) - 1
+
+    def linear(X, W):
+        return R.cauchy(X, [w.t() for w in W], lambda a, b: a @ b)
+
+    def loss(*series):
+        p = dict(zip(names, series))
+        Bt, T = inp.shape
+        x = [w[inp] for w in p["emb"]]
+        for l in range(layers):
+            h = R.rms_norm(x, (d,), p[f"n1.{l}"])
+            split = lambda Y: [y.view(Bt, T, heads, d // heads).transpose(1, 2) for y in Y]   # noqa: E731
+            q, k, v = (split(linear(h, p[f"{nm}.{l}"])) for nm in ("wq", "wk", "wv"))
+            a = [y.transpose(1, 2).reshape(Bt, T, d) for y in R.attention(q, k, v, is_causal=True)]
+            x = [u + w for u, w in zip(x, linear(a, p[f"wo.{l}"]))]
+            h = R.rms_norm(x, (d,), p[f"n2.{l}"])
+            x = [u + w for u, w in zip(x, linear(R.gelu(linear(h, p[f"w1.{l}"])), p[f"w2.{l}"]))]
+        logits = linear(R.rms_norm(x, (d,), p["nf"]), p["head"])
+        ce = R.cross_entropy([z.reshape(-1, vocab) for z in logits], tgt.reshape(-1))
+        factor = [torch.tensor(1.0, dtype=dtype), torch.tensor(-lam, dtype=dtype)] + \
+                 [torch.tensor(0.0, dtype=dtype)] * (n - 1)   # 1 - lam Z, Z = (0, 1, 0, ...)
+        return R.cauchy(ce, factor)
+
+    series = [[c.to(dtype) for c in init[k]] for k in names]
+    seed = [torch.tensor(1.0, dtype=dtype)] + [torch.tensor(0.0, dtype=dtype)] * n
+    t0 = time.perf_counter()
+    leaves = [[c.detach().clone().requires_grad_(True) for c in X] for X in series]
+    out = loss(*leaves)
+    objective = sum((seed[k] * out[n - k]).sum() for k in range(n + 1))
+    flat = [c for X in leaves for c in X]
+    grads = torch.autograd.grad(objective, flat, allow_unused=True)
+    dt = time.perf_counter() - t0
+    result, pos = {}, 0
+    for name, X in zip(names, leaves):
+        g = [grads[pos + i] if grads[pos + i] is not None else torch.zeros_like(X[i]) for i in range(n + 1)]
+        pos += n + 1
+        result[name] = [g[n - j].detach() for j in range(n + 1)]
+    return dt, [c.detach() for c in out], result
+
+
+def train_config(layers):
+    """The configs[4] workload description, identical in both arms of the bench."""
+    return {"workload": f"train transformer layers={layers} d=768 heads=12 mlp=3072 vocab=32000 seq=1024 "
+                        f"global_batch=64 degree 3 float32 SGD(lr=0.1)",
+            "layers": layers, "d_model": 768, "heads": 12, "mlp": 3072, "vocab": 32000, "seq": 1024,
+            "global_batch": 64, "degree": 3, "dtype": "float32", "l2": "inputs and weights larger than L2 (no flush)"}
+
+
+def matmul_config(cfg):
+    M, n = cfg["M"], cfg["degree"]
+    return {"workload": f"poly_matmul M=N=K={M} degree {n} {cfg['dtype']}", "M": M, "N": cfg["N"], "K": cfg["K"],
+            "degree": n, "dtype": cfg["dtype"], "l2": "inputs larger than L2 (no flush)"}
+
+
+def train_sample_ids(batch, seq, seed=4321):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, 32000, (batch, seq + 1), generator=g)
+
+
+def train_parity_and_cpu(layers, device, threads, batch=1, seq=256):
+    """configs[4] at full width on a bounded sample (batch x seq tokens, parameters with nonzero
+    higher coefficients): the GPU forward + backward against the oracle in float64 (parity), and
+    the oracle in float32 timed on the host cores (the CPU baseline)."""
+    from oracle import polyref as R
     from polytensors_b200 import PolyTensor
+
+    init = transformer_init(layers=layers, seed=0, higher_seed=7)
+    ids = train_sample_ids(batch, seq)
+    model = TinyGPT(device, init, layers=layers)
+    Z = PolyTensor((torch.tensor(0.0, device=device), 1.0), degree=3)
+    dev_ids = ids.to(device)
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        loss = model.loss(dev_ids[:, :-1], dev_ids[:, 1:], Z, 0.5)
+        loss.backward()
+    got_loss = [c.detach().cpu() for c in loss.coeffs]
+    got = {k: [c.detach().cpu() for c in p.grad.coeffs] for k, p in model.p.items()}
+    del model, loss
+    torch.cuda.empty_cache()
+    _, want_loss, want = oracle_train_sample(init, ids, layers, torch.float64, threads)
+    loss_err = max(R.plane_errors(got_loss, want_loss))
+    grad_err, worst = 0.0, None
+    for k in want:
+        e = max(R.plane_errors(got[k], want[k]))
+        if e > grad_err:
+            grad_err, worst = e, k
+    dt, _, _ = oracle_train_sample(init, ids, layers, torch.float32, threads)
+    tokens = batch * seq
+    parity = {"max_plane_err": max(loss_err, grad_err), "loss_max_plane_err": loss_err,
+              "grad_max_plane_err": grad_err, "worst_grad": worst, "tol": 1e-4,
+              "metric": "per coefficient plane max|gpu - oracle| / max|oracle|",
+              "against": "oracle restatement of the reference's plain-range rules, float64, CPU",
+              "sample": f"forward + backward of the full-width model on {batch} x {seq} tokens, "
+                        "weights with N(0,0.02)/k! higher coefficients"}
+    cpu = {"value": tokens / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+           "sample": f"oracle forward + series backward, full width ({layers} layers), {batch} x {seq} tokens, "
+                     f"float32, {dt:.1f} s",
+           "extrapolated_s_per_step": dt * 64 * 1024 / tokens}
+    return parity, cpu
+
+
+def run_train(args, rank, world, device):
+    """configs[4] (the default workload): global batch 64 x seq 1024 sharded over the ranks,
+    micro-batches of args.micro sequences per rank with gradient accumulation, one bucketed
+    NCCL all-reduce of the gradient series, SGD(lr=0.1, foreach=False).  A timed step is the
+    whole global batch (unless --micro-batches bounds it); value = tokens/s of the whole job.
+    The configs[1] polynomial product is measured first on every rank and reported under
+    ``poly_matmul``."""
+    from polytensors_b200 import PolyTensor, _lib
     from polytensors_b200.parallel import allreduce_gradients
 
+    threads = os.cpu_count() or 1
+    extras = {}
+    if not args.no_matmul:
+        mm_args = argparse.Namespace(steps=min(args.steps, 10), warmup=max(args.warmup, 1))
+        mm = run_matmul(mm_args, WORKLOADS["poly_matmul"], rank, world, device, parity=(rank == 0))
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            rate, desc = cpu_matmul_rate(WORKLOADS["poly_matmul"], threads)
+            mm["cpu_baseline"] = {"value": rate, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc}
+        extras["poly_matmul"] = {k: mm.get(k) for k in ("metric", "value", "unit", "ms_per_step", "steps", "config",
+                                                        "e2e", "roofline", "parity", "cpu_baseline", "gpu_launches",
+                                                        "kernel_ms_per_launch", "clocks")}
+        torch.cuda.empty_cache()
+
+    parity = cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        parity, cpu = train_parity_and_cpu(args.layers, device, threads)
+
     seq, global_batch, n = 1024, 64, 3
-    model = TinyGPT(device, layers=args.layers)
+    model = TinyGPT(device, transformer_init(layers=args.layers, seed=0), layers=args.layers)
     opt = torch.optim.SGD(model.parameters(), lr=0.1, foreach=False)
     Z = PolyTensor((torch.tensor(0.0, device=device), 1.0), degree=n)
     per_rank = global_batch // world
     g = torch.Generator().manual_seed(1234)
-    ids = torch.randint(0, 32000, (global_batch, seq + 1), generator=g)[rank * per_rank:(rank + 1) * per_rank]
-    ids = ids.to(device)
+    ids_host = torch.randint(0, 32000, (global_batch, seq + 1), generator=g)[rank * per_rank:(rank + 1) * per_rank]
+    ids_host = ids_host.contiguous().pin_memory()
+    ids = ids_host.to(device)
     micro = min(args.micro, per_rank)
     n_micro = per_rank // micro if args.micro_batches <= 0 else min(args.micro_batches, per_rank // micro)
+    stream = torch.cuda.current_stream(device)
+    ar_events = []
 
-    def step():
+    def step(ids_dev, record_allreduce=False):
         opt.zero_grad(set_to_none=True)
+        total = None
         with PolyTensor.plain_range():
             for m in range(n_micro):
-                chunk = ids[m * micro:(m + 1) * micro]
+                chunk = ids_dev[m * micro:(m + 1) * micro]
                 with PolyTensor.retain_wrappers():
                     loss = model.loss(chunk[:, :-1], chunk[:, 1:], Z, 0.5) * (micro / per_rank)
                     loss.backward()
+                    planes = torch.stack([c.detach() for c in loss.coeffs])
+                    total = planes if total is None else total + planes
+            if record_allreduce:
+                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev[0].record(stream)
             allreduce_gradients(model.parameters())
+            if record_allreduce:
+                ev[1].record(stream)
+                ar_events.append(ev)
             with PolyTensor.retain_wrappers():
                 opt.step()
+        return total
 
-    ms, clocks = _timed(step, args.steps, args.warmup, device, world)
-    # device time per kernel family over one more step, with the library's launch timing on
-    # (outside the timed region: the per-launch events would perturb it)
-    from polytensors_b200 import _lib
+    for _ in range(args.warmup):
+        step(ids)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    _lib.launch_count(reset=True)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index) as clocks:
+        torch.cuda.synchronize(device)
+        barrier(world)
+        start.record(stream)
+        for _ in range(args.steps):
+            last = step(ids, record_allreduce=True)
+        end.record(stream)
+        torch.cuda.synchronize(device)
+        barrier(world)
+    launches = _lib.launch_count()
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps, world, device)
+    ar_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ar_events) / len(ar_events), world, device)
+    final_loss = [float(x) for x in last.cpu()]
 
+    # end to end through the public API: every step copies the rank's token ids in from pinned
+    # host memory and the loss series out to pinned host memory
+    e2e_steps = min(args.steps, 5)
+    loss_host = torch.empty(n + 1, dtype=torch.float32).pin_memory()
+    dev_ids = torch.empty_like(ids)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(e2e_steps):
+        dev_ids.copy_(ids_host, non_blocking=True)
+        loss_host.copy_(step(dev_ids), non_blocking=True)
+    e_end.record(stream)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_end) / e2e_steps, world, device)
+
+    # device time per kernel family and the products' algorithmic flops over one more step, with
+    # the library's launch timing on (outside the timed region: per-launch events perturb it)
     names = ("poly_gemm", "flash_attn_fwd", "attn_probs_gemm", "attn_dscores_gemm", "attn_probs", "attn_dscores",
              "rmsnorm_fwd", "rmsnorm_bwd", "series_map", "softmax_fwd", "softmax_bwd", "cross_entropy_fwd",
              "cross_entropy_bwd")
     for nm in names:
         _lib.profile_query(nm)
+    _lib.take_gemm_flops()
     _lib.profile_enable(True)
-    step()
+    step(ids)
     torch.cuda.synchronize(device)
     _lib.profile_enable(False)
+    gemm_flops = _lib.take_gemm_flops()
     breakdown = {}
     for nm in names:
         kt, kl = _lib.profile_query(nm)
         if kl:
             breakdown[nm] = {"ms_per_step": kt, "launches_per_step": kl}
+    gemm_ms = breakdown.get("poly_gemm", {}).get("ms_per_step")
+    pk, source = peaks()
+    peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+    achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms else None
     tokens = world * n_micro * micro * seq
     tps = tokens / (ms / 1e3)
-    return {
-        "metric": "train tokens/s (configs[4]: 12-layer d768 PolyTensor transformer, degree 3, float32)",
+    whole = n_micro * micro == per_rank
+    result = {
+        "metric": "train tokens/s (configs[4]: 12-layer d768 PolyTensor transformer, degree 3, float32, "
+                  "global batch 64 x 1024)",
         "value": tps, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic: uniform random token ids, N(0,0.02) weights with zero higher coefficients",
-        "config": {"workload": f"transformer layers={args.layers} d=768 heads=12 mlp=3072 vocab=32000 seq=1024 "
-                               f"global_batch=64 degree 3", "parallelism": f"dp{world}",
-                   "micro_batch": micro, "micro_batches_timed_per_rank": n_micro},
-        "steps_per_s": tps / (global_batch * seq) if n_micro * micro == per_rank else None,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32 (polynomial products as bf16x3 splits on tcgen05, fp32 accumulate)",
+        "data": "synthetic: uniform random token ids, random-init N(0,0.02) weights with zero higher coefficients",
+        "config": train_config(args.layers),
+        "parallelism": f"dp{world}", "micro_batch": micro, "micro_batches_per_rank": n_micro,
+        "steps_per_s": 1e3 / ms if whole else None,
         "extrapolated_steps_per_s": tps / (global_batch * seq),
+        "final_loss": final_loss,
+        "allreduce": {"ms_per_step": ar_ms, "share_of_step": ar_ms / ms,
+                      "what": "allreduce_gradients (pack, NCCL all-reduce AVG, unpack) per step, CUDA events on the "
+                              "compute stream, max over ranks"},
+        "e2e": {"value": world * n_micro * micro * seq / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": ids_host.numel() * ids_host.element_size() * world,
+                "d2h_bytes_per_step": (n + 1) * 4 * world, "ms_per_step": e2e_ms, "steps": e2e_steps,
+                "api": "PolyTensor API (F.embedding / F.linear / F.rms_norm / SDPA / F.gelu / F.cross_entropy, "
+                       "backward, SGD) with token ids copied in from pinned host memory and the loss series "
+                       "copied out every step"},
+        "roofline": {"bound": "tensor", "kernel": "polynomial products (tc_poly_gemm / tc_allplanes)",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak if achieved else None, "traffic": None,
+                     "peak_source": f"bf16_tflops_sustained ({source}): a kernel timed inside a long step",
+                     "device_ms_per_step": gemm_ms, "algorithmic_tflop_per_step": gemm_flops / 1e12,
+                     "note": "algorithmic flops of the product launches as issued (float32 products execute "
+                             "3 bf16 MMAs each); traffic: see the profiles summary"},
+        "step_tflops": gemm_flops / (ms / 1e3) / 1e12,
+        "gpu_launches": launches,
+        "gpu_launches_per_step": launches / args.steps,
         "kernels": breakdown,
-        "clocks": clocks,
+        "parity": parity,
+        "cpu_baseline": cpu,
+        "clocks": clocks.summary(),
     }
+    result.update(extras)
+    return result
 
 
 def run_matmul_sweep(args, rank, world, device):
@@ -681,24 +932,62 @@ def max_over_ranks(x, world, device):
 
 
 def reference_arm(args, cfg):
+    """--impl reference for the poly_matmul workload: the reference algorithm (oracle restatement
+    of plain_polynomial_product) on all host cores over bounded row samples of the same config."""
     threads = os.cpu_count() or 1
-    samples = []
-    for _ in range(max(1, args.warmup) if args.warmup else 0):
-        pass
-    desc = ""
+    samples, desc = [], ""
+    if args.warmup:
+        cpu_matmul_rate(cfg, threads, target_s=2.0)
     for _ in range(args.steps):
         rate, desc = cpu_matmul_rate(cfg, threads, target_s=8.0)
         samples.append(rate)
     value = statistics.median(samples)
+    M, n = cfg["M"], cfg["degree"]
     return {
         "impl": "reference",
-        "metric": f"poly-matmul coeff TFLOP/s ({cfg['dtype']}, M=N=K={cfg['M']}, degree {cfg['degree']})",
+        "metric": f"poly-matmul coeff TFLOP/s ({cfg['dtype']}, M=N=K={M}, degree {n})",
         "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"],
         "data": "synthetic: planes N(0,1)/k!, seeded",
-        "config": {"workload": f"poly_matmul M=N=K={cfg['M']} degree {cfg['degree']} {cfg['dtype']}"},
+        "config": matmul_config(cfg),
+        "parallelism": "host CPU",
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def reference_arm_train(args, budget_s=150.0):
+    """--impl reference for the default (configs[4] training) workload: the reference algorithm
+    (oracle restatement of its plain-range rules) for the full-width model's forward and series
+    backward on the host cores, each step a bounded sample of 1 x 256 tokens; steps beyond a
+    ~150 s budget are not run (the count is reported)."""
+    threads = os.cpu_count() or 1
+    init = transformer_init(layers=args.layers, seed=0)
+    ids = train_sample_ids(1, 256)
+    for _ in range(min(args.warmup, 1)):
+        oracle_train_sample(init, ids, args.layers, torch.float32, threads)
+    rates, used = [], 0.0
+    for _ in range(args.steps):
+        dt, _, _ = oracle_train_sample(init, ids, args.layers, torch.float32, threads)
+        rates.append(256 / dt)
+        used += dt
+        if used > budget_s:
+            break
+    value = statistics.median(rates)
+    sample = (f"oracle forward + series backward of the full-width model ({args.layers} layers), 1 x 256 tokens "
+              f"per step, float32, {len(rates)} of {args.steps} steps run")
+    return {
+        "impl": "reference",
+        "metric": "train tokens/s (configs[4]: 12-layer d768 PolyTensor transformer, degree 3, float32, "
+                  "global batch 64 x 1024)",
+        "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": len(rates), "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: uniform random token ids, random-init N(0,0.02) weights with zero higher coefficients",
+        "config": train_config(args.layers),
+        "parallelism": "host CPU",
+        "extrapolated_s_per_step": 64 * 1024 / value,
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 
@@ -707,9 +996,10 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="poly_matmul",
+    ap.add_argument("--workload", default="train",
                     choices=sorted(WORKLOADS) + ["norm_ce", "attention", "attention_fwd", "train",
                                                  "poly_matmul_sweep"])
+    ap.add_argument("--no-matmul", action="store_true", help="train: skip the configs[1] product line")
     ap.add_argument("--impl", default="polykern", choices=["polykern", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rows", type=int, default=16384, help="norm_ce: rows (batch*seq)")
@@ -729,12 +1019,15 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
 
     if args.impl == "reference":
+        # the reference's CPU path on the host cores; under torchrun rank 0 alone runs it
         if rank == 0:
-            if cfg is None:
-                print(json.dumps({"impl": "reference", "unavailable": f"--impl reference times the default workload; "
-                                  f"see --workload {args.workload} --cpu-only"}), flush=True)
-            else:
+            if args.workload == "train":
+                print(json.dumps(reference_arm_train(args)), flush=True)
+            elif cfg is not None:
                 print(json.dumps(reference_arm(args, cfg)), flush=True)
+            else:
+                print(json.dumps({"impl": "reference", "unavailable": f"--impl reference covers the train and "
+                                  f"poly_matmul workloads, not {args.workload}"}), flush=True)
         return
 
     if args.warmup < 3:
@@ -756,7 +1049,7 @@ def main():
         if world > 1:
             torch.distributed.destroy_process_group()
         return
-    result = run_matmul(args, cfg, rank, world, device)
+    result = run_matmul(args, cfg, rank, world, device, parity=(rank == 0))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, desc = cpu_matmul_rate(cfg, os.cpu_count() or 1)
         result["cpu_baseline"] = {"value": rate, "unit": "TFLOP/s", "cores": os.cpu_count() or 1,

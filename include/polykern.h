@@ -80,6 +80,13 @@ PK_API int pk_profile_enable(int on);
 PK_API int pk_profile_query(const char* kernel, double* total_ms, int64_t* launches);
 
 /*
+ * Number of kernels the library has launched in this process (all entry points, all
+ * devices and streams), for counting launches inside a timed region; reset != 0 returns
+ * the count and sets it to zero.  No counterpart in the reference.
+ */
+PK_API int64_t pk_launch_count(int reset);
+
+/*
  * Polynomial (block-Toeplitz) matrix product, C_k = sum_{i=0..k} A_i @ B_{k-i},
  * k = 0..degree, for a batch of matrices.
  * Replaces plain_polynomial_product(matrix=True)   (src/polytensors/_plain.py:118-128)

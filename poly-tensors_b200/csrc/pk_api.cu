@@ -2,6 +2,7 @@
 // word, the cached SM count and the runtime-resolved TMA descriptor encoder.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <string>
@@ -13,10 +14,17 @@ __device__ int pk_device_status_word = 0;
 
 namespace pk {
 
+// Device address of the status word on the current device, looked up once per device.
+// The lookup is serialised: two host threads making their first call on one device would
+// otherwise both write the cache slot.  (A cudaDeviceReset invalidates the address; the
+// library is not meant to outlive a reset of its context.)
+static std::mutex g_status_mutex;
+
 int* device_status_ptr() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
     static int* cache[64] = {nullptr};
+    std::lock_guard<std::mutex> lock(g_status_mutex);
     if (!cache[dev]) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, pk_device_status_word) == cudaSuccess) cache[dev] = static_cast<int*>(p);
@@ -41,14 +49,15 @@ int cuda_fail(cudaError_t err, const char* what) {
 int num_sms() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-    static int cache[64] = {0};
+    // Racing first calls store the same value; atomics keep that well defined.
+    static std::atomic<int> cache[64];
     if (dev < 0 || dev >= 64) return 148;
-    if (cache[dev] == 0) {
-        int n = 0;
+    int n = cache[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-        cache[dev] = n;
+        cache[dev].store(n, std::memory_order_relaxed);
     }
-    return cache[dev];
+    return n;
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -94,6 +103,10 @@ static cudaEvent_t take_event(ProfRecord& r) {
 }
 
 bool profiling() { return g_prof_on; }
+
+static std::atomic<int64_t> g_launches{0};
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 void prof_begin(const char* name, cudaStream_t stream, void** token) {
     *token = nullptr;
@@ -145,6 +158,10 @@ int pk_profile_query(const char* name, double* total_ms, int64_t* launches) {
     }
     r.pending.clear();
     return 0;
+}
+
+int64_t pk_launch_count(int reset) {
+    return reset ? pk::g_launches.exchange(0) : pk::g_launches.load();
 }
 
 const char* pk_version(void) { return "polykern 0.1 (sm_100a)"; }

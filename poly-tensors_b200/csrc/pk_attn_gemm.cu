@@ -564,7 +564,7 @@ static int launch_ag(const AgMaps& maps, AgParams& p, cudaStream_t stream) {
     const int grid = static_cast<int>(std::min<int64_t>(p.total_units, num_sms()));
     void* tok;
     prof_begin(MODE == AG_PROBS ? "attn_probs_gemm" : "attn_dscores_gemm", stream, &tok);
-    attn_score_gemm_kernel<NP, MODE><<<grid, AG_THREADS, AG_SMEM_BYTES, stream>>>(maps, p);
+    PK_LAUNCHED(attn_score_gemm_kernel<NP, MODE><<<grid, AG_THREADS, AG_SMEM_BYTES, stream>>>(maps, p));
     prof_end(MODE == AG_PROBS ? "attn_probs_gemm" : "attn_dscores_gemm", stream, tok);
     PK_CHECK_LAUNCH("pk_attn_score_gemm: kernel launch");
     return PK_OK;

@@ -29,11 +29,20 @@ CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, cuuint32_t rank,
 bool profiling();
 void prof_begin(const char* name, cudaStream_t stream, void** token);
 void prof_end(const char* name, cudaStream_t stream, void* token);
+// Count of kernel launches issued by the library (pk_launch_count).
+void note_launch();
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int64_t round_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
 
 }  // namespace pk
+
+// Every kernel launch goes through PK_LAUNCHED so that pk_launch_count() sees it.
+#define PK_LAUNCHED(...)        \
+    do {                        \
+        __VA_ARGS__;            \
+        ::pk::note_launch();    \
+    } while (0)
 
 #define PK_CHECK_LAUNCH(what)                                            \
     do {                                                                 \

@@ -158,9 +158,9 @@ template <typename T, int NP>
 static void launch_map_np(const MapParams& p, int grid, bool vec, cudaStream_t s) {
     if (vec) {
         const int g = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(grid, ceil_div(p.numel, 256 * ROW_VEC))));
-        series_map_vec_kernel<T, NP><<<g, 256, 0, s>>>(p);
+        PK_LAUNCHED(series_map_vec_kernel<T, NP><<<g, 256, 0, s>>>(p));
     } else {
-        series_map_kernel<T, NP><<<grid, 256, 0, s>>>(p);
+        PK_LAUNCHED(series_map_kernel<T, NP><<<grid, 256, 0, s>>>(p));
     }
 }
 
@@ -313,8 +313,8 @@ __global__ void scatter_add_rows_kernel(const RowParams p) {
 
 template <typename T, int NP>
 static void launch_reduce(const ReduceParams& p, bool rows, int atomic, dim3 grid, cudaStream_t s) {
-    if (rows) reduce_rows_kernel<T, NP><<<grid, 256, 0, s>>>(p);
-    else reduce_cols_kernel<T, NP><<<grid, 256, 0, s>>>(p, atomic);
+    if (rows) PK_LAUNCHED(reduce_rows_kernel<T, NP><<<grid, 256, 0, s>>>(p));
+    else PK_LAUNCHED(reduce_cols_kernel<T, NP><<<grid, 256, 0, s>>>(p, atomic));
 }
 
 template <typename T>
@@ -484,8 +484,8 @@ int pk_series_gather_rows(int dtype, int degree, int64_t n_idx, int64_t dim, con
     if (n_idx * dim == 0) return PK_OK;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int grid = grid_for(n_idx * dim);
-    if (dtype == PK_F32) gather_rows_kernel<float><<<grid, 256, 0, s>>>(p);
-    else if (dtype == PK_F64) gather_rows_kernel<double><<<grid, 256, 0, s>>>(p);
+    if (dtype == PK_F32) PK_LAUNCHED(gather_rows_kernel<float><<<grid, 256, 0, s>>>(p));
+    else if (dtype == PK_F64) PK_LAUNCHED(gather_rows_kernel<double><<<grid, 256, 0, s>>>(p));
     else return fail(PK_ERR_UNSUPPORTED, "pk_series_gather_rows: float32/float64 only");
     PK_CHECK_LAUNCH("pk_series_gather_rows");
     return PK_OK;
@@ -515,8 +515,8 @@ int pk_series_scatter_add_rows(int dtype, int degree, int64_t n_idx, int64_t dim
     }
     if (n_idx * dim == 0) return PK_OK;
     const int grid = grid_for(n_idx * dim);
-    if (dtype == PK_F32) scatter_add_rows_kernel<float><<<grid, 256, 0, s>>>(p);
-    else scatter_add_rows_kernel<double><<<grid, 256, 0, s>>>(p);
+    if (dtype == PK_F32) PK_LAUNCHED(scatter_add_rows_kernel<float><<<grid, 256, 0, s>>>(p));
+    else PK_LAUNCHED(scatter_add_rows_kernel<double><<<grid, 256, 0, s>>>(p));
     PK_CHECK_LAUNCH("pk_series_scatter_add_rows");
     return PK_OK;
 }

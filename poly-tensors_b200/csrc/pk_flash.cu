@@ -530,7 +530,7 @@ static int launch_flash(const FlashMaps& maps, const FlashParams& p, cudaStream_
     dim3 grid(static_cast<unsigned>(p.q_tiles * p.n_slices), static_cast<unsigned>(p.bh));
     void* tok;
     prof_begin("flash_attn_fwd", s, &tok);
-    flash_fwd_kernel<NP, DCH><<<grid, FA_THREADS, smem, s>>>(maps, p);
+    PK_LAUNCHED(flash_fwd_kernel<NP, DCH><<<grid, FA_THREADS, smem, s>>>(maps, p));
     prof_end("flash_attn_fwd", s, tok);
     PK_CHECK_LAUNCH("pk_flash_attn_fwd");
     return PK_OK;

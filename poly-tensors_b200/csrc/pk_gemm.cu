@@ -298,14 +298,14 @@ static int launch_stage(const StageParams& p, int64_t batch, bool has_kind[5], c
                 if (reinterpret_cast<uintptr_t>(p.plane[k].src) % 8) vec = false;
             const int64_t total = batch * p.planes * p.rows * (p.Kp / 4);
             const int grid = static_cast<int>(std::min<int64_t>(ceil_div(total, 256), static_cast<int64_t>(num_sms()) * 32));
-            copy16_direct_kernel<<<grid, 256, 0, stream>>>(p, batch, vec ? 1 : 0);
+            PK_LAUNCHED(copy16_direct_kernel<<<grid, 256, 0, stream>>>(p, batch, vec ? 1 : 0));
             PK_CHECK_LAUNCH("pk_poly_gemm: copy kernel launch");
             return PK_OK;
         }
         if (p.s_r == 1 && ceil_div(p.rows, 64) <= 65535 && batch * p.planes <= 65535) {
             dim3 grid(static_cast<unsigned>(ceil_div(p.Kp, 64)), static_cast<unsigned>(ceil_div(p.rows, 64)),
                       static_cast<unsigned>(batch * p.planes));
-            copy16_transpose_kernel<<<grid, 256, 0, stream>>>(p);
+            PK_LAUNCHED(copy16_transpose_kernel<<<grid, 256, 0, stream>>>(p));
             PK_CHECK_LAUNCH("pk_poly_gemm: copy transpose kernel launch");
             return PK_OK;
         }
@@ -322,7 +322,7 @@ static int launch_stage(const StageParams& p, int64_t batch, bool has_kind[5], c
             const int64_t lines = batch * p.planes * p.rows;
             const int64_t warps = ceil_div(lines, 32 / lpl);
             const int grid = static_cast<int>(std::min<int64_t>(ceil_div(warps, 8), static_cast<int64_t>(num_sms()) * 16));
-            split_direct_kernel<<<grid, 256, 0, stream>>>(p, batch, vec ? 1 : 0, lpl);
+            PK_LAUNCHED(split_direct_kernel<<<grid, 256, 0, stream>>>(p, batch, vec ? 1 : 0, lpl));
             PK_CHECK_LAUNCH("pk_poly_gemm: split kernel launch");
             return PK_OK;
         }
@@ -332,7 +332,7 @@ static int launch_stage(const StageParams& p, int64_t batch, bool has_kind[5], c
             bool vec = p.s_k % 4 == 0 && p.s_b % 4 == 0;
             for (int k = 0; k < p.planes; ++k)
                 if (reinterpret_cast<uintptr_t>(p.plane[k].src) % 16) vec = false;
-            split_transpose_kernel<<<grid, 256, 0, stream>>>(p, vec ? 1 : 0);
+            PK_LAUNCHED(split_transpose_kernel<<<grid, 256, 0, stream>>>(p, vec ? 1 : 0));
             PK_CHECK_LAUNCH("pk_poly_gemm: split transpose kernel launch");
             return PK_OK;
         }
@@ -341,11 +341,11 @@ static int launch_stage(const StageParams& p, int64_t batch, bool has_kind[5], c
     const int64_t gx = ceil_div(p.Kp, 64), gy = ceil_div(p.rows, 32), gz = batch * p.planes;
     if (gy > 65535 || gz > 65535) return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: operand too large to stage");
     dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy), static_cast<unsigned>(gz));
-    if (has_kind[STAGE_SPLIT_BF16]) stage_kernel<STAGE_SPLIT_BF16><<<grid, 256, 0, stream>>>(p);
-    if (has_kind[STAGE_COPY_16]) stage_kernel<STAGE_COPY_16><<<grid, 256, 0, stream>>>(p);
-    if (has_kind[STAGE_F64]) stage_kernel<STAGE_F64><<<grid, 256, 0, stream>>>(p);
-    if (has_kind[STAGE_C128_A]) stage_kernel<STAGE_C128_A><<<grid, 256, 0, stream>>>(p);
-    if (has_kind[STAGE_C128_B]) stage_kernel<STAGE_C128_B><<<grid, 256, 0, stream>>>(p);
+    if (has_kind[STAGE_SPLIT_BF16]) PK_LAUNCHED(stage_kernel<STAGE_SPLIT_BF16><<<grid, 256, 0, stream>>>(p));
+    if (has_kind[STAGE_COPY_16]) PK_LAUNCHED(stage_kernel<STAGE_COPY_16><<<grid, 256, 0, stream>>>(p));
+    if (has_kind[STAGE_F64]) PK_LAUNCHED(stage_kernel<STAGE_F64><<<grid, 256, 0, stream>>>(p));
+    if (has_kind[STAGE_C128_A]) PK_LAUNCHED(stage_kernel<STAGE_C128_A><<<grid, 256, 0, stream>>>(p));
+    if (has_kind[STAGE_C128_B]) PK_LAUNCHED(stage_kernel<STAGE_C128_B><<<grid, 256, 0, stream>>>(p));
     PK_CHECK_LAUNCH("pk_poly_gemm: stage kernel launch");
     return PK_OK;
 }
@@ -788,7 +788,7 @@ static int launch_tc(TcParams& p, const TcOperand& a, const TcOperand& b, cudaSt
     const int grid = static_cast<int>(std::min<int64_t>(total, num_sms()));
     void* tok;
     prof_begin("poly_gemm", stream, &tok);
-    tc_poly_gemm_kernel<BN, SPLIT><<<grid, TC_THREADS, Cfg::SMEM_BYTES, stream>>>(maps, p);
+    PK_LAUNCHED(tc_poly_gemm_kernel<BN, SPLIT><<<grid, TC_THREADS, Cfg::SMEM_BYTES, stream>>>(maps, p));
     prof_end("poly_gemm", stream, tok);
     PK_CHECK_LAUNCH("pk_poly_gemm: tcgen05 kernel launch");
     return PK_OK;
@@ -1079,7 +1079,7 @@ static int launch_allplanes(TcParams& p, const TcOperand& a, const TcOperand& b,
     const int grid = static_cast<int>(std::min<int64_t>(total, num_sms()));
     void* tok;
     prof_begin("poly_gemm", stream, &tok);
-    tc_allplanes_kernel<NP><<<grid, TC_THREADS, AP_SMEM_BYTES, stream>>>(maps, p);
+    PK_LAUNCHED(tc_allplanes_kernel<NP><<<grid, TC_THREADS, AP_SMEM_BYTES, stream>>>(maps, p));
     prof_end("poly_gemm", stream, tok);
     PK_CHECK_LAUNCH("pk_poly_gemm: tcgen05 all-planes kernel launch");
     return PK_OK;
@@ -1365,8 +1365,8 @@ static int poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N,
         for (int p = 0; p < P; ++p) {
             const bool cplx = dtype == PK_C128 && (p >= a_complex_from || p >= b_complex_from);
             const int e = dtype == PK_C128 ? (cplx ? 16 : 8) : esz;
-            zero_planes_kernel<<<592, 256, 0, stream>>>(nullptr, static_cast<char*>(c_planes[p]), M, N, c_rs, c_bs,
-                                                        batch, e);
+            PK_LAUNCHED(zero_planes_kernel<<<592, 256, 0, stream>>>(nullptr, static_cast<char*>(c_planes[p]), M, N, c_rs, c_bs,
+                                                        batch, e));
         }
         PK_CHECK_LAUNCH("pk_poly_gemm: zero fill");
         return PK_OK;
@@ -1532,7 +1532,7 @@ static int poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N,
               static_cast<unsigned>(gz));
     void* tok;
     prof_begin("poly_gemm", stream, &tok);
-    dmma_poly_gemm_kernel<<<grid, DM_THREADS, smem, stream>>>(dp);
+    PK_LAUNCHED(dmma_poly_gemm_kernel<<<grid, DM_THREADS, smem, stream>>>(dp));
     prof_end("poly_gemm", stream, tok);
     PK_CHECK_LAUNCH("pk_poly_gemm: dmma kernel launch");
     return PK_OK;

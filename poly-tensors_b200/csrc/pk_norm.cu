@@ -751,7 +751,7 @@ static int reduce_dw(const NormParams& p, void* const* dw, int parts, cudaStream
     NormParams q = p;
     for (int k = 0; k < p.np; ++k) q.g[k] = dw[k];
     const int64_t total = static_cast<int64_t>(p.np) * p.cols;
-    rmsnorm_dw_reduce_kernel<T, NP><<<static_cast<int>(ceil_div(total, 32)), 256, 0, s>>>(q, parts);
+    PK_LAUNCHED(rmsnorm_dw_reduce_kernel<T, NP><<<static_cast<int>(ceil_div(total, 32)), 256, 0, s>>>(q, parts));
     PK_CHECK_LAUNCH("pk_rmsnorm_bwd: weight reduction");
     return PK_OK;
 }
@@ -801,6 +801,7 @@ static int bwd_stream(NormParams& p, void* const* dw, void* ws, size_t ws_bytes,
     void* tok;
     prof_begin("rmsnorm_bwd", s, &tok);
     e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e == cudaSuccess) ::pk::note_launch();
     if (e != cudaSuccess) return cuda_fail(e, "pk_rmsnorm_bwd: cluster launch");
     PK_CHECK_LAUNCH("pk_rmsnorm_bwd");
     if (dw) {
@@ -834,7 +835,7 @@ static bool stream_row_forward(const NormParams& p, cudaStream_t s) {
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
             return false;
         const int grid = static_cast<int>(std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * per_sm));
-        kern<<<grid, threads, smem, s>>>(p);
+        PK_LAUNCHED(kern<<<grid, threads, smem, s>>>(p));
         return true;
     }
 }
@@ -865,9 +866,9 @@ static bool reg_row_forward(const NormParams& p, cudaStream_t s) {
             return false;
         const int grid = static_cast<int>(std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * per_sm));
         const int th = static_cast<int>(threads);
-        if (steps == 1) rmsnorm_fwd_reg_kernel<T, NP, 1><<<grid, th, 0, s>>>(p);
-        else if (steps == 2) rmsnorm_fwd_reg_kernel<T, NP, 2><<<grid, th, 0, s>>>(p);
-        else rmsnorm_fwd_reg_kernel<T, NP, 4><<<grid, th, 0, s>>>(p);
+        if (steps == 1) PK_LAUNCHED(rmsnorm_fwd_reg_kernel<T, NP, 1><<<grid, th, 0, s>>>(p));
+        else if (steps == 2) PK_LAUNCHED(rmsnorm_fwd_reg_kernel<T, NP, 2><<<grid, th, 0, s>>>(p));
+        else PK_LAUNCHED(rmsnorm_fwd_reg_kernel<T, NP, 4><<<grid, th, 0, s>>>(p));
         return true;
     }
 }
@@ -889,7 +890,7 @@ static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, siz
         prof_begin("rmsnorm_fwd", s, &tok);
         if (!stream_row_forward<T, NP>(p, s) && !reg_row_forward<T, NP>(p, s)) {
             const int grid = static_cast<int>(std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * 8));
-            rmsnorm_fwd_kernel<T, NP><<<grid, threads, 0, s>>>(p);
+            PK_LAUNCHED(rmsnorm_fwd_kernel<T, NP><<<grid, threads, 0, s>>>(p));
         }
         prof_end("rmsnorm_fwd", s, tok);
         PK_CHECK_LAUNCH("pk_rmsnorm_fwd");
@@ -961,14 +962,15 @@ static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, siz
             void* tok;
             prof_begin("rmsnorm_bwd", s, &tok);
             e = cudaLaunchKernelEx(&cfg, kern, p);
+            if (e == cudaSuccess) ::pk::note_launch();
             if (e != cudaSuccess) return cuda_fail(e, "pk_rmsnorm_bwd: cluster launch");
             PK_CHECK_LAUNCH("pk_rmsnorm_bwd");
             if (dw) {
                 NormParams q = p;
                 for (int k = 0; k < p.np; ++k) q.g[k] = dw[k];
                 const int64_t total = static_cast<int64_t>(p.np) * p.cols;
-                rmsnorm_dw_reduce_kernel<T, NP><<<static_cast<int>(ceil_div(total, 32)), 256, 0, s>>>(
-                    q, static_cast<int>(clusters));
+                PK_LAUNCHED(rmsnorm_dw_reduce_kernel<T, NP><<<static_cast<int>(ceil_div(total, 32)), 256, 0, s>>>(
+                    q, static_cast<int>(clusters)));
                 PK_CHECK_LAUNCH("pk_rmsnorm_bwd: weight reduction");
             }
             prof_end("rmsnorm_bwd", s, tok);
@@ -991,13 +993,13 @@ static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, siz
     }
     void* tok;
     prof_begin("rmsnorm_bwd", s, &tok);
-    rmsnorm_bwd_kernel<T, NP><<<grid, bthreads, smem, s>>>(p);
+    PK_LAUNCHED(rmsnorm_bwd_kernel<T, NP><<<grid, bthreads, smem, s>>>(p));
     PK_CHECK_LAUNCH("pk_rmsnorm_bwd");
     if (dw) {
         NormParams q = p;
         for (int k = 0; k < p.np; ++k) q.g[k] = dw[k];
         const int64_t total = static_cast<int64_t>(p.np) * p.cols;
-        rmsnorm_dw_reduce_kernel<T, NP><<<static_cast<int>(ceil_div(total, 32)), 256, 0, s>>>(q, grid);
+        PK_LAUNCHED(rmsnorm_dw_reduce_kernel<T, NP><<<static_cast<int>(ceil_div(total, 32)), 256, 0, s>>>(q, grid));
         PK_CHECK_LAUNCH("pk_rmsnorm_bwd: weight reduction");
     }
     prof_end("rmsnorm_bwd", s, tok);

@@ -327,12 +327,12 @@ static void launch_rows(int which, const SoftmaxParams& p, cudaStream_t s) {
     const int threads = row_threads(p.cols);
     const int grid = static_cast<int>(std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * 8));
     switch (which) {
-        case SM_FWD: softmax_fwd_kernel<T, NP><<<grid, threads, 0, s>>>(p); break;
-        case SM_BWD: softmax_bwd_kernel<T, NP><<<grid, threads, 0, s>>>(p); break;
-        case CE_FWD: ce_fwd_kernel<T, NP><<<grid, threads, 0, s>>>(p); break;
-        case ATTN_P: attn_probs_kernel<T, NP><<<grid, threads, 0, s>>>(p); break;
-        case ATTN_DS: attn_dscores_kernel<T, NP><<<grid, std::min(threads, 256), 0, s>>>(p); break;
-        default: ce_bwd_kernel<T, NP><<<grid, threads, 0, s>>>(p); break;
+        case SM_FWD: PK_LAUNCHED(softmax_fwd_kernel<T, NP><<<grid, threads, 0, s>>>(p)); break;
+        case SM_BWD: PK_LAUNCHED(softmax_bwd_kernel<T, NP><<<grid, threads, 0, s>>>(p)); break;
+        case CE_FWD: PK_LAUNCHED(ce_fwd_kernel<T, NP><<<grid, threads, 0, s>>>(p)); break;
+        case ATTN_P: PK_LAUNCHED(attn_probs_kernel<T, NP><<<grid, threads, 0, s>>>(p)); break;
+        case ATTN_DS: PK_LAUNCHED(attn_dscores_kernel<T, NP><<<grid, std::min(threads, 256), 0, s>>>(p)); break;
+        default: PK_LAUNCHED(ce_bwd_kernel<T, NP><<<grid, threads, 0, s>>>(p)); break;
     }
 }
 

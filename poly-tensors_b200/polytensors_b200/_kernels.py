@@ -61,6 +61,36 @@ def gemm_dtype(a_planes, b_planes):
     return _DTYPE_CODE[base], P, P, [base] * P
 
 
+def _band_count(M, K, band, off):
+    """Admissible (row, column) pairs of an M x K band: 1: k >= m + off, 2: k <= m + off."""
+    m = torch.arange(M, dtype=torch.int64)
+    if band == 1:
+        return int((K - (m + off).clamp(0, K)).sum())
+    return int((m + off + 1).clamp(0, K).sum())
+
+
+def product_flops(code, degree, batch, M, N, K, acf, bcf, band=0, band_offset=0):
+    """Algorithmic flops of one polynomial product: 2*M*N*K per real plane product over the
+    (n+1)(n+2)/2 products; a complex128 plane product counts 4 real products (2 when one side
+    is real), and banded products count only their admissible region."""
+    P = degree + 1
+    terms = 0
+    for k in range(P):
+        for i in range(k + 1):
+            if code == _lib.PK_C128:
+                ca, cb = i >= acf, (k - i) >= bcf
+                terms += 4 if (ca and cb) else (2 if (ca or cb) else 1)
+            else:
+                terms += 1
+    if band in (1, 2):
+        pairs = _band_count(M, K, band, band_offset) * N
+    elif band == 3:
+        pairs = _band_count(M, N, 2, band_offset) * K
+    else:
+        pairs = M * N * K
+    return 2.0 * batch * pairs * terms
+
+
 def poly_matmul(a_planes, b_planes, out=None, accumulate=False, band=0, band_offset=0):
     """C_k = sum_{i+j=k} A_i @ B_j for planes of shape (M, K) x (K, N) or (B, M, K) x (B, K, N).
 
@@ -118,6 +148,8 @@ def poly_matmul(a_planes, b_planes, out=None, accumulate=False, band=0, band_off
         c_bs, c_rs = (st[0], st[1]) if batched else (0, st[0])
     lib = _lib.load()
     degree = P - 1
+    if _lib.profiling():
+        _lib.add_gemm_flops(product_flops(code, degree, batch, M, N, K, acf, bcf, band, band_offset))
     pa, ka = _lib.pointer_array(a_planes)
     pb, kb = _lib.pointer_array(b_planes)
     pc, kc = _lib.pointer_array(outs)
@@ -234,8 +266,24 @@ def series_reduce(planes, outer, red, inner, scale=1.0):
     return out
 
 
+def _check_indices(idx, upper, what, ignore=None):
+    """Raise IndexError, as the reference's torch ops do, when an index lies outside
+    [0, upper) (``ignore`` is an allowed sentinel, e.g. cross entropy's ignore_index).
+    The kernels skip such rows instead of faulting, so the check runs on the host side
+    before the launch: one reduction over the indices and one read of its result."""
+    if idx.numel() == 0:
+        return
+    bad = (idx < 0) | (idx >= upper)
+    if ignore is not None:
+        bad &= idx != ignore
+    if bool(bad.any()):
+        first = idx[bad].reshape(-1)[0].item()
+        raise IndexError(f"{what}: index {first} is out of range [0, {upper})")
+
+
 def gather_rows(weight_planes, idx):
     """out[i, :] = W[idx[i], :] per plane (embedding)."""
+    _check_indices(idx, weight_planes[0].shape[0], "embedding")
     w = weight_planes if _same_strides(weight_planes) and weight_planes[0].stride(-1) == 1 else \
         [p.contiguous() for p in weight_planes]
     _require_cuda((*w, idx), "embedding")
@@ -252,6 +300,7 @@ def gather_rows(weight_planes, idx):
 
 def scatter_add_rows(grad_planes, idx, num_rows, padding_idx=-1):
     """out[idx[i], :] += G[i, :] over zeroed (num_rows, d) planes (embedding backward)."""
+    _check_indices(idx, num_rows, "embedding backward")
     d = grad_planes[0].shape[-1]
     g = [p.reshape(-1, d) for p in grad_planes]
     if not _same_strides(g) or g[0].stride(-1) != 1:
@@ -363,6 +412,7 @@ def softmax_bwd(g_planes, y_planes, log):
 def cross_entropy_fwd(z_planes, target, ignore_index, softcap):
     """Per-row loss series (float32, or float64 for float64 logits) and row statistics."""
     rows, cols = z_planes[0].shape
+    _check_indices(target, cols, "cross_entropy target", ignore=int(ignore_index))
     z = z_planes if (_same_strides(z_planes) and z_planes[0].stride(-1) == 1) else [p.contiguous() for p in z_planes]
     t = target.to(torch.int64).contiguous()
     _require_cuda((*z, t), "cross_entropy")

@@ -27,6 +27,7 @@ SIGNATURES = {
     "pk_last_error": (ctypes.c_char_p, []),
     "pk_device_status": (_i32, [_i32]),
     "pk_profile_enable": (_i32, [_i32]),
+    "pk_launch_count": (_i64, [_i32]),
     "pk_profile_query": (_i32, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
     "pk_poly_gemm_workspace_size": (_sz, [_i32, _i32, _i64, _i64, _i64, _i64, _i32, _i32]),
     "pk_poly_gemm_workspace_query": (_i32, [_i32, _i32, _i64, _i64, _i64, _i64,
@@ -115,8 +116,28 @@ def check(status, what):
         raise RuntimeError(f"{what} failed ({status}): {last_error()}")
 
 
+# Host-side companion of the launch timing: while it is on, the tensor-level wrappers add the
+# algorithmic flops of every polynomial product they launch (benchmark rooflines).
+_profile = {"on": False, "gemm_flops": 0.0}
+
+
 def profile_enable(on=True):
     load().pk_profile_enable(1 if on else 0)
+    _profile["on"] = bool(on)
+
+
+def profiling():
+    return _profile["on"]
+
+
+def add_gemm_flops(flops):
+    _profile["gemm_flops"] += flops
+
+
+def take_gemm_flops():
+    """Algorithmic flops of the polynomial products launched while timing was on, since the last call."""
+    value, _profile["gemm_flops"] = _profile["gemm_flops"], 0.0
+    return value
 
 
 def profile_query(kernel):
@@ -124,6 +145,11 @@ def profile_query(kernel):
     ms, n = ctypes.c_double(), ctypes.c_int64()
     check(load().pk_profile_query(kernel.encode(), ctypes.byref(ms), ctypes.byref(n)), "pk_profile_query")
     return ms.value, n.value
+
+
+def launch_count(reset=False):
+    """Kernels launched by the library so far (pk_launch_count); ``reset`` zeroes the count."""
+    return load().pk_launch_count(1 if reset else 0)
 
 
 def pointer_array(tensors):

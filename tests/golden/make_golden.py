@@ -1,13 +1,13 @@
 """Generate golden input/output vectors from the reference implementation itself.
 
-Runs samuel-gunn/poly-tensors (imported from a local checkout given by
-``POLYTENSORS_REFERENCE`` or ``/root/reference/src``) on small seeded inputs, in
+Runs samuel-gunn/poly-tensors (imported from the ``src`` directory of a local checkout,
+named by the ``POLYTENSORS_REFERENCE`` environment variable) on small seeded inputs, in
 ``PolyTensor.plain_range()`` mode unless a case says otherwise, and saves inputs and
 outputs to ``tests/golden/*.pt``.  The reference is not needed afterwards: the CPU
 tests pin the oracle (``oracle/polyref.py``) against these files and the GPU tests
 compare the CUDA kernels against both.
 
-    python tests/golden/make_golden.py
+    POLYTENSORS_REFERENCE=<checkout>/src python tests/golden/make_golden.py
 """
 
 import math
@@ -19,7 +19,9 @@ import torch
 import torch.nn.functional as F
 
 HERE = pathlib.Path(__file__).resolve().parent
-REF = os.environ.get("POLYTENSORS_REFERENCE", "/root/reference/src")
+REF = os.environ.get("POLYTENSORS_REFERENCE")
+if not REF:
+    sys.exit("set POLYTENSORS_REFERENCE to the reference checkout's src directory")
 sys.path.insert(0, REF)
 from polytensors import PolyTensor  # noqa: E402  (the reference)
 

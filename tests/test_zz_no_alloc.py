@@ -4,10 +4,15 @@ device footprint, code with no allocator to link).  It takes its scratch from a 
 64 MiB array inside the library instead of a caller workspace.
 
 Checked through the C ABI against pk_poly_gemm (the entry point with a caller-allocated
-workspace), on two calls in a row so that the second call runs on scratch that still
-holds the first call's contents.  Tolerance: per-plane max |diff| / max |ref| <= 1e-4
-for float32 and 1e-10 for float64 (the kernels are the same, so the results agree far
-more closely)."""
+workspace) and against the CPU oracle, on calls in a row: a larger product first, so the
+scratch array holds its staged operands, then products whose reduction length is not a
+multiple of the staging pitch (K = 317) and whose B operand is a transposed view, so the
+second call stages padded rows over the first call's leftovers.  Tolerance: per-plane
+max |diff| / max |ref| <= 1e-4 for float32 and 1e-10 for float64.
+
+The file name sorts last on purpose: pytest collects files in name order, so a run that
+stops at the first failure has already run every other test before this one, which holds
+library-wide state (the shared scratch array) for the rest of the process."""
 
 import ctypes
 import math
@@ -18,10 +23,13 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def planes(shape, n, seed, dtype):
+def planes(shape, n, seed, dtype, transpose=False):
     g = torch.Generator().manual_seed(seed)
-    return [(torch.randn(*shape, generator=g, dtype=torch.float64) / math.factorial(k)).to(dtype).cuda()
-            for k in range(n + 1)]
+    out = []
+    for k in range(n + 1):
+        x = torch.randn(*shape, generator=g, dtype=torch.float64) / math.factorial(k)
+        out.append(x.t().contiguous().t() if transpose else x)   # transpose: same values, column-major
+    return [x.to(dtype).cuda() for x in out]
 
 
 def call(lib, entry, code, A, B, use_workspace):
@@ -35,11 +43,15 @@ def call(lib, entry, code, A, B, use_workspace):
     pb, kb = _lib.pointer_array(B)
     pc, kc = _lib.pointer_array(C)
     stream = torch.cuda.current_stream().cuda_stream
-    args = (code, degree, 1, M, N, K, pa, 0, K, 1, pb, 0, N, 1, pc, 0, N, degree + 1, degree + 1)
+    (a_rs, a_cs), (b_rs, b_cs) = A[0].stride(), B[0].stride()
+    args = (code, degree, 1, M, N, K, pa, 0, a_rs, a_cs, pb, 0, b_rs, b_cs, pc, 0, N, degree + 1, degree + 1)
     if use_workspace:
-        size = lib.pk_poly_gemm_workspace_size(code, degree, 1, M, N, K, degree + 1, degree + 1)
-        ws = torch.empty(size, dtype=torch.uint8, device="cuda")
-        status = entry(*args, ws.data_ptr(), size, stream)
+        size = ctypes.c_size_t(0)
+        _lib.check(lib.pk_poly_gemm_workspace_query(code, degree, 1, M, N, K, pa, 0, a_rs, a_cs, pb, 0, b_rs, b_cs,
+                                                    degree + 1, degree + 1, ctypes.byref(size)),
+                   "pk_poly_gemm_workspace_query")
+        ws = torch.empty(max(size.value, 1), dtype=torch.uint8, device="cuda")
+        status = entry(*args, ws.data_ptr(), size.value, stream)
     else:
         status = entry(*args, stream)
     _lib.check(status, entry.__name__)
@@ -50,23 +62,29 @@ def call(lib, entry, code, A, B, use_workspace):
 def max_plane_error(got, want):
     errs = []
     for g, w in zip(got, want):
-        denom = w.abs().max().item()
-        errs.append((g.double() - w.double()).abs().max().item() / denom)
+        w = w.cpu().double()
+        errs.append((g.cpu().double() - w).abs().max().item() / w.abs().max().item())
     return max(errs)
 
 
 @pytest.mark.parametrize("dtype,code,tol", [(torch.float32, 0, 1e-4), (torch.float64, 1, 1e-10)])
-def test_noalloc_matches_workspace_entry_point(dtype, code, tol):
+def test_noalloc_matches_workspace_entry_point_and_oracle(dtype, code, tol):
+    from oracle import polyref
     from polytensors_b200 import _lib
 
     lib = _lib.load()
-    for call_index in range(2):   # second call reuses scratch left over from the first
-        A = planes((384, 320), 2, 10 + call_index, dtype)
-        B = planes((320, 272), 2, 20 + call_index, dtype)
+    # (M, K, N, degree, B transposed): the first product fills more scratch than the later ones
+    # use; K = 317 leaves padding columns in every staged row of the later products.
+    cases = [(512, 1024, 384, 2, False), (200, 317, 144, 2, True), (136, 317, 200, 3, True)]
+    for i, (M, K, N, n, bt) in enumerate(cases):
+        A = planes((M, K), n, 10 + i, dtype)
+        B = planes((K, N), n, 20 + i, dtype, transpose=bt)
         want = call(lib, lib.pk_poly_gemm, code, A, B, use_workspace=True)
         got = call(lib, lib.pk_poly_gemm_noalloc, code, A, B, use_workspace=False)
         assert all(torch.isfinite(c).all() for c in got)
-        assert max_plane_error(got, want) <= tol
+        assert max_plane_error(got, want) <= tol, (i, "vs pk_poly_gemm")
+        oracle = polyref.poly_matmul([a.cpu().double() for a in A], [b.cpu().double() for b in B])
+        assert max_plane_error(got, oracle) <= tol, (i, "vs oracle")
 
 
 def test_noalloc_rejects_products_beyond_its_scratch():
