@@ -673,10 +673,13 @@ def train_sample_ids(batch, seq, seed=4321):
     return torch.randint(0, 32000, (batch, seq + 1), generator=g)
 
 
-def train_parity_and_cpu(layers, device, threads, batch=1, seq=256):
+def train_parity_and_cpu(layers, device, threads, batch=4, seq=256):
     """configs[4] at full width on a bounded sample (batch x seq tokens, parameters with nonzero
     higher coefficients): the GPU forward + backward against the oracle in float64 (parity), and
-    the oracle in float32 timed on the host cores (the CPU baseline)."""
+    the oracle in float32 timed on the host cores (the CPU baseline).  The float32 oracle's own
+    distance from float64 is reported beside the GPU's: some loss and gradient coefficients are
+    ill-conditioned in float32 whatever computes them, so the pass criterion per plane is
+    err <= max(1e-4, 3 x the float32 reference's err), as in the training parity tests."""
     from oracle import polyref as R
     from polytensors_b200 import PolyTensor
 
@@ -693,20 +696,28 @@ def train_parity_and_cpu(layers, device, threads, batch=1, seq=256):
     del model, loss
     torch.cuda.empty_cache()
     _, want_loss, want = oracle_train_sample(init, ids, layers, torch.float64, threads)
-    loss_err = max(R.plane_errors(got_loss, want_loss))
-    grad_err, worst = 0.0, None
-    for k in want:
-        e = max(R.plane_errors(got[k], want[k]))
-        if e > grad_err:
-            grad_err, worst = e, k
-    dt, _, _ = oracle_train_sample(init, ids, layers, torch.float32, threads)
+    dt, r32_loss, r32 = oracle_train_sample(init, ids, layers, torch.float32, threads)
+    worst = {"err": 0.0, "ratio": 0.0}
+    ok = True
+    for name, g, w, r in [("loss", got_loss, want_loss, r32_loss)] + [(k, got[k], want[k], r32[k]) for k in want]:
+        e_gpu, e_ref = R.plane_errors(g, w), R.plane_errors(r, w)
+        for k, (a, b) in enumerate(zip(e_gpu, e_ref)):
+            bound = max(1e-4, 3 * b)
+            ok &= a <= bound
+            if a > worst["err"]:
+                worst.update(err=a, name=f"{name}[{k}]", reference_f32_err=b)
+            if a / bound > worst["ratio"]:
+                worst.update(ratio=a / bound, ratio_at=f"{name}[{k}]")
     tokens = batch * seq
-    parity = {"max_plane_err": max(loss_err, grad_err), "loss_max_plane_err": loss_err,
-              "grad_max_plane_err": grad_err, "worst_grad": worst, "tol": 1e-4,
-              "metric": "per coefficient plane max|gpu - oracle| / max|oracle|",
+    parity = {"max_plane_err": worst["err"], "at": worst.get("name"),
+              "reference_f32_err_there": worst.get("reference_f32_err"),
+              "max_err_over_bound": worst["ratio"], "bound_worst_at": worst.get("ratio_at"),
+              "within_tolerance": bool(ok),
+              "tol": "per plane: err <= max(1e-4, 3 x the float32 reference's err)",
+              "metric": "per coefficient plane max|x - oracle64| / max|oracle64|",
               "against": "oracle restatement of the reference's plain-range rules, float64, CPU",
               "sample": f"forward + backward of the full-width model on {batch} x {seq} tokens, "
-                        "weights with N(0,0.02)/k! higher coefficients"}
+                        "weights with N(0,0.02)/k! higher coefficients: loss and every parameter gradient"}
     cpu = {"value": tokens / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
            "sample": f"oracle forward + series backward, full width ({layers} layers), {batch} x {seq} tokens, "
                      f"float32, {dt:.1f} s",
@@ -959,22 +970,22 @@ def reference_arm(args, cfg):
 def reference_arm_train(args, budget_s=150.0):
     """--impl reference for the default (configs[4] training) workload: the reference algorithm
     (oracle restatement of its plain-range rules) for the full-width model's forward and series
-    backward on the host cores, each step a bounded sample of 1 x 256 tokens; steps beyond a
+    backward on the host cores, each step a bounded sample of 4 x 256 tokens; steps beyond a
     ~150 s budget are not run (the count is reported)."""
     threads = os.cpu_count() or 1
     init = transformer_init(layers=args.layers, seed=0)
-    ids = train_sample_ids(1, 256)
+    ids = train_sample_ids(4, 256)
     for _ in range(min(args.warmup, 1)):
         oracle_train_sample(init, ids, args.layers, torch.float32, threads)
     rates, used = [], 0.0
     for _ in range(args.steps):
         dt, _, _ = oracle_train_sample(init, ids, args.layers, torch.float32, threads)
-        rates.append(256 / dt)
+        rates.append(ids[:, 1:].numel() / dt)
         used += dt
         if used > budget_s:
             break
     value = statistics.median(rates)
-    sample = (f"oracle forward + series backward of the full-width model ({args.layers} layers), 1 x 256 tokens "
+    sample = (f"oracle forward + series backward of the full-width model ({args.layers} layers), 4 x 256 tokens "
               f"per step, float32, {len(rates)} of {args.steps} steps run")
     return {
         "impl": "reference",

@@ -354,8 +354,23 @@ static int launch_stage(const StageParams& p, int64_t batch, bool has_kind[5], c
 // tcgen05 path
 
 constexpr int TC_BM = 128;
+// k blocks (of 64) accumulated in tensor memory before a float32 product adds the segment into
+// its fp32 register sum (see the seg_iters comment in pk_poly_gemm)
+#ifndef PK_F32_SEGMENT
+#define PK_F32_SEGMENT 16
+#endif
+constexpr int PK_F32_SEGMENT_KBLOCKS = PK_F32_SEGMENT;
 constexpr int TC_EPI_WARPS = 8;  // two per TMEM lane quadrant, each draining half of the columns
 constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;  // warp 0: TMA, warp 1: MMA + TMEM owner, rest: epilogue
+// The float32 (split) product keeps a tile's running fp32 sum in the epilogue's registers, so it
+// has four epilogue warps per lane quadrant (a quarter of the columns each): at 256-column tiles
+// that is 64 sums per thread, which fit beside the loads without spilling.
+template <bool SPLIT>
+struct TcWarps {
+    static constexpr int EPI = SPLIT ? 16 : TC_EPI_WARPS;
+    static constexpr int GROUPS = EPI / 4;  // column groups per lane quadrant
+    static constexpr int THREADS = 64 + 32 * EPI;
+};
 
 // One tensor map per operand plane (3-D: k or rows innermost, then the other, then batch).
 // float32 products use a[0] / b[0] only, over the whole staged workspace.
@@ -379,6 +394,7 @@ struct TcParams {
                      // 3: only outputs n <= m + band_off are needed (causal scores)
     int64_t band_off;
     int K;           // reduction length (banded k ranges)
+    int seg_iters;   // float32 split: k-block iterations per accumulation segment (0 = one segment per tile)
     int64_t c_bs, c_rs;
     void* c[PK_MAX_PLANES];
     int* status;
@@ -520,8 +536,36 @@ __device__ __forceinline__ void store_row_chunk(const TcParams& p, int plane, in
     }
 }
 
+// W = 32: store_row_chunk.  W = 16 (a quarter of a 64-column float32 tile): the first 16 values of
+// r, float32 output (the only output kind of the split product).
+__device__ __forceinline__ void store_row_chunk_n(const TcParams& p, int plane, int b, int row, int col0,
+                                                  const uint32_t (&r)[32], int W) {
+    if (W == 32) {
+        store_row_chunk(p, plane, b, row, col0, r);
+        return;
+    }
+    if (row >= p.M) return;
+    const int64_t off = static_cast<int64_t>(b) * p.c_bs + static_cast<int64_t>(row) * p.c_rs + col0;
+    float* dst = static_cast<float*>(p.c[plane]) + off;
+    if ((col0 + 16 <= p.N) && p.vec_ok) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+            float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                   __uint_as_float(r[j + 3]));
+            if (p.accumulate) {
+                const float4 o = *reinterpret_cast<const float4*>(dst + j);
+                v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+            }
+            *reinterpret_cast<float4*>(dst + j) = v;
+        }
+    } else {
+        for (int j = 0; j < 16 && col0 + j < p.N; ++j)
+            dst[j] = __uint_as_float(r[j]) + (p.accumulate ? dst[j] : 0.f);
+    }
+}
+
 template <int BN, bool SPLIT>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+__global__ void __launch_bounds__(TcWarps<SPLIT>::THREADS, 1)
     tc_poly_gemm_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
     using Cfg = TcConfig<BN, SPLIT>;
     constexpr int STAGES = Cfg::STAGES;
@@ -547,7 +591,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(&acc_full[s], 1);
-            mbar_init(&acc_empty[s], 32 * TC_EPI_WARPS);
+            mbar_init(&acc_empty[s], 32 * TcWarps<SPLIT>::EPI);
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
@@ -655,14 +699,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 int kb0, kb1;
                 tile_kblocks(p, tc.tm, tc.tn, BN, kb0, kb1);
                 if (kb1 <= kb0) continue;  // no k block in the band: the epilogue writes the zeros
+                const int iters = (tc.plane + 1) * (kb1 - kb0);
+                // float32: the reduction runs in segments of seg_iters k blocks, each into a fresh
+                // accumulator (the two buffers alternate), summed by the epilogue in fp32 registers
+                const int seg = (SPLIT && p.seg_iters > 0) ? p.seg_iters : iters;
+                for (int s0 = 0; s0 < iters && ok; s0 += seg) {
+                const int s1 = min(iters, s0 + seg);
                 if (!mbar_wait_or_abort(&acc_empty[abuf], aphase ^ 1, abort_flag, p.status, 102)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + abuf * BN;
-                const int iters = (tc.plane + 1) * (kb1 - kb0);
-                for (int it = 0; it < iters; ++it) {
+                for (int it = s0; it < s1; ++it) {
                     if (!mbar_wait_or_abort(&full_bar[stage], phase, abort_flag, p.status, 103)) {
                         ok = false;
                         break;
@@ -679,7 +728,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const uint64_t b_step = p.b_mn ? (2048 >> 4) : (32 >> 4);
 #pragma unroll
                     for (int kk = 0; kk < TC_BK / 16; ++kk) {
-                        tc_mma_f16(d_tmem, ahd + kk * a_step, bhd + kk * b_step, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+                        tc_mma_f16(d_tmem, ahd + kk * a_step, bhd + kk * b_step, idesc, (it > s0 || kk > 0) ? 1u : 0u);
                         if constexpr (SPLIT) {
                             tc_mma_f16(d_tmem, ahd + kk * 2, sw128_kmajor_desc(b_lo) + kk * 2, idesc, 1u);
                             tc_mma_f16(d_tmem, sw128_kmajor_desc(a_lo) + kk * 2, bhd + kk * 2, idesc, 1u);
@@ -693,10 +742,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                 }
                 if (!ok) break;
-                tc_commit(&acc_full[abuf]);  // accumulator ready for the epilogue
+                tc_commit(&acc_full[abuf]);  // accumulator (segment) ready for the epilogue
                 if (++abuf == 2) {
                     abuf = 0;
                     aphase ^= 1;
+                }
                 }
             }
             if (!ok && issued) {
@@ -710,7 +760,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     } else {
         // ---------------- epilogue: TMEM -> registers -> global ----------------
-        // warp w drains lanes 32*(w%4).. (its TMEM lane quadrant) and column half (w-2)/4
+        // warp w drains lanes 32*(w%4).. (its TMEM lane quadrant) and column group (w-2)/4 (of two,
+        // or four for the float32 product)
         const uint32_t lane_base = 32u * (warp & 3);
         const int half = (warp - 2) >> 2;
         uint32_t abuf = 0, aphase = 0;
@@ -725,11 +776,58 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     uint32_t z[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j) z[j] = 0u;
-                    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c)
-                        store_row_chunk(p, tc.plane, tc.b, row, tc.tn * BN + c * 32, z);
+                    constexpr int GC = BN / TcWarps<SPLIT>::GROUPS;  // columns of this warp's group
+                    for (int c = 0; c < GC; c += 32)
+                        store_row_chunk_n(p, tc.plane, tc.b, row, tc.tn * BN + half * GC + c, z, GC < 32 ? GC : 32);
                 }
                 continue;
             }
+            if constexpr (SPLIT) {
+                // the tile's segments: each accumulator is read into registers and released at once,
+                // the partial sums added with round-to-nearest fp32 adds; stores after the last one
+                const int iters = (tc.plane + 1) * (kb1 - kb0);
+                const int seg = p.seg_iters > 0 ? p.seg_iters : iters;
+                const int nseg = (iters + seg - 1) / seg;
+                constexpr int GC = BN / TcWarps<SPLIT>::GROUPS;  // this thread's columns: 64, 32 or 16
+                constexpr int W = 16;                              // columns per TMEM load (registers)
+                constexpr int CH = GC / W;
+                float sum[CH][W];
+#pragma unroll
+                for (int c = 0; c < CH; ++c)
+#pragma unroll
+                    for (int j = 0; j < W; ++j) sum[c][j] = 0.f;
+                bool ok = true;
+                for (int sg = 0; sg < nseg; ++sg) {
+                    if (!mbar_wait_or_abort(&acc_full[abuf], aphase, abort_flag, p.status, 104)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int c = 0; c < CH; ++c) {
+                        uint32_t r[W];
+                        const uint32_t taddr = tmem_base + (lane_base << 16) + abuf * BN + half * GC + c * W;
+                        tmem_ld_32x32b_x16(taddr, r);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int j = 0; j < W; ++j) sum[c][j] = __fadd_rn(sum[c][j], __uint_as_float(r[j]));
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&acc_empty[abuf]);
+                    if (++abuf == 2) {
+                        abuf = 0;
+                        aphase ^= 1;
+                    }
+                }
+                if (!ok) break;
+#pragma unroll
+                for (int c = 0; c < CH; ++c) {
+                    uint32_t r[32];
+#pragma unroll
+                    for (int j = 0; j < W; ++j) r[j] = __float_as_uint(sum[c][j]);
+                    store_row_chunk_n(p, tc.plane, tc.b, row, tc.tn * BN + half * GC + c * W, r, W);
+                }
+            } else {
             if (!mbar_wait_or_abort(&acc_full[abuf], aphase, abort_flag, p.status, 104)) break;
             tc_fence_after();
 #pragma unroll 1
@@ -744,6 +842,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (++abuf == 2) {
                 abuf = 0;
                 aphase ^= 1;
+            }
             }
         }
     }
@@ -788,7 +887,7 @@ static int launch_tc(TcParams& p, const TcOperand& a, const TcOperand& b, cudaSt
     const int grid = static_cast<int>(std::min<int64_t>(total, num_sms()));
     void* tok;
     prof_begin("poly_gemm", stream, &tok);
-    PK_LAUNCHED(tc_poly_gemm_kernel<BN, SPLIT><<<grid, TC_THREADS, Cfg::SMEM_BYTES, stream>>>(maps, p));
+    PK_LAUNCHED(tc_poly_gemm_kernel<BN, SPLIT><<<grid, TcWarps<SPLIT>::THREADS, Cfg::SMEM_BYTES, stream>>>(maps, p));
     prof_end("poly_gemm", stream, tok);
     PK_CHECK_LAUNCH("pk_poly_gemm: tcgen05 kernel launch");
     return PK_OK;
@@ -1432,6 +1531,11 @@ static int poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N,
         tp.band = band;
         tp.band_off = band_off;
         tp.K = static_cast<int>(K);
+        // float32: the tensor core's fp32 accumulation loses precision in proportion to the number
+        // of k steps summed into one accumulator (measured: plane error ~3.7e-9 per k element at
+        // 8192^3, i.e. 1.4e-4 at degree 4), so the reduction of an output tile runs in segments of
+        // PK_F32_SEGMENT_KBLOCKS 64-wide k blocks whose results are added in fp32 registers
+        tp.seg_iters = dtype == PK_F32 ? PK_F32_SEGMENT_KBLOCKS : 0;
         tp.status = device_status_ptr();
         const int64_t tiles256 = ceil_div(M, TC_BM) * ceil_div(N, 256) * batch * P;
         // 256-column tiles when N fills them (a 128-wide N would leave half of every MMA on the

@@ -73,8 +73,11 @@ def check_product(M, n, dtype, tol, rows, complex_from=None, seed=0):
     torch.cuda.empty_cache()
     want = ref.poly_matmul(Ah, Bh)
     errs = assert_close(got, want, tol, f"{dtype} M=N=K={M} degree {n}")
+    print(f"product {dtype} M=N=K={M} degree {n}: plane errors {errs}")
     if dtype == torch.float64:
-        assert elementwise_rel(got, want) <= 1e-9
+        rel = elementwise_rel(got, want)
+        print(f"  elementwise relative error (entries >= 1e-2 max): {rel}")
+        assert rel <= 1e-9
     return errs
 
 
@@ -112,7 +115,7 @@ def test_attention_forward_at_config_length(dtype, tol):
     with torch.no_grad(), PolyTensor.plain_range():
         o = F.scaled_dot_product_attention(*(PolyTensor(tuple(X)) for X in (Q, Kp, V)), is_causal=True)
     want = ref.attention(_host(Q), _host(Kp), _host(V), is_causal=True)
-    assert_close([c.float().cpu() for c in o.coeffs], want, tol, "o")
+    print(f"attention forward {dtype} L=4096:", assert_close([c.float().cpu() for c in o.coeffs], want, tol, "o"))
 
 
 @pytest.mark.parametrize("dtype,tol_o,tol_g", [(torch.float32, 1e-4, 1e-4), (torch.bfloat16, 2e-2, 5e-2)])
@@ -128,10 +131,10 @@ def test_attention_backward_at_1024(dtype, tol_o, tol_g):
         o.backward(PolyTensor(tuple(G)))
     fn = lambda a, b, c: ref.attention(a, b, c, is_causal=True)   # noqa: E731
     host = [_host(X) for X in (Q, Kp, V, G)]
-    assert_close([c.float().cpu() for c in o.coeffs], fn(*host[:3]), tol_o, "o")
+    print(f"attention {dtype} L=1024 o:", assert_close([c.float().cpu() for c in o.coeffs], fn(*host[:3]), tol_o, "o"))
     want = ref.series_vjp(fn, host[:3], host[3])
     for name, t, w in (("dq", q, want[0]), ("dk", k, want[1]), ("dv", v, want[2])):
-        assert_close([c.float().cpu() for c in t.grad.coeffs], w, tol_g, name)
+        print(f"  {name}:", assert_close([c.float().cpu() for c in t.grad.coeffs], w, tol_g, name))
 
 
 # ----------------------------------------------------------------------------------------
@@ -139,7 +142,12 @@ def test_attention_backward_at_1024(dtype, tol_o, tol_g):
 
 def test_norm_gelu_linear_ce_chain_at_config_width():
     """256 rows of the configs[2] chain (hidden 4096, vocabulary 32000, degree 4, float32),
-    forward and backward through the API, against the oracle's series backward in float64."""
+    forward and backward through the API, against the oracle's series backward in float64.
+
+    The per-row loss planes (reduction 'none') are checked at 1e-4 of their plane max-norm.  The
+    mean loss is a scalar per plane whose value can be far smaller than its terms (the mean of
+    256 row losses of both signs), so its error is measured against the same per-row max-norm:
+    the scale of the numbers being averaged."""
     from polytensors_b200 import PolyTensor
 
     n, R, H, V = 4, 256, 4096, 32000
@@ -152,17 +160,25 @@ def test_norm_gelu_linear_ce_chain_at_config_width():
         x = PolyTensor(tuple(X), requires_grad=True)
         w = PolyTensor((w0.cuda(),), degree=n, requires_grad=True)
         W = PolyTensor((W0.cuda(),), degree=n, requires_grad=True)
-        loss = F.cross_entropy(F.linear(F.gelu(F.rms_norm(x, (H,), w)), W), target.cuda())
+        logits = F.linear(F.gelu(F.rms_norm(x, (H,), w)), W)
+        rows = F.cross_entropy(logits, target.cuda(), reduction="none")
+        loss = F.cross_entropy(logits, target.cuda())
         loss.backward()
 
-    def chain(xs, ws, wl):
+    def chain(xs, ws, wl, reduction="mean"):
         h = ref.gelu(ref.rms_norm(xs, (H,), ws))
-        return ref.cross_entropy(ref.cauchy(h, [t.t() for t in wl], lambda a, b: a @ b), target)
+        return ref.cross_entropy(ref.cauchy(h, [t.t() for t in wl], lambda a, b: a @ b), target, reduction=reduction)
 
     zeros = lambda t: [t.double()] + [torch.zeros_like(t, dtype=torch.float64) for _ in range(n)]   # noqa: E731
     inputs = [_host(X), zeros(w0), zeros(W0)]
-    assert_close([c.cpu() for c in loss.coeffs], chain(*inputs), 1e-4, "loss")
+    want_rows = chain(*inputs, reduction="none")
+    print("chain row losses:", assert_close([c.detach().cpu() for c in rows.coeffs], want_rows, 1e-4, "row losses"))
+    want = chain(*inputs)
+    for k, (got_k, want_k, rk) in enumerate(zip(loss.coeffs, want, want_rows)):
+        err = abs(got_k.item() - want_k.item()) / rk.abs().max().item()
+        print(f"  mean loss plane {k}: error / max row loss = {err:.3g}")
+        assert err <= 1e-4, (k, err)
     seed = [torch.tensor(1.0, dtype=torch.float64)] + [torch.tensor(0.0, dtype=torch.float64)] * n
-    want = ref.series_vjp(chain, inputs, seed)
-    for name, t, wt in (("dx", x, want[0]), ("dw", w, want[1]), ("dW", W, want[2])):
-        assert_close([c.cpu() for c in t.grad.coeffs], wt, 1e-4, name)
+    grads = ref.series_vjp(chain, inputs, seed)
+    for name, t, wt in (("dx", x, grads[0]), ("dw", w, grads[1]), ("dW", W, grads[2])):
+        print(f"  {name}:", assert_close([c.cpu() for c in t.grad.coeffs], wt, 1e-4, name))
