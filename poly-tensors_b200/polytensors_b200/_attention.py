@@ -37,13 +37,11 @@ _FUSED_BLOCK_BYTES = 16 << 30
 
 
 def _poly_cls():
-    from ._tensor import PolyTensor
-
-    return PolyTensor
+    return _state.poly_cls()
 
 
-def _planes(x, degree):
-    P = _poly_cls()
+def _planes(x, degree, P=None):
+    P = P or _poly_cls()
     if isinstance(x, P):
         return list(x.coeffs)
     return [x] + [torch.zeros_like(x) for _ in range(degree)]
@@ -295,16 +293,17 @@ class _SeriesAttention(torch.autograd.Function):
         ctx.saved = (Q, Kp, V, O, stats)
         ctx.meta = (causal, scale, D, query.shape, key.shape, value.shape)
         ctx.poly = tuple(isinstance(t, P) for t in (query, key, value))
+        ctx.cls = P
         out_shape = (*query.shape[:-1], value.shape[-1])
         return P(tuple(o.view(out_shape) for o in O))
 
     @staticmethod
     @torch.autograd.function.once_differentiable
     def backward(ctx, grad):
-        P = _poly_cls()
+        P = ctx.cls
         Q, Kp, V, O, stats = ctx.saved
         causal, scale, D, qs, ks, vs = ctx.meta
-        dO = _flat(_planes(grad, D), (*qs[:-1], vs[-1]))
+        dO = _flat(_planes(grad, D, P), (*qs[:-1], vs[-1]))
         need = tuple(p and n for p, n in zip(ctx.poly, ctx.needs_input_grad[:3]))
         dQ, dK, dV = backward_planes(Q, Kp, V, O, dO, causal, scale, need, stats)
         grads = []

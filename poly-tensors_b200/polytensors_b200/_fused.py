@@ -17,9 +17,7 @@ from . import _state
 
 
 def _poly_cls():
-    from ._tensor import PolyTensor
-
-    return PolyTensor
+    return _state.poly_cls()
 
 
 def _planes(x, degree):
@@ -29,9 +27,8 @@ def _planes(x, degree):
     return [x] + [torch.zeros_like(x) for _ in range(degree)]
 
 
-def _grad_planes(g, degree):
+def _grad_planes(g, degree, P):
     """Incoming gradient: a PolyTensor, or an ordinary tensor meaning zero higher planes."""
-    P = _poly_cls()
     if isinstance(g, P):
         return list(g.coeffs)
     return [g] + [torch.zeros_like(g) for _ in range(degree)]
@@ -69,12 +66,13 @@ class _SeriesRMSNorm(torch.autograd.Function):
         ctx.cols, ctx.shape, ctx.eps, ctx.degree = cols, shape, eps, D
         ctx.w_poly = isinstance(weight, P)
         ctx.w_shape = weight.shape if weight is not None else None
+        ctx.cls = P
         return P(tuple(y))
 
     @staticmethod
     def backward(ctx, grad):
-        P = _poly_cls()
-        G = _grad_planes(grad, ctx.degree)
+        P = ctx.cls
+        G = _grad_planes(grad, ctx.degree, P)
         want_dw = ctx.w_planes is not None and ctx.needs_input_grad[1]
         if torch.is_grad_enabled():
             # Further reverse derivatives: differentiable series operations instead of the kernel.
@@ -145,13 +143,14 @@ class _SeriesCrossEntropy(torch.autograd.Function):
         loss, stats = K.cross_entropy_fwd(Z, target, ignore_index, softcap)
         ctx.z, ctx.target, ctx.stats = Z, target, stats
         ctx.ignore_index, ctx.softcap, ctx.degree = ignore_index, softcap, logits.degree
+        ctx.cls = P
         return P(tuple(loss))
 
     @staticmethod
     @torch.autograd.function.once_differentiable
     def backward(ctx, grad):
-        P = _poly_cls()
-        G = _grad_planes(grad, ctx.degree)
+        P = ctx.cls
+        G = _grad_planes(grad, ctx.degree, P)
         dz = K.cross_entropy_bwd(ctx.z, ctx.target, ctx.ignore_index, ctx.softcap, ctx.stats, G)
         return P(tuple(dz)), None, None, None
 

@@ -9,7 +9,7 @@ is one CUDA kernel over all coefficient planes (see ``_dispatch.py`` and ``_fuse
 """
 
 import contextlib
-import contextvars
+import functools
 import operator
 
 import torch
@@ -17,11 +17,109 @@ import torch
 from . import _state
 from ._dispatch import dispatch
 
-_COMPLEX_OF = {torch.float16: torch.complex32, torch.float32: torch.complex64, torch.float64: torch.complex128}
+# Complex dtype that may carry the directions of a real constant coefficient.
+_DIRECTION_DTYPE = {torch.float16: torch.complex32, torch.float32: torch.complex64, torch.float64: torch.complex128}
 
 
-def _overlaps(a, b):
+def _shares_memory(a, b):
     return torch._C._overlaps(a, b)
+
+
+def _is_canonical(planes):
+    """True when ``planes`` can be used as they are: plain dense tensors on one device with one
+    shape, a floating or complex constant coefficient, every higher coefficient of a single
+    dtype (the constant's, or its complex counterpart), and no two coefficients sharing memory."""
+    if not planes or any(type(c) is not torch.Tensor or c.layout != torch.strided for c in planes):
+        return False
+    head, rest = planes[0], planes[1:]
+    if not (head.dtype.is_floating_point or head.dtype.is_complex):
+        return False
+    if any(c.shape != head.shape or c.device != head.device for c in rest):
+        return False
+    if rest:
+        kinds = {c.dtype for c in rest}
+        if len(kinds) != 1 or kinds.pop() not in (head.dtype, _DIRECTION_DTYPE.get(head.dtype)):
+            return False
+    return not any(_shares_memory(planes[i], planes[j]) for i in range(1, len(planes)) for j in range(i))
+
+
+def _degree_argument(degree):
+    if degree is None:
+        return None
+    if isinstance(degree, bool):
+        raise TypeError("PolyTensor degree must be an int, not a bool")
+    degree = operator.index(degree)   # TypeError for floats and other non-integers
+    if degree < 0:
+        raise ValueError(f"PolyTensor degree must be nonnegative, got {degree}")
+    return degree
+
+
+def _to_tensors(items):
+    """Coefficients as tensors.  The constant coefficient fixes the device; a Python integer
+    there becomes the default floating dtype.  Later Python numbers are created directly at the
+    precision they promote to against the constant (no float32 round trip)."""
+    head = items[0]
+    if isinstance(head, torch.Tensor):
+        anchor = head
+    else:
+        anchor = torch.as_tensor(head)
+        if not (anchor.is_floating_point() or anchor.is_complex()):
+            anchor = anchor.to(torch.get_default_dtype())
+    out = []
+    for c in items:
+        if isinstance(c, torch.Tensor):
+            out.append(c)
+        else:
+            kind = torch.promote_types(anchor.dtype, torch.as_tensor(c).dtype)
+            out.append(torch.as_tensor(c, dtype=kind, device=anchor.device))
+    return out
+
+
+def _check_kinds(tensors):
+    device = tensors[0].device
+    for c in tensors:
+        if isinstance(c, PolyTensor):
+            raise TypeError("PolyTensor coefficients cannot themselves be PolyTensors (nested series)")
+        if c.layout != torch.strided:
+            raise TypeError(f"PolyTensor coefficients must be dense strided tensors, got layout {c.layout}")
+        if not (c.is_floating_point() or c.is_complex()):
+            raise TypeError(f"PolyTensor coefficients must have a floating-point or complex dtype, got {c.dtype}")
+        if c.device != device:
+            raise ValueError(f"PolyTensor coefficients must all be on the same device ({device} and {c.device})")
+
+
+def _planes_from(coeffs, degree=None):
+    """The coefficient tuple a PolyTensor stores for ``coeffs`` (a sequence or a PolyTensor)."""
+    items = tuple(coeffs.coeffs if isinstance(coeffs, PolyTensor) else coeffs)
+    if degree is None and _is_canonical(items):
+        return items
+    if not items:
+        raise ValueError("a PolyTensor needs at least one coefficient")
+    degree = _degree_argument(degree)
+    tensors = _to_tensors(items)
+    _check_kinds(tensors)
+    # one promoted dtype: the constant keeps its real precision unless it is complex itself;
+    # once any direction is complex, every direction is stored complex
+    widest = functools.reduce(torch.promote_types, (c.dtype for c in tensors))
+    real = widest.to_real() if widest.is_complex else widest
+    directions_complex = any(c.is_complex() for c in tensors[1:])
+    kinds = [widest if (c.is_complex() or (k and directions_complex)) else real for k, c in enumerate(tensors)]
+    tensors = [c.to(kind) for c, kind in zip(tensors, kinds)]
+    if degree is not None:
+        if degree + 1 < len(tensors):
+            raise ValueError(f"degree {degree} is lower than the {len(tensors) - 1} the coefficients need "
+                             "(it must be at least their degree)")
+        filler = tensors[-1]
+        tensors.extend(torch.zeros_like(filler) for _ in range(degree + 1 - len(tensors)))
+    shape = torch.broadcast_shapes(*(c.shape for c in tensors))
+    planes = []
+    for c in tensors:
+        if c.shape != shape:
+            c = c.expand(shape).clone()   # every order gets storage of its own shape
+        elif any(_shares_memory(c, q) for q in planes):
+            c = c.clone()                 # an in-place update of one order must not touch another
+        planes.append(c)
+    return tuple(planes)
 
 
 class PolyTensor(torch.Tensor):
@@ -39,111 +137,26 @@ class PolyTensor(torch.Tensor):
 
     @staticmethod
     def _coerce_coeffs(coeffs, degree=None):
-        """Validate and normalise a coefficient sequence (rules of src/polytensors/_tensor.py:37-96)."""
-        if isinstance(coeffs, PolyTensor):
-            coeffs = coeffs.coeffs
-        coeffs = tuple(coeffs)
-        if degree is None and PolyTensor._well_formed(coeffs):
-            return coeffs
-        if not coeffs:
-            raise ValueError("at least one coefficient is required")
-        if degree is not None:
-            if isinstance(degree, bool):
-                raise TypeError("degree must be a nonnegative integer")
-            degree = operator.index(degree)
-            if degree < 0:
-                raise ValueError("degree must be nonnegative")
-        first = coeffs[0]
-        base = first if isinstance(first, torch.Tensor) else torch.as_tensor(first)
-        if not isinstance(first, torch.Tensor) and not (base.is_floating_point() or base.is_complex()):
-            base = base.to(torch.get_default_dtype())
-        tensors = []
-        for c in coeffs:
-            if isinstance(c, torch.Tensor):
-                tensors.append(c)
-            else:
-                # Python numbers take the base's precision without a float32 round trip.
-                tensors.append(torch.as_tensor(c, device=base.device,
-                                               dtype=torch.promote_types(base.dtype, torch.as_tensor(c).dtype)))
-        for c in tensors:
-            if isinstance(c, PolyTensor):
-                raise TypeError("nested PolyTensor coefficients are not supported")
-            if c.layout != torch.strided:
-                raise TypeError("coefficients must be dense strided tensors")
-            if not (c.is_floating_point() or c.is_complex()):
-                raise TypeError("tensor coefficients must have floating-point or complex dtype")
-            if c.device != base.device:
-                raise ValueError("all coefficients must be on the same device")
-        common = tensors[0].dtype
-        for c in tensors[1:]:
-            common = torch.promote_types(common, c.dtype)
-        real = torch.empty((), dtype=common).real.dtype
-        complex_dirs = any(c.is_complex() for c in tensors[1:])
-        tensors = [c.to(dtype=common if (c.is_complex() or (k > 0 and complex_dirs)) else real)
-                   for k, c in enumerate(tensors)]
-        if degree is not None:
-            if degree < len(tensors) - 1:
-                raise ValueError("degree must be at least the degree of coeffs")
-            template = tensors[-1] if len(tensors) > 1 else tensors[0]
-            tensors += [torch.zeros_like(template) for _ in range(degree + 1 - len(tensors))]
-        shape = torch.broadcast_shapes(*(c.shape for c in tensors))
-        tensors = [c if c.shape == shape else c.expand(shape).clone() for c in tensors]
-        # Orders must be independently mutable: an in-place update of one order must not
-        # write into another through shared storage.
-        out = []
-        for c in tensors:
-            if any(_overlaps(c, prev) for prev in out):
-                c = c.clone()
-            out.append(c)
-        return tuple(out)
-
-    @staticmethod
-    def _well_formed(coeffs):
-        """Whether ``coeffs`` already satisfies every construction rule (the common case for
-        rule outputs), so construction can skip normalisation."""
-        if not coeffs:
-            return False
-        base = coeffs[0]
-        if type(base) is not torch.Tensor or base.layout != torch.strided:
-            return False
-        dtype = base.dtype
-        if not (dtype.is_floating_point or dtype.is_complex):
-            return False
-        higher = None
-        for c in coeffs[1:]:
-            if type(c) is not torch.Tensor or c.layout != torch.strided or c.shape != base.shape \
-                    or c.device != base.device:
-                return False
-            if higher is None:
-                higher = c.dtype
-                if higher != dtype and _COMPLEX_OF.get(dtype) != higher:
-                    return False
-            elif c.dtype != higher:
-                return False
-        for i in range(1, len(coeffs)):
-            for j in range(i):
-                if _overlaps(coeffs[i], coeffs[j]):
-                    return False
-        return True
+        """The normalised coefficient tuple (the constructor's rules; see ``_planes_from``)."""
+        return _planes_from(coeffs, degree)
 
     def _set_coeffs(self, coeffs):
-        self.coeffs = self._coerce_coeffs(coeffs)
+        self.coeffs = _planes_from(coeffs)
         self.degree = len(self.coeffs) - 1
 
     @staticmethod
     def __new__(cls, coeffs, *, degree=None, requires_grad=False):
-        coeffs = cls._coerce_coeffs(coeffs, degree)
-        base = coeffs[0]
-        out = torch.Tensor._make_wrapper_subclass(
-            cls, base.shape, strides=base.stride(), storage_offset=base.storage_offset(),
-            dtype=base.dtype, layout=base.layout, device=base.device, requires_grad=requires_grad)
-        out.coeffs = coeffs
-        out.degree = len(coeffs) - 1
-        # Autograd may keep only the C++ TensorImpl of a saved wrapper; retention scopes
-        # keep the Python object (and its coefficients) alive through backward.
-        for refs in _state.retention_scopes.get():
-            refs.append(out)
-        return out
+        planes = _planes_from(coeffs, degree)
+        head = planes[0]
+        self = torch.Tensor._make_wrapper_subclass(
+            cls, head.shape, strides=head.stride(), storage_offset=head.storage_offset(), dtype=head.dtype,
+            layout=head.layout, device=head.device, requires_grad=requires_grad)
+        self.coeffs, self.degree = planes, len(planes) - 1
+        # Autograd may hold only the C++ side of a saved wrapper; every open retention scope keeps
+        # the Python object (and so its coefficients) alive until the scope closes.
+        for scope in _state.retention_scopes.get():
+            scope.append(self)
+        return self
 
     def __init__(self, coeffs, *, degree=None, requires_grad=False):
         pass
@@ -239,21 +252,27 @@ class PolyTensor(torch.Tensor):
         return cross_entropy(logits, target, softcap=softcap, ignore_index=ignore_index, reduction=reduction)
 
     def backward(self, gradient=None, retain_graph=None, create_graph=False, inputs=None):
-        if gradient is None:
-            if self.numel() != 1:
-                raise RuntimeError("grad can be implicitly created only for scalar outputs")
-            if self.is_complex():
-                raise RuntimeError("an explicit gradient is required for a complex output")
-            gradient = PolyTensor.constant(torch.ones_like(self.value), self.degree)
-        elif not isinstance(gradient, PolyTensor):
-            gradient = PolyTensor.constant(gradient, self.degree)
-        torch.autograd.backward(self, gradient, retain_graph=retain_graph, create_graph=create_graph,
-                                inputs=inputs)
+        """Reverse-mode through the series: the seed is ``gradient`` as a PolyTensor of this degree
+        (an ordinary tensor is its constant term); with no gradient, a real scalar seeds 1."""
+        torch.autograd.backward(self, self._seed(gradient), retain_graph=retain_graph,
+                                create_graph=create_graph, inputs=inputs)
+
+    def _seed(self, gradient):
+        if isinstance(gradient, PolyTensor):
+            return gradient
+        if gradient is not None:
+            return PolyTensor.constant(gradient, self.degree)
+        if self.numel() != 1:
+            raise RuntimeError("backward() of a non-scalar PolyTensor needs an explicit gradient "
+                               "(grad can be implicitly created only for scalar outputs)")
+        if self.is_complex():
+            raise RuntimeError("backward() of a complex PolyTensor needs an explicit gradient")
+        return PolyTensor.constant(torch.ones_like(self.value), self.degree)
 
     def __repr__(self):
-        if not hasattr(self, "coeffs"):
-            return f"PolyTensor(<uninitialized>, requires_grad={self.requires_grad})"
-        return f"PolyTensor({self.coeffs}, requires_grad={self.requires_grad})"
+        planes = getattr(self, "coeffs", None)
+        body = "<uninitialized>" if planes is None else repr(planes)
+        return f"PolyTensor({body}, requires_grad={self.requires_grad})"
 
     # ------------------------------------------------------------------ interception
 

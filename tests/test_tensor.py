@@ -180,3 +180,35 @@ def test_checkpoint_round_trip_stacked_planes(tmp_path):
     torch.save({"x": 1}, bad)
     with pytest.raises(ValueError):
         checkpoint.load(bad)
+
+
+def test_construction_matches_the_reference_rules():
+    """Differential check of the constructor against the reference's own class (when the reference
+    package is installed): dtypes, shapes, values and storage independence of the coefficients."""
+    from refpkg import reference_package
+
+    ref = reference_package()
+    t = torch.tensor
+    base = torch.arange(3.0)
+    cases = [
+        ([1, 2], 4), ([1.5], None), ([t(1.0, dtype=torch.float64), 2 + 3j], 3), ([base, 1.0, base[:1]], None),
+        ([t([1.0, 2.0], dtype=torch.float16), t(3.0)], 2), ([t(1.0, dtype=torch.bfloat16), 0.5], None),
+        ([t(1.0), t(2.0, dtype=torch.complex64)], 1), ([t(1.0, dtype=torch.complex128), t(1.0)], None),
+        ([base, base, base], None), ([base.view(3, 1), t([1.0, 2.0])], 2), ([0.1234567891234], 1),
+        ([t(2.0, dtype=torch.float64), 0.1234567891234], None), ([True], 1),
+    ]
+    for coeffs, degree in cases:
+        got = PolyTensor(list(coeffs), degree=degree)
+        want = ref.PolyTensor(list(coeffs), degree=degree)
+        assert got.degree == want.degree, coeffs
+        for a, b in zip(got.coeffs, want.coeffs):
+            assert a.dtype == b.dtype and a.shape == b.shape and torch.equal(a, b), (coeffs, a, b)
+        for i in range(len(got.coeffs)):
+            for j in range(i):
+                assert not torch._C._overlaps(got.coeffs[i], got.coeffs[j])
+    for bad, degree, kind in (([], None, ValueError), ([1.0], -1, ValueError), ([1.0], True, TypeError),
+                              ([1.0], 1.5, TypeError), ([1.0, 2.0], 0, ValueError),
+                              ([t(1)], None, TypeError)):
+        for cls in (PolyTensor, ref.PolyTensor):
+            with pytest.raises(kind):
+                cls(list(bad), degree=degree)
