@@ -747,6 +747,19 @@ def run_train(args, rank, world, device):
                                                         "e2e", "roofline", "parity", "cpu_baseline", "gpu_launches",
                                                         "kernel_ms_per_launch", "clocks")}
         torch.cuda.empty_cache()
+    if world == 1 and not args.no_extras:
+        # configs[2] and configs[3] on the same GPU, a few steps each (per-op lines carried here so
+        # that every config is measured in the default run)
+        ns = argparse.Namespace(steps=min(args.steps, 3), warmup=2, rows=16384, seq=4096, batch=8,
+                                no_cpu_baseline=args.no_cpu_baseline, dtype="bf16")
+        keep = ("metric", "value", "unit", "ms_per_step", "steps", "config", "roofline", "kernels", "linear",
+                "forward", "cpu_baseline", "clocks")
+        extras["norm_ce"] = {k: v for k, v in run_norm_ce(ns, rank, world, device).items() if k in keep}
+        torch.cuda.empty_cache()
+        for dt in ("bf16", "f32"):
+            ns.dtype = dt
+            extras[f"attention_{dt}"] = {k: v for k, v in run_attention(ns, rank, world, device).items() if k in keep}
+            torch.cuda.empty_cache()
 
     parity = cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1011,6 +1024,7 @@ def main():
                     choices=sorted(WORKLOADS) + ["norm_ce", "attention", "attention_fwd", "train",
                                                  "poly_matmul_sweep"])
     ap.add_argument("--no-matmul", action="store_true", help="train: skip the configs[1] product line")
+    ap.add_argument("--no-extras", action="store_true", help="train: skip the configs[2] / configs[3] lines")
     ap.add_argument("--impl", default="polykern", choices=["polykern", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rows", type=int, default=16384, help="norm_ce: rows (batch*seq)")

@@ -152,6 +152,28 @@ PK_API int pk_poly_gemm_accumulate(int dtype, int degree, int64_t batch, int64_t
                  int a_complex_from, int b_complex_from,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * float32 polynomial product whose operands may arrive already split for the bf16 tensor
+ * cores: with a_hilo != 0, a_planes holds 2(n+1) bfloat16 planes hi_0, lo_0, hi_1, lo_1, ...
+ * (x_k ~= hi_k + lo_k, strides in bf16 elements) that are read in place — no staging pass —
+ * either k-contiguous or rows-contiguous, 16-byte aligned, other strides multiples of 8
+ * elements; with a_hilo == 0, n+1 float32 planes as in pk_poly_gemm (staged into the
+ * workspace).  Likewise for B.  Output: n+1 float32 planes, written or (accumulate != 0)
+ * added to; band / band_offset as in pk_poly_gemm_banded.  degree <= 7 when an operand is
+ * pre-split.  Used by the float32 attention (probability and score-gradient planes come out of
+ * the score kernels already split).  Replaces the same rule as pk_poly_gemm
+ * (src/polytensors/_plain.py:118-128) for that case.
+ */
+PK_API int pk_poly_gemm_hilo_workspace_query(int degree, int64_t batch, int64_t M, int64_t N, int64_t K,
+                                             const void* const* a_planes, int64_t a_bs, int64_t a_rs, int64_t a_cs,
+                                             int a_hilo, const void* const* b_planes, int64_t b_bs, int64_t b_rs,
+                                             int64_t b_cs, int b_hilo, size_t* bytes);
+PK_API int pk_poly_gemm_hilo(int degree, int64_t batch, int64_t M, int64_t N, int64_t K, const void* const* a_planes,
+                             int64_t a_bs, int64_t a_rs, int64_t a_cs, int a_hilo, const void* const* b_planes,
+                             int64_t b_bs, int64_t b_rs, int64_t b_cs, int b_hilo, void* const* c_planes,
+                             int64_t c_bs, int64_t c_rs, int accumulate, int band, int64_t band_offset,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------------
  * Elementwise series operations.  out = f(a) or f(a, b) for every element, all planes
  * at once.  Shapes broadcast through strides (0 for a broadcast dimension, at most 6

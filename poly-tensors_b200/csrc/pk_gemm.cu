@@ -395,6 +395,7 @@ struct TcParams {
     int64_t band_off;
     int K;           // reduction length (banded k ranges)
     int seg_iters;   // float32 split: k-block iterations per accumulation segment (0 = one segment per tile)
+    int a_pre, b_pre;  // float32 split: operand given as bf16 hi/lo planes read in place (maps 2i, 2i+1)
     int64_t c_bs, c_rs;
     void* c[PK_MAX_PLANES];
     int* status;
@@ -633,17 +634,39 @@ __global__ void __launch_bounds__(TcWarps<SPLIT>::THREADS, 1)
                         uint8_t* st = smem + stage * Cfg::STAGE_BYTES;
                         mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
                         if constexpr (SPLIT) {
-                            // staged workspace: z walks (batch, plane, hi/lo) sub-planes
+                            // staged workspace: z walks (batch, plane, hi/lo) sub-planes; a pre-split
+                            // operand has one map per hi / lo plane, K-major or MN-major (64-row atoms)
                             const int za = (tc.b * p.planes + i) * NSUB;
                             const int zb = (tc.b * p.planes + j) * NSUB;
 #pragma unroll
-                            for (int h = 0; h < NSUB; ++h)
-                                tma_load_3d(st + h * Cfg::A_BYTES, &maps.a[0], &full_bar[stage], kb * TC_BK,
-                                            tc.tm * TC_BM, za + h);
+                            for (int h = 0; h < NSUB; ++h) {
+                                uint8_t* dst = st + h * Cfg::A_BYTES;
+                                if (!p.a_pre) {
+                                    tma_load_3d(dst, &maps.a[0], &full_bar[stage], kb * TC_BK, tc.tm * TC_BM, za + h);
+                                } else if (p.a_mn) {
 #pragma unroll
-                            for (int h = 0; h < NSUB; ++h)
-                                tma_load_3d(st + NSUB * Cfg::A_BYTES + h * Cfg::B_BYTES, &maps.b[0], &full_bar[stage],
-                                            kb * TC_BK, tc.tn * BN, zb + h);
+                                    for (int hh = 0; hh < TC_BM / 64; ++hh)
+                                        tma_load_3d(dst + hh * 8192, &maps.a[2 * i + h], &full_bar[stage],
+                                                    tc.tm * TC_BM + hh * 64, kb * TC_BK, tc.b);
+                                } else {
+                                    tma_load_3d(dst, &maps.a[2 * i + h], &full_bar[stage], kb * TC_BK, tc.tm * TC_BM,
+                                                tc.b);
+                                }
+                            }
+#pragma unroll
+                            for (int h = 0; h < NSUB; ++h) {
+                                uint8_t* dst = st + NSUB * Cfg::A_BYTES + h * Cfg::B_BYTES;
+                                if (!p.b_pre) {
+                                    tma_load_3d(dst, &maps.b[0], &full_bar[stage], kb * TC_BK, tc.tn * BN, zb + h);
+                                } else if (p.b_mn) {
+#pragma unroll
+                                    for (int hh = 0; hh < BN / 64; ++hh)
+                                        tma_load_3d(dst + hh * 8192, &maps.b[2 * j + h], &full_bar[stage],
+                                                    tc.tn * BN + hh * 64, kb * TC_BK, tc.b);
+                                } else {
+                                    tma_load_3d(dst, &maps.b[2 * j + h], &full_bar[stage], kb * TC_BK, tc.tn * BN, tc.b);
+                                }
+                            }
                         } else {
                             // one map per plane, z = batch; MN-major tiles arrive as 64-row atoms
                             if (p.a_mn) {
@@ -730,8 +753,10 @@ __global__ void __launch_bounds__(TcWarps<SPLIT>::THREADS, 1)
                     for (int kk = 0; kk < TC_BK / 16; ++kk) {
                         tc_mma_f16(d_tmem, ahd + kk * a_step, bhd + kk * b_step, idesc, (it > s0 || kk > 0) ? 1u : 0u);
                         if constexpr (SPLIT) {
-                            tc_mma_f16(d_tmem, ahd + kk * 2, sw128_kmajor_desc(b_lo) + kk * 2, idesc, 1u);
-                            tc_mma_f16(d_tmem, sw128_kmajor_desc(a_lo) + kk * 2, bhd + kk * 2, idesc, 1u);
+                            const uint64_t ald = p.a_mn ? sw128_mnmajor_desc_lbo(a_lo, 8192) : sw128_kmajor_desc(a_lo);
+                            const uint64_t bld = p.b_mn ? sw128_mnmajor_desc_lbo(b_lo, 8192) : sw128_kmajor_desc(b_lo);
+                            tc_mma_f16(d_tmem, ahd + kk * a_step, bld + kk * b_step, idesc, 1u);
+                            tc_mma_f16(d_tmem, ald + kk * a_step, bhd + kk * b_step, idesc, 1u);
                         }
                     }
                     issued = true;
@@ -870,12 +895,16 @@ static int launch_tc(TcParams& p, const TcOperand& a, const TcOperand& b, cudaSt
     }
     TcMaps maps;
     std::memset(&maps, 0, sizeof(maps));
-    int rc = encode_operand(maps.a, a, p.planes, SPLIT, TC_BM);
+    // float32 operands are staged (one map over the workspace) or pre-split hi/lo planes read in
+    // place (one map per hi and lo plane)
+    p.a_pre = (SPLIT && a.mode != OPM_STAGED) ? 1 : 0;
+    p.b_pre = (SPLIT && b.mode != OPM_STAGED) ? 1 : 0;
+    int rc = encode_operand(maps.a, a, p.a_pre ? 2 * p.planes : p.planes, SPLIT && !p.a_pre, TC_BM);
     if (rc) return rc;
-    rc = encode_operand(maps.b, b, p.planes, SPLIT, BN);
+    rc = encode_operand(maps.b, b, p.b_pre ? 2 * p.planes : p.planes, SPLIT && !p.b_pre, BN);
     if (rc) return rc;
-    p.a_mn = (!SPLIT && a.mode == OPM_MNMAJOR) ? 1 : 0;
-    p.b_mn = (!SPLIT && b.mode == OPM_MNMAJOR) ? 1 : 0;
+    p.a_mn = a.mode == OPM_MNMAJOR ? 1 : 0;
+    p.b_mn = b.mode == OPM_MNMAJOR ? 1 : 0;
     p.tiles_m = static_cast<int>(ceil_div(p.M, TC_BM));
     p.tiles_n = static_cast<int>(ceil_div(p.N, BN));
     // row-tile groups of 16: a wave of ~148 tiles spans 16 row tiles x ~9 column tiles, so each
@@ -1345,6 +1374,7 @@ static int elem_size(int dtype) {
 
 struct GemmPlan {
     int a_mode = OPM_STAGED, b_mode = OPM_STAGED;
+    bool unaddressable = false;  // a pre-split (hi/lo) operand the tensor maps cannot read in place
     int64_t Kp = 0;
     int64_t a_subs = 0, b_subs = 0;  // per batch entry
     size_t a_bytes = 0, b_bytes = 0, total = 0;
@@ -1384,13 +1414,19 @@ static GemmPlan plan_gemm(int dtype, int degree, int64_t batch, int64_t M, int64
 }
 
 // The plan for one call: operands read in place need no workspace.
+// float32 operands may come pre-split (a_hilo / b_hilo): 2(n+1) bf16 planes hi_0, lo_0, hi_1, ...
+// read in place, so they are never staged.
 static GemmPlan plan_call(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K, int acf, int bcf,
                           const void* const* a_planes, int64_t a_bs, int64_t a_rs, int64_t a_cs,
-                          const void* const* b_planes, int64_t b_bs, int64_t b_rs, int64_t b_cs) {
+                          const void* const* b_planes, int64_t b_bs, int64_t b_rs, int64_t b_cs, int a_hilo = 0,
+                          int b_hilo = 0) {
     GemmPlan g = plan_gemm(dtype, degree, batch, M, N, K, acf, bcf);
     const int P = degree + 1;
-    g.a_mode = operand_mode(dtype, a_planes, P, batch, M, K, a_bs, a_rs, a_cs);
-    g.b_mode = operand_mode(dtype, b_planes, P, batch, N, K, b_bs, b_cs, b_rs);
+    g.a_mode = a_hilo ? operand_mode(PK_BF16, a_planes, 2 * P, batch, M, K, a_bs, a_rs, a_cs)
+                      : operand_mode(dtype, a_planes, P, batch, M, K, a_bs, a_rs, a_cs);
+    g.b_mode = b_hilo ? operand_mode(PK_BF16, b_planes, 2 * P, batch, N, K, b_bs, b_cs, b_rs)
+                      : operand_mode(dtype, b_planes, P, batch, N, K, b_bs, b_cs, b_rs);
+    g.unaddressable = (a_hilo && g.a_mode == OPM_STAGED) || (b_hilo && g.b_mode == OPM_STAGED);
     if (g.a_mode != OPM_STAGED) g.a_bytes = 0;
     if (g.b_mode != OPM_STAGED) g.b_bytes = 0;
     g.total = (g.a_bytes + g.b_bytes) ? g.a_bytes + g.b_bytes + 1024 : 0;
@@ -1437,7 +1473,7 @@ static int poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N,
                      int64_t a_bs, int64_t a_rs, int64_t a_cs, const void* const* b_planes, int64_t b_bs, int64_t b_rs,
                      int64_t b_cs, void* const* c_planes, int64_t c_bs, int64_t c_rs, int a_complex_from,
                      int b_complex_from, void* workspace, size_t workspace_bytes, void* stream_ptr, int accumulate,
-                     int band = 0, int64_t band_off = 0) {
+                     int band = 0, int64_t band_off = 0, int a_hilo = 0, int b_hilo = 0) {
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     if (degree < 0 || degree >= PK_MAX_PLANES)
         return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm: degree must be in [0, " + std::to_string(PK_MAX_PLANES - 1) + "]");
@@ -1472,10 +1508,18 @@ static int poly_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N,
     }
 
     if (!a_planes || !b_planes) return fail(PK_ERR_ARG, "pk_poly_gemm: null operand plane array");
-    for (int p = 0; p < P; ++p)
-        if (!a_planes[p] || !b_planes[p]) return fail(PK_ERR_ARG, "pk_poly_gemm: null operand plane pointer");
+    if ((a_hilo || b_hilo) && (dtype != PK_F32 || 2 * P > PK_MAX_PLANES))
+        return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm_hilo: pre-split operands are float32 products of degree <= 7");
+    for (int p = 0; p < (a_hilo ? 2 * P : P); ++p)
+        if (!a_planes[p]) return fail(PK_ERR_ARG, "pk_poly_gemm: null operand plane pointer");
+    for (int p = 0; p < (b_hilo ? 2 * P : P); ++p)
+        if (!b_planes[p]) return fail(PK_ERR_ARG, "pk_poly_gemm: null operand plane pointer");
     const GemmPlan g = plan_call(dtype, degree, batch, M, N, K, a_complex_from, b_complex_from, a_planes, a_bs, a_rs,
-                                 a_cs, b_planes, b_bs, b_rs, b_cs);
+                                 a_cs, b_planes, b_bs, b_rs, b_cs, a_hilo, b_hilo);
+    if (g.unaddressable)
+        return fail(PK_ERR_UNSUPPORTED,
+                    "pk_poly_gemm_hilo: pre-split planes need 16-byte aligned bases, k or rows contiguous and the "
+                    "other strides multiples of 8 elements");
     if (g.total > 0 && (!workspace || workspace_bytes < g.total))
         return fail(PK_ERR_WORKSPACE, "pk_poly_gemm: workspace of " + std::to_string(g.total) + " bytes required");
     char* ws = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(workspace) + 1023) & ~uintptr_t(1023));
@@ -1673,6 +1717,35 @@ int pk_poly_gemm_accumulate(int dtype, int degree, int64_t batch, int64_t M, int
                             void* workspace, size_t workspace_bytes, void* stream) {
     return poly_gemm(dtype, degree, batch, M, N, K, a_planes, a_bs, a_rs, a_cs, b_planes, b_bs, b_rs, b_cs, c_planes,
                      c_bs, c_rs, a_complex_from, b_complex_from, workspace, workspace_bytes, stream, 1);
+}
+
+int pk_poly_gemm_hilo_workspace_query(int degree, int64_t batch, int64_t M, int64_t N, int64_t K,
+                                      const void* const* a_planes, int64_t a_bs, int64_t a_rs, int64_t a_cs, int a_hilo,
+                                      const void* const* b_planes, int64_t b_bs, int64_t b_rs, int64_t b_cs, int b_hilo,
+                                      size_t* bytes) {
+    if (!bytes) return fail(PK_ERR_ARG, "pk_poly_gemm_hilo_workspace_query: null result pointer");
+    *bytes = 0;
+    if (degree < 0 || 2 * (degree + 1) > PK_MAX_PLANES || batch < 0 || M < 0 || N < 0 || K < 0)
+        return fail(PK_ERR_ARG, "pk_poly_gemm_hilo_workspace_query: invalid degree or size");
+    if (batch == 0 || M == 0 || N == 0 || K == 0) return PK_OK;
+    if (!a_planes || !b_planes) return fail(PK_ERR_ARG, "pk_poly_gemm_hilo_workspace_query: null operand plane array");
+    const GemmPlan g = plan_call(PK_F32, degree, batch, M, N, K, degree + 1, degree + 1, a_planes, a_bs, a_rs, a_cs,
+                                 b_planes, b_bs, b_rs, b_cs, a_hilo ? 1 : 0, b_hilo ? 1 : 0);
+    if (g.unaddressable)
+        return fail(PK_ERR_UNSUPPORTED, "pk_poly_gemm_hilo_workspace_query: pre-split planes not addressable in place");
+    *bytes = g.total;
+    return PK_OK;
+}
+
+int pk_poly_gemm_hilo(int degree, int64_t batch, int64_t M, int64_t N, int64_t K, const void* const* a_planes,
+                      int64_t a_bs, int64_t a_rs, int64_t a_cs, int a_hilo, const void* const* b_planes, int64_t b_bs,
+                      int64_t b_rs, int64_t b_cs, int b_hilo, void* const* c_planes, int64_t c_bs, int64_t c_rs,
+                      int accumulate, int band, int64_t band_offset, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+    if (band < 0 || band > 3) return fail(PK_ERR_ARG, "pk_poly_gemm_hilo: band must be 0, 1, 2 or 3");
+    return poly_gemm(PK_F32, degree, batch, M, N, K, a_planes, a_bs, a_rs, a_cs, b_planes, b_bs, b_rs, b_cs, c_planes,
+                     c_bs, c_rs, degree + 1, degree + 1, workspace, workspace_bytes, stream, accumulate ? 1 : 0, band,
+                     band_offset, a_hilo ? 1 : 0, b_hilo ? 1 : 0);
 }
 
 }  // extern "C"

@@ -172,6 +172,70 @@ def poly_matmul(a_planes, b_planes, out=None, accumulate=False, band=0, band_off
     return outs
 
 
+def split_hilo(planes):
+    """float32 planes -> [hi_0, lo_0, hi_1, lo_1, ...] bfloat16 planes with x ~= hi + lo (the
+    operand form pk_poly_gemm_hilo reads in place)."""
+    out = []
+    for x in planes:
+        hi = x.to(torch.bfloat16)
+        out += [hi, (x - hi.float()).to(torch.bfloat16)]
+    return out
+
+
+def poly_matmul_hilo(a, a_hilo, b, b_hilo, out=None, accumulate=False, band=0, band_offset=0):
+    """float32 polynomial product (pk_poly_gemm_hilo) whose operands are float32 planes (n+1) or,
+    with ``*_hilo``, pre-split bf16 planes [hi_0, lo_0, ...] (2(n+1)) read in place.  Shapes
+    (M, K) x (K, N) or batched (B, M, K) x (B, K, N); returns / fills float32 output planes."""
+    P = len(a) // (2 if a_hilo else 1)
+    if P != len(b) // (2 if b_hilo else 1) or P == 0:
+        raise ValueError("poly_matmul_hilo: operands must have the same degree")
+    _require_cuda((*a, *b), "poly_matmul_hilo")
+    for planes, hilo in ((a, a_hilo), (b, b_hilo)):
+        want = torch.bfloat16 if hilo else torch.float32
+        if any(t.dtype != want for t in planes):
+            raise NotImplementedError(f"poly_matmul_hilo: expected {want} planes")
+    a, b = _uniform(a), _uniform(b)
+    a0, b0 = a[0], b[0]
+    batched = a0.dim() == 3
+    if batched:
+        batch, M, K = a0.shape
+        N = b0.shape[2]
+        (a_bs, a_rs, a_cs), (b_bs, b_rs, b_cs) = a0.stride(), b0.stride()
+    else:
+        batch, (M, K), N = 1, a0.shape, b0.shape[1]
+        a_bs, (a_rs, a_cs) = 0, a0.stride()
+        b_bs, (b_rs, b_cs) = 0, b0.stride()
+    shape = (batch, M, N) if batched else (M, N)
+    if out is None:
+        if accumulate:
+            raise ValueError("poly_matmul_hilo: accumulate needs output planes")
+        outs = [torch.empty(shape, dtype=torch.float32, device=a0.device) for _ in range(P)]
+    else:
+        outs = list(out)
+        if any(tuple(o.shape) != shape or o.dtype != torch.float32 or o.stride() != outs[0].stride() for o in outs):
+            raise ValueError("poly_matmul_hilo: output planes must match the product's shape and strides")
+        if outs[0].stride(-1) != 1:
+            raise NotImplementedError("poly_matmul_hilo: output planes need unit column stride")
+    st = outs[0].stride()
+    c_bs, c_rs = (st[0], st[1]) if batched else (0, st[0])
+    lib = _lib.load()
+    if _lib.profiling():
+        _lib.add_gemm_flops(product_flops(_lib.PK_F32, P - 1, batch, M, N, K, P, P, band, band_offset))
+    pa, ka = _lib.pointer_array(a)
+    pb, kb = _lib.pointer_array(b)
+    pc, kc = _lib.pointer_array(outs)
+    ws_bytes = ctypes.c_size_t(0)
+    _lib.check(lib.pk_poly_gemm_hilo_workspace_query(P - 1, batch, M, N, K, pa, a_bs, a_rs, a_cs, int(a_hilo),
+                                                     pb, b_bs, b_rs, b_cs, int(b_hilo), ctypes.byref(ws_bytes)),
+               "pk_poly_gemm_hilo_workspace_query")
+    ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device=a0.device) if ws_bytes.value else None
+    status = lib.pk_poly_gemm_hilo(P - 1, batch, M, N, K, pa, a_bs, a_rs, a_cs, int(a_hilo), pb, b_bs, b_rs, b_cs,
+                                   int(b_hilo), pc, c_bs, c_rs, 1 if accumulate else 0, int(band), int(band_offset),
+                                   ws.data_ptr() if ws is not None else None, ws_bytes.value, _stream(a0.device))
+    _lib.check(status, "pk_poly_gemm_hilo")
+    return outs
+
+
 # ------------------------------------------------------------------------------------
 # elementwise series operations, reductions, gathers
 

@@ -49,6 +49,10 @@ SIGNATURES = {
                                        _pp, _i64, _i64, _i64,
                                        _pp, _i64, _i64,
                                        _i32, _i32, _vp, _sz, _vp]),
+    "pk_poly_gemm_hilo_workspace_query": (_i32, [_i32, _i64, _i64, _i64, _i64, _pp, _i64, _i64, _i64, _i32,
+                                                 _pp, _i64, _i64, _i64, _i32, ctypes.POINTER(ctypes.c_size_t)]),
+    "pk_poly_gemm_hilo": (_i32, [_i32, _i64, _i64, _i64, _i64, _pp, _i64, _i64, _i64, _i32,
+                                 _pp, _i64, _i64, _i64, _i32, _pp, _i64, _i64, _i32, _i32, _i64, _vp, _sz, _vp]),
     "pk_series_map": (_i32, [_i32, _i32, _i32, _i32, _p64, _pp, _p64, _pp, _i32, _p64, _pp, _i32, _p64,
                              ctypes.c_double, ctypes.c_double, _vp]),
     "pk_series_reduce": (_i32, [_i32, _i32, _i64, _i64, _i64, _pp, _pp, ctypes.c_double, _vp]),

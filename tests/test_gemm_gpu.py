@@ -291,3 +291,31 @@ def test_device_status_clean():
     from polytensors_b200 import _lib
 
     assert _lib.load().pk_device_status(1) == 0
+
+
+@pytest.mark.parametrize("M,N,K,n,a_mn,b_mn", [(256, 192, 320, 3, False, False), (200, 136, 512, 3, True, False),
+                                               (384, 64, 1000, 2, True, True), (130, 264, 256, 1, False, True)])
+def test_hilo_product_reads_presplit_operands(M, N, K, n, a_mn, b_mn):
+    """pk_poly_gemm_hilo: A (and B) given as bf16 hi/lo planes, k-contiguous or rows-contiguous
+    (MN-major), read in place; against the float32 product of the same values (hi + lo) and the
+    float64 oracle, plain and accumulated (tolerance 1e-4 of the plane max-norm)."""
+    from gpu_util import assert_close
+    from polytensors_b200 import _kernels as K_
+
+    A = [a.cuda() for a in series((M, K), n, 71, torch.float32)]
+    B = [b.cuda() for b in series((K, N), n, 72, torch.float32)]
+    Ahl, Bhl = K_.split_hilo(A), K_.split_hilo(B)
+    if a_mn:
+        Ahl = [t.t().contiguous().t() for t in Ahl]
+    if b_mn:
+        Bhl = [t.t().contiguous().t() for t in Bhl]
+    # the values the pre-split operands carry exactly
+    A2 = [Ahl[2 * k].float() + Ahl[2 * k + 1].float() for k in range(n + 1)]
+    B2 = [Bhl[2 * k].float() + Bhl[2 * k + 1].float() for k in range(n + 1)]
+    want = ref.poly_matmul([a.cpu().double() for a in A2], [b.cpu().double() for b in B2])
+    for a_args, b_args in (((Ahl, True), (B, False)), ((A, False), (Bhl, True)), ((Ahl, True), (Bhl, True))):
+        got = K_.poly_matmul_hilo(*a_args, *b_args)
+        assert_close([g.cpu() for g in got], want, 1e-4, f"hilo {a_args[1]} {b_args[1]}")
+    C = [torch.ones(M, N, device="cuda") for _ in range(n + 1)]
+    K_.poly_matmul_hilo(Ahl, True, Bhl, True, out=C, accumulate=True)
+    assert_close([c.cpu() for c in C], [w + 1 for w in want], 1e-4, "accumulate")
