@@ -312,6 +312,9 @@ PK_API int pk_attn_dscores(int dtype, int degree, int64_t rows, int64_t cols,
  * admissible for query i when j <= i (causal != 0).  Generalises the degree-1 Triton forward
  * (src/polytensors/_attention_kernels.py:27-82) and replaces the decomposition of
  * src/polytensors/_decompositions.py:28-43 (whose (L, S) score series it never forms).
+ * dtype PK_F32 (float32 attention, head dim 64): q, k, v each hold 2(n+1) bf16 planes
+ * hi_0, lo_0, hi_1, ... with x ~= hi + lo, every product evaluated as hi*hi + hi*lo + lo*hi
+ * with fp32 accumulation; o holds n+1 float32 planes.
  */
 PK_API int pk_flash_attn_fwd(int dtype, int degree, int64_t bh, int64_t L, int64_t S, int64_t D,
                              const void* const* q, const void* const* k, const void* const* v,
@@ -338,6 +341,10 @@ PK_API int pk_flash_attn_fwd(int dtype, int degree, int64_t bh, int64_t L, int64
  * Together they replace the score and softmax-backward steps of the reference's attention
  * backward (src/polytensors/_decompositions.py:28-43 through src/polytensors/_plain.py:342-347;
  * degree-1 Triton form src/polytensors/_attention_kernels.py:84-201).
+ * dtype PK_F32 (float32 attention, reduction <= 64): every plane array — operands, probs and
+ * the output — holds 2(n+1) bf16 planes hi_0, lo_0, hi_1, ... (x ~= hi + lo); products are
+ * hi*hi + hi*lo + lo*hi in fp32 and the outputs are written split the same way, ready for
+ * pk_poly_gemm_hilo.
  */
 PK_API int pk_attn_probs_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K,
                               const void* const* q, int64_t q_bs, int64_t q_rs, int64_t q_cs,

@@ -41,7 +41,7 @@ constexpr int AG_MAX_K = 128;                     // reduction held resident (he
 constexpr int AG_MAX_STAGES = 24;
 constexpr int AG_WARP_OUT = 32 * 16 * 2;          // one epilogue warp's 32 rows x 16 columns of one plane, bf16
 constexpr int AG_OUT_BYTES = AG_EPI_WARPS * 2 * AG_WARP_OUT;  // 2 buffers per epilogue warp (TMA-store staging)
-constexpr int AG_SMEM_BUDGET = 220 * 1024;        // resident A + B ring + output staging
+constexpr int AG_SMEM_BUDGET = 224 * 1024;        // resident A + B ring + output staging
 constexpr int AG_SMEM_BYTES = AG_SMEM_BUDGET + 1024 + 512;
 constexpr int AG_CHUNK = 8;                       // B tiles per work unit
 constexpr int AG_MAX_NP = 4;
@@ -50,10 +50,12 @@ constexpr int64_t AG_FAR_KEYS = 192;              // causal == 2: zero tiles wri
 
 enum { AG_PROBS = 0, AG_DSCORES = 1 };
 
+// Plane i (sub-plane h of NS: bf16 planes NS = 1; float32 attention NS = 2, x ~= hi + lo) at index
+// i * NS + h of each array.
 struct AgMaps {
-    CUtensorMap a[AG_MAX_NP];
-    CUtensorMap b[AG_MAX_NP];
-    CUtensorMap c[AG_MAX_NP];  // output planes, boxes of 16 columns x 32 rows (per-warp TMA stores)
+    CUtensorMap a[2 * AG_MAX_NP];
+    CUtensorMap b[2 * AG_MAX_NP];
+    CUtensorMap c[2 * AG_MAX_NP];  // output planes, boxes of 16 columns x 32 rows (per-warp TMA stores)
 };
 
 struct AgParams {
@@ -69,9 +71,9 @@ struct AgParams {
     int vec_ok;        // 16-byte vector access to the output (and probability) planes
     int tma_store;     // output planes written by TMA stores from shared-memory staging
     int64_t c_bs, c_rs;
-    void* c[AG_MAX_NP];
+    void* c[2 * AG_MAX_NP];
     int64_t p_bs, p_rs;              // AG_DSCORES: probability planes
-    const void* pr[AG_MAX_NP];
+    const void* pr[2 * AG_MAX_NP];
     const float* rowv;               // AG_PROBS: (lse_0, logz_1..n); AG_DSCORES: dsum; per row
     int64_t rowv_bs;                 // floats between batch entries (rows are NP floats apart)
     int* status;
@@ -146,7 +148,10 @@ __device__ __forceinline__ void s_exp_fast(float (&x)[NP]) {
     for (int k = 0; k < NP; ++k) x[k] = r[k];
 }
 
-template <int NP, int MODE>
+// NS = 1: bfloat16 planes.  NS = 2 (float32 attention): every operand, probability and output plane
+// is a pair of bf16 planes (hi, lo) with x ~= hi + lo; each product is evaluated as
+// a_hi b_hi + a_hi b_lo + a_lo b_hi (fp32 accumulation) and outputs are split the same way.
+template <int NP, int MODE, int NS>
 __global__ void __launch_bounds__(AG_THREADS, 1)
     attn_score_gemm_kernel(const __grid_constant__ AgMaps maps, const __grid_constant__ AgParams p) {
     constexpr int TMEM_COLS = 2 * NP * AG_BN <= 128 ? 128 : (2 * NP * AG_BN <= 256 ? 256 : 512);
@@ -183,7 +188,7 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
         fence_mbar_init();
-        for (int i = 0; i < NP; ++i) {
+        for (int i = 0; i < NP * NS; ++i) {
             tma_prefetch_desc(&maps.a[i]);
             tma_prefetch_desc(&maps.b[i]);
             if (p.tma_store) tma_prefetch_desc(&maps.c[i]);
@@ -214,7 +219,7 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
                     break;
                 }
                 mbar_arrive_expect_tx(a_full, static_cast<uint32_t>(p.a_bytes));
-                for (int i = 0; i < NP; ++i) {
+                for (int i = 0; i < NP * NS; ++i) {
                     for (int kb = 0; kb < p.kblocks; ++kb) {
                         uint8_t* dst = a_res + (i * p.kblocks + kb) * AG_A_BYTES;
                         if (p.a_mn) {
@@ -231,7 +236,9 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
                 for (int tn = un.tn0; tn < un.tn1 && ok; ++tn) {
                     if (ag_masked(p, AgTile{un.b, un.tm, tn})) break;  // later tiles are masked too
                     for (int kb = 0; kb < p.kblocks && ok; ++kb) {
-                        for (int i = 0; i < NP; ++i) {
+                        // stage order within a k block: sub-plane major (all hi planes, then all lo)
+                        for (int t = 0; t < NP * NS; ++t) {
+                            const int i = (t % NP) * NS + t / NP;  // map index of plane t % NP, sub t / NP
                             if (!mbar_wait_or_abort(&empty_bar[stage], phase ^ 1, abort_flag, p.status, 121)) {
                                 ok = false;
                                 break;
@@ -294,9 +301,9 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + abuf * (NP * AG_BN);
                     for (int kb = 0; kb < p.kblocks && ok; ++kb) {
-                        uint32_t st[NP];
+                        uint32_t st[NP * NS];
 #pragma unroll
-                        for (int i = 0; i < NP; ++i) {
+                        for (int i = 0; i < NP * NS; ++i) {
                             if (!mbar_wait_or_abort(&full_bar[stage], phase, abort_flag, p.status, 123)) {
                                 ok = false;
                                 break;
@@ -311,13 +318,16 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
                         tc_fence_after();
                         // descriptors built once per k block; each 16-wide k step advances the
                         // start address field by a constant (32 B K-major, 2048 B MN-major)
-                        uint64_t ad[NP], bd[NP];
+                        uint64_t ad[NP][NS], bd[NP][NS];
 #pragma unroll
                         for (int i = 0; i < NP; ++i) {
-                            const uint32_t a_s = smem_u32(a_res + (i * p.kblocks + kb) * AG_A_BYTES);
-                            const uint32_t b_s = smem_u32(ring + st[i] * AG_B_BYTES);
-                            ad[i] = p.a_mn ? sw128_mnmajor_desc_lbo(a_s, 8192) : sw128_kmajor_desc(a_s);
-                            bd[i] = p.b_mn ? sw128_mnmajor_desc_lbo(b_s, 8192) : sw128_kmajor_desc(b_s);
+#pragma unroll
+                            for (int h = 0; h < NS; ++h) {
+                                const uint32_t a_s = smem_u32(a_res + ((i * NS + h) * p.kblocks + kb) * AG_A_BYTES);
+                                const uint32_t b_s = smem_u32(ring + st[h * NP + i] * AG_B_BYTES);
+                                ad[i][h] = p.a_mn ? sw128_mnmajor_desc_lbo(a_s, 8192) : sw128_kmajor_desc(a_s);
+                                bd[i][h] = p.b_mn ? sw128_mnmajor_desc_lbo(b_s, 8192) : sw128_kmajor_desc(b_s);
+                            }
                         }
                         const uint64_t a_step = p.a_mn ? 2048 >> 4 : 32 >> 4;
                         const uint64_t b_step = p.b_mn ? 2048 >> 4 : 32 >> 4;
@@ -328,14 +338,21 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
 #pragma unroll
                             for (int i = 0; i < NP; ++i) {
 #pragma unroll
-                                for (int k = i; k < NP; ++k)
-                                    tc_mma_f16(d_tmem + k * AG_BN, ad[i] + kk * a_step, bd[k - i] + kk * b_step, idesc,
-                                               (kb > 0 || i > 0 || kk > 0) ? 1u : 0u);
+                                for (int k = i; k < NP; ++k) {
+                                    tc_mma_f16(d_tmem + k * AG_BN, ad[i][0] + kk * a_step, bd[k - i][0] + kk * b_step,
+                                               idesc, (kb > 0 || i > 0 || kk > 0) ? 1u : 0u);
+                                    if constexpr (NS == 2) {
+                                        tc_mma_f16(d_tmem + k * AG_BN, ad[i][0] + kk * a_step,
+                                                   bd[k - i][1] + kk * b_step, idesc, 1u);
+                                        tc_mma_f16(d_tmem + k * AG_BN, ad[i][1] + kk * a_step,
+                                                   bd[k - i][0] + kk * b_step, idesc, 1u);
+                                    }
+                                }
                             }
                         }
                         issued = true;
 #pragma unroll
-                        for (int i = 0; i < NP; ++i) tc_commit(&empty_bar[st[i]]);
+                        for (int i = 0; i < NP * NS; ++i) tc_commit(&empty_bar[st[i]]);
                     }
                     if (!ok) break;
                     tc_commit(&acc_full[abuf]);
@@ -391,20 +408,22 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
             const int cbase = tc.tn * AG_BN + grp * 16;
             // score gradient: this thread's 16 probabilities of every plane, requested before the
             // accumulator wait so that their latency overlaps it (bf16 pairs, zero outside the matrix)
-            uint32_t pw[NP][8];
+            // bf16: all 16 columns of every plane loaded before the accumulator wait; float32 (hi/lo
+            // pairs): each 8-column half loaded just before its use (registers), pw[k * NS + h][0..3]
+            uint32_t pw[NP * NS][NS == 1 ? 8 : 4];
             if constexpr (MODE == AG_DSCORES) {
                 // the unit's next tile: its probability rows (64 columns = one 128-byte line per
                 // row and plane) go to L2 now, a whole tile ahead of their loads
                 const int ncol = (tn + 1) * AG_BN;
                 if (grp == 0 && row_ok && tn + 1 < un.tn1 && ncol < p.N && !ag_masked(p, AgTile{un.b, un.tm, tn + 1})) {
 #pragma unroll
-                    for (int k = 0; k < NP; ++k)
+                    for (int k = 0; k < NP * NS; ++k)
                         prefetch_l2_line(static_cast<const __nv_bfloat16*>(p.pr[k]) + tc.b * p.p_bs +
                                          static_cast<int64_t>(r) * p.p_rs + ncol);
                 }
                 const int valid16 = row_ok ? max(0, min(16, p.N - cbase)) : 0;
 #pragma unroll
-                for (int k = 0; k < NP; ++k) {
+                for (int k = 0; k < (NS == 1 ? NP : 0); ++k) {
                     const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(p.pr[k]) + tc.b * p.p_bs +
                                                static_cast<int64_t>(r) * p.p_rs + cbase;
                     if (masked_tile) {
@@ -429,11 +448,36 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
                 if (mbar_wait_or_abort(&acc_full[abuf], aphase, abort_flag, p.status, 124)) tc_fence_after();
                 else masked_tile = true;  // no accumulator to read: write zeros
             }
-            // this thread's 16 columns of every plane as bf16 pairs: ypk[k][0..7]
-            uint32_t ypk[NP][8];
+            // this thread's 16 columns of every plane as bf16 pairs, ypk[k][0..7], stored after both
+            // halves; float32 (hi/lo pairs): one 8-column half at a time, ypk[k * NS + h][0..3],
+            // stored as soon as it is formed (registers)
+            constexpr int YW = NS == 1 ? 8 : 4;
+            uint32_t ypk[NP * NS][YW];
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 const int cb = cbase + c * 8;
+                if constexpr (MODE == AG_DSCORES && NS == 2) {
+                    const int valid8 = row_ok ? max(0, min(8, p.N - cb)) : 0;
+#pragma unroll
+                    for (int k = 0; k < NP * NS; ++k) {
+                        const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(p.pr[k]) + tc.b * p.p_bs +
+                                                   static_cast<int64_t>(r) * p.p_rs + cb;
+                        if (masked_tile) {
+#pragma unroll
+                            for (int t = 0; t < 4; ++t) pw[k][t] = 0u;
+                        } else if (vec && valid8 == 8) {
+                            const uint4 w0 = *reinterpret_cast<const uint4*>(src);
+                            pw[k][0] = w0.x; pw[k][1] = w0.y; pw[k][2] = w0.z; pw[k][3] = w0.w;
+                        } else {
+#pragma unroll
+                            for (int t = 0; t < 4; ++t) {
+                                const uint32_t lo = 2 * t < valid8 ? __bfloat16_as_ushort(src[2 * t]) : 0u;
+                                const uint32_t hi = 2 * t + 1 < valid8 ? __bfloat16_as_ushort(src[2 * t + 1]) : 0u;
+                                pw[k][t] = lo | (hi << 16);
+                            }
+                        }
+                    }
+                }
                 if (!masked_tile) {
                     uint32_t x[NP][8];
 #pragma unroll
@@ -472,8 +516,13 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
 #pragma unroll
                                 for (int k = 0; k < NP; ++k) {
                                     g[k] = __uint_as_float(x[k][ee]) - rv[k];
-                                    const uint32_t wbits = pw[k][c * 4 + ee / 2];
+                                    const int wi = NS == 1 ? c * 4 + ee / 2 : ee / 2;
+                                    const uint32_t wbits = pw[k * NS][wi];
                                     pe[k] = __uint_as_float((ee & 1) ? (wbits & 0xFFFF0000u) : (wbits << 16));
+                                    if constexpr (NS == 2) {
+                                        const uint32_t lbits = pw[k * NS + 1][wi];
+                                        pe[k] += __uint_as_float((ee & 1) ? (lbits & 0xFFFF0000u) : (lbits << 16));
+                                    }
                                 }
                                 s_mul<NP, float>(pe, g, d);
 #pragma unroll
@@ -481,23 +530,50 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
                             }
                         }
 #pragma unroll
-                        for (int k = 0; k < NP; ++k) ypk[k][c * 4 + e / 2] = bf16x2_bits(v2[0][k], v2[1][k]);
+                        for (int k = 0; k < NP; ++k) {
+                            const uint32_t hb = bf16x2_bits(v2[0][k], v2[1][k]);
+                            const int yi = NS == 1 ? c * 4 + e / 2 : e / 2;
+                            ypk[k * NS][yi] = hb;
+                            if constexpr (NS == 2) {
+                                // lo = bf16(x - hi): the part of x the rounded hi misses
+                                ypk[k * NS + 1][yi] = bf16x2_bits(v2[0][k] - __uint_as_float(hb << 16),
+                                                                  v2[1][k] - __uint_as_float(hb & 0xFFFF0000u));
+                            }
+                        }
                     }
                 } else {
 #pragma unroll
-                    for (int k = 0; k < NP; ++k)
+                    for (int k = 0; k < NP * NS; ++k)
 #pragma unroll
-                        for (int t = 0; t < 4; ++t) ypk[k][c * 4 + t] = 0u;
+                        for (int t = 0; t < 4; ++t) ypk[k][NS == 1 ? c * 4 + t : t] = 0u;
+                }
+                if constexpr (NS == 2) {
+                    const int valid = row_ok ? max(0, min(8, p.N - cb)) : 0;
+#pragma unroll
+                    for (int k = 0; k < NP * NS; ++k) {
+                        if (valid <= 0) break;
+                        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c[k]) + tc.b * p.c_bs +
+                                             static_cast<int64_t>(r) * p.c_rs + cb;
+                        if (vec && valid == 8) {
+                            *reinterpret_cast<uint4*>(dst) = make_uint4(ypk[k][0], ypk[k][1], ypk[k][2], ypk[k][3]);
+                        } else {
+                            for (int t = 0; t < valid; ++t)
+                                dst[t] = __ushort_as_bfloat16(
+                                    static_cast<unsigned short>((ypk[k][t / 2] >> (16 * (t & 1))) & 0xFFFFu));
+                        }
+                    }
                 }
             }
-            if (p.tma_store) {
+            if constexpr (NS == 2) {
+                // stored half by half above
+            } else if (p.tma_store) {
                 // Per plane: the warp writes its 32 rows x 16 columns into its own staging block
                 // (row t at 32 t bytes) and its lane 0 stores the block with TMA, so no other warp
                 // takes part and the only synchronisation is within the warp.  Two blocks per warp
                 // alternate; a block is rewritten only after its previous store has read it.
                 const int q = warp & 3, ew = warp - 2;
 #pragma unroll
-                for (int k = 0; k < NP; ++k) {
+                for (int k = 0; k < NP * NS; ++k) {
                     uint8_t* blk = out_stage + (ew * 2 + (k & 1)) * AG_WARP_OUT;
                     if (lane == 0) {
                         if (k == 0) bulk_wait_group_read<0>();
@@ -521,7 +597,7 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
                     const int valid = max(0, min(8, p.N - cb));
                     if (valid <= 0) continue;
 #pragma unroll
-                    for (int k = 0; k < NP; ++k) {
+                    for (int k = 0; k < NP * NS; ++k) {
                         __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c[k]) + tc.b * p.c_bs +
                                              static_cast<int64_t>(r) * p.c_rs + cb;
                         if (vec && valid == 8) {
@@ -550,13 +626,13 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
     }
 }
 
-template <int NP, int MODE>
+template <int NP, int MODE, int NS>
 static int launch_ag(const AgMaps& maps, AgParams& p, cudaStream_t stream) {
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(attn_score_gemm_kernel<NP, MODE>,
+        cudaError_t e = cudaFuncSetAttribute(attn_score_gemm_kernel<NP, MODE, NS>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, AG_SMEM_BYTES);
         if (e != cudaSuccess) return cuda_fail(e, "pk_attn_score_gemm: cudaFuncSetAttribute");
         attr_set[dev] = true;
@@ -564,7 +640,7 @@ static int launch_ag(const AgMaps& maps, AgParams& p, cudaStream_t stream) {
     const int grid = static_cast<int>(std::min<int64_t>(p.total_units, num_sms()));
     void* tok;
     prof_begin(MODE == AG_PROBS ? "attn_probs_gemm" : "attn_dscores_gemm", stream, &tok);
-    PK_LAUNCHED(attn_score_gemm_kernel<NP, MODE><<<grid, AG_THREADS, AG_SMEM_BYTES, stream>>>(maps, p));
+    PK_LAUNCHED(attn_score_gemm_kernel<NP, MODE, NS><<<grid, AG_THREADS, AG_SMEM_BYTES, stream>>>(maps, p));
     prof_end(MODE == AG_PROBS ? "attn_probs_gemm" : "attn_dscores_gemm", stream, tok);
     PK_CHECK_LAUNCH("pk_attn_score_gemm: kernel launch");
     return PK_OK;
@@ -590,25 +666,32 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
                            int64_t p_rs, const void* rowv, int64_t rowv_bs, double scale, int causal,
                            int64_t causal_shift, void* stream_ptr) {
     const std::string w(what);
-    if (dtype != PK_BF16) return fail(PK_ERR_UNSUPPORTED, w + ": bfloat16 planes only");
+    // bfloat16 planes, or float32 attention given as bf16 (hi, lo) plane pairs: every plane array
+    // then holds 2(n+1) pointers hi_0, lo_0, hi_1, ... (operands, probabilities and outputs alike)
+    if (dtype != PK_BF16 && dtype != PK_F32)
+        return fail(PK_ERR_UNSUPPORTED, w + ": bfloat16 planes or float32 as bf16 hi/lo pairs only");
+    const int NS = dtype == PK_F32 ? 2 : 1;
     if (degree < 0 || degree >= AG_MAX_NP) return fail(PK_ERR_UNSUPPORTED, w + ": degree must be in [0, 3]");
     if (batch < 0 || M < 0 || N < 0 || K < 0) return fail(PK_ERR_ARG, w + ": negative size");
     if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff || batch > 0x7fffffff)
         return fail(PK_ERR_UNSUPPORTED, w + ": dimension exceeds 2^31-1");
     if (batch == 0 || M == 0 || N == 0) return PK_OK;
     if (K == 0) return fail(PK_ERR_UNSUPPORTED, w + ": empty reduction");
-    if (K > AG_MAX_K) return fail(PK_ERR_UNSUPPORTED, w + ": reduction (head dimension) above 128");
+    if (K > AG_MAX_K / NS)
+        return fail(PK_ERR_UNSUPPORTED, w + (NS == 2 ? ": float32 reduction (head dimension) above 64"
+                                                     : ": reduction (head dimension) above 128"));
     const int P = degree + 1;
+    const int NPL = P * NS;  // plane pointers per array
     if (!a_planes || !b_planes || !c_planes || !rowv) return fail(PK_ERR_ARG, w + ": null plane array or row values");
-    for (int k = 0; k < P; ++k)
+    for (int k = 0; k < NPL; ++k)
         if (!a_planes[k] || !b_planes[k] || !c_planes[k]) return fail(PK_ERR_ARG, w + ": null plane pointer");
     if (mode == AG_DSCORES) {
         if (!probs) return fail(PK_ERR_ARG, w + ": null probability planes");
-        for (int k = 0; k < P; ++k)
+        for (int k = 0; k < NPL; ++k)
             if (!probs[k]) return fail(PK_ERR_ARG, w + ": null probability plane pointer");
     }
-    const int am = operand_mode(dtype, a_planes, P, batch, M, K, a_bs, a_rs, a_cs);
-    const int bm = operand_mode(dtype, b_planes, P, batch, N, K, b_bs, b_cs, b_rs);
+    const int am = operand_mode(PK_BF16, a_planes, NPL, batch, M, K, a_bs, a_rs, a_cs);
+    const int bm = operand_mode(PK_BF16, b_planes, NPL, batch, N, K, b_bs, b_cs, b_rs);
     if (am == OPM_STAGED || bm == OPM_STAGED)
         return fail(PK_ERR_UNSUPPORTED, w + ": operand planes must be 16-byte aligned with k or rows contiguous "
                                             "and the other strides multiples of 8 elements");
@@ -617,9 +700,9 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
     std::memset(&maps, 0, sizeof(maps));
     const TcOperand oa{am, M, K, K, batch, a_planes, a_bs, a_rs, a_cs, nullptr, nullptr, 0, false};
     const TcOperand ob{bm, N, K, K, batch, b_planes, b_bs, b_cs, b_rs, nullptr, nullptr, 0, false};
-    int rc = encode_operand(maps.a, oa, P, false, AG_BM);
+    int rc = encode_operand(maps.a, oa, NPL, false, AG_BM);
     if (rc) return rc;
-    rc = encode_operand(maps.b, ob, P, false, AG_BN);
+    rc = encode_operand(maps.b, ob, NPL, false, AG_BN);
     if (rc) return rc;
 
     AgParams p{};
@@ -633,9 +716,10 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
     const int64_t total = static_cast<int64_t>(p.tiles_m) * p.n_chunks * batch;
     if (total > 0x7fffffff) return fail(PK_ERR_UNSUPPORTED, w + ": too many tiles");
     p.total_units = static_cast<int>(total);
-    p.a_bytes = P * p.kblocks * AG_A_BYTES;
+    p.a_bytes = NPL * p.kblocks * AG_A_BYTES;
     p.nstages = std::min(AG_MAX_STAGES, (AG_SMEM_BUDGET - AG_OUT_BYTES - p.a_bytes) / AG_B_BYTES);
-    if (p.nstages < P + 2)
+    // a k block's NPL B stages must be resident together; bf16 keeps two more for prefetch
+    if (p.a_bytes + AG_OUT_BYTES > AG_SMEM_BUDGET || p.nstages < NPL + (NS == 1 ? 2 : 0))
         return fail(PK_ERR_UNSUPPORTED, w + ": reduction too long for the resident operand");
     p.a_mn = am == OPM_MNMAJOR;
     p.b_mn = bm == OPM_MNMAJOR;
@@ -651,7 +735,7 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
     // TMA stores of the output planes: 16-byte aligned bases and row / batch strides, rows and
     // batch entries not overlapping
     bool tstore = vec && c_rs >= N && (batch == 1 || c_bs >= M * c_rs);
-    for (int k = 0; k < P; ++k) {
+    for (int k = 0; k < NPL; ++k) {
         p.c[k] = c_planes[k];
         if (reinterpret_cast<uintptr_t>(c_planes[k]) % 16) vec = tstore = false;
         if (mode == AG_DSCORES) {
@@ -663,10 +747,10 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
     p.vec_ok = vec ? 1 : 0;
     if (tstore) {
         const int64_t sb = batch > 1 ? c_bs * 2 : M * c_rs * 2;
-        for (int k = 0; k < P && tstore; ++k)
+        for (int k = 0; k < NPL && tstore; ++k)
             if (encode_out_map(&maps.c[k], c_planes[k], N, M, batch, c_rs * 2, sb) != PK_OK) tstore = false;
     }
-    p.tma_store = tstore ? 1 : 0;
+    p.tma_store = (tstore && NS == 1) ? 1 : 0;
     p.rowv = static_cast<const float*>(rowv);
     p.rowv_bs = rowv_bs;
     p.status = device_status_ptr();
@@ -702,15 +786,23 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
         p.n_groups = g;
     }
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-    switch (P * 2 + mode) {
-        case 2: return launch_ag<1, AG_PROBS>(maps, p, stream);
-        case 3: return launch_ag<1, AG_DSCORES>(maps, p, stream);
-        case 4: return launch_ag<2, AG_PROBS>(maps, p, stream);
-        case 5: return launch_ag<2, AG_DSCORES>(maps, p, stream);
-        case 6: return launch_ag<3, AG_PROBS>(maps, p, stream);
-        case 7: return launch_ag<3, AG_DSCORES>(maps, p, stream);
-        case 8: return launch_ag<4, AG_PROBS>(maps, p, stream);
-        default: return launch_ag<4, AG_DSCORES>(maps, p, stream);
+    switch ((P * 2 + mode) * 2 + (NS - 1)) {
+        case 4: return launch_ag<1, AG_PROBS, 1>(maps, p, stream);
+        case 5: return launch_ag<1, AG_PROBS, 2>(maps, p, stream);
+        case 6: return launch_ag<1, AG_DSCORES, 1>(maps, p, stream);
+        case 7: return launch_ag<1, AG_DSCORES, 2>(maps, p, stream);
+        case 8: return launch_ag<2, AG_PROBS, 1>(maps, p, stream);
+        case 9: return launch_ag<2, AG_PROBS, 2>(maps, p, stream);
+        case 10: return launch_ag<2, AG_DSCORES, 1>(maps, p, stream);
+        case 11: return launch_ag<2, AG_DSCORES, 2>(maps, p, stream);
+        case 12: return launch_ag<3, AG_PROBS, 1>(maps, p, stream);
+        case 13: return launch_ag<3, AG_PROBS, 2>(maps, p, stream);
+        case 14: return launch_ag<3, AG_DSCORES, 1>(maps, p, stream);
+        case 15: return launch_ag<3, AG_DSCORES, 2>(maps, p, stream);
+        case 16: return launch_ag<4, AG_PROBS, 1>(maps, p, stream);
+        case 17: return launch_ag<4, AG_PROBS, 2>(maps, p, stream);
+        case 18: return launch_ag<4, AG_DSCORES, 1>(maps, p, stream);
+        default: return launch_ag<4, AG_DSCORES, 2>(maps, p, stream);
     }
 }
 

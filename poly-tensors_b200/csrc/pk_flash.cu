@@ -47,10 +47,11 @@ constexpr int FA_SOFTMAX_WARPS = 16;         // 4 per TMEM lane quadrant, each o
 constexpr int FA_THREADS = 64 + 32 * FA_SOFTMAX_WARPS;
 constexpr int FA_MAX_NP = 4;
 
+// Plane a, sub-plane h (NS = 2: float32 planes as bf16 hi / lo pairs) at index a * NS + h.
 struct FlashMaps {
-    CUtensorMap q[FA_MAX_NP];
-    CUtensorMap k[FA_MAX_NP];
-    CUtensorMap v[FA_MAX_NP];
+    CUtensorMap q[2 * FA_MAX_NP];
+    CUtensorMap k[2 * FA_MAX_NP];
+    CUtensorMap v[2 * FA_MAX_NP];
 };
 
 struct FlashParams {
@@ -75,14 +76,18 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
            (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(hi))) << 16);
 }
 
-template <int NP, int DCH>
+// NS = 1: bfloat16 planes, bf16 output.  NS = 2 (float32 attention): Q, K, V arrive as bf16
+// (hi, lo) plane pairs; every product is a_hi b_hi + a_hi b_lo + a_lo b_hi, the probabilities are
+// written into TMEM as hi pairs (columns 16g .. 16g+7 of a key group) and lo pairs (16g+8 ..
+// 16g+15, the columns whose fp32 scores the same warp has already read), and O is float32.
+template <int NP, int DCH, int NS>
 __global__ void __launch_bounds__(FA_THREADS, 1)
     flash_fwd_kernel(const __grid_constant__ FlashMaps maps, const FlashParams p) {
     using Cfg = FlashCfg<NP>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sq = smem;
-    uint8_t* ring = sq + NP * DCH * FA_QTILE;
+    uint8_t* ring = sq + NP * NS * DCH * FA_QTILE;
     uint64_t* full = reinterpret_cast<uint64_t*>(ring + FA_STAGES * FA_TILE);
     uint64_t* empty = full + FA_STAGES;
     uint64_t* q_full = empty + FA_STAGES;
@@ -131,8 +136,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            mbar_arrive_expect_tx(q_full, NP * DCH * FA_QTILE);
-            for (int a = 0; a < NP; ++a)
+            mbar_arrive_expect_tx(q_full, NP * NS * DCH * FA_QTILE);
+            for (int a = 0; a < NP * NS; ++a)
                 for (int c = 0; c < DCH; ++c)
                     tma_load_3d(sq + (a * DCH + c) * FA_QTILE, &maps.q[a], q_full, c * 64, q0, bh);
             uint32_t stage = 0, phase = 0;
@@ -141,21 +146,21 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             for (int s = 0; s < FA_STAGES; ++s) issued_parity[s] = -1;
             bool ok = true;
             for (int j = 0; j < nblocks && ok; ++j) {
-                for (int t = 0; t < NP * DCH + NP && ok; ++t) {
+                for (int t = 0; t < NS * NP * (DCH + 1) && ok; ++t) {
                     if (!mbar_wait_or_abort(&empty[stage], phase ^ 1, abort_flag, p.status, 401)) {
                         ok = false;
                         break;
                     }
                     uint8_t* dst = ring + stage * FA_TILE;
                     mbar_arrive_expect_tx(&full[stage], FA_TILE);
-                    if (t < NP * DCH) {
-                        // head-dimension chunk major, plane minor: a chunk's K planes fill
-                        // consecutive stages (one wide MMA reads them together)
-                        const int c = t / NP, b = t % NP;
-                        tma_load_3d(dst, &maps.k[b], &full[stage], c * 64, j * FA_BN, bh);
+                    if (t < NS * NP * DCH) {
+                        // head-dimension chunk major, then sub-plane, plane minor: a chunk's K planes
+                        // of one sub-plane fill consecutive stages (one wide MMA reads them together)
+                        const int c = t / (NS * NP), h = (t / NP) % NS, b = t % NP;
+                        tma_load_3d(dst, &maps.k[b * NS + h], &full[stage], c * 64, j * FA_BN, bh);
                     } else {
-                        const int b = t - NP * DCH;
-                        tma_load_3d(dst, &maps.v[b], &full[stage], slice * FA_DS, j * FA_BN, bh);
+                        const int u = t - NS * NP * DCH, h = u / NP, b = u % NP;
+                        tma_load_3d(dst, &maps.v[b * NS + h], &full[stage], slice * FA_DS, j * FA_BN, bh);
                     }
                     issued_parity[stage] = static_cast<int>(phase);
                     if (++stage == FA_STAGES) {
@@ -213,30 +218,38 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                 tc_fence_after();
                 // S_k = sum_{a+b=k} Q_a K_b^T over the head dimension (DCH chunks of 64)
                 for (int c = 0; c < DCH && ok; ++c) {
-                    uint32_t kst[NP];
-                    for (int b = 0; b < NP; ++b) {
-                        if (!mbar_wait_or_abort(&full[stage], phase, abort_flag, p.status, 404)) {
-                            ok = false;
-                            break;
-                        }
-                        kst[b] = stage;
-                        if (++stage == FA_STAGES) {
-                            stage = 0;
-                            phase ^= 1;
+                    uint32_t kst[NS][NP];
+                    for (int h = 0; h < NS && ok; ++h) {
+                        for (int b = 0; b < NP; ++b) {
+                            if (!mbar_wait_or_abort(&full[stage], phase, abort_flag, p.status, 404)) {
+                                ok = false;
+                                break;
+                            }
+                            kst[h][b] = stage;
+                            if (++stage == FA_STAGES) {
+                                stage = 0;
+                                phase ^= 1;
+                            }
                         }
                     }
                     if (!ok) break;
                     tc_fence_after();
-                    const int wrap = min(NP, FA_STAGES - static_cast<int>(kst[0]));
+                    // products of sub-planes (hq of Q, hk of K): (hi, hi), then for float32 (hi, lo), (lo, hi)
                     auto qk = [&](int a, int b0, int b1) {
-                        const uint64_t qd = q_desc + ((a * DCH + c) * FA_QTILE >> 4);
-                        segments(b0, b1, wrap, [&](int s0, int s1) {
-                            const uint64_t kd = ring_kdesc + (kst[s0] * FA_TILE >> 4);
 #pragma unroll
-                            for (int kk = 0; kk < 4; ++kk)
-                                tc_mma_f16(tmem + (a + s0) * FA_BN, qd + kk * 2, kd + kk * 2,
-                                           idesc_qk0 | n_field(s1 - s0), (c == 0 && a == 0 && kk == 0) ? 0u : 1u);
-                        });
+                        for (int cb = 0; cb < (NS == 2 ? 3 : 1); ++cb) {
+                            const int hq = cb == 2 ? 1 : 0, hk = cb == 1 ? 1 : 0;
+                            const int wrap = min(NP, FA_STAGES - static_cast<int>(kst[hk][0]));
+                            const uint64_t qd = q_desc + (((a * NS + hq) * DCH + c) * FA_QTILE >> 4);
+                            segments(b0, b1, wrap, [&](int s0, int s1) {
+                                const uint64_t kd = ring_kdesc + (kst[hk][s0] * FA_TILE >> 4);
+#pragma unroll
+                                for (int kk = 0; kk < 4; ++kk)
+                                    tc_mma_f16(tmem + (a + s0) * FA_BN, qd + kk * 2, kd + kk * 2,
+                                               idesc_qk0 | n_field(s1 - s0),
+                                               (c == 0 && a == 0 && kk == 0 && cb == 0) ? 0u : 1u);
+                            });
+                        }
                     };
                     if (c + 1 < DCH) {
                         qk(0, 0, NP);
@@ -251,7 +264,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                     for (int a = 1; a < NP; ++a) qk(a, 0, NP - a);
                     issued = true;
 #pragma unroll
-                    for (int b = 0; b < NP; ++b) tc_commit(&empty[kst[b]]);
+                    for (int h = 0; h < NS; ++h)
+#pragma unroll
+                        for (int b = 0; b < NP; ++b) tc_commit(&empty[kst[h][b]]);
                 }
                 if (!ok) break;
                 tc_commit(s_full);
@@ -263,30 +278,38 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                     ok = false;
                     break;
                 }
-                uint32_t vst[NP];
-                for (int b = 0; b < NP && ok; ++b) {
-                    if (!mbar_wait_or_abort(&full[stage], phase, abort_flag, p.status, 406)) {
-                        ok = false;
-                        break;
-                    }
-                    vst[b] = stage;
-                    if (++stage == FA_STAGES) {
-                        stage = 0;
-                        phase ^= 1;
+                uint32_t vst[NS][NP];
+                for (int h = 0; h < NS && ok; ++h) {
+                    for (int b = 0; b < NP; ++b) {
+                        if (!mbar_wait_or_abort(&full[stage], phase, abort_flag, p.status, 406)) {
+                            ok = false;
+                            break;
+                        }
+                        vst[h][b] = stage;
+                        if (++stage == FA_STAGES) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
                     }
                 }
                 if (!ok) break;
                 tc_fence_after();
-                const int vwrap = min(NP, FA_STAGES - static_cast<int>(vst[0]));
+                // products (he of E, hv of V): (hi, hi), then for float32 (hi, lo), (lo, hi); E's lo
+                // pairs of keys 16kk.. sit 8 columns after its hi pairs
                 auto pv = [&](int a) {
-                    segments(0, NP - a, vwrap, [&](int s0, int s1) {
-                        const uint64_t vd = ring_vdesc + (vst[s0] * FA_TILE >> 4);
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            tc_mma_f16_ts(tmem + Cfg::O_BASE + (a + s0) * FA_DS, tmem + a * FA_BN + kk * 16,
-                                          vd + kk * (2048 >> 4), idesc_pv0 | n_field(s1 - s0),
-                                          (j == 0 && a == 0 && kk == 0) ? 0u : 1u);
-                    });
+                    for (int cb = 0; cb < (NS == 2 ? 3 : 1); ++cb) {
+                        const int he = cb == 2 ? 1 : 0, hv = cb == 1 ? 1 : 0;
+                        const int vwrap = min(NP, FA_STAGES - static_cast<int>(vst[hv][0]));
+                        segments(0, NP - a, vwrap, [&](int s0, int s1) {
+                            const uint64_t vd = ring_vdesc + (vst[hv][s0] * FA_TILE >> 4);
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk)
+                                tc_mma_f16_ts(tmem + Cfg::O_BASE + (a + s0) * FA_DS, tmem + a * FA_BN + kk * 16 + he * 8,
+                                              vd + kk * (2048 >> 4), idesc_pv0 | n_field(s1 - s0),
+                                              (j == 0 && a == 0 && kk == 0 && cb == 0) ? 0u : 1u);
+                        });
+                    }
                 };
                 pv(0);
                 if (!mbar_wait_or_abort(p_ready, j & 1, abort_flag, p.status, 405)) {
@@ -297,7 +320,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 #pragma unroll
                 for (int a = 1; a < NP; ++a) pv(a);
 #pragma unroll
-                for (int b = 0; b < NP; ++b) tc_commit(&empty[vst[b]]);
+                for (int h = 0; h < NS; ++h)
+#pragma unroll
+                    for (int b = 0; b < NP; ++b) tc_commit(&empty[vst[h][b]]);
                 tc_commit(pv_done);
             }
             if (!ok && issued) {
@@ -370,6 +395,15 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 #pragma unroll
                 for (int t = 0; t < 8; ++t) packed0[t] = pack_bf16x2(w[2 * t], w[2 * t + 1]);
                 tmem_st_32x32b_x8(trow + g * 16, packed0);
+                if constexpr (NS == 2) {
+                    // lo = bf16(E - hi), the part of E the rounded hi misses
+                    uint32_t lo0[8];
+#pragma unroll
+                    for (int t = 0; t < 8; ++t)
+                        lo0[t] = pack_bf16x2(w[2 * t] - __uint_as_float(packed0[t] << 16),
+                                             w[2 * t + 1] - __uint_as_float(packed0[t] & 0xFFFF0000u));
+                    tmem_st_32x32b_x8(trow + g * 16 + 8, lo0);
+                }
             }
             // rescale this warp's 16 columns of every O~ plane where the row maximum moved
             if (__any_sync(0xffffffffu, rescale)) {
@@ -400,6 +434,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                 for (int k = 1; k < NP; ++k) tmem_ld_32x32b_x16(trow + k * FA_BN + g * 16, r[k]);
                 tmem_ld_wait();
                 uint32_t packed[NP][8];
+                uint32_t packed_lo[NS == 2 ? NP : 1][8];
 #pragma unroll
                 for (int t = 0; t < 16; t += 2) {
                     float e2[2][NP];
@@ -417,10 +452,18 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                         }
                     }
 #pragma unroll
-                    for (int k = 1; k < NP; ++k) packed[k][t / 2] = pack_bf16x2(e2[0][k], e2[1][k]);
+                    for (int k = 1; k < NP; ++k) {
+                        packed[k][t / 2] = pack_bf16x2(e2[0][k], e2[1][k]);
+                        if constexpr (NS == 2)
+                            packed_lo[k][t / 2] = pack_bf16x2(e2[0][k] - __uint_as_float(packed[k][t / 2] << 16),
+                                                              e2[1][k] - __uint_as_float(packed[k][t / 2] & 0xFFFF0000u));
+                    }
                 }
 #pragma unroll
-                for (int k = 1; k < NP; ++k) tmem_st_32x32b_x8(trow + k * FA_BN + g * 16, packed[k]);
+                for (int k = 1; k < NP; ++k) {
+                    tmem_st_32x32b_x8(trow + k * FA_BN + g * 16, packed[k]);
+                    if constexpr (NS == 2) tmem_st_32x32b_x8(trow + k * FA_BN + g * 16 + 8, packed_lo[k]);
+                }
                 tmem_st_wait();
                 tc_fence_before();
             }
@@ -478,7 +521,17 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                         o[k][t] = acc * inv;
                     }
                 }
-                if (q < p.L) {
+                if (q < p.L && NS == 2) {
+#pragma unroll
+                    for (int k = 0; k < NP; ++k) {
+                        float* dst = static_cast<float*>(p.o[k]) + (static_cast<int64_t>(bh) * p.L + q) * p.D +
+                                     slice * FA_DS + g * 16;
+                        float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+                        for (int t = 0; t < 4; ++t)
+                            d4[t] = make_float4(o[k][4 * t], o[k][4 * t + 1], o[k][4 * t + 2], o[k][4 * t + 3]);
+                    }
+                } else if (q < p.L) {
 #pragma unroll
                     for (int k = 0; k < NP; ++k) {
                         uint32_t w[8];
@@ -516,21 +569,21 @@ static int encode_plane_map(CUtensorMap* map, const void* base, int64_t rows, in
     return PK_OK;
 }
 
-template <int NP, int DCH>
+template <int NP, int DCH, int NS>
 static int launch_flash(const FlashMaps& maps, const FlashParams& p, cudaStream_t s) {
-    const int smem = NP * DCH * FA_QTILE + FA_STAGES * FA_TILE + 1024 + 512 + 4 * 128 * (NP + 1) * 4;
+    const int smem = NP * NS * DCH * FA_QTILE + FA_STAGES * FA_TILE + 1024 + 512 + 4 * 128 * (NP + 1) * 4;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel<NP, DCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel<NP, DCH, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return cuda_fail(e, "pk_flash_attn_fwd: cudaFuncSetAttribute");
         attr_set[dev] = true;
     }
     dim3 grid(static_cast<unsigned>(p.q_tiles * p.n_slices), static_cast<unsigned>(p.bh));
     void* tok;
     prof_begin("flash_attn_fwd", s, &tok);
-    PK_LAUNCHED(flash_fwd_kernel<NP, DCH><<<grid, FA_THREADS, smem, s>>>(maps, p));
+    PK_LAUNCHED(flash_fwd_kernel<NP, DCH, NS><<<grid, FA_THREADS, smem, s>>>(maps, p));
     prof_end("flash_attn_fwd", s, tok);
     PK_CHECK_LAUNCH("pk_flash_attn_fwd");
     return PK_OK;
@@ -543,23 +596,33 @@ using namespace pk;
 extern "C" int pk_flash_attn_fwd(int dtype, int degree, int64_t bh, int64_t L, int64_t S, int64_t D,
                                  const void* const* q, const void* const* k, const void* const* v, void* const* o,
                                  int causal, double scale, void* stats, void* stream) {
-    if (dtype != PK_BF16) return fail(PK_ERR_UNSUPPORTED, "pk_flash_attn_fwd: bfloat16 planes only");
+    // bfloat16 planes; or float32 attention with q / k / v given as bf16 (hi, lo) plane pairs
+    // (2(n+1) pointers each: hi_0, lo_0, hi_1, ...) and float32 output planes
+    if (dtype != PK_BF16 && dtype != PK_F32)
+        return fail(PK_ERR_UNSUPPORTED, "pk_flash_attn_fwd: bfloat16 planes, or float32 as bf16 hi/lo pairs");
+    const int NS = dtype == PK_F32 ? 2 : 1;
     if (degree < 0 || degree >= FA_MAX_NP) return fail(PK_ERR_UNSUPPORTED, "pk_flash_attn_fwd: degree must be <= 3");
-    if (D != 64 && D != 128) return fail(PK_ERR_UNSUPPORTED, "pk_flash_attn_fwd: head dimension must be 64 or 128");
+    if (NS == 1 && D != 64 && D != 128)
+        return fail(PK_ERR_UNSUPPORTED, "pk_flash_attn_fwd: head dimension must be 64 or 128");
+    if (NS == 2 && D != 64) return fail(PK_ERR_UNSUPPORTED, "pk_flash_attn_fwd: float32 head dimension must be 64");
     if (bh <= 0 || L <= 0 || S <= 0) return bh == 0 || L == 0 ? PK_OK : fail(PK_ERR_ARG, "pk_flash_attn_fwd: empty keys");
     if (bh > 65535 || L > (1LL << 30) || S > (1LL << 30)) return fail(PK_ERR_UNSUPPORTED, "pk_flash_attn_fwd: too large");
     const int NP = degree + 1;
     FlashMaps maps;
     memset(&maps, 0, sizeof(maps));
-    for (int a = 0; a < NP; ++a) {
-        if (!q[a] || !k[a] || !v[a] || !o[a]) return fail(PK_ERR_ARG, "pk_flash_attn_fwd: null plane");
-        if ((reinterpret_cast<uintptr_t>(q[a]) | reinterpret_cast<uintptr_t>(k[a]) | reinterpret_cast<uintptr_t>(v[a]) |
-             reinterpret_cast<uintptr_t>(o[a])) % 16)
+    for (int a = 0; a < NP * NS; ++a) {
+        if (!q[a] || !k[a] || !v[a]) return fail(PK_ERR_ARG, "pk_flash_attn_fwd: null plane");
+        if ((reinterpret_cast<uintptr_t>(q[a]) | reinterpret_cast<uintptr_t>(k[a]) | reinterpret_cast<uintptr_t>(v[a])) %
+            16)
             return fail(PK_ERR_ARG, "pk_flash_attn_fwd: planes must be 16-byte aligned");
         int rc = encode_plane_map(&maps.q[a], q[a], L, D, bh, FA_BM);
         if (!rc) rc = encode_plane_map(&maps.k[a], k[a], S, D, bh, FA_BN);
         if (!rc) rc = encode_plane_map(&maps.v[a], v[a], S, D, bh, FA_BN);
         if (rc) return rc;
+    }
+    for (int a = 0; a < NP; ++a) {
+        if (!o[a]) return fail(PK_ERR_ARG, "pk_flash_attn_fwd: null output plane");
+        if (reinterpret_cast<uintptr_t>(o[a]) % 16) return fail(PK_ERR_ARG, "pk_flash_attn_fwd: planes must be 16-byte aligned");
     }
     FlashParams p{};
     p.bh = static_cast<int>(bh);
@@ -575,8 +638,16 @@ extern "C" int pk_flash_attn_fwd(int dtype, int degree, int64_t bh, int64_t L, i
     p.status = device_status_ptr();
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int dch = static_cast<int>(D / 64);
+    if (NS == 2) {
+        switch (NP) {
+            case 1: return launch_flash<1, 1, 2>(maps, p, s);
+            case 2: return launch_flash<2, 1, 2>(maps, p, s);
+            case 3: return launch_flash<3, 1, 2>(maps, p, s);
+            default: return launch_flash<4, 1, 2>(maps, p, s);
+        }
+    }
 #define PK_FLASH(NPV)                                                              \
-    case NPV: return dch == 1 ? launch_flash<NPV, 1>(maps, p, s) : launch_flash<NPV, 2>(maps, p, s);
+    case NPV: return dch == 1 ? launch_flash<NPV, 1, 1>(maps, p, s) : launch_flash<NPV, 2, 1>(maps, p, s);
     switch (NP) {
         PK_FLASH(1)
         PK_FLASH(2)

@@ -18,7 +18,9 @@ P is recomputed in backward from the saved inputs; only the per-row normaliser s
 single-kernel forward (pk_flash_attn_fwd) and a backward over all queries of a block of heads
 with the softmax in the score products' epilogue (pk_attn_probs_gemm / pk_attn_dscores_gemm)
 and banded gradient products (pk_poly_gemm_banded).  Other dtypes tile the queries under a causal
-mask, so that their row-wise softmax passes and operand staging skip the masked half.
+mask, so that their row-wise softmax passes and operand staging skip the masked half; float32
+planes with head dimension 64 (degree <= 3) run the same single-kernel forward and score-epilogue
+backward on bf16 hi/lo plane pairs (products as hi*hi + hi*lo + lo*hi, fp32 accumulation).
 """
 
 import math
@@ -123,6 +125,33 @@ def flash_forward(Q, Kp, V, causal, scale, stats=None):
     return O
 
 
+def f32_split_eligible(Q, Kp, V):
+    """Whether float32 attention runs on the split kernels: float32 planes, degree <= 3, head
+    dimension 64 for queries, keys and values.  Q, K, V (and dO) are split once into bf16 hi/lo
+    plane pairs; the single-kernel forward and the score-epilogue products evaluate every product
+    as hi*hi + hi*lo + lo*hi with fp32 accumulation, and the probability / score-gradient planes
+    come out already split, so the gradient products read them in place (pk_poly_gemm_hilo)."""
+    return (Q[0].dtype == torch.float32 and len(Q) <= 4 and Q[0].shape[-1] == 64
+            and Kp[0].shape[-1] == 64 and V[0].shape[-1] == 64)
+
+
+def _flash_f32(Q, Kp, V, causal, scale, stats=None):
+    """pk_flash_attn_fwd on float32 planes given as hi/lo pairs; float32 O planes."""
+    BH, L, D = Q[0].shape
+    S = Kp[0].shape[1]
+    Qh, Kh, Vh = (K.split_hilo(X) for X in (Q, Kp, V))
+    O = [torch.empty_like(q) for q in Q]
+    pq, k1 = _lib.pointer_array(Qh)
+    pk_, k2 = _lib.pointer_array(Kh)
+    pv, k3 = _lib.pointer_array(Vh)
+    po, k4 = _lib.pointer_array(O)
+    status = _lib.load().pk_flash_attn_fwd(_lib.PK_F32, len(Q) - 1, BH, L, S, D, pq, pk_, pv, po,
+                                           1 if causal else 0, float(scale),
+                                           stats.data_ptr() if stats is not None else None, K._stream(Q[0].device))
+    _lib.check(status, "pk_flash_attn_fwd")
+    return O
+
+
 def fused_backward_eligible(Q, Kp, V):
     """Whether the backward builds probabilities and score gradients in the epilogue of their
     products (pk_attn_probs_gemm / pk_attn_dscores_gemm): bfloat16 planes, degree <= 3, head
@@ -147,6 +176,8 @@ def forward_planes(Q, Kp, V, causal, scale, stats=None):
     the compute dtype) receives each query row's softmax normaliser series."""
     if flash_eligible(Q, Kp, V):
         return flash_forward(Q, Kp, V, causal, scale, stats)
+    if f32_split_eligible(Q, Kp, V):
+        return _flash_f32(Q, Kp, V, causal, scale, stats)
     BH, L, _ = Q[0].shape
     S = Kp[0].shape[1]
     hb = _block_heads(L, S, len(Q), Q[0].element_size(), BH)
@@ -164,11 +195,14 @@ def forward_planes(Q, Kp, V, causal, scale, stats=None):
     return outs
 
 
-def _score_gemm(name, A, B, out, rows, scale, causal, shift, probs=None):
+def _score_gemm(name, A, B, out, rows, scale, causal, shift, probs=None, split=False):
     """pk_attn_probs_gemm / pk_attn_dscores_gemm on (hb, M, K) x (hb, K, N) bf16 plane views;
     ``rows``: float32 (hb, M, n+1) view (statistics or dsum) with unit inner strides.  ``causal``:
     False, True, or 2 (causal; tiles lying wholly more than 192 keys past the admissible region are
-    left unwritten, for consumers that only read near it)."""
+    left unwritten, for consumers that only read near it).  ``split``: float32 attention, every plane
+    list (A, B, out, probs) holding bf16 hi/lo pairs [hi_0, lo_0, hi_1, ...]."""
+    code = _lib.PK_F32 if split else _lib.PK_BF16
+    degree = len(A) // (2 if split else 1) - 1
     hb, M, Kd = A[0].shape
     N = B[0].shape[2]
     pa, k1 = _lib.pointer_array(A)
@@ -178,13 +212,13 @@ def _score_gemm(name, A, B, out, rows, scale, causal, shift, probs=None):
     lib = _lib.load()
     stream = K._stream(A[0].device)
     if name == "probs":
-        status = lib.pk_attn_probs_gemm(_lib.PK_BF16, len(A) - 1, hb, M, N, Kd, pa, *a_s, pb, *b_s, po, o_s[0], o_s[1],
+        status = lib.pk_attn_probs_gemm(code, degree, hb, M, N, Kd, pa, *a_s, pb, *b_s, po, o_s[0], o_s[1],
                                         rows.data_ptr(), rows.stride(0), float(scale), int(causal), shift,
                                         stream)
     else:
         pp, k4 = _lib.pointer_array(probs)
         p_s = probs[0].stride()
-        status = lib.pk_attn_dscores_gemm(_lib.PK_BF16, len(A) - 1, hb, M, N, Kd, pa, *a_s, pb, *b_s, pp, p_s[0],
+        status = lib.pk_attn_dscores_gemm(code, degree, hb, M, N, Kd, pa, *a_s, pb, *b_s, pp, p_s[0],
                                           p_s[1], rows.data_ptr(), rows.stride(0), float(scale),
                                           int(causal), shift, po, o_s[0], o_s[1], stream)
     _lib.check(status, f"pk_attn_{name}_gemm")
@@ -223,6 +257,39 @@ def _fused_backward(Q, Kp, V, dO, dsum, stats, causal, scale, dQ, dK, dV):
             K.poly_matmul([d.transpose(1, 2) for d in dS], [q[hs] for q in Q], out=[t[hs] for t in dK], band=lower)
 
 
+def _fused_backward_f32(Q, Kp, V, dO, dsum, stats, causal, scale, dQ, dK, dV):
+    """float32 backward (D = 64, degree <= 3) on the split kernels: the structure of the bf16
+    backward, with Q, K, V, dO split once into hi/lo pairs, probabilities and score gradients
+    written as hi/lo pairs by the score-epilogue products, and the banded gradient products
+    reading those pairs in place (pk_poly_gemm_hilo)."""
+    BH, L, _ = Q[0].shape
+    S = Kp[0].shape[1]
+    NP = len(Q)
+    per_head = 2 * 2 * NP * L * S * 2   # probability and score-gradient hi/lo pairs, bf16
+    hb = max(1, min(BH, _FUSED_BLOCK_BYTES // max(per_head, 1)))
+    lower, upper = (1, 2) if causal else (0, 0)
+    mode = 2 if causal else 0
+    Qh, Kh, Vh, dOh = (K.split_hilo(X) for X in (Q, Kp, V, dO))
+    for h0 in range(0, BH, hb):
+        hs = slice(h0, min(BH, h0 + hb))
+        hbn = hs.stop - hs.start
+        Pr = [torch.empty(hbn, L, S, dtype=torch.bfloat16, device=Q[0].device) for _ in range(2 * NP)]
+        _score_gemm("probs", [q[hs] for q in Qh], [k[hs].transpose(1, 2) for k in Kh], Pr, stats[hs], scale,
+                    mode, 0, split=True)
+        if dV is not None:
+            K.poly_matmul_hilo([p.transpose(1, 2) for p in Pr], True, [g[hs] for g in dOh], True,
+                               out=[t[hs] for t in dV], band=lower)
+        dS = [torch.empty_like(p) for p in Pr]
+        _score_gemm("dscores", [g[hs] for g in dOh], [v[hs].transpose(1, 2) for v in Vh], dS, dsum[hs], scale,
+                    mode, 0, probs=Pr, split=True)
+        del Pr
+        if dQ is not None:
+            K.poly_matmul_hilo(dS, True, [k[hs] for k in Kh], True, out=[t[hs] for t in dQ], band=upper)
+        if dK is not None:
+            K.poly_matmul_hilo([d.transpose(1, 2) for d in dS], True, [q[hs] for q in Qh], True,
+                               out=[t[hs] for t in dK], band=lower)
+
+
 def backward_planes(Q, Kp, V, O, dO, causal, scale, need, stats=None):
     BH, L, _ = Q[0].shape
     S = Kp[0].shape[1]
@@ -242,6 +309,9 @@ def backward_planes(Q, Kp, V, O, dO, causal, scale, need, stats=None):
     fused = stats is not None and fused_backward_eligible(Q, Kp, V)
     if fused:
         _fused_backward(Q, Kp, V, dO, dsum, stats, causal, scale, dQ, dK, dV)
+        return dQ, dK, dV
+    if stats is not None and f32_split_eligible(Q, Kp, V):
+        _fused_backward_f32(Q, Kp, V, dO, dsum, stats, causal, scale, dQ, dK, dV)
         return dQ, dK, dV
     for h0 in range(0, BH, hb):
         h1 = min(BH, h0 + hb)
@@ -287,7 +357,7 @@ class _SeriesAttention(torch.autograd.Function):
         Kp = _flat(_planes(key, D), key.shape)
         V = _flat(_planes(value, D), value.shape)
         stats = None
-        if fused_backward_eligible(Q, Kp, V):
+        if fused_backward_eligible(Q, Kp, V) or f32_split_eligible(Q, Kp, V):
             stats = torch.empty(*Q[0].shape[:2], len(Q), dtype=torch.float32, device=Q[0].device)
         O = forward_planes(Q, Kp, V, causal, scale, stats)
         ctx.saved = (Q, Kp, V, O, stats)

@@ -450,3 +450,35 @@ def test_flash_forward_row_statistics():
     Sc = _kernels.poly_matmul([p.float() for p in flat[0]], [k.float().transpose(1, 2) for k in flat[1]])
     want = _attention._probs(Sc, L, 1 / 128 ** 0.5, True).view(BH, L, n + 1)
     torch.testing.assert_close(stats, want, rtol=2e-3, atol=2e-3)
+
+
+@pytest.mark.parametrize("n,shape,causal", [(3, (1, 2, 256, 64), True), (3, (2, 2, 600, 64), True),
+                                            (2, (1, 3, 200, 64), False), (1, (1, 2, 130, 64), True),
+                                            (0, (1, 2, 77, 64), False), (3, (1, 1, 1024, 64), True)])
+def test_f32_split_attention_against_oracle(n, shape, causal):
+    """float32 attention with head dimension 64 on the split kernels (single-kernel forward,
+    score-epilogue backward and hi/lo gradient products), forward and backward against the float64
+    oracle of the reference decomposition; tolerance 1e-4 of the plane max-norm."""
+    from polytensors_b200 import PolyTensor, _lib
+
+    Q, Kp, V, G = (series(shape, n, s, torch.float32) for s in (81, 82, 83, 84))
+    ref64 = [[p.double() for p in s] for s in (Q, Kp, V, G)]
+    fn = lambda q, k, v: ref.attention(q, k, v, is_causal=causal)   # noqa: E731
+    want_o = fn(*ref64[:3])
+    want = ref.series_vjp(fn, ref64[:3], ref64[3])
+    for nm in ("flash_attn_fwd", "attn_probs_gemm", "attn_dscores_gemm"):
+        _lib.profile_query(nm)
+    _lib.profile_enable(True)
+    try:
+        with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+            q, k, v = (poly(s, requires_grad=True) for s in (Q, Kp, V))
+            o = F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+            o.backward(poly(G))
+        torch.cuda.synchronize()
+    finally:
+        _lib.profile_enable(False)
+    for nm in ("flash_attn_fwd", "attn_probs_gemm", "attn_dscores_gemm"):
+        assert _lib.profile_query(nm)[1] > 0, f"{nm} did not run"
+    assert_close(coeffs(o), want_o, F32, "o")
+    for name, t, w in (("dq", q, want[0]), ("dk", k, want[1]), ("dv", v, want[2])):
+        assert_close(coeffs(t.grad), w, F32, name)

@@ -137,6 +137,25 @@ def test_attention_backward_at_1024(dtype, tol_o, tol_g):
         print(f"  {name}:", assert_close([c.float().cpu() for c in t.grad.coeffs], w, tol_g, name))
 
 
+def test_attention_f32_training_shape_forward_backward():
+    """configs[4]'s attention: float32, head dimension 64, sequence 1024, degree 3, causal, on
+    12 heads, forward and backward (the split kernels) against the float64 oracle."""
+    from polytensors_b200 import PolyTensor
+
+    n, shape = 3, (1, 12, 1024, 64)
+    Q, Kp, V, G = (cuda_series(shape, n, s, torch.float32) for s in (41, 42, 43, 44))
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        q, k, v = (PolyTensor(tuple(X), requires_grad=True) for X in (Q, Kp, V))
+        o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+        o.backward(PolyTensor(tuple(G)))
+    fn = lambda a, b, c: ref.attention(a, b, c, is_causal=True)   # noqa: E731
+    host = [_host(X) for X in (Q, Kp, V, G)]
+    print("attention f32 D=64 L=1024 o:", assert_close([c.cpu() for c in o.coeffs], fn(*host[:3]), 1e-4, "o"))
+    want = ref.series_vjp(fn, host[:3], host[3])
+    for name, t, w in (("dq", q, want[0]), ("dk", k, want[1]), ("dv", v, want[2])):
+        print(f"  {name}:", assert_close([c.cpu() for c in t.grad.coeffs], w, 1e-4, name))
+
+
 # ----------------------------------------------------------------------------------------
 # configs[2]: RMSNorm -> GELU -> linear(32000) -> cross entropy, width 4096, degree 4
 
