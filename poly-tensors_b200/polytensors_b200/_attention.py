@@ -273,13 +273,16 @@ def _fused_backward_f32(Q, Kp, V, dO, dsum, stats, causal, scale, dQ, dK, dV):
     for h0 in range(0, BH, hb):
         hs = slice(h0, min(BH, h0 + hb))
         hbn = hs.stop - hs.start
-        Pr = [torch.empty(hbn, L, S, dtype=torch.bfloat16, device=Q[0].device) for _ in range(2 * NP)]
+        # rows padded to a multiple of 8 keys: the gradient products read these planes in place,
+        # which needs 16-byte row pitches
+        Sp = -(-S // 8) * 8
+        Pr = [torch.empty(hbn, L, Sp, dtype=torch.bfloat16, device=Q[0].device)[..., :S] for _ in range(2 * NP)]
         _score_gemm("probs", [q[hs] for q in Qh], [k[hs].transpose(1, 2) for k in Kh], Pr, stats[hs], scale,
                     mode, 0, split=True)
         if dV is not None:
             K.poly_matmul_hilo([p.transpose(1, 2) for p in Pr], True, [g[hs] for g in dOh], True,
                                out=[t[hs] for t in dV], band=lower)
-        dS = [torch.empty_like(p) for p in Pr]
+        dS = [torch.empty(hbn, L, Sp, dtype=torch.bfloat16, device=Q[0].device)[..., :S] for _ in range(2 * NP)]
         _score_gemm("dscores", [g[hs] for g in dOh], [v[hs].transpose(1, 2) for v in Vh], dS, dsum[hs], scale,
                     mode, 0, probs=Pr, split=True)
         del Pr
