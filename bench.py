@@ -333,16 +333,16 @@ def _timed(fn, steps, warmup, device, world):
 
 
 def _kernel_rates(names_bytes, steps):
-    """Per-kernel achieved GB/s from the library's event timings: {name: (GB/s, ms per launch)}."""
+    """Per-kernel achieved GB/s from the library's event timings over ``steps`` steps; names_bytes:
+    {name: algorithmic bytes per step} (a step may launch a kernel once, or once per chunk)."""
     from polytensors_b200 import _lib
 
     out = {}
     for name, nbytes in names_bytes.items():
         ms, launches = _lib.profile_query(name)
         if launches:
-            per = ms / launches
-            out[name] = {"GB/s": nbytes / (per / 1e3) / 1e9, "ms_per_launch": per, "launches": launches,
-                         "algorithmic_bytes": nbytes}
+            out[name] = {"GB/s": nbytes * steps / (ms / 1e3) / 1e9, "ms_per_step": ms / steps,
+                         "launches_per_step": launches / steps, "algorithmic_bytes_per_step": nbytes}
     return out
 
 
@@ -358,16 +358,27 @@ def run_norm_ce(args, rank, world, device):
     W = PolyTensor(((0.02 * torch.randn(V, H, generator=g)).to(device),), degree=n, requires_grad=True)
     target = torch.randint(0, V, (R,), generator=g).to(device)
 
+    fused_head = getattr(args, "fused_head", False)
+
     def step():
         for t in (x, w, W):
             t.grad = None
         with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
             h = F.gelu(F.rms_norm(x, (H,), w))
-            loss = F.cross_entropy(F.linear(h, W), target)
+            if fused_head:
+                # linear + cross entropy over row chunks: the logit planes are never all formed
+                loss = PolyTensor.linear_cross_entropy(h, W, target)
+            else:
+                loss = F.cross_entropy(F.linear(h, W), target)
             loss.backward()
 
     for _ in range(args.warmup):
         step()
+    torch.cuda.synchronize(device)
+    torch.cuda.reset_peak_memory_stats(device)
+    step()
+    torch.cuda.synchronize(device)
+    peak_gb = torch.cuda.max_memory_allocated(device) / 1e9
     for name in ("rmsnorm_fwd", "rmsnorm_bwd", "cross_entropy_fwd", "cross_entropy_bwd", "poly_gemm", "series_map"):
         _lib.profile_query(name)
     _lib.profile_enable(True)
@@ -378,9 +389,10 @@ def run_norm_ce(args, rank, world, device):
                            "cross_entropy_fwd": P * R * V * 4, "cross_entropy_bwd": 2 * P * R * V * 4}, args.steps)
     gms, glaunch = _lib.profile_query("poly_gemm")
     T = (n + 1) * (n + 2) / 2
-    gemm_flops = 3 * 2 * R * H * V * T   # forward + the two backward products
-    mem_bytes = sum(r["algorithmic_bytes"] * r["launches"] for r in rates.values())
-    mem_ms = sum(r["ms_per_launch"] * r["launches"] for r in rates.values())
+    # forward + the two backward products (+ the logits recomputed in backward with the fused head)
+    gemm_flops = (4 if fused_head else 3) * 2 * R * H * V * T
+    mem_bytes = sum(r["algorithmic_bytes_per_step"] for r in rates.values())
+    mem_ms = sum(r["ms_per_step"] for r in rates.values())
     pk, source = peaks()
     value = mem_bytes / (mem_ms / 1e3) / 1e9
     cpu = None
@@ -390,6 +402,8 @@ def run_norm_ce(args, rank, world, device):
                "ms_per_step_extrapolated": dt * 1e3 * 16384 / 64}
     return {
         "cpu_baseline": cpu,
+        "peak_memory_gb": peak_gb,
+        "fused_head": bool(fused_head),
         "metric": "norm/CE kernels GB/s (configs[2]: RMSNorm+GELU+linear(32000)+CE fwd+bwd, degree 4, float32)",
         "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -397,8 +411,8 @@ def run_norm_ce(args, rank, world, device):
         "config": {"workload": f"norm_gelu_linear_ce rows={R} hidden={H} vocab={V} degree {n}",
                    "l2": "inputs larger than L2"},
         "kernels": rates,
-        "linear": {"TFLOP/s": gemm_flops * (glaunch / 3) / (gms / 1e3) / 1e12 if glaunch else None,
-                   "launches": glaunch, "flops_per_step": gemm_flops},
+        "linear": {"TFLOP/s": gemm_flops * args.steps / (gms / 1e3) / 1e12 if glaunch else None,
+                   "launches_per_step": glaunch / args.steps, "flops_per_step": gemm_flops},
         "roofline": {"bound": "hbm", "achieved": value, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": value / pk["hbm_gbs"], "traffic": None, "peak_source": f"hbm_gbs ({source})"},
         "clocks": clocks,
@@ -754,7 +768,13 @@ def run_train(args, rank, world, device):
                                 no_cpu_baseline=args.no_cpu_baseline, dtype="bf16")
         keep = ("metric", "value", "unit", "ms_per_step", "steps", "config", "roofline", "kernels", "linear",
                 "forward", "cpu_baseline", "clocks")
+        keep = keep + ("peak_memory_gb", "fused_head")
         extras["norm_ce"] = {k: v for k, v in run_norm_ce(ns, rank, world, device).items() if k in keep}
+        torch.cuda.empty_cache()
+        ns.fused_head, ns.no_cpu_baseline = True, True
+        extras["norm_ce_fused_head"] = {k: v for k, v in run_norm_ce(ns, rank, world, device).items()
+                                        if k in keep and k != "cpu_baseline"}
+        ns.fused_head, ns.no_cpu_baseline = False, args.no_cpu_baseline
         torch.cuda.empty_cache()
         for dt in ("bf16", "f32"):
             ns.dtype = dt
@@ -1036,6 +1056,8 @@ def main():
     ap.add_argument("--micro-batches", type=int, default=0,
                     help="train: micro-batches per rank and step (0 = the whole global batch)")
     ap.add_argument("--full-sweep", action="store_true")
+    ap.add_argument("--fused-head", action="store_true",
+                    help="norm_ce: linear + cross entropy through PolyTensor.linear_cross_entropy (chunked logits)")
     args = ap.parse_args()
     cfg = WORKLOADS.get(args.workload)
 

@@ -198,6 +198,119 @@ def cross_entropy(logits, target, softcap=None, ignore_index=-100, reduction="me
 
 
 # ======================================================================================
+# Linear + cross entropy with chunked logits (a fusion the reference does not have: its fused
+# cross entropy, src/polytensors/_fused_cross_entropy.py:131-170, starts from materialised logits)
+
+_LOGITS_CHUNK_BYTES = 1 << 30
+
+
+class _LinearCrossEntropy(torch.autograd.Function):
+    """Per-row cross entropy of ``h W^T`` (series) over row chunks: at most one chunk of logit
+    planes exists at a time, in forward and in backward (which recomputes each chunk's logits)."""
+
+    @staticmethod
+    def forward(ctx, h, weight, target, ignore_index, softcap, chunk):
+        P = _poly_cls()
+        D = h.degree
+        H = [x.reshape(-1, x.shape[-1]) for x in h.coeffs]
+        W = _planes(weight, D)
+        R, V = H[0].shape[0], W[0].shape[0]
+        cdt = K.compute_dtype(H[0].dtype)
+        losses = [torch.empty(R, dtype=cdt, device=H[0].device) for _ in H]
+        stats = torch.empty(R, D + 1, dtype=cdt, device=H[0].device)
+        t = target.reshape(-1)
+        for r0 in range(0, R, chunk):
+            r1 = min(R, r0 + chunk)
+            z = K.poly_matmul([x[r0:r1] for x in H], [w.t() for w in W])
+            loss, st = K.cross_entropy_fwd(z, t[r0:r1], ignore_index, softcap)
+            for dst, src in zip(losses, loss):
+                dst[r0:r1].copy_(src)
+            stats[r0:r1].copy_(st)
+            del z
+        ctx.H, ctx.W, ctx.target, ctx.stats = H, W, t, stats
+        ctx.meta = (ignore_index, softcap, chunk, D, h.shape, isinstance(weight, P), weight.shape, P)
+        return P(tuple(losses))
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, grad):
+        ignore_index, softcap, chunk, D, h_shape, w_poly, w_shape, P = ctx.meta
+        H, W, t, stats = ctx.H, ctx.W, ctx.target, ctx.stats
+        G = _grad_planes(grad, D, P)
+        R = H[0].shape[0]
+        need_h, need_w = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        dH = [torch.empty_like(x) for x in H] if need_h else None
+        dW = [torch.empty(w_shape, dtype=W[0].dtype, device=W[0].device) for _ in W] if need_w else None
+        for r0 in range(0, R, chunk):
+            r1 = min(R, r0 + chunk)
+            Hc = [x[r0:r1] for x in H]
+            z = K.poly_matmul(Hc, [w.t() for w in W])
+            dz = K.cross_entropy_bwd(z, t[r0:r1], ignore_index, softcap, stats[r0:r1],
+                                     [g.expand(R)[r0:r1] for g in G])
+            del z
+            if need_h:
+                K.poly_matmul(dz, W, out=[x[r0:r1] for x in dH])
+            if need_w:
+                K.poly_matmul([d.t() for d in dz], Hc, out=dW, accumulate=r0 > 0)
+        gh = P(tuple(x.view(h_shape) for x in dH)) if need_h else None
+        gw = (P(tuple(dW)) if w_poly else dW[0]) if need_w else None
+        return gh, gw, None, None, None, None
+
+
+def linear_cross_entropy_eligible(h, weight, target):
+    P = _poly_cls()
+    if not isinstance(h, P) or _state.coefficient_autograd.get() or h.degree >= 16 or h.dim() < 1:
+        return False
+    if isinstance(target, P) or not isinstance(target, torch.Tensor) or target.dtype != torch.int64:
+        return False
+    if isinstance(weight, P) and weight.degree != h.degree:
+        return False
+    if weight.dim() != 2 or weight.shape[1] != h.shape[-1] or target.numel() * h.shape[-1] != h.numel():
+        return False
+    planes = list(h.coeffs) + _planes(weight, h.degree)
+    return (_supported(planes) and all(p.dtype == planes[0].dtype for p in planes)
+            and planes[0].dtype in (torch.float32, torch.float64) and target.is_cuda)
+
+
+def linear_cross_entropy(h, weight, target, ignore_index=-100, reduction="mean", softcap=None, chunk_rows=None):
+    """Cross entropy of the logits ``h @ weight.T`` (optionally capped as ``softcap * tanh(z / softcap)``)
+    without forming all of them: rows go through the linear and the streaming cross-entropy
+    kernel in chunks (``chunk_rows``, default: logit planes of at most 1 GiB per chunk), and the
+    backward recomputes each chunk's logits.  Same result as
+    ``F.cross_entropy(F.linear(h, weight), target, ...)`` on a PolyTensor ``h`` of shape (..., d)
+    with targets of shape (...); ``weight`` (V, d) is a PolyTensor of the same degree or an
+    ordinary tensor (zero higher coefficients).  reduction: "mean", "sum" or "none"."""
+    if reduction not in ("none", "mean", "sum"):
+        raise ValueError(f"unsupported reduction {reduction!r}")
+    if not linear_cross_entropy_eligible(h, weight, target):
+        raise NotImplementedError("linear_cross_entropy: needs a CUDA PolyTensor input (float32 or float64) and "
+                                  "int64 targets with one target per row")
+    V = weight.shape[0]
+    rows = target.numel()
+    if chunk_rows is None:
+        per_row = (h.degree + 1) * V * h.coeffs[0].element_size()
+        chunk_rows = max(128, min(rows, _LOGITS_CHUNK_BYTES // max(per_row, 1)) // 128 * 128)
+    chunk_rows = max(1, int(chunk_rows))
+    if torch.is_grad_enabled() and (h.requires_grad or weight.requires_grad):
+        losses = _LinearCrossEntropy.apply(h, weight, target, int(ignore_index), softcap, chunk_rows)
+    else:
+        with torch.no_grad():
+            losses = _LinearCrossEntropy.forward(_NoCtxLCE(), h, weight, target, int(ignore_index), softcap,
+                                                 chunk_rows)
+    if reduction == "none":
+        return losses
+    total = losses.sum()
+    if reduction == "sum":
+        return total
+    count = (target != ignore_index).sum().to(losses.value.dtype)
+    return total / count
+
+
+class _NoCtxLCE:
+    needs_input_grad = (False, False, False, False, False, False)
+
+
+# ======================================================================================
 # Attention (src/polytensors/_decompositions.py:28-43, :80-98)
 
 def attention_decomposed(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False, scale=None,

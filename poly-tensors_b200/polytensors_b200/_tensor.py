@@ -251,6 +251,17 @@ class PolyTensor(torch.Tensor):
 
         return cross_entropy(logits, target, softcap=softcap, ignore_index=ignore_index, reduction=reduction)
 
+    @staticmethod
+    def linear_cross_entropy(input, weight, target, ignore_index=-100, reduction="mean", softcap=None,
+                             chunk_rows=None):
+        """``F.cross_entropy(F.linear(input, weight), target)`` without materialising all logits:
+        row chunks of the series linear go straight into the streaming cross-entropy kernel, and
+        backward recomputes each chunk (no counterpart in the reference)."""
+        from ._fused import linear_cross_entropy
+
+        return linear_cross_entropy(input, weight, target, ignore_index=ignore_index, reduction=reduction,
+                                    softcap=softcap, chunk_rows=chunk_rows)
+
     def backward(self, gradient=None, retain_graph=None, create_graph=False, inputs=None):
         """Reverse-mode through the series: the seed is ``gradient`` as a PolyTensor of this degree
         (an ordinary tensor is its constant term); with no gradient, a real scalar seeds 1."""

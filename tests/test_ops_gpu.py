@@ -482,3 +482,73 @@ def test_f32_split_attention_against_oracle(n, shape, causal):
     assert_close(coeffs(o), want_o, F32, "o")
     for name, t, w in (("dq", q, want[0]), ("dk", k, want[1]), ("dv", v, want[2])):
         assert_close(coeffs(t.grad), w, F32, name)
+
+
+@pytest.mark.parametrize("reduction,softcap,dtype,chunk", [("mean", None, torch.float32, 64),
+                                                           ("sum", 30.0, torch.float32, 100),
+                                                           ("none", None, torch.float64, 50),
+                                                           ("mean", None, torch.float32, None)])
+def test_linear_cross_entropy_matches_the_unfused_chain(reduction, softcap, dtype, chunk):
+    """PolyTensor.linear_cross_entropy (row chunks of the series linear streamed into the
+    cross-entropy kernel, logits recomputed in backward) against F.linear + cross entropy through
+    the API and, without softcap, against the float64 oracle: loss and the gradients of the input
+    and of a weight with nonzero higher coefficients; rows with ignore_index included."""
+    from polytensors_b200 import PolyTensor
+
+    n, R, d, V = 3, 300, 96, 1000
+    tol = F32 if dtype == torch.float32 else F64
+    X = series((R, d), n, 91, dtype)
+    W = [w * 0.1 for w in series((V, d), n, 92, dtype)]
+    g = torch.Generator().manual_seed(93)
+    target = torch.randint(0, V, (R,), generator=g)
+    target[::17] = -100
+    Gr = series((R,), n, 94, dtype) if reduction == "none" else None
+
+    def run(fused):
+        with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+            h, w = poly(X, requires_grad=True), poly(W, requires_grad=True)
+            if fused:
+                loss = PolyTensor.linear_cross_entropy(h, w, target.cuda(), reduction=reduction, softcap=softcap,
+                                                       chunk_rows=chunk)
+            else:
+                loss = PolyTensor.cross_entropy(F.linear(h, w), target.cuda(), reduction=reduction, softcap=softcap)
+            loss.backward(poly(Gr) if Gr is not None else None)
+            return coeffs(loss), coeffs(h.grad), coeffs(w.grad)
+
+    got, want = run(True), run(False)
+    for a, b, what in zip(got, want, ("loss", "dh", "dW")):
+        assert_close(a, b, tol, what)
+    if softcap is None:
+        fn = lambda x, w: ref.cross_entropy(ref.cauchy(x, [t.t() for t in w], lambda a, b: a @ b), target,
+                                            reduction=reduction)   # noqa: E731
+        ref64 = [[p.double() for p in X], [p.double() for p in W]]
+        out = fn(*ref64)
+        seed = [p.double() for p in Gr] if Gr is not None else \
+            [torch.tensor(1.0, dtype=torch.float64)] + [torch.tensor(0.0, dtype=torch.float64)] * n
+        grads = ref.series_vjp(fn, ref64, seed)
+        if reduction == "none":
+            assert_close(got[0], out, tol, "loss vs oracle")
+        assert_close(got[1], grads[0], tol, "dh vs oracle")
+        assert_close(got[2], grads[1], tol, "dW vs oracle")
+
+
+def test_linear_cross_entropy_keeps_one_logit_chunk():
+    """Peak device memory of the fused form stays below one full set of logit planes."""
+    from polytensors_b200 import PolyTensor
+
+    n, R, d, V = 3, 4096, 256, 32000
+    X = [x.cuda() for x in series((R, d), n, 95, torch.float32)]
+    W = torch.randn(V, d, device="cuda") * 0.02
+    target = torch.randint(0, V, (R,), device="cuda")
+    logits_bytes = (n + 1) * R * V * 4
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    base = torch.cuda.memory_allocated()
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        h = PolyTensor(tuple(X), requires_grad=True)
+        loss = PolyTensor.linear_cross_entropy(h, W, target, chunk_rows=512)
+        loss.backward()
+    torch.cuda.synchronize()
+    peak = torch.cuda.max_memory_allocated() - base
+    assert peak < logits_bytes / 2, (peak, logits_bytes)
+    assert torch.isfinite(h.grad.coeffs[0]).all()
