@@ -923,6 +923,108 @@ def run_train(args, rank, world, device):
     return result
 
 
+def _reference_package():
+    """The reference package (samuel-gunn/poly-tensors) pip-installed into baseline/_ref."""
+    import importlib
+
+    path = ROOT / "baseline" / "_ref"
+    if not (path / "polytensors").is_dir():
+        return None
+    if str(path) not in sys.path:
+        sys.path.insert(0, str(path))
+    return importlib.import_module("polytensors")
+
+
+def run_degree1(args, rank, world, device):
+    """Same-box bar: the reference's degree-1 Triton kernels (its fused attention, cross entropy,
+    RMSNorm and activation gates, through its own PolyTensor API inside plain_range()) against the
+    pk:: kernels through this package's API, forward + backward, same inputs; per op the device
+    time per step of both and the largest plane difference between their results."""
+    import torch.nn.functional as F
+    from polytensors_b200 import PolyTensor as Ours
+
+    ref = _reference_package()
+    if ref is None:
+        return {"metric": "degree-1 pk:: vs reference Triton", "unavailable": "baseline/_ref is not installed"}
+    Ref = ref.PolyTensor
+    g = torch.Generator(device=device).manual_seed(5)
+
+    def planes(shape, dtype):
+        return tuple(torch.randn(*shape, generator=g, device=device, dtype=torch.float32).to(dtype) for _ in range(2))
+
+    cases = {
+        "attention_bf16_D128": ([(4, 16, 2048, 128)] * 3, torch.bfloat16,
+                                lambda q, k, v: F.scaled_dot_product_attention(q, k, v, is_causal=True)),
+        "attention_bf16_D64": ([(4, 16, 2048, 64)] * 3, torch.bfloat16,
+                               lambda q, k, v: F.scaled_dot_product_attention(q, k, v, is_causal=True)),
+        "cross_entropy_softcap_V32000": ([(8192, 32000)], torch.float32, None),
+        "rms_norm_4096": ([(16384, 4096)], torch.float32, lambda x: F.rms_norm(x, (4096,))),
+        "gelu": ([(16384, 4096)], torch.float32, lambda x: F.gelu(x)),
+    }
+    target = torch.randint(0, 32000, (8192,), generator=g, device=device)
+    out = {}
+    for name, (shapes, dtype, fn) in cases.items():
+        data = [planes(sh, dtype) for sh in shapes]
+        grad_seed = planes(shapes[0], dtype) if fn is not None else None
+        res = {}
+        for impl, P in (("reference_triton", Ref), ("polykern", Ours)):
+            xs = [P(d, requires_grad=True) for d in data]
+
+            def step(P=P, xs=xs):
+                for x in xs:
+                    x.grad = None
+                with P.plain_range(), P.retain_wrappers():
+                    if fn is None:
+                        y = P.cross_entropy(xs[0], target, softcap=30.0)
+                        y.backward()
+                    else:
+                        y = fn(*xs)
+                        y.backward(P(grad_seed))
+                    return [c.detach() for c in y.coeffs], [c.detach() for c in xs[0].grad.coeffs]
+            try:
+                for _ in range(max(args.warmup, 2)):
+                    step()
+                ms, _ = _timed(step, max(3, min(args.steps, 10)), 0, device, world)
+                res[impl] = {"ms_per_step": ms, "result": step()}
+            except Exception as e:   # noqa: BLE001  (a reference path that does not run here is reported)
+                res[impl] = {"error": f"{type(e).__name__}: {e}"[:300]}
+        entry = {k: {kk: vv for kk, vv in v.items() if kk != "result"} for k, v in res.items()}
+        if all("result" in v for v in res.values()):
+            diffs = []
+            for a, b in zip(sum(res["polykern"]["result"], []), sum(res["reference_triton"]["result"], [])):
+                a, b = a.double(), b.double()
+                diffs.append(((a - b).abs().max() / b.abs().max().clamp_min(1e-30)).item())
+            entry["max_plane_diff"] = max(diffs)
+            entry["speedup"] = res["reference_triton"]["ms_per_step"] / res["polykern"]["ms_per_step"]
+        out[name] = entry
+        torch.cuda.empty_cache()
+    # kernel level for the activation: the reference's Triton kernel through its gate function
+    # (src/polytensors/_fused_activation.py:5-24, forward and backward) against pk_series_map
+    from importlib import import_module
+
+    from polytensors_b200 import _kernels as K
+
+    act = import_module(f"{ref.__name__}._fused_activation")
+    X = planes((16384, 4096), torch.float32)
+    Gs = planes((16384, 4096), torch.float32)
+    kern = {}
+    for impl, fwd, bwd in (("reference_triton", lambda: act.maybe_activation(X, "gelu"),
+                            lambda: act.maybe_activation(X, "gelu", Gs)),
+                           ("polykern", lambda: K.series_map("gelu", 1, list(X)),
+                            lambda: K.series_map("gelu_bwd", 1, list(Gs), list(X)))):
+        step = lambda fwd=fwd, bwd=bwd: (fwd(), bwd())   # noqa: E731
+        for _ in range(3):
+            step()
+        ms, _ = _timed(step, 10, 0, device, world)
+        kern[impl] = {"ms_per_step": ms, "GB/s": 2 * 4 * 16384 * 4096 * (2 + 3) / (ms / 1e3) / 1e9}
+    kern["speedup"] = kern["reference_triton"]["ms_per_step"] / kern["polykern"]["ms_per_step"]
+    out["gelu_kernels_fwd_bwd"] = kern
+    return {"metric": "degree-1 forward+backward ms per step: pk:: kernels vs the reference's Triton kernels "
+                      "(same B200, each through its own PolyTensor API in plain_range; gelu_kernels_fwd_bwd: the "
+                      "activation kernels called directly)",
+            "value": None, "unit": "ms", "n_gpus": world, "ops": out}
+
+
 def run_matmul_sweep(args, rank, world, device):
     """every size / degree / dtype point, one line per point in 'sweep'."""
     from polytensors_b200 import _kernels
@@ -1042,7 +1144,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="train",
                     choices=sorted(WORKLOADS) + ["norm_ce", "attention", "attention_fwd", "train",
-                                                 "poly_matmul_sweep"])
+                                                 "poly_matmul_sweep", "degree1"])
     ap.add_argument("--no-matmul", action="store_true", help="train: skip the configs[1] product line")
     ap.add_argument("--no-extras", action="store_true", help="train: skip the configs[2] / configs[3] lines")
     ap.add_argument("--impl", default="polykern", choices=["polykern", "reference"])
@@ -1087,7 +1189,7 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=device)
     secondary = {"norm_ce": run_norm_ce, "attention": run_attention, "attention_fwd": run_attention_fwd,
-                 "train": run_train,
+                 "train": run_train, "degree1": run_degree1,
                  "poly_matmul_sweep": run_matmul_sweep}
     if args.workload in secondary:
         result = secondary[args.workload](args, rank, world, device)
