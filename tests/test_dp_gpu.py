@@ -19,7 +19,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, queue):
+def _worker(rank, world, port, queue, overlapped=False):
     import sys
 
     here = os.path.dirname(os.path.abspath(__file__))
@@ -29,7 +29,7 @@ def _worker(rank, world, port, queue):
     import torch.distributed as dist
     import torch.nn.functional as F
     from polytensors_b200 import PolyTensor
-    from polytensors_b200.parallel import allreduce_gradients
+    from polytensors_b200.parallel import OverlappedAllReduce, allreduce_gradients
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -43,6 +43,7 @@ def _worker(rank, world, port, queue):
         P = {k: torch.nn.Parameter(PolyTensor((v.to(dev),), degree=n)) for k, v in init.items()}
         Z = PolyTensor((torch.tensor(0.0, device=dev), 1.0), degree=n)
         opt = torch.optim.SGD(list(P.values()), lr=cfg["lr"], foreach=False)
+        reducer = OverlappedAllReduce(list(P.values()), bucket_bytes=1 << 16) if overlapped else None
         per = Bt // world
         ids = g["ids"][:, rank * per:(rank + 1) * per].to(dev)
         losses = []
@@ -62,8 +63,13 @@ def _worker(rank, world, port, queue):
                         x = x + F.linear(F.gelu(F.linear(h, P[f"w1.{l}"])), P[f"w2.{l}"])
                     logits = F.linear(F.rms_norm(x, (d,), P["nf"]), P["head"])
                     loss = F.cross_entropy(logits.reshape(-1, V), tgt.reshape(-1)) * (1 - cfg["lam"] * Z)
+                    if reducer is not None:
+                        reducer.arm()
                     loss.backward()
-                    allreduce_gradients(list(P.values()))
+                    if reducer is not None:
+                        reducer.finish()
+                    else:
+                        allreduce_gradients(list(P.values()))
                     opt.step()
         # numpy arrays travel by value; a tensor would travel through shared memory that this
         # process removes when it exits, possibly before the parent has received it
@@ -74,7 +80,8 @@ def _worker(rank, world, port, queue):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_rank_training_matches_reference(golden):
+@pytest.mark.parametrize("overlapped", [False, True])
+def test_two_rank_training_matches_reference(golden, overlapped):
     import torch.multiprocessing as mp
 
     from test_training_gpu import _as_accurate
@@ -82,7 +89,7 @@ def test_two_rank_training_matches_reference(golden):
     world, port = 2, _free_port()
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, queue)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue, overlapped)) for r in range(world)]
     for p in procs:
         p.start()
     results = {r: {k: [torch.from_numpy(c) for c in v] for k, v in final.items()}

@@ -95,3 +95,70 @@ def test_failed_rank_surfaces_as_error_not_hang():
             p.kill()
     assert procs[1].exitcode == 3
     assert rank == 0 and message.startswith("error"), message
+
+
+def _overlap_worker(rank, world, port, queue):
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "poly-tensors_b200"))
+    from polytensors_b200.parallel import OverlappedAllReduce
+
+    _init(rank, world, port)
+    try:
+        torch.manual_seed(0)
+        layers = [torch.nn.Linear(6, 6) for _ in range(4)]
+        unused = torch.nn.Parameter(torch.zeros(3))   # never gets a gradient (skipped on every rank)
+        params = [p for l in layers for p in l.parameters()] + [unused]
+        ar = OverlappedAllReduce(params, bucket_bytes=200)   # several buckets
+        x_all = torch.randn(2, 3, 6, generator=torch.Generator().manual_seed(1))
+        for step in range(2):   # the first step finds the unused parameter, the second runs without it
+            for p in params:
+                p.grad = None
+            for micro in range(3):   # gradient accumulation; only the last backward launches buckets
+                x = x_all[rank] * (micro + 1)
+                for l in layers:
+                    x = torch.tanh(l(x))
+                if micro == 2:
+                    ar.arm()
+                x.sum().backward()
+            launched_during = ar.next_launch
+            ar.finish()
+        got = [p.grad.tolist() if p.grad is not None else None for p in params]
+        queue.put((rank, got, launched_during, len(ar.buckets)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_overlapped_allreduce_matches_the_average():
+    """Buckets are launched from the gradient hooks during the last backward (several of them before
+    finish()), and the result equals the average over ranks of each rank's accumulated gradient."""
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_overlap_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {r: (g, n, nb) for r, g, n, nb in (queue.get(timeout=120) for _ in range(world))}
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # reference: each rank's accumulated gradients computed here, then averaged
+    torch.manual_seed(0)
+    layers = [torch.nn.Linear(6, 6) for _ in range(4)]
+    x_all = torch.randn(2, 3, 6, generator=torch.Generator().manual_seed(1))
+    per_rank = []
+    for rank in range(world):
+        for l in layers:
+            l.zero_grad()
+        for micro in range(3):
+            x = x_all[rank] * (micro + 1)
+            for l in layers:
+                x = torch.tanh(l(x))
+            x.sum().backward()
+        per_rank.append([p.grad.clone() for l in layers for p in l.parameters()])
+    want = [(a + b) / 2 for a, b in zip(*per_rank)]
+    for rank in range(world):
+        got, launched, nbuckets = results[rank]
+        assert nbuckets > 2 and launched >= nbuckets - 1, (launched, nbuckets)
+        assert got[-1] is None
+        for g, w in zip(got[:-1], want):
+            assert torch.allclose(torch.tensor(g), w, atol=1e-6)
