@@ -447,18 +447,18 @@ def cpu_norm_ce_rate(rows, threads):
     return nbytes / dt / 1e9, dt, f"{rows} of 16384 rows, fwd + series backward, float32, {dt:.1f} s"
 
 
-def cpu_attention_rate(L, threads):
-    """Reference SDPA decomposition (oracle) on a (1, 4, L, 128) head slice, causal, degree 3,
+def cpu_attention_rate(L, threads, D=128):
+    """Reference SDPA decomposition (oracle) on a (1, 4, L, D) head slice, causal, degree 3,
     forward + series backward, float32.  Returns (coefficient TFLOP/s, description)."""
     from oracle import polyref
 
     torch.set_num_threads(threads)
-    n, shape = 3, (1, 4, L, 128)
+    n, shape = 3, (1, 4, L, D)
     Q, Kp, V, G = (make_series(shape, n, s, torch.float32) for s in (1, 2, 3, 4))
     t0 = time.perf_counter()
     polyref.series_vjp(lambda q, k, v: polyref.attention(q, k, v, is_causal=True), [Q, Kp, V], G)
     dt = time.perf_counter() - t0
-    return attention_flops(1, 4, L, 128, n) / dt / 1e12, f"(1, 4, {L}, 128) head slice, fwd + backward, {dt:.1f} s"
+    return attention_flops(1, 4, L, D, n) / dt / 1e12, f"(1, 4, {L}, {D}) head slice, fwd + backward, {dt:.1f} s"
 
 
 def attention_flops(B, H, L, D, n):
@@ -489,11 +489,11 @@ def run_attention_fwd(args, rank, world, device):
 
 def run_attention(args, rank, world, device):
     """causal series attention (8, 32, L, 128), degree 3, forward + backward
-    (--batch changes the batch for profiling runs)."""
+    (--batch / --heads / --head-dim change the shape, e.g. configs[4]'s (8, 12, 1024, 64))."""
     import torch.nn.functional as F
     from polytensors_b200 import PolyTensor
 
-    n, B, H, L, D = 3, args.batch, 32, args.seq, 128
+    n, B, H, L, D = 3, args.batch, getattr(args, "heads", 32), args.seq, getattr(args, "head_dim", 128)
     dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
     q, k, v = (_series_poly((B, H, L, D), n, s, dtype, device, requires_grad=True) for s in (1, 2, 3))
     G = _series_poly((B, H, L, D), n, 4, dtype, device)
@@ -536,15 +536,15 @@ def run_attention(args, rank, world, device):
     value = world * flops / (ms / 1e3) / 1e12
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, desc = cpu_attention_rate(min(L, 1024), os.cpu_count() or 1)
+        rate, desc = cpu_attention_rate(min(L, 1024), os.cpu_count() or 1, D)
         cpu = {"value": rate, "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port", "sample": desc}
     return {
         "cpu_baseline": cpu,
-        "metric": f"poly-attention coeff TFLOP/s (configs[3]: causal, ({B}, 32, {L}, 128), degree 3, {args.dtype}, fwd+bwd)",
+        "metric": f"poly-attention coeff TFLOP/s (causal, ({B}, {H}, {L}, {D}), degree 3, {args.dtype}, fwd+bwd)",
         "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.dtype,
         "data": "synthetic: planes N(0,1)/k!, seeded",
-        "config": {"workload": f"attention B={B} H=32 L={L} D=128 degree 3 causal {args.dtype}",
+        "config": {"workload": f"attention B={B} H={H} L={L} D={D} degree 3 causal {args.dtype}",
                    "flops": "12*T*B*H*L(L+1)/2*D (causal pairs, no recompute)"},
         "roofline": {"bound": "tensor", "achieved": value / world, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": value / world / pk["bf16_tflops"], "traffic": None,
@@ -1163,6 +1163,8 @@ def main():
     ap.add_argument("--seq", type=int, default=4096, help="attention: sequence length")
     ap.add_argument("--batch", type=int, default=8, help="attention / attention_fwd: batch")
     ap.add_argument("--dtype", default="f32", choices=["f32", "bf16"], help="attention: storage dtype")
+    ap.add_argument("--heads", type=int, default=32, help="attention: heads")
+    ap.add_argument("--head-dim", type=int, default=128, help="attention: head dimension")
     ap.add_argument("--layers", type=int, default=12, help="train: transformer layers")
     ap.add_argument("--micro", type=int, default=8, help="train: sequences per micro-batch")
     ap.add_argument("--micro-batches", type=int, default=0,
