@@ -345,6 +345,10 @@ PK_API int pk_flash_attn_fwd(int dtype, int degree, int64_t bh, int64_t L, int64
  * the output — holds 2(n+1) bf16 planes hi_0, lo_0, hi_1, ... (x ~= hi + lo); products are
  * hi*hi + hi*lo + lo*hi in fp32 and the outputs are written split the same way, ready for
  * pk_poly_gemm_hilo.
+ *
+ * In this form pk_attn_dscores_gemm writes its output key-major, dscores[b][key][query] at
+ * b * ds_bs + key * ds_rs + query (the transpose of the bf16 layout), so that its stores are
+ * coalesced; both gradient products read that layout in place.
  */
 PK_API int pk_attn_probs_gemm(int dtype, int degree, int64_t batch, int64_t M, int64_t N, int64_t K,
                               const void* const* q, int64_t q_bs, int64_t q_rs, int64_t q_cs,

@@ -451,7 +451,10 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
             // this thread's 16 columns of every plane as bf16 pairs, ypk[k][0..7], stored after both
             // halves; float32 (hi/lo pairs): one 8-column half at a time, ypk[k * NS + h][0..3],
             // stored as soon as it is formed (registers)
-            constexpr int YW = NS == 1 ? 8 : 4;
+            // the split probabilities keep all 16 columns too, so that each row's 32-byte sector of a
+            // plane leaves in one go
+            constexpr bool FULL = NS == 1 || MODE == AG_PROBS;
+            constexpr int YW = FULL ? 8 : 4;
             uint32_t ypk[NP * NS][YW];
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
@@ -532,7 +535,7 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
 #pragma unroll
                         for (int k = 0; k < NP; ++k) {
                             const uint32_t hb = bf16x2_bits(v2[0][k], v2[1][k]);
-                            const int yi = NS == 1 ? c * 4 + e / 2 : e / 2;
+                            const int yi = FULL ? c * 4 + e / 2 : e / 2;
                             ypk[k * NS][yi] = hb;
                             if constexpr (NS == 2) {
                                 // lo = bf16(x - hi): the part of x the rounded hi misses
@@ -545,26 +548,43 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
 #pragma unroll
                     for (int k = 0; k < NP * NS; ++k)
 #pragma unroll
-                        for (int t = 0; t < 4; ++t) ypk[k][NS == 1 ? c * 4 + t : t] = 0u;
+                        for (int t = 0; t < 4; ++t) ypk[k][FULL ? c * 4 + t : t] = 0u;
                 }
-                if constexpr (NS == 2) {
+                if constexpr (NS == 2 && !FULL) {
+                    // split score gradient, stored key-major (plane [key][query], c_rs apart per key):
+                    // for each of the half's 8 keys the warp's 32 lanes write 32 consecutive queries
                     const int valid = row_ok ? max(0, min(8, p.N - cb)) : 0;
 #pragma unroll
                     for (int k = 0; k < NP * NS; ++k) {
-                        if (valid <= 0) break;
-                        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c[k]) + tc.b * p.c_bs +
-                                             static_cast<int64_t>(r) * p.c_rs + cb;
-                        if (vec && valid == 8) {
-                            *reinterpret_cast<uint4*>(dst) = make_uint4(ypk[k][0], ypk[k][1], ypk[k][2], ypk[k][3]);
-                        } else {
-                            for (int t = 0; t < valid; ++t)
-                                dst[t] = __ushort_as_bfloat16(
-                                    static_cast<unsigned short>((ypk[k][t / 2] >> (16 * (t & 1))) & 0xFFFFu));
-                        }
+                        unsigned short* dst = static_cast<unsigned short*>(p.c[k]) + tc.b * p.c_bs +
+                                              static_cast<int64_t>(cb) * p.c_rs + r;
+#pragma unroll
+                        for (int t = 0; t < 8; ++t)
+                            if (t < valid)
+                                dst[static_cast<int64_t>(t) * p.c_rs] =
+                                    static_cast<unsigned short>((ypk[k][t / 2] >> (16 * (t & 1))) & 0xFFFFu);
                     }
                 }
             }
-            if constexpr (NS == 2) {
+            if constexpr (NS == 2 && FULL) {
+                // split probabilities: each row's 16 columns of every hi / lo plane as one 32-byte store pair
+                const int valid = row_ok ? max(0, min(16, p.N - cbase)) : 0;
+#pragma unroll
+                for (int k = 0; k < NP * NS; ++k) {
+                    if (valid <= 0) break;
+                    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c[k]) + tc.b * p.c_bs +
+                                         static_cast<int64_t>(r) * p.c_rs + cbase;
+                    if (vec && valid == 16) {
+                        uint4* d4 = reinterpret_cast<uint4*>(dst);
+                        d4[0] = make_uint4(ypk[k][0], ypk[k][1], ypk[k][2], ypk[k][3]);
+                        d4[1] = make_uint4(ypk[k][4], ypk[k][5], ypk[k][6], ypk[k][7]);
+                    } else {
+                        for (int t = 0; t < valid; ++t)
+                            dst[t] = __ushort_as_bfloat16(
+                                static_cast<unsigned short>((ypk[k][t / 2] >> (16 * (t & 1))) & 0xFFFFu));
+                    }
+                }
+            } else if constexpr (NS == 2) {
                 // stored half by half above
             } else if (p.tma_store) {
                 // Per plane: the warp writes its 32 rows x 16 columns into its own staging block
@@ -717,9 +737,13 @@ static int attn_score_gemm(int mode, const char* what, int dtype, int degree, in
     if (total > 0x7fffffff) return fail(PK_ERR_UNSUPPORTED, w + ": too many tiles");
     p.total_units = static_cast<int>(total);
     p.a_bytes = NPL * p.kblocks * AG_A_BYTES;
-    p.nstages = std::min(AG_MAX_STAGES, (AG_SMEM_BUDGET - AG_OUT_BYTES - p.a_bytes) / AG_B_BYTES);
+    // the split form stores its outputs directly (no TMA-store staging), so the staging area's
+    // shared memory goes to the B ring: 12 stages at degree 3, so that the next tile's stages
+    // load while a tile's products run
+    const int out_bytes = NS == 1 ? AG_OUT_BYTES : 0;
+    p.nstages = std::min(AG_MAX_STAGES, (AG_SMEM_BUDGET - out_bytes - p.a_bytes) / AG_B_BYTES);
     // a k block's NPL B stages must be resident together; bf16 keeps two more for prefetch
-    if (p.a_bytes + AG_OUT_BYTES > AG_SMEM_BUDGET || p.nstages < NPL + (NS == 1 ? 2 : 0))
+    if (p.a_bytes + out_bytes > AG_SMEM_BUDGET || p.nstages < NPL + (NS == 1 ? 2 : 0))
         return fail(PK_ERR_UNSUPPORTED, w + ": reduction too long for the resident operand");
     p.a_mn = am == OPM_MNMAJOR;
     p.b_mn = bm == OPM_MNMAJOR;

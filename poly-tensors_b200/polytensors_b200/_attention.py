@@ -282,15 +282,17 @@ def _fused_backward_f32(Q, Kp, V, dO, dsum, stats, causal, scale, dQ, dK, dV):
         if dV is not None:
             K.poly_matmul_hilo([p.transpose(1, 2) for p in Pr], True, [g[hs] for g in dOh], True,
                                out=[t[hs] for t in dV], band=lower)
-        dS = [torch.empty(hbn, L, Sp, dtype=torch.bfloat16, device=Q[0].device)[..., :S] for _ in range(2 * NP)]
-        _score_gemm("dscores", [g[hs] for g in dOh], [v[hs].transpose(1, 2) for v in Vh], dS, dsum[hs], scale,
+        # the split score gradient is written key-major (coalesced stores): dSt[b][key][query]
+        Lp = -(-L // 8) * 8
+        dSt = [torch.empty(hbn, S, Lp, dtype=torch.bfloat16, device=Q[0].device)[..., :L] for _ in range(2 * NP)]
+        _score_gemm("dscores", [g[hs] for g in dOh], [v[hs].transpose(1, 2) for v in Vh], dSt, dsum[hs], scale,
                     mode, 0, probs=Pr, split=True)
         del Pr
         if dQ is not None:
-            K.poly_matmul_hilo(dS, True, [k[hs] for k in Kh], True, out=[t[hs] for t in dQ], band=upper)
+            K.poly_matmul_hilo([d.transpose(1, 2) for d in dSt], True, [k[hs] for k in Kh], True,
+                               out=[t[hs] for t in dQ], band=upper)
         if dK is not None:
-            K.poly_matmul_hilo([d.transpose(1, 2) for d in dS], True, [q[hs] for q in Qh], True,
-                               out=[t[hs] for t in dK], band=lower)
+            K.poly_matmul_hilo(dSt, True, [q[hs] for q in Qh], True, out=[t[hs] for t in dK], band=lower)
 
 
 def backward_planes(Q, Kp, V, O, dO, causal, scale, need, stats=None):
