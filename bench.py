@@ -36,9 +36,14 @@ import torch  # noqa: E402
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one product launch, from the ncu
-# capture summarised in profiles/tc_poly_gemm_f32_n4_2048_and_8192.md, per configuration.
-_GEMM_TRAFFIC = {(8192, 4, "float32"): 56470521088 + 1338964736}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one product launch: the 2048^3
+# degree-4 capture of the current kernel (522 MB) scaled x64 by the units processed, see
+# profiles/tc_poly_gemm_f32_n4_2048_and_8192.md.
+_GEMM_TRAFFIC = {(8192, 4, "float32"): 522.0e6 * 64}
+# DRAM bytes per algorithmic flop of the training step's product launches: 66.6 GB over 19.42 TFLOP
+# in a 2-layer, 1-micro-batch step (profiles/tc_poly_gemm_train_dram.md); the full step's traffic is
+# this ratio times its algorithmic product flops.
+_TRAIN_GEMM_BYTES_PER_FLOP = 66.6e9 / 19.42e12
 
 WORKLOADS = {
     "poly_matmul": dict(M=8192, N=8192, K=8192, degree=4, dtype="float32"),
@@ -916,11 +921,14 @@ def run_train(args, rank, world, device):
                        "copied out every step"},
         "roofline": {"bound": "tensor", "kernel": "polynomial products (tc_poly_gemm / tc_allplanes)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak if achieved else None, "traffic": None,
+                     "frac": achieved / peak if achieved else None,
+                     "traffic": _TRAIN_GEMM_BYTES_PER_FLOP * gemm_flops,
+                     "traffic_unit": "DRAM bytes per step, all product launches (ncu capture of a reduced step "
+                                     "scaled by algorithmic flops)",
                      "peak_source": f"bf16_tflops_sustained ({source}): a kernel timed inside a long step",
                      "device_ms_per_step": gemm_ms, "algorithmic_tflop_per_step": gemm_flops / 1e12,
                      "note": "algorithmic flops of the product launches as issued (float32 products execute "
-                             "3 bf16 MMAs each); traffic: see the profiles summary"},
+                             "3 bf16 MMAs each)"},
         "step_tflops": gemm_flops / (ms / 1e3) / 1e12,
         "gpu_launches": launches,
         "gpu_launches_per_step": launches / args.steps,
