@@ -744,6 +744,108 @@ def train_parity_and_cpu(layers, device, threads, batch=4, seq=256):
     return parity, cpu
 
 
+def readme_fit_data(seed=0):
+    """the README's regression data, seeded: Y = X A + b + E (noise 0.1), independent
+    X', Y' of matching variance, and the ten minibatches of 16 indices each."""
+    g = torch.Generator().manual_seed(seed)
+    n, d, noise = 64, 3, 0.1
+    A, b = torch.randn(d, generator=g), torch.randn((), generator=g)
+    X = torch.randn(n, d, generator=g)
+    E = noise * torch.randn(n, generator=g)
+    Y = X @ A + b + E
+    Xp = torch.randn(n, d, generator=g)
+    Yp = (d + 1 + noise ** 2) ** 0.5 * torch.randn(n, generator=g)
+    batches = [(torch.randint(n, (16,), generator=g), torch.randint(n, (16,), generator=g)) for _ in range(10)]
+    return X, Y, Xp, Yp, batches
+
+
+def gpu_readme_fit(device, data, degree=5):
+    """The README fit through this package's API on the GPU (plain range): 10 SGD steps of
+    loss = (signal + (1 - Z) noise) / 2; returns the coefficient planes of w and c."""
+    from polytensors_b200 import PolyTensor
+
+    X, Y, Xp, Yp = (t.to(device) for t in data[:4])
+    batches = [(i.to(device), j.to(device)) for i, j in data[4]]
+    Z = PolyTensor((torch.tensor(0.0, device=device), 1.0), degree=degree)
+    w = (torch.zeros(X.shape[1], device=device) + 0 * Z).requires_grad_()
+    c = (torch.zeros((), device=device) + 0 * Z).requires_grad_()
+    opt = torch.optim.SGD([w, c], lr=0.1, foreach=False)
+    with PolyTensor.plain_range():
+        for i, j in batches:
+            opt.zero_grad(set_to_none=True)
+            with PolyTensor.retain_wrappers():
+                signal = (X[i] @ w + c - Y[i]).square().mean()
+                noise = (Xp[j] @ w + c - Yp[j]).square().mean()
+                loss = (signal + (1 - Z) * noise) / 2
+                loss.backward()
+                opt.step()
+    return list(w.detach().coeffs), list(c.detach().coeffs)
+
+
+def oracle_readme_fit(data, dtype, degree=5):
+    """The same fit through the oracle restatement of the reference's plain-range rules on the
+    CPU: series residuals, squares and means, the (1 - Z) weight, the series backward and the
+    per-plane SGD update."""
+    from oracle import polyref as R
+
+    X, Y, Xp, Yp = (t.to(dtype) for t in data[:4])
+    d, P = X.shape[1], degree + 1
+    w = [torch.zeros(d, dtype=dtype) for _ in range(P)]
+    c = [torch.zeros((), dtype=dtype) for _ in range(P)]
+    one_minus_z = [torch.tensor(1.0, dtype=dtype), torch.tensor(-1.0, dtype=dtype)] + \
+                  [torch.tensor(0.0, dtype=dtype)] * (P - 2)
+    seed = [torch.tensor(1.0, dtype=dtype)] + [torch.tensor(0.0, dtype=dtype)] * degree
+
+    def loss(i, j):
+        def mse(Xs, Ys, ws, cs):
+            r = [Xs @ wk + ck - (Ys if k == 0 else 0) for k, (wk, ck) in enumerate(zip(ws, cs))]
+            return [q.mean() for q in R.cauchy(r, r)]
+        return lambda ws, cs: [(a + b) / 2 for a, b in zip(mse(X[i], Y[i], ws, cs),
+                                                           R.cauchy(one_minus_z, mse(Xp[j], Yp[j], ws, cs)))]
+
+    for i, j in data[4]:
+        gw, gc = R.series_vjp(loss(i, j), [w, c], seed)
+        w = [a - 0.1 * g for a, g in zip(w, gw)]
+        c = [a - 0.1 * g for a, g in zip(c, gc)]
+    return w, c
+
+
+def readme_fit_line(device, steps, warmup):
+    """device time of the README fit (10 SGD steps) through the API, and its final
+    w, c series against the float64 oracle (with the float32 oracle's own error beside it)."""
+    from oracle import polyref as R
+
+    data = readme_fit_data()
+    for _ in range(max(1, warmup)):
+        gw, gc = gpu_readme_fit(device, data)
+    torch.cuda.synchronize(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream(device)
+    s.record(stream)
+    for _ in range(steps):
+        gw, gc = gpu_readme_fit(device, data)
+    e.record(stream)
+    torch.cuda.synchronize(device)
+    ms = s.elapsed_time(e) / steps
+    w64, c64 = oracle_readme_fit(data, torch.float64)
+    t0 = time.perf_counter()
+    w32, c32 = oracle_readme_fit(data, torch.float32)
+    cpu_ms = (time.perf_counter() - t0) * 1e3
+    worst, ok = 0.0, True
+    for got, r32, want in ((gw, w32, w64), (gc, c32, c64)):
+        for a, b in zip(R.plane_errors([x.cpu() for x in got], want), R.plane_errors(r32, want)):
+            worst = max(worst, a)
+            ok &= a <= max(1e-4, 3 * b)
+    return {"metric": "README fit (configs[0]): 10 SGD steps of the degree-5 series regression, ms per fit",
+            "value": ms, "unit": "ms", "higher_is_better": False, "steps": steps,
+            "config": {"workload": "readme_fit n=64 d=3 degree 5 float32 SGD(lr=0.1) 10 steps, plain range"},
+            "parity": {"max_plane_err": worst, "within_tolerance": bool(ok),
+                       "tol": "per plane: err <= max(1e-4, 3 x the float32 oracle's err)",
+                       "against": "oracle restatement of the fit, float64, CPU"},
+            "cpu_baseline": {"value": cpu_ms, "unit": "ms", "cores": 1, "kind": "port",
+                             "sample": "the whole fit through the oracle, float32"}}
+
+
 def run_train(args, rank, world, device):
     """configs[4] (the default workload): global batch 64 x seq 1024 sharded over the ranks,
     micro-batches of args.micro sequences per rank with gradient accumulation, one bucketed
@@ -767,6 +869,7 @@ def run_train(args, rank, world, device):
                                                         "kernel_ms_per_launch", "clocks")}
         torch.cuda.empty_cache()
     if world == 1 and not args.no_extras:
+        extras["readme_fit"] = readme_fit_line(device, min(args.steps, 5), args.warmup)
         # configs[2] and configs[3] on the same GPU, a few steps each (per-op lines carried here so
         # that every config is measured in the default run)
         ns = argparse.Namespace(steps=min(args.steps, 3), warmup=2, rows=16384, seq=4096, batch=8,

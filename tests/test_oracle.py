@@ -113,3 +113,17 @@ def test_series_ops(golden):
     }
     for key, got in checks.items():
         assert_series_close(got, g[key], 1e-12)
+
+
+def test_bench_readme_fit_oracle_matches_the_reference_run(golden):
+    """bench.py's configs[0] CPU leg (the README fit through the oracle) reproduces the reference's
+    own README run (tests/golden/readme_fit_plain.pt): the seeded data follow the README's draws."""
+    import bench
+
+    g = golden("readme_fit_plain")
+    data = bench.readme_fit_data()
+    assert torch.equal(data[0], g["X"]) and torch.equal(data[3], g["Y_prime"])
+    for dtype in (torch.float32, torch.float64):   # the fixture is the reference's float32 run
+        w, c = bench.oracle_readme_fit(data, dtype)
+        assert max(ref.plane_errors(w, g["w"])) <= 1e-5, dtype
+        assert max(ref.plane_errors(c, g["c"])) <= 1e-5, dtype
