@@ -115,7 +115,7 @@ def dispatch(func, args, kwargs):
     if not polys:
         return func(*args, **kwargs)
     if _state.coefficient_autograd.get():
-        raise NotImplementedError("PolyTensor.coefficient_autograd() is not implemented by the polykern kernels")
+        return _coefficient_dispatch(func, args, kwargs, polys)
     degree = polys[0].degree
     if any(p.degree != degree for p in polys[1:]):
         raise ValueError("PolyTensor operands must have the same degree")
@@ -133,6 +133,113 @@ def dispatch(func, args, kwargs):
     if fn is None:
         raise NotImplementedError(f"PolyTensor does not implement {func}")
     return fn(Ctx(func, args, kwargs, degree, polys[0].value))
+
+
+# ======================================================================================
+# coefficient_autograd(): ordinary autograd graphs on the coefficient tensors
+#
+# In this mode (the reference's src/polytensors/_tensor.py:290-323) the user makes coefficient
+# tensors autograd leaves and differentiates output coefficients with torch.autograd.grad.  The
+# reference gets that by running its rules, which are torch operations, with autograd enabled.
+# Here a rule launches kernels, so each operation becomes ONE autograd Function over all input
+# coefficient planes: forward runs the rule, backward evaluates the coefficient map's
+# vector-Jacobian product through the swapped-cotangent identity the reference documents for its
+# fused kernels (src/polytensors/_fused_attention.py:18-22): for output cotangents c_0..c_n, the
+# cotangent of input plane m is coefficient n - m of the wrapper gradient series of the same
+# operation for the gradient series G_k = c_{n-k}; the operation is re-run under wrapper autograd
+# in backward to obtain it.  Further (second-order) derivatives in this mode are not supported.
+
+def _replace_polys(x, mapping):
+    if is_poly(x) and id(x) in mapping:
+        return mapping[id(x)]
+    if isinstance(x, (list, tuple)):
+        return type(x)(_replace_polys(v, mapping) for v in x)
+    if isinstance(x, dict):
+        return {k: _replace_polys(v, mapping) for k, v in x.items()}
+    return x
+
+
+class _CoefficientMap(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, func, args, kwargs, polys, *planes):
+        from ._tensor import PolyTensor
+
+        with torch.no_grad():
+            out = dispatch(func, args, kwargs)
+        if not isinstance(out, PolyTensor):
+            raise NotImplementedError(f"PolyTensor.coefficient_autograd(): {func} does not return one PolyTensor")
+        ctx.func, ctx.args, ctx.kwargs, ctx.polys = func, args, kwargs, polys
+        ctx.out_meta = [(c.shape, c.dtype) for c in out.coeffs]
+        ctx.save_for_backward(*planes)
+        # outputs must not alias the inputs (view rules return per-plane views)
+        return tuple(c.clone() if c._is_view() else c for c in out.coeffs)
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, *cots):
+        from ._tensor import PolyTensor
+
+        planes = ctx.saved_tensors
+        mapping, leaves, pos = {}, [], 0
+        for p in ctx.polys:
+            n = p.degree + 1
+            leaf = PolyTensor(tuple(t.detach() for t in planes[pos:pos + n]), requires_grad=True)
+            mapping[id(p)] = leaf
+            leaves.append(leaf)
+            pos += n
+        args = _replace_polys(ctx.args, mapping)
+        kwargs = _replace_polys(ctx.kwargs, mapping)
+        cots = [torch.zeros(shape, dtype=dt, device=planes[0].device) if c is None else c
+                for c, (shape, dt) in zip(cots, ctx.out_meta)]
+        token = _state.coefficient_autograd.set(False)
+        try:
+            with torch.enable_grad(), PolyTensor.retain_wrappers():
+                y = ctx.func(*args, **kwargs)
+                grads = torch.autograd.grad(y, leaves, PolyTensor(tuple(reversed(cots))), allow_unused=True)
+        finally:
+            _state.coefficient_autograd.reset(token)
+        out = []
+        for leaf, g in zip(leaves, grads):
+            n = leaf.degree + 1
+            out.extend([None] * n if g is None else [c.to(t.dtype) for c, t in zip(reversed(g.coeffs), leaf.coeffs)])
+        return (None, None, None, None, *out)
+
+
+def _coefficient_dispatch(func, args, kwargs, polys):
+    from ._tensor import PolyTensor
+
+    token = _state.coefficient_autograd.set(False)
+    try:
+        planes = [c for p in polys for c in p.coeffs]
+        others = []
+        _collect_plain_tensors((args, kwargs), others)
+        if any(t.requires_grad for t in others):
+            raise NotImplementedError("PolyTensor.coefficient_autograd(): ordinary tensors that require grad "
+                                      "cannot be mixed with PolyTensors in this mode")
+        if not (torch.is_grad_enabled() and any(c.requires_grad for c in planes)):
+            with torch.no_grad():
+                return dispatch(func, args, kwargs)
+        schema = getattr(func, "_schema", None)
+        if schema is not None and schema.is_mutable:
+            raise NotImplementedError(f"PolyTensor.coefficient_autograd(): in-place {func} on coefficients "
+                                      "that require grad")
+        outs = _CoefficientMap.apply(func, args, kwargs, polys, *planes)
+        return PolyTensor(tuple(outs), requires_grad=False)
+    finally:
+        _state.coefficient_autograd.reset(token)
+
+
+def _collect_plain_tensors(x, out):
+    if is_poly(x):
+        return
+    if isinstance(x, torch.Tensor):
+        out.append(x)
+    elif isinstance(x, (list, tuple)):
+        for v in x:
+            _collect_plain_tensors(v, out)
+    elif isinstance(x, dict):
+        for v in x.values():
+            _collect_plain_tensors(v, out)
 
 
 # ======================================================================================

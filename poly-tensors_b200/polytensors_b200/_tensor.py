@@ -234,8 +234,10 @@ class PolyTensor(torch.Tensor):
     @classmethod
     @contextlib.contextmanager
     def coefficient_autograd(cls):
-        """Ordinary autograd graphs on the coefficient tensors (reference mode of the same
-        name).  Not implemented by the polykern kernels: operations raise inside it."""
+        """Ordinary autograd graphs on the coefficient tensors (the reference's mode of the same
+        name): make coefficient tensors autograd leaves, build PolyTensors with
+        ``requires_grad=False`` and differentiate output coefficients with ``torch.autograd.grad``.
+        Each kernel-backed operation is one node of that graph (first-order derivatives)."""
         token = _state.coefficient_autograd.set(True)
         try:
             yield
@@ -301,9 +303,15 @@ class PolyTensor(torch.Tensor):
     @classmethod
     def __torch_dispatch__(cls, func, types, args=(), kwargs=None):
         # Coefficients may carry conjugate / negative view bits of their own; restore their
-        # value semantics (and native view tracking) while the rules run below autograd.
+        # value semantics (and native view tracking) while the rules run below autograd.  In
+        # coefficient_autograd() mode the autograd keys are re-enabled as well, so that the
+        # operations on the coefficient tensors record their own graph.
+        keys = [torch._C.DispatchKey.Conjugate, torch._C.DispatchKey.Negative, torch._C.DispatchKey.ADInplaceOrView]
+        if _state.coefficient_autograd.get():
+            keys += [torch._C.DispatchKey.Autograd, torch._C.DispatchKey.AutogradFunctionality,
+                     torch._C.DispatchKey.AutogradOther, torch._C.DispatchKey.AutogradCPU,
+                     torch._C.DispatchKey.AutogradCUDA]
         with contextlib.ExitStack() as stack:
-            for key in (torch._C.DispatchKey.Conjugate, torch._C.DispatchKey.Negative,
-                        torch._C.DispatchKey.ADInplaceOrView):
+            for key in keys:
                 stack.enter_context(torch._C._SetExcludeDispatchKeyGuard(key, False))
             return dispatch(func, args, {} if kwargs is None else kwargs)

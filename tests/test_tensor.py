@@ -142,11 +142,22 @@ def test_context_managers_are_context_local():
     assert not _state.plain_range.get()
 
 
-def test_coefficient_autograd_mode_raises_explicitly():
-    x = PolyTensor((torch.randn(2), torch.randn(2)), degree=1)
+def test_coefficient_autograd_mode_on_shape_operations():
+    """coefficient_autograd(): output coefficients are ordinary tensors with a graph back to the
+    input coefficients (shape operations need no GPU); the coefficient map of a transpose is the
+    per-plane transpose, so d sum(W * y_1) / d x_1 = W^T and d / d x_0 = 0."""
+    c0, c1 = torch.randn(2, 3, requires_grad=True), torch.randn(2, 3, requires_grad=True)
+    x = PolyTensor((c0, c1), requires_grad=False)
+    W = torch.randn(3, 2)
     with PolyTensor.coefficient_autograd():
-        with pytest.raises(NotImplementedError, match="coefficient_autograd"):
-            x.t()
+        y = x.t()
+    assert y.coeffs[1].grad_fn is not None and not y.requires_grad
+    g0, g1 = torch.autograd.grad((y.coeffs[1] * W).sum(), (c0, c1), allow_unused=True)
+    assert torch.equal(g1, W.t())
+    assert g0 is None or torch.equal(g0, torch.zeros_like(c0))
+    other = torch.randn(3, 2, requires_grad=True)
+    with PolyTensor.coefficient_autograd(), pytest.raises(NotImplementedError, match="coefficient_autograd"):
+        torch.mm(x, other)
 
 
 def test_checkpoint_round_trip_stacked_planes(tmp_path):
