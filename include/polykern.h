@@ -201,6 +201,12 @@ enum pk_series_op {
     PK_OP_TANH_BWD = 36,   /* a = gradient, b = output: a * (1 - b^2), src/polytensors/_plain.py:316-320 */
     PK_OP_SIGMOID_BWD = 37 /* a = gradient, b = output: a * b * (1 - b), src/polytensors/_plain.py:321-325 */
 };
+/* float32 planes (numel contiguous elements each, degree + 1 of them) -> bf16 hi/lo pairs
+ * out = [hi_0, lo_0, hi_1, ...] with hi = bf16(x) and lo = bf16(x - hi) (round to nearest): the
+ * operand form read in place by pk_poly_gemm_hilo and the float32 attention kernels.  No
+ * counterpart in the reference (its float32 products are single PyTorch matmuls). */
+PK_API int pk_split_hilo(int degree, int64_t numel, const void* const* x, void* const* out, void* stream);
+
 PK_API int pk_series_map(int op, int dtype, int degree, int ndim, const int64_t* shape,
                          void* const* out, const int64_t* out_strides,
                          const void* const* a, int a_planes, const int64_t* a_strides,
@@ -304,6 +310,17 @@ PK_API int pk_attn_probs(int dtype, int degree, int64_t rows, int64_t cols, int6
 PK_API int pk_attn_dscores(int dtype, int degree, int64_t rows, int64_t cols,
                            const void* const* probs, int64_t p_rs, const void* const* dprobs, int64_t dp_rs,
                            const void* dsum, double scale, void* const* dscores, int64_t ds_rs, void* stream);
+/* float32 forms whose probabilities and score gradients are bf16 hi/lo pairs (2(n+1) planes
+ * hi_0, lo_0, hi_1, ...; x ~= hi + lo), the operand form pk_poly_gemm_hilo reads without staging.
+ * Scores and dprobs stay float32 (n+1 planes).  degree <= 7; outputs must not alias inputs.
+ * They replace the same reference rules as pk_attn_probs / pk_attn_dscores
+ * (src/polytensors/_plain.py:262-273, :342-347). */
+PK_API int pk_attn_probs_hilo(int degree, int64_t rows, int64_t cols, int64_t q_len,
+                              const void* const* scores, int64_t s_rs, double scale, int causal,
+                              int64_t causal_shift, void* const* probs, int64_t p_rs, void* stats, void* stream);
+PK_API int pk_attn_dscores_hilo(int degree, int64_t rows, int64_t cols,
+                                const void* const* probs, int64_t p_rs, const void* const* dprobs, int64_t dp_rs,
+                                const void* dsum, double scale, void* const* dscores, int64_t ds_rs, void* stream);
 
 /*
  * Series flash attention forward in one kernel: O = softmax(scale * Q K^T, causal) V with

@@ -336,11 +336,78 @@ static int grid_for(int64_t work, int per_block = 256) {
     return static_cast<int>(std::min<int64_t>(blocks, static_cast<int64_t>(num_sms()) * 16));
 }
 
+// float32 planes -> bf16 hi/lo pairs (hi = bf16(x), lo = bf16(x - hi)), the operand form of the
+// float32 tensor-core products: one read of x and one write of each pair, four elements per
+// thread and step; blockIdx.y selects the plane.
+struct SplitParams {
+    int64_t numel;
+    const float* x[PK_MAX_PLANES];
+    __nv_bfloat16* out[2 * PK_MAX_PLANES];
+    int vec;
+};
+
+__global__ void __launch_bounds__(256) split_hilo_kernel(const SplitParams p) {
+    const int k = blockIdx.y;
+    const float* x = p.x[k];
+    __nv_bfloat16* hi = p.out[2 * k];
+    __nv_bfloat16* lo = p.out[2 * k + 1];
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * ROW_VEC;
+    for (int64_t off = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * ROW_VEC; off < p.numel;
+         off += stride) {
+        const int valid = vec_count(p.numel, off);
+        float v[4] = {0.f, 0.f, 0.f, 0.f}, h[4], l[4];
+        if (p.vec && valid == ROW_VEC) load_vec4<float>(x + off, v);
+        else
+            for (int u = 0; u < valid; ++u) v[u] = x[off + u];
+#pragma unroll
+        for (int u = 0; u < ROW_VEC; ++u) {
+            h[u] = __bfloat162float(__float2bfloat16_rn(v[u]));
+            l[u] = v[u] - h[u];
+        }
+        if (p.vec && valid == ROW_VEC) {
+            store_vec4<__nv_bfloat16>(hi + off, h);
+            store_vec4<__nv_bfloat16>(lo + off, l);
+        } else {
+            for (int u = 0; u < valid; ++u) {
+                hi[off + u] = __float2bfloat16_rn(h[u]);
+                lo[off + u] = __float2bfloat16_rn(l[u]);
+            }
+        }
+    }
+}
+
 }  // namespace pk
 
 using namespace pk;
 
 extern "C" {
+
+int pk_split_hilo(int degree, int64_t numel, const void* const* x, void* const* out, void* stream) {
+    if (degree < 0 || degree >= PK_MAX_PLANES) return fail(PK_ERR_UNSUPPORTED, "pk_split_hilo: degree out of range");
+    if (numel < 0 || !x || !out) return fail(PK_ERR_ARG, "pk_split_hilo: bad arguments");
+    if (numel == 0) return PK_OK;
+    SplitParams p{};
+    p.numel = numel;
+    bool vec = true;
+    for (int k = 0; k <= degree; ++k) {
+        p.x[k] = static_cast<const float*>(x[k]);
+        p.out[2 * k] = static_cast<__nv_bfloat16*>(out[2 * k]);
+        p.out[2 * k + 1] = static_cast<__nv_bfloat16*>(out[2 * k + 1]);
+        if (!p.x[k] || !p.out[2 * k] || !p.out[2 * k + 1]) return fail(PK_ERR_ARG, "pk_split_hilo: null plane");
+        vec = vec && reinterpret_cast<uintptr_t>(p.x[k]) % 16 == 0 && reinterpret_cast<uintptr_t>(p.out[2 * k]) % 8 == 0 &&
+              reinterpret_cast<uintptr_t>(p.out[2 * k + 1]) % 8 == 0;
+    }
+    p.vec = vec ? 1 : 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t blocks = ceil_div(numel, 256 * ROW_VEC);
+    const int gx = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(num_sms()) * 8)));
+    void* tok;
+    prof_begin("split_hilo", s, &tok);
+    PK_LAUNCHED(split_hilo_kernel<<<dim3(gx, degree + 1), 256, 0, s>>>(p));
+    prof_end("split_hilo", s, tok);
+    PK_CHECK_LAUNCH("pk_split_hilo");
+    return PK_OK;
+}
 
 int pk_series_map(int op, int dtype, int degree, int ndim, const int64_t* shape, void* const* out,
                   const int64_t* out_strides, const void* const* a, int a_planes, const int64_t* a_strides,

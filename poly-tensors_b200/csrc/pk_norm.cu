@@ -169,7 +169,18 @@ __global__ void __launch_bounds__(512, 1) rmsnorm_fwd_reg_kernel(const NormParam
 }
 
 // Rows beyond the next one that the streaming kernels prefetch into L2.
-constexpr int NORM_L2_AHEAD = 2;
+// Rows bulk-prefetched into L2 beyond the one streaming into shared memory.  Measured at 16384 x
+// 4096 float32 rows (degree 4 / degree 1): forward 0.56 / 0.20 ms with 2 rows, 0.40 / 0.18 with 1,
+// 0.45 / 0.18 with none; backward 0.78 / 0.31 ms with 1 or 2 rows, 0.72 / 0.29 with none (deeper
+// prefetch competes with the rows being read for HBM and L2 capacity).
+#ifndef PK_NORM_FWD_L2_AHEAD
+#define PK_NORM_FWD_L2_AHEAD 1
+#endif
+#ifndef PK_NORM_BWD_L2_AHEAD
+#define PK_NORM_BWD_L2_AHEAD 0
+#endif
+constexpr int NORM_FWD_L2_AHEAD = PK_NORM_FWD_L2_AHEAD;
+constexpr int NORM_BWD_L2_AHEAD = PK_NORM_BWD_L2_AHEAD;
 
 // The forward with the next row streaming in while this one is computed: thread t owns the column
 // quads q = s * blockDim + t (s < STEPS) and copies its quads of the NEXT row's x planes into the
@@ -214,18 +225,18 @@ __global__ void __launch_bounds__(512, 1) rmsnorm_fwd_stream_kernel(const NormPa
     int64_t row = blockIdx.x;
     if (row < p.rows) issue(row, 0);
 #pragma unroll
-    for (int a = 1; a <= NORM_L2_AHEAD; ++a) prefetch(row + static_cast<int64_t>(a) * gridDim.x);
+    for (int a = 1; a <= NORM_FWD_L2_AHEAD; ++a) prefetch(row + static_cast<int64_t>(a) * gridDim.x);
     for (int64_t i = 0; row < p.rows; ++i, row += gridDim.x) {
         const int stage = static_cast<int>(i & 1);
         const int64_t nrow = row + gridDim.x;
-        prefetch(row + static_cast<int64_t>(NORM_L2_AHEAD + 1) * gridDim.x);
+        if (NORM_FWD_L2_AHEAD > 0) prefetch(row + static_cast<int64_t>(NORM_FWD_L2_AHEAD + 1) * gridDim.x);
         if (nrow < p.rows) issue(nrow, stage ^ 1);
         else cp_async_commit();  // an empty group keeps the wait count below uniform
         cp_async_wait<1>();      // this thread's copies of `row` have landed
         const T* const xs = stages + stage * stage_elems;
-        C acc[NP];
+        C acc[NP], diag[NP];
 #pragma unroll
-        for (int k = 0; k < NP; ++k) acc[k] = C(0);
+        for (int k = 0; k < NP; ++k) acc[k] = diag[k] = C(0);
 #pragma unroll
         for (int s = 0; s < STEPS; ++s) {
             const int64_t q = static_cast<int64_t>(s) * blockDim.x + threadIdx.x;
@@ -235,14 +246,14 @@ __global__ void __launch_bounds__(512, 1) rmsnorm_fwd_stream_kernel(const NormPa
             for (int k = 0; k < NP; ++k) load_vec4<T>(xs + k * p.cols + q * ROW_VEC, xv[k]);
 #pragma unroll
             for (int u = 0; u < ROW_VEC; ++u) {
-                C x[NP], sq[NP];
+                C x[NP];
 #pragma unroll
                 for (int k = 0; k < NP; ++k) x[k] = xv[k][u];
-                s_mul<NP, C>(x, x, sq);
-#pragma unroll
-                for (int k = 0; k < NP; ++k) acc[k] += sq[k];
+                s_square_acc<NP, C>(x, acc, diag);
             }
         }
+#pragma unroll
+        for (int k = 0; k < NP; ++k) acc[k] = C(2) * acc[k] + diag[k];
         block_sum<NP, C>(acc, scratch);
         C m[NP], r[NP];
 #pragma unroll
@@ -577,12 +588,12 @@ __global__ void __launch_bounds__(STEPS == 1 ? 512 : 256, 1) rmsnorm_bwd_stream_
         load_r(row, rn);
     }
 #pragma unroll
-    for (int a = 1; a <= NORM_L2_AHEAD; ++a) prefetch(row + a * n_clusters);
+    for (int a = 1; a <= NORM_BWD_L2_AHEAD; ++a) prefetch(row + a * n_clusters);
     int par = 0;
     for (int64_t i = 0; row < p.rows; ++i, row += n_clusters, par ^= 1) {
         const int stage = static_cast<int>(i & 1);
         const int64_t nrow = row + n_clusters;
-        prefetch(row + (NORM_L2_AHEAD + 1) * n_clusters);
+        if (NORM_BWD_L2_AHEAD > 0) prefetch(row + (NORM_BWD_L2_AHEAD + 1) * n_clusters);
         if (nrow < p.rows) issue(nrow, stage ^ 1);
         else cp_async_commit();  // an empty group keeps the wait count below uniform
         C r[NP];
@@ -608,28 +619,23 @@ __global__ void __launch_bounds__(STEPS == 1 ? 512 : 256, 1) rmsnorm_bwd_stream_
             }
 #pragma unroll
             for (int u = 0; u < ROW_VEC; ++u) {
-                C x[NP], g[NP], gx[NP], t[NP];
+                C x[NP], g[NP], rg[NP], a[NP];
 #pragma unroll
                 for (int k = 0; k < NP; ++k) {
                     x[k] = xv[k][u];
                     g[k] = gv[k][u];
                 }
-                // gx = g (*) x feeds the weight gradient (gx (*) r) and the row sum
-                // (gy (*) x = w (*) gx) with gy = g (*) w
-                s_mul<NP, C>(g, x, gx);
-                if (want_dw) {
-                    s_mul<NP, C>(gx, r, t);
-#pragma unroll
-                    for (int k = 0; k < NP; ++k) dwa[s][u][k] += t[k];
-                }
-                s_mul<NP, C>(w[s][u], gx, t);
-#pragma unroll
-                for (int k = 0; k < NP; ++k) d[k] += t[k];
+                // rg = r (*) g feeds the weight gradient (rg (*) x) and a = rg (*) w, the first
+                // term of dx; the row sum is accumulated as a (*) x = r (*) (gy (*) x), gy = g (*) w
+                // (r is constant along the row, so the row total is r (*) d and the coefficient
+                // below takes r (*) r instead of r^3)
+                s_mul<NP, C>(r, g, rg);
+                if (want_dw) s_mul_acc<NP, C>(rg, x, dwa[s][u]);
+                s_mul<NP, C>(rg, w[s][u], a);
+                s_mul_acc<NP, C>(a, x, d);
                 if constexpr (sizeof(T) == 4) {
-                    s_mul<NP, C>(g, w[s][u], t);
-                    s_mul<NP, C>(r, t, t);
 #pragma unroll
-                    for (int k = 0; k < NP; ++k) gv[k][u] = t[k];  // g of element u is no longer needed
+                    for (int k = 0; k < NP; ++k) gv[k][u] = a[k];  // g of element u is no longer needed
                 }
             }
             if constexpr (sizeof(T) == 4) {
@@ -659,9 +665,9 @@ __global__ void __launch_bounds__(STEPS == 1 ? 512 : 256, 1) rmsnorm_bwd_stream_
             for (int j = 1; j < CL; ++j) t += j == h ? d[k] : xslot[par][j][k];
             d[k] = t;
         }
+        // d holds r (*) sum gy (*) x here, so coef = r^3 (*) sum gy (*) x / cols = r (*) r (*) d / cols
         C coef[NP];
         s_mul<NP, C>(r, r, coef);
-        s_mul<NP, C>(coef, r, coef);
         s_mul<NP, C>(coef, d, coef);
 #pragma unroll
         for (int k = 0; k < NP; ++k) coef[k] *= inv_cols;
@@ -679,19 +685,18 @@ __global__ void __launch_bounds__(STEPS == 1 ? 512 : 256, 1) rmsnorm_bwd_stream_
             C out[ROW_VEC][NP];
 #pragma unroll
             for (int u = 0; u < ROW_VEC; ++u) {
-                C x[NP], a[NP], b[NP];
+                C x[NP], a[NP];
 #pragma unroll
                 for (int k = 0; k < NP; ++k) {
                     x[k] = xv[k][u];
                     a[k] = av[k][u];
                 }
                 if constexpr (sizeof(T) != 4) {
-                    s_mul<NP, C>(a, w[s][u], a);  // the stage holds g: a = r (*) g (*) w
-                    s_mul<NP, C>(r, a, a);
+                    C rg[NP];
+                    s_mul<NP, C>(r, a, rg);  // the stage holds g: a = r (*) g (*) w
+                    s_mul<NP, C>(rg, w[s][u], a);
                 }
-                s_mul<NP, C>(coef, x, b);
-#pragma unroll
-                for (int k = 0; k < NP; ++k) out[u][k] = a[k] - b[k];
+                s_sub_mul<NP, C>(a, coef, x, out[u]);
             }
             store_planes4<NP, T, C>(p.y, NP, yb + q * ROW_VEC, ROW_VEC, true, out);
         }
@@ -756,6 +761,15 @@ static int reduce_dw(const NormParams& p, void* const* dw, int parts, cudaStream
     return PK_OK;
 }
 
+// Tuning of the streaming backward: the cluster size tried first, and the half-row width (in
+// column quads) from which a thread takes two quads per row.
+#ifndef PK_NORM_BWD_CL
+#define PK_NORM_BWD_CL 2
+#endif
+#ifndef PK_NORM_BWD_STEP2_QUADS
+#define PK_NORM_BWD_STEP2_QUADS 256
+#endif
+
 // The streaming backward (rmsnorm_bwd_stream_kernel) for rows that split into CL-CTA clusters of
 // at most 512 threads x 4 columns with two stages of x and g in shared memory.  Returns 1 when the
 // shape does not suit it (the caller uses another kernel), else a status.
@@ -767,7 +781,7 @@ static int bwd_stream(NormParams& p, void* const* dw, void* ws, size_t ws_bytes,
     if (quads < 64 || quads > 512 || smem > 200 * 1024) return 1;
     // two column quads per thread once a half row has 256 of them: the per-row work (block
     // reduction, exchange, rsqrt-series coefficients) is shared by twice the elements
-    const int steps = quads >= 256 ? 2 : 1;
+    const int steps = quads >= PK_NORM_BWD_STEP2_QUADS ? 2 : 1;
     const int threads = static_cast<int>(round_up(ceil_div(quads, steps), 32));
     auto kern = steps == 2 ? rmsnorm_bwd_stream_kernel<T, NP, 2, CL> : rmsnorm_bwd_stream_kernel<T, NP, 1, CL>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -900,7 +914,8 @@ static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, siz
         // next rows streamed into shared memory: half rows over 2-CTA clusters, quarter rows
         // over 4-CTA clusters for rows too long for a pair (a 4-CTA split of 4096-column rows
         // measured slower: 3.4 against 4.0 TB/s)
-        int st = bwd_stream<T, NP, 2>(p, dw, ws, ws_bytes, s);
+        int st = bwd_stream<T, NP, PK_NORM_BWD_CL>(p, dw, ws, ws_bytes, s);
+        if (st == 1) st = bwd_stream<T, NP, 2>(p, dw, ws, ws_bytes, s);
         if (st == 1) st = bwd_stream<T, NP, 4>(p, dw, ws, ws_bytes, s);
         if (st != 1) return st;
     }

@@ -225,6 +225,64 @@ __device__ __forceinline__ void store_planes4(void* const* planes, int np, int64
     }
 }
 
+// float32 values written as bf16 hi/lo pairs: planes[2k] = hi_k = bf16(y_k), planes[2k + 1] =
+// lo_k = bf16(y_k - hi_k), so that y_k ~= hi_k + lo_k to about 2^-16 relative (the split the
+// float32 tensor-core products read; the same rounding as the operand staging).
+template <int NP>
+__device__ __forceinline__ void store_planes4_hilo(void* const* planes, int np, int64_t off, int valid, bool vec,
+                                                   const float (&y)[ROW_VEC][NP]) {
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+        if (k >= np) continue;
+        __nv_bfloat16* hi = static_cast<__nv_bfloat16*>(planes[2 * k]) + off;
+        __nv_bfloat16* lo = static_cast<__nv_bfloat16*>(planes[2 * k + 1]) + off;
+        float h[4], l[4];
+#pragma unroll
+        for (int u = 0; u < ROW_VEC; ++u) {
+            h[u] = __bfloat162float(__float2bfloat16_rn(y[u][k]));
+            l[u] = y[u][k] - h[u];
+        }
+        if (vec && valid == ROW_VEC) {
+            store_vec4<__nv_bfloat16>(hi, h);
+            store_vec4<__nv_bfloat16>(lo, l);
+        } else {
+#pragma unroll
+            for (int u = 0; u < ROW_VEC; ++u)
+                if (u < valid) {
+                    hi[u] = __float2bfloat16_rn(h[u]);
+                    lo[u] = __float2bfloat16_rn(l[u]);
+                }
+        }
+    }
+}
+
+// bf16 hi/lo pairs (planes[2k], planes[2k + 1]) read back as float32 hi + lo.
+template <int NP>
+__device__ __forceinline__ void load_planes4_hilo(const void* const* planes, int np, int64_t off, int valid, bool vec,
+                                                  float (&x)[ROW_VEC][NP]) {
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+        float h[4] = {0.f, 0.f, 0.f, 0.f}, l[4] = {0.f, 0.f, 0.f, 0.f};
+        if (k < np) {
+            const __nv_bfloat16* hi = static_cast<const __nv_bfloat16*>(planes[2 * k]) + off;
+            const __nv_bfloat16* lo = static_cast<const __nv_bfloat16*>(planes[2 * k + 1]) + off;
+            if (vec && valid == ROW_VEC) {
+                load_vec4<__nv_bfloat16>(hi, h);
+                load_vec4<__nv_bfloat16>(lo, l);
+            } else {
+#pragma unroll
+                for (int u = 0; u < ROW_VEC; ++u)
+                    if (u < valid) {
+                        h[u] = __bfloat162float(hi[u]);
+                        l[u] = __bfloat162float(lo[u]);
+                    }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < ROW_VEC; ++u) x[u][k] = h[u] + l[u];
+    }
+}
+
 // Whether planes (base pointers) and a row stride allow ROW_VEC-element vector access.
 inline bool row_vec_ok(const void* const* planes, int np, int64_t row_stride, int elem_bytes) {
     const uintptr_t align = static_cast<uintptr_t>(ROW_VEC) * elem_bytes;

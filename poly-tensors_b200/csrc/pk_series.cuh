@@ -58,6 +58,44 @@ __device__ __forceinline__ void s_mul(const C (&a)[NP], const C (&b)[NP], C (&ou
     for (int k = 0; k < NP; ++k) out[k] = r[k];
 }
 
+// acc += a (*) b (one multiply-add per term; acc must not alias a or b)
+template <int NP, typename C>
+__device__ __forceinline__ void s_mul_acc(const C (&a)[NP], const C (&b)[NP], C (&acc)[NP]) {
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+#pragma unroll
+        for (int i = 0; i <= k; ++i) acc[k] += a[i] * b[k - i];
+    }
+}
+
+// out = base - a (*) b
+template <int NP, typename C>
+__device__ __forceinline__ void s_sub_mul(const C (&base)[NP], const C (&a)[NP], const C (&b)[NP], C (&out)[NP]) {
+    C r[NP];
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+        C acc = base[k];
+#pragma unroll
+        for (int i = 0; i <= k; ++i) acc -= a[i] * b[k - i];
+        r[k] = acc;
+    }
+#pragma unroll
+    for (int k = 0; k < NP; ++k) out[k] = r[k];
+}
+
+// Sum of squares accumulated in two halves: cross += sum over i < k - i of x_i x_{k-i}, diag +=
+// x_{k/2}^2 for even k, so that x (*) x = 2 cross + diag takes about half the multiply-adds of a
+// general product (the factor 2 is applied once, after the accumulation).
+template <int NP, typename C>
+__device__ __forceinline__ void s_square_acc(const C (&x)[NP], C (&cross)[NP], C (&diag)[NP]) {
+#pragma unroll
+    for (int k = 0; k < NP; ++k) {
+#pragma unroll
+        for (int i = 0; 2 * i < k; ++i) cross[k] += x[i] * x[k - i];
+        if (k % 2 == 0) diag[k] += x[k / 2] * x[k / 2];
+    }
+}
+
 // out = a / b (quotient recurrence, src/polytensors/_range_ops.py:86-93)
 template <int NP, typename C>
 __device__ __forceinline__ void s_div(const C (&a)[NP], const C (&b)[NP], C (&out)[NP]) {

@@ -13,6 +13,7 @@
 // element (src/polytensors/_plain.py:348-354 after the NLL scatter of
 // src/polytensors/_dispatch.py:556-562), optionally through a softcap z -> c tanh(z/c)
 // (src/polytensors/_cross_entropy_kernels.py:7-17, generalised to any degree).
+#include <type_traits>
 #include <algorithm>
 
 #include "pk_rows.cuh"
@@ -242,7 +243,9 @@ __global__ void __launch_bounds__(512) ce_bwd_kernel(const SoftmaxParams p) {
 
 // Attention probabilities from raw score series x = Q K^T (all planes):  P = softmax(scale * x)
 // along keys with causal masking, written as series; stats receive (lse_0, logz_1..n) per row.
-template <typename T, int NP>
+// HILO (float32 scores only): P is written as bf16 hi/lo pairs (2 np output planes), the operand
+// form of the float32 tensor-core products that consume it.
+template <typename T, int NP, bool HILO = false>
 __global__ void __launch_bounds__(512) attn_probs_kernel(const SoftmaxParams p) {
     using C = typename Compute<T>::type;
     __shared__ C scratch[16 * (NP + 1)];
@@ -280,7 +283,8 @@ __global__ void __launch_bounds__(512) attn_probs_kernel(const SoftmaxParams p) 
                     for (int k = 0; k < NP; ++k) x[u][k] = C(0);
                 }
             }
-            store_planes4<NP, T, C>(p.out, p.np, yb + c0, valid, p.vec != 0, x);
+            if constexpr (HILO) store_planes4_hilo<NP>(p.out, p.np, yb + c0, valid, p.vec != 0, x);
+            else store_planes4<NP, T, C>(p.out, p.np, yb + c0, valid, p.vec != 0, x);
         }
     }
 }
@@ -289,8 +293,9 @@ __global__ void __launch_bounds__(512) attn_probs_kernel(const SoftmaxParams p) 
 // (src/polytensors/_plain.py:342-347) through the score scaling:
 //   d scores = scale * P (*) (dP - dsum_row),   dsum_row = sum_d dO (*) O.
 // P arrives in p.y, dP in p.g, the output goes to p.out (may alias p.g); masked entries
-// have P = 0 and so get a zero gradient.
-template <typename T, int NP>
+// have P = 0 and so get a zero gradient.  HILO (float32 only): P arrives and the output leaves as
+// bf16 hi/lo pairs (2 np planes each); dP stays float32.
+template <typename T, int NP, bool HILO = false>
 __global__ void __launch_bounds__(256) attn_dscores_kernel(const SoftmaxParams p) {
     using C = typename Compute<T>::type;
     const C sc = C(p.scale);
@@ -303,7 +308,8 @@ __global__ void __launch_bounds__(256) attn_dscores_kernel(const SoftmaxParams p
              c0 += static_cast<int64_t>(blockDim.x) * ROW_VEC) {
             const int valid = vec_count(p.cols, c0);
             C P[ROW_VEC][NP], g[ROW_VEC][NP], r[ROW_VEC][NP];
-            load_planes4<NP, T, C>(p.y, p.np, yb + c0, valid, p.vec != 0, P);
+            if constexpr (HILO) load_planes4_hilo<NP>(p.y, p.np, yb + c0, valid, p.vec != 0, P);
+            else load_planes4<NP, T, C>(p.y, p.np, yb + c0, valid, p.vec != 0, P);
             load_planes4<NP, T, C>(p.g, p.np, gb + c0, valid, p.vec != 0, g);
 #pragma unroll
             for (int u = 0; u < ROW_VEC; ++u) {
@@ -313,12 +319,13 @@ __global__ void __launch_bounds__(256) attn_dscores_kernel(const SoftmaxParams p
 #pragma unroll
                 for (int k = 0; k < NP; ++k) r[u][k] *= sc;
             }
-            store_planes4<NP, T, C>(p.out, p.np, ob + c0, valid, p.vec != 0, r);
+            if constexpr (HILO) store_planes4_hilo<NP>(p.out, p.np, ob + c0, valid, p.vec != 0, r);
+            else store_planes4<NP, T, C>(p.out, p.np, ob + c0, valid, p.vec != 0, r);
         }
     }
 }
 
-enum { SM_FWD = 0, SM_BWD = 1, CE_FWD = 2, CE_BWD = 3, ATTN_P = 4, ATTN_DS = 5 };
+enum { SM_FWD = 0, SM_BWD = 1, CE_FWD = 2, CE_BWD = 3, ATTN_P = 4, ATTN_DS = 5, ATTN_P_HILO = 6, ATTN_DS_HILO = 7 };
 
 static int row_threads(int64_t cols) { return cols >= 4096 ? 512 : (cols >= 1024 ? 256 : 128); }
 
@@ -332,6 +339,14 @@ static void launch_rows(int which, const SoftmaxParams& p, cudaStream_t s) {
         case CE_FWD: PK_LAUNCHED(ce_fwd_kernel<T, NP><<<grid, threads, 0, s>>>(p)); break;
         case ATTN_P: PK_LAUNCHED(attn_probs_kernel<T, NP><<<grid, threads, 0, s>>>(p)); break;
         case ATTN_DS: PK_LAUNCHED(attn_dscores_kernel<T, NP><<<grid, std::min(threads, 256), 0, s>>>(p)); break;
+        case ATTN_P_HILO:
+            if constexpr (std::is_same<T, float>::value)
+                PK_LAUNCHED(attn_probs_kernel<T, NP, true><<<grid, threads, 0, s>>>(p));
+            break;
+        case ATTN_DS_HILO:
+            if constexpr (std::is_same<T, float>::value)
+                PK_LAUNCHED(attn_dscores_kernel<T, NP, true><<<grid, std::min(threads, 256), 0, s>>>(p));
+            break;
         default: PK_LAUNCHED(ce_bwd_kernel<T, NP><<<grid, threads, 0, s>>>(p)); break;
     }
 }
@@ -359,9 +374,12 @@ static int dispatch_rows(int which, int dtype, SoftmaxParams& p, void* stream, c
         bool ok = p.cols % ROW_VEC == 0;
         const void* const* sets[4] = {p.x, p.y, p.g, reinterpret_cast<const void* const*>(p.out)};
         const int64_t strides[4] = {p.x_rs, p.y_rs, p.g_rs, 0};
+        // hi/lo kinds: the probabilities (y, for the score gradient) and the output are 2 np bf16 planes
+        const bool hilo = which == ATTN_P_HILO || which == ATTN_DS_HILO;
+        const bool split_set[4] = {false, hilo, false, hilo};
         for (int i = 0; i < 4 && ok; ++i) {
             if (!sets[i][0]) continue;
-            ok = row_vec_ok(sets[i], p.np, strides[i], eb);
+            ok = split_set[i] ? row_vec_ok(sets[i], 2 * p.np, strides[i], 2) : row_vec_ok(sets[i], p.np, strides[i], eb);
         }
         // output planes share the row stride of their input role (x_rs or y_rs)
         ok = ok && p.x_rs % ROW_VEC == 0 && p.y_rs % ROW_VEC == 0 && p.g_rs % ROW_VEC == 0;
@@ -518,6 +536,51 @@ int pk_attn_dscores(int dtype, int degree, int64_t rows, int64_t cols, const voi
         p.out[k] = dscores[k];
     }
     return dispatch_rows(ATTN_DS, dtype, p, stream, "attn_dscores");
+}
+
+int pk_attn_probs_hilo(int degree, int64_t rows, int64_t cols, int64_t q_len, const void* const* scores, int64_t s_rs,
+                       double scale, int causal, int64_t causal_shift, void* const* probs, int64_t p_rs, void* stats,
+                       void* stream) {
+    if (int rc = check_common(degree, rows, cols, "pk_attn_probs_hilo")) return rc;
+    if (2 * (degree + 1) > PK_MAX_PLANES) return fail(PK_ERR_UNSUPPORTED, "pk_attn_probs_hilo: degree > 7");
+    if (!stats || q_len <= 0) return fail(PK_ERR_ARG, "pk_attn_probs_hilo: null stats or bad q_len");
+    SoftmaxParams p{};
+    p.np = degree + 1;
+    p.rows = rows;
+    p.cols = cols;
+    p.x_rs = s_rs;
+    p.y_rs = p_rs;
+    p.scale = scale;
+    p.causal = causal;
+    p.q_len = q_len;
+    p.causal_shift = causal_shift;
+    p.stats = stats;
+    for (int k = 0; k < p.np; ++k) p.x[k] = scores[k];
+    for (int k = 0; k < 2 * p.np; ++k) p.out[k] = probs[k];
+    return dispatch_rows(ATTN_P_HILO, PK_F32, p, stream, "attn_probs");
+}
+
+int pk_attn_dscores_hilo(int degree, int64_t rows, int64_t cols, const void* const* probs, int64_t p_rs,
+                         const void* const* dprobs, int64_t dp_rs, const void* dsum, double scale,
+                         void* const* dscores, int64_t ds_rs, void* stream) {
+    if (int rc = check_common(degree, rows, cols, "pk_attn_dscores_hilo")) return rc;
+    if (2 * (degree + 1) > PK_MAX_PLANES) return fail(PK_ERR_UNSUPPORTED, "pk_attn_dscores_hilo: degree > 7");
+    if (!dsum) return fail(PK_ERR_ARG, "pk_attn_dscores_hilo: null dsum");
+    SoftmaxParams p{};
+    p.np = degree + 1;
+    p.rows = rows;
+    p.cols = cols;
+    p.y_rs = p_rs;
+    p.g_rs = dp_rs;
+    p.x_rs = ds_rs;
+    p.scale = scale;
+    p.dsum = dsum;
+    for (int k = 0; k < p.np; ++k) p.g[k] = dprobs[k];
+    for (int k = 0; k < 2 * p.np; ++k) {
+        p.y[k] = probs[k];
+        p.out[k] = dscores[k];
+    }
+    return dispatch_rows(ATTN_DS_HILO, PK_F32, p, stream, "attn_dscores");
 }
 
 }  // extern "C"

@@ -18,9 +18,11 @@ P is recomputed in backward from the saved inputs; only the per-row normaliser s
 single-kernel forward (pk_flash_attn_fwd) and a backward over all queries of a block of heads
 with the softmax in the score products' epilogue (pk_attn_probs_gemm / pk_attn_dscores_gemm)
 and banded gradient products (pk_poly_gemm_banded).  Other dtypes tile the queries under a causal
-mask, so that their row-wise softmax passes and operand staging skip the masked half; float32
+mask, so that their row-wise softmax passes and products skip the masked half; float32
 planes with head dimension 64 (degree <= 3) run the same single-kernel forward and score-epilogue
-backward on bf16 hi/lo plane pairs (products as hi*hi + hi*lo + lo*hi, fp32 accumulation).
+backward on bf16 hi/lo plane pairs (products as hi*hi + hi*lo + lo*hi, fp32 accumulation); other
+float32 shapes tile the queries with Q, K, V, dO split once into hi/lo pairs and probabilities and
+score gradients written as pairs by the row kernels, so every product reads its operands in place.
 """
 
 import math
@@ -178,6 +180,8 @@ def forward_planes(Q, Kp, V, causal, scale, stats=None):
         return flash_forward(Q, Kp, V, causal, scale, stats)
     if f32_split_eligible(Q, Kp, V):
         return _flash_f32(Q, Kp, V, causal, scale, stats)
+    if tiled_f32_eligible(Q, Kp, V):
+        return _forward_f32_tiled(Q, Kp, V, causal, scale, stats)
     BH, L, _ = Q[0].shape
     S = Kp[0].shape[1]
     hb = _block_heads(L, S, len(Q), Q[0].element_size(), BH)
@@ -295,6 +299,113 @@ def _fused_backward_f32(Q, Kp, V, dO, dsum, stats, causal, scale, dQ, dK, dV):
             K.poly_matmul_hilo(dSt, True, [q[hs] for q in Qh], True, out=[t[hs] for t in dK], band=lower)
 
 
+def tiled_f32_eligible(Q, Kp, V):
+    """Whether float32 attention outside the split kernels (head dimension other than 64, degree
+    up to 7) runs on hi/lo operands: Q, K, V (and dO) split once into bf16 pairs, probabilities and
+    score gradients written as pairs by the row kernels (pk_attn_probs_hilo /
+    pk_attn_dscores_hilo), every product reading its operands in place (pk_poly_gemm_hilo), so no
+    score tile is staged again.  Head dimensions must keep 16-byte row pitches for the pairs."""
+    return (Q[0].dtype == torch.float32 and len(Q) <= 8 and Q[0].shape[-1] % 8 == 0
+            and Kp[0].shape[-1] % 8 == 0 and V[0].shape[-1] % 8 == 0)
+
+
+def _tile_heads(tiles, n_planes, heads):
+    """Heads per block for the tiled float32 path: a query tile holds float32 scores (reused for
+    dP) and two hi/lo pair sets (probabilities, score gradient), 12 bytes per score per plane."""
+    per_head = 12 * n_planes * max((q1 - q0) * kend for q0, q1, kend in tiles)
+    return max(1, min(heads, _BLOCK_BYTES // max(per_head, 1)))
+
+
+def _hilo_scores(hb, rows, cols, n_planes, device):
+    """2 n_planes bf16 planes (hb, rows, cols) with rows padded to a multiple of 8 columns (16-byte
+    pitches for the products that read them in place)."""
+    cp = -(-cols // 8) * 8
+    return [torch.empty(hb, rows, cp, dtype=torch.bfloat16, device=device)[..., :cols] for _ in range(2 * n_planes)]
+
+
+def _probs_hilo(Sc, Pr, q_len, scale, causal, shift):
+    """float32 scores -> probabilities as hi/lo pairs (pk_attn_probs_hilo); returns the row statistics."""
+    hb, Lq, S = Sc[0].shape
+    rows = hb * Lq
+    stats = torch.empty(rows, len(Sc), dtype=torch.float32, device=Sc[0].device)
+    ps, k1 = _lib.pointer_array(Sc)
+    pp, k2 = _lib.pointer_array(Pr)
+    status = _lib.load().pk_attn_probs_hilo(len(Sc) - 1, rows, S, q_len, ps, Sc[0].stride(1), float(scale),
+                                            1 if causal else 0, shift, pp, Pr[0].stride(1), stats.data_ptr(),
+                                            K._stream(Sc[0].device))
+    _lib.check(status, "pk_attn_probs_hilo")
+    return stats
+
+
+def _forward_f32_tiled(Q, Kp, V, causal, scale, stats=None):
+    """float32 forward per block of heads and causal query tile on hi/lo operands: scores
+    Q Kᵀ (float32), probabilities as hi/lo pairs, O = P V banded to the admissible keys."""
+    BH, L, _ = Q[0].shape
+    S = Kp[0].shape[1]
+    NP = len(Q)
+    Qh, Kh, Vh = (K.split_hilo(X) for X in (Q, Kp, V))
+    tiles = _query_tiles(L, S, causal)
+    hb = _tile_heads(tiles, NP, BH)
+    outs = [torch.empty(BH, L, V[0].shape[2], dtype=torch.float32, device=Q[0].device) for _ in Q]
+    for h0 in range(0, BH, hb):
+        hs = slice(h0, min(BH, h0 + hb))
+        for q0, q1, kend in tiles:
+            qs = slice(q0, q1)
+            Sc = K.poly_matmul_hilo([q[hs, qs] for q in Qh], True, [k[hs, :kend].transpose(1, 2) for k in Kh], True)
+            Pr = _hilo_scores(hs.stop - hs.start, q1 - q0, kend, NP, Q[0].device)
+            st = _probs_hilo(Sc, Pr, q1 - q0, scale, causal, q0)
+            del Sc
+            if stats is not None:
+                stats[hs, qs].copy_(st.view(hs.stop - hs.start, q1 - q0, -1))
+            K.poly_matmul_hilo(Pr, True, [v[hs, :kend] for v in Vh], True, out=[o[hs, qs] for o in outs],
+                               band=2 if causal else 0, band_offset=q0 if causal else 0)
+    return outs
+
+
+def _backward_f32_tiled(Q, Kp, V, dO, dsum, causal, scale, dQ, dK, dV):
+    """float32 backward per block of heads and causal query tile on hi/lo operands: probabilities
+    recomputed as hi/lo pairs, dP = dO Vᵀ (float32), the score gradient as hi/lo pairs, and the
+    three gradient products banded to the admissible keys."""
+    BH, L, _ = Q[0].shape
+    S = Kp[0].shape[1]
+    NP = len(Q)
+    Qh, Kh, Vh, dOh = (K.split_hilo(X) for X in (Q, Kp, V, dO))
+    tiles = _query_tiles(L, S, causal)
+    hb = _tile_heads(tiles, NP, BH)
+    for h0 in range(0, BH, hb):
+        hs = slice(h0, min(BH, h0 + hb))
+        hbn = hs.stop - hs.start
+        for t in (dK or []) + (dV or []):
+            t[hs].zero_()
+        for q0, q1, kend in tiles:
+            qs, ks = slice(q0, q1), slice(0, kend)
+            lower = dict(band=1, band_offset=-q0) if causal else {}
+            upper = dict(band=2, band_offset=q0) if causal else {}
+            Sc = K.poly_matmul_hilo([q[hs, qs] for q in Qh], True, [k[hs, ks].transpose(1, 2) for k in Kh], True)
+            Pr = _hilo_scores(hbn, q1 - q0, kend, NP, Q[0].device)
+            _probs_hilo(Sc, Pr, q1 - q0, scale, causal, q0)
+            if dV is not None:
+                K.poly_matmul_hilo([p.transpose(1, 2) for p in Pr], True, [g[hs, qs] for g in dOh], True,
+                                   out=[t[hs, ks] for t in dV], accumulate=True, **lower)
+            dP = K.poly_matmul_hilo([g[hs, qs] for g in dOh], True, [v[hs, ks].transpose(1, 2) for v in Vh], True,
+                                    out=Sc)
+            dS = _hilo_scores(hbn, q1 - q0, kend, NP, Q[0].device)
+            ds_rows = dsum[hs, qs].contiguous()
+            pp, k1 = _lib.pointer_array(Pr)
+            pd, k2 = _lib.pointer_array(dP)
+            po, k3 = _lib.pointer_array(dS)
+            status = _lib.load().pk_attn_dscores_hilo(NP - 1, hbn * (q1 - q0), kend, pp, Pr[0].stride(1), pd,
+                                                      dP[0].stride(1), ds_rows.data_ptr(), float(scale), po,
+                                                      dS[0].stride(1), K._stream(Q[0].device))
+            _lib.check(status, "pk_attn_dscores_hilo")
+            del Pr, Sc, dP
+            if dQ is not None:
+                K.poly_matmul_hilo(dS, True, [k[hs, ks] for k in Kh], True, out=[t[hs, qs] for t in dQ], **upper)
+            if dK is not None:
+                K.poly_matmul_hilo([d.transpose(1, 2) for d in dS], True, [q[hs, qs] for q in Qh], True,
+                                   out=[t[hs, ks] for t in dK], accumulate=True, **lower)
+
+
 def backward_planes(Q, Kp, V, O, dO, causal, scale, need, stats=None):
     BH, L, _ = Q[0].shape
     S = Kp[0].shape[1]
@@ -317,6 +428,9 @@ def backward_planes(Q, Kp, V, O, dO, causal, scale, need, stats=None):
         return dQ, dK, dV
     if stats is not None and f32_split_eligible(Q, Kp, V):
         _fused_backward_f32(Q, Kp, V, dO, dsum, stats, causal, scale, dQ, dK, dV)
+        return dQ, dK, dV
+    if tiled_f32_eligible(Q, Kp, V):
+        _backward_f32_tiled(Q, Kp, V, dO, dsum, causal, scale, dQ, dK, dV)
         return dQ, dK, dV
     for h0 in range(0, BH, hb):
         h1 = min(BH, h0 + hb)

@@ -175,10 +175,15 @@ def poly_matmul(a_planes, b_planes, out=None, accumulate=False, band=0, band_off
 def split_hilo(planes):
     """float32 planes -> [hi_0, lo_0, hi_1, lo_1, ...] bfloat16 planes with x ~= hi + lo (the
     operand form pk_poly_gemm_hilo reads in place)."""
-    out = []
-    for x in planes:
-        hi = x.to(torch.bfloat16)
-        out += [hi, (x - hi.float()).to(torch.bfloat16)]
+    planes = [x if x.is_contiguous() else x.contiguous() for x in planes]
+    _require_cuda(planes, "split_hilo")
+    if any(x.dtype != torch.float32 for x in planes) or len(planes) > _lib.PK_MAX_PLANES:
+        raise NotImplementedError("split_hilo: float32 planes, degree <= 15")
+    out = [torch.empty_like(planes[i // 2], dtype=torch.bfloat16) for i in range(2 * len(planes))]
+    px, k1 = _lib.pointer_array(planes)
+    po, k2 = _lib.pointer_array(out)
+    _lib.check(_lib.load().pk_split_hilo(len(planes) - 1, planes[0].numel(), px, po, _stream(planes[0].device)),
+               "pk_split_hilo")
     return out
 
 

@@ -287,6 +287,27 @@ def test_golden_vectors(golden):
         assert max(errs) <= tol, (name, errs)
 
 
+@pytest.mark.parametrize("shape,n", [((4, 1000), 3), ((7, 13), 0), ((3, 5, 1023), 5), ((1,), 2)])
+def test_split_hilo_kernel_is_bit_exact(shape, n):
+    """pk_split_hilo: hi = bf16(x), lo = bf16(x - hi), round to nearest, bit for bit against the
+    same split done with torch conversions (vector and element-by-element tails, odd sizes, a
+    non-contiguous input made contiguous first)."""
+    from polytensors_b200 import _kernels
+
+    g = torch.Generator().manual_seed(sum(shape) + n)
+    planes = [(torch.randn(*shape, generator=g) * 10 ** (k - 2)).cuda() for k in range(n + 1)]
+    if len(shape) > 1:
+        planes = [p.transpose(0, -1) for p in planes]
+    got = _kernels.split_hilo(planes)
+    assert len(got) == 2 * len(planes)
+    for k, x in enumerate(planes):
+        hi = x.to(torch.bfloat16)
+        lo = (x - hi.float()).to(torch.bfloat16)
+        assert got[2 * k].shape == x.shape and got[2 * k].dtype == torch.bfloat16
+        assert torch.equal(got[2 * k].view(torch.int16), hi.contiguous().view(torch.int16))
+        assert torch.equal(got[2 * k + 1].view(torch.int16), lo.contiguous().view(torch.int16))
+
+
 def test_device_status_clean():
     from polytensors_b200 import _lib
 

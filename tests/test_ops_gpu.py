@@ -484,6 +484,42 @@ def test_f32_split_attention_against_oracle(n, shape, causal):
         assert_close(coeffs(t.grad), w, F32, name)
 
 
+@pytest.mark.parametrize("n,shape,causal", [(3, (1, 2, 600, 128), True), (3, (2, 2, 77, 128), False),
+                                            (5, (1, 2, 300, 96), True), (4, (1, 3, 520, 64), True),
+                                            (7, (1, 1, 130, 32), False)])
+def test_f32_tiled_hilo_attention_against_oracle(n, shape, causal):
+    """float32 attention outside the split kernels (head dimension other than 64, or degree above
+    3) on the tiled path with hi/lo operands: the probability and score-gradient pairs come from
+    pk_attn_probs_hilo / pk_attn_dscores_hilo and every product reads its operands in place
+    (ragged key counts exercise the padded pair pitches).  Forward and backward against the
+    float64 oracle; tolerance 1e-4 of the plane max-norm."""
+    from polytensors_b200 import PolyTensor, _attention, _lib
+
+    Q, Kp, V, G = (series(shape, n, s, torch.float32) for s in (91, 92, 93, 94))
+    ref64 = [[p.double() for p in s] for s in (Q, Kp, V, G)]
+    fn = lambda q, k, v: ref.attention(q, k, v, is_causal=causal)   # noqa: E731
+    want_o = fn(*ref64[:3])
+    want = ref.series_vjp(fn, ref64[:3], ref64[3])
+    flat = [p.cuda().reshape(-1, *shape[-2:]) for p in Q]
+    assert _attention.tiled_f32_eligible(flat, flat, flat) and not _attention.f32_split_eligible(flat, flat, flat)
+    for nm in ("attn_probs", "attn_dscores", "flash_attn_fwd"):
+        _lib.profile_query(nm)
+    _lib.profile_enable(True)
+    try:
+        with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+            q, k, v = (poly(s, requires_grad=True) for s in (Q, Kp, V))
+            o = F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+            o.backward(poly(G))
+        torch.cuda.synchronize()
+    finally:
+        _lib.profile_enable(False)
+    assert _lib.profile_query("attn_probs")[1] > 0 and _lib.profile_query("attn_dscores")[1] > 0
+    assert _lib.profile_query("flash_attn_fwd")[1] == 0
+    assert_close(coeffs(o), want_o, F32, "o")
+    for name, t, w in (("dq", q, want[0]), ("dk", k, want[1]), ("dv", v, want[2])):
+        assert_close(coeffs(t.grad), w, F32, name)
+
+
 @pytest.mark.parametrize("reduction,softcap,dtype,chunk", [("mean", None, torch.float32, 64),
                                                            ("sum", 30.0, torch.float32, 100),
                                                            ("none", None, torch.float64, 50),
