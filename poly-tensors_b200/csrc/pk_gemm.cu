@@ -405,6 +405,17 @@ struct TileCoord {
     int plane, b, tm, tn;
 };
 
+// The k-th tile of this CTA.  Tiles come heaviest first (below), so a plain round robin gives the
+// low-numbered CTAs the most work in every round; the boustrophedon order (snake_rank) alternates
+// the direction each round, which evens out the per-CTA totals.
+#ifndef PK_TC_SNAKE
+#define PK_TC_SNAKE 1
+#endif
+__device__ __forceinline__ int tc_tile_rank(int k) {
+    if constexpr (PK_TC_SNAKE != 0) return snake_rank(k);
+    return k * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x);
+}
+
 // Tiles are ordered heaviest first (output plane n has n+1 products), then by batch,
 // then in groups of `group_m` row tiles so that CTAs running concurrently share
 // operand tiles in L2.
@@ -620,7 +631,7 @@ __global__ void __launch_bounds__(TcWarps<SPLIT>::THREADS, 1)
 #pragma unroll
             for (int s = 0; s < STAGES; ++s) issued_parity[s] = -1;
             bool ok = true;
-            for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+            for (int rk = 0, t = tc_tile_rank(0); t < p.total_tiles && ok; t = tc_tile_rank(++rk)) {
                 const TileCoord tc = decode_tile(p, t);
                 int kb0, kb1;
                 tile_kblocks(p, tc.tm, tc.tn, BN, kb0, kb1);
@@ -717,7 +728,7 @@ __global__ void __launch_bounds__(TcWarps<SPLIT>::THREADS, 1)
             uint32_t abuf = 0, aphase = 0;
             bool ok = true;
             bool issued = false;
-            for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+            for (int rk = 0, t = tc_tile_rank(0); t < p.total_tiles && ok; t = tc_tile_rank(++rk)) {
                 const TileCoord tc = decode_tile(p, t);
                 int kb0, kb1;
                 tile_kblocks(p, tc.tm, tc.tn, BN, kb0, kb1);
@@ -790,7 +801,7 @@ __global__ void __launch_bounds__(TcWarps<SPLIT>::THREADS, 1)
         const uint32_t lane_base = 32u * (warp & 3);
         const int half = (warp - 2) >> 2;
         uint32_t abuf = 0, aphase = 0;
-        for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+        for (int rk = 0, t = tc_tile_rank(0); t < p.total_tiles; t = tc_tile_rank(++rk)) {
             const TileCoord tc = decode_tile(p, t);
             const int row = tc.tm * TC_BM + lane_base + lane;
             int kb0, kb1;
