@@ -129,6 +129,7 @@ __device__ __forceinline__ int vec_count(int64_t end, int64_t c0) {
 
 template <typename T>
 __device__ __forceinline__ void load_vec4(const T* p, float (&v)[4]);
+// (generic loads: the row kernels also read their shared-memory stages through this helper)
 template <>
 __device__ __forceinline__ void load_vec4<float>(const float* p, float (&v)[4]) {
     const float4 t = *reinterpret_cast<const float4*>(p);
