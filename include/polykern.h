@@ -212,6 +212,18 @@ PK_API int pk_series_map(int op, int dtype, int degree, int ndim, const int64_t*
                          const void* const* a, int a_planes, const int64_t* a_strides,
                          const void* const* b, int b_planes, const int64_t* b_strides,
                          double p0, double p1, void* stream);
+/* pk_series_map on series with complex planes: plane k of out / a / b holds interleaved
+ * (re, im) pairs of real_dtype (PK_F32 -> complex64, PK_F64 -> complex128) when bit k of
+ * out_complex / a_complex / b_complex is set, else real values of real_dtype; strides count
+ * elements.  Every operation of pk_series_map; PK_OP_TANH, PK_OP_GELU and PK_OP_GELU_BWD need a
+ * real base (plane 0 of their series argument), which the caller checks.  Replaces the
+ * reference's plain-range rules on complex coefficients (src/polytensors/_plain.py, with the
+ * real-base / complex-direction promotion of :77-80). */
+PK_API int pk_series_map_complex(int op, int real_dtype, int degree, int ndim, const int64_t* shape,
+                                 void* const* out, const int64_t* out_strides, uint32_t out_complex,
+                                 const void* const* a, int a_planes, const int64_t* a_strides, uint32_t a_complex,
+                                 const void* const* b, int b_planes, const int64_t* b_strides, uint32_t b_complex,
+                                 double p0, double p1, void* stream);
 
 /*
  * out[o, i] = scale * sum_r x[o, r, i] for every plane; x is contiguous [outer][red][inner],

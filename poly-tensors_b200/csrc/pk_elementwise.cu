@@ -15,6 +15,7 @@
 #include "pk_common.cuh"
 #include "pk_rows.cuh"
 #include "pk_series.cuh"
+#include "pk_complex.cuh"
 
 namespace pk {
 
@@ -188,6 +189,73 @@ static void launch_map_np(const MapParams& p, int grid, bool vec, cudaStream_t s
         PK_LAUNCHED(series_map_vec_kernel<T, NP, Q><<<g, 256, 0, s>>>(p));
     } else {
         PK_LAUNCHED(series_map_kernel<T, NP><<<grid, 256, 0, s>>>(p));
+    }
+}
+
+// Series with complex planes (a real base with complex directions, or complex throughout):
+// planes flagged in a mask hold interleaved (re, im) pairs of R, the others plain R values; the
+// arithmetic runs in cplx<R> through the same operation table.  Strides count elements (a
+// complex element is one element).  Element by element with strided indexing: the complex forms
+// serve API completeness, not the configs' hot loops.
+template <typename R>
+__device__ __forceinline__ cplx<R> load_cplx(const void* plane, int64_t off, bool is_complex) {
+    if (is_complex) {
+        const R* q = static_cast<const R*>(plane) + 2 * off;
+        return cplx<R>(q[0], q[1]);
+    }
+    return cplx<R>(static_cast<const R*>(plane)[off], R(0));
+}
+
+template <typename R, int NP>
+__global__ void __launch_bounds__(256) series_map_cplx_kernel(const MapParams p, uint32_t a_cm, uint32_t b_cm,
+                                                                uint32_t o_cm) {
+    using C = cplx<R>;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < p.numel; idx += stride) {
+        int64_t oo = idx, oa = idx, ob = idx;
+        if (!p.contig) {
+            oo = oa = ob = 0;
+            int64_t rem = idx;
+            for (int d = p.ndim - 1; d >= 0; --d) {
+                const int64_t c = rem % p.shape[d];
+                rem /= p.shape[d];
+                oo += c * p.so[d];
+                oa += c * p.sa[d];
+                ob += c * p.sb[d];
+            }
+        }
+        C a[NP], b[NP], y[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+            a[k] = (k < p.a_np && k < p.np) ? load_cplx<R>(p.a[k], oa, (a_cm >> k) & 1u) : C(0);
+            b[k] = (p.b[0] != nullptr && k < p.b_np && k < p.np) ? load_cplx<R>(p.b[k], ob, (b_cm >> k) & 1u) : C(0);
+        }
+        apply_op<NP, C>(p, a, b, y);
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+            if (k >= p.np) continue;
+            if ((o_cm >> k) & 1u) {
+                R* q = static_cast<R*>(p.out[k]) + 2 * oo;
+                q[0] = y[k].re;
+                q[1] = y[k].im;
+            } else {
+                static_cast<R*>(p.out[k])[oo] = y[k].re;
+            }
+        }
+    }
+}
+
+template <typename R>
+static void launch_map_cplx(const MapParams& p, int grid, uint32_t a_cm, uint32_t b_cm, uint32_t o_cm,
+                            cudaStream_t s) {
+    switch (p.np) {
+        case 1: PK_LAUNCHED(series_map_cplx_kernel<R, 1><<<grid, 256, 0, s>>>(p, a_cm, b_cm, o_cm)); break;
+        case 2: PK_LAUNCHED(series_map_cplx_kernel<R, 2><<<grid, 256, 0, s>>>(p, a_cm, b_cm, o_cm)); break;
+        case 3: PK_LAUNCHED(series_map_cplx_kernel<R, 3><<<grid, 256, 0, s>>>(p, a_cm, b_cm, o_cm)); break;
+        case 4: PK_LAUNCHED(series_map_cplx_kernel<R, 4><<<grid, 256, 0, s>>>(p, a_cm, b_cm, o_cm)); break;
+        case 5: case 6: PK_LAUNCHED(series_map_cplx_kernel<R, 6><<<grid, 256, 0, s>>>(p, a_cm, b_cm, o_cm)); break;
+        case 7: case 8: case 9: PK_LAUNCHED(series_map_cplx_kernel<R, 9><<<grid, 256, 0, s>>>(p, a_cm, b_cm, o_cm)); break;
+        default: PK_LAUNCHED(series_map_cplx_kernel<R, 16><<<grid, 256, 0, s>>>(p, a_cm, b_cm, o_cm)); break;
     }
 }
 
@@ -403,6 +471,57 @@ __global__ void __launch_bounds__(256) split_hilo_kernel(const SplitParams p) {
     }
 }
 
+// Validated parameters of one pk_series_map / pk_series_map_complex call (p.numel == 0: nothing to do).
+static int fill_map_params(MapParams& p, const char* what, int op, int degree, int ndim, const int64_t* shape,
+                           void* const* out, const int64_t* out_strides, const void* const* a, int a_planes,
+                           const int64_t* a_strides, const void* const* b, int b_planes, const int64_t* b_strides,
+                           double p0, double p1) {
+    const std::string w(what);
+    if (degree < 0 || degree >= PK_MAX_PLANES) return fail(PK_ERR_UNSUPPORTED, w + ": degree out of range");
+    if (ndim < 0 || ndim > MAP_MAX_DIMS) return fail(PK_ERR_UNSUPPORTED, w + ": more than 6 dimensions");
+    const int np = degree + 1;
+    const bool binary = is_binary(op);
+    if (op < 0 || op > PK_OP_SIGMOID_BWD || (op > PK_OP_POWI && op < PK_OP_ADD))
+        return fail(PK_ERR_ARG, w + ": unknown op " + std::to_string(op));
+    if (!out || !a || (binary && !b)) return fail(PK_ERR_ARG, w + ": null plane array");
+    if (a_planes != 1 && a_planes != np) return fail(PK_ERR_ARG, w + ": a_planes must be 1 or degree+1");
+    if (binary && b_planes != 1 && b_planes != np) return fail(PK_ERR_ARG, w + ": b_planes must be 1 or degree+1");
+    p.op = op;
+    p.np = np;
+    p.ndim = ndim;
+    p.a_np = a_planes;
+    p.b_np = binary ? b_planes : 0;
+    p.p0 = p0;
+    p.p1 = p1;
+    p.numel = 1;
+    for (int d = 0; d < ndim; ++d) {
+        if (shape[d] < 0) return fail(PK_ERR_ARG, w + ": negative extent");
+        p.numel *= shape[d];
+        p.shape[d] = shape[d];
+        p.so[d] = out_strides[d];
+        p.sa[d] = a_strides[d];
+        p.sb[d] = binary ? b_strides[d] : 0;
+    }
+    if (p.numel == 0) return PK_OK;
+    for (int k = 0; k < np; ++k) {
+        if (!out[k]) return fail(PK_ERR_ARG, w + ": null output plane");
+        p.out[k] = out[k];
+    }
+    for (int k = 0; k < a_planes; ++k) {
+        if (!a[k]) return fail(PK_ERR_ARG, w + ": null input plane");
+        p.a[k] = a[k];
+    }
+    if (binary) {
+        for (int k = 0; k < b_planes; ++k) {
+            if (!b[k]) return fail(PK_ERR_ARG, w + ": null input plane");
+            p.b[k] = b[k];
+        }
+    }
+    p.contig = dense(ndim, shape, out_strides) && dense(ndim, shape, a_strides) &&
+               (!binary || dense(ndim, shape, b_strides));
+    return PK_OK;
+}
+
 }  // namespace pk
 
 using namespace pk;
@@ -440,49 +559,13 @@ int pk_series_map(int op, int dtype, int degree, int ndim, const int64_t* shape,
                   const int64_t* out_strides, const void* const* a, int a_planes, const int64_t* a_strides,
                   const void* const* b, int b_planes, const int64_t* b_strides, double p0, double p1,
                   void* stream) {
-    if (degree < 0 || degree >= PK_MAX_PLANES) return fail(PK_ERR_UNSUPPORTED, "pk_series_map: degree out of range");
-    if (ndim < 0 || ndim > MAP_MAX_DIMS) return fail(PK_ERR_UNSUPPORTED, "pk_series_map: more than 6 dimensions");
-    const int np = degree + 1;
-    const bool binary = is_binary(op);
-    if (op < 0 || op > PK_OP_SIGMOID_BWD || (op > PK_OP_POWI && op < PK_OP_ADD))
-        return fail(PK_ERR_ARG, "pk_series_map: unknown op " + std::to_string(op));
-    if (!out || !a || (binary && !b)) return fail(PK_ERR_ARG, "pk_series_map: null plane array");
-    if (a_planes != 1 && a_planes != np) return fail(PK_ERR_ARG, "pk_series_map: a_planes must be 1 or degree+1");
-    if (binary && b_planes != 1 && b_planes != np) return fail(PK_ERR_ARG, "pk_series_map: b_planes must be 1 or degree+1");
     MapParams p{};
-    p.op = op;
-    p.np = np;
-    p.ndim = ndim;
-    p.a_np = a_planes;
-    p.b_np = binary ? b_planes : 0;
-    p.p0 = p0;
-    p.p1 = p1;
-    p.numel = 1;
-    for (int d = 0; d < ndim; ++d) {
-        if (shape[d] < 0) return fail(PK_ERR_ARG, "pk_series_map: negative extent");
-        p.numel *= shape[d];
-        p.shape[d] = shape[d];
-        p.so[d] = out_strides[d];
-        p.sa[d] = a_strides[d];
-        p.sb[d] = binary ? b_strides[d] : 0;
-    }
+    if (int rc = fill_map_params(p, "pk_series_map", op, degree, ndim, shape, out, out_strides, a, a_planes,
+                                 a_strides, b, b_planes, b_strides, p0, p1))
+        return rc;
     if (p.numel == 0) return PK_OK;
-    for (int k = 0; k < np; ++k) {
-        if (!out[k]) return fail(PK_ERR_ARG, "pk_series_map: null output plane");
-        p.out[k] = out[k];
-    }
-    for (int k = 0; k < a_planes; ++k) {
-        if (!a[k]) return fail(PK_ERR_ARG, "pk_series_map: null input plane");
-        p.a[k] = a[k];
-    }
-    if (binary) {
-        for (int k = 0; k < b_planes; ++k) {
-            if (!b[k]) return fail(PK_ERR_ARG, "pk_series_map: null input plane");
-            p.b[k] = b[k];
-        }
-    }
-    p.contig = dense(ndim, shape, out_strides) && dense(ndim, shape, a_strides) &&
-               (!binary || dense(ndim, shape, b_strides));
+    const int np = p.np;
+    const bool binary = is_binary(op);
     const int grid = grid_for(p.numel);
     bool vec = p.contig != 0;
     if (vec) {
@@ -502,6 +585,29 @@ int pk_series_map(int op, int dtype, int degree, int ndim, const int64_t* shape,
     }
     prof_end("series_map", s, tok);
     PK_CHECK_LAUNCH("pk_series_map");
+    return PK_OK;
+}
+
+int pk_series_map_complex(int op, int real_dtype, int degree, int ndim, const int64_t* shape, void* const* out,
+                          const int64_t* out_strides, uint32_t out_complex, const void* const* a, int a_planes,
+                          const int64_t* a_strides, uint32_t a_complex, const void* const* b, int b_planes,
+                          const int64_t* b_strides, uint32_t b_complex, double p0, double p1, void* stream) {
+    MapParams p{};
+    if (int rc = fill_map_params(p, "pk_series_map_complex", op, degree, ndim, shape, out, out_strides, a,
+                                 a_planes, a_strides, b, b_planes, b_strides, p0, p1))
+        return rc;
+    if (p.numel == 0) return PK_OK;
+    const int grid = grid_for(p.numel);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    void* tok;
+    prof_begin("series_map", s, &tok);
+    switch (real_dtype) {
+        case PK_F32: launch_map_cplx<float>(p, grid, a_complex, b_complex, out_complex, s); break;
+        case PK_F64: launch_map_cplx<double>(p, grid, a_complex, b_complex, out_complex, s); break;
+        default: return fail(PK_ERR_UNSUPPORTED, "pk_series_map_complex: real_dtype must be PK_F32 or PK_F64");
+    }
+    prof_end("series_map", s, tok);
+    PK_CHECK_LAUNCH("pk_series_map_complex");
     return PK_OK;
 }
 

@@ -252,8 +252,18 @@ def _complex_dtype(dtype):
 
 def _real_planes(planes, what):
     if any(p.is_complex() for p in planes):
-        raise NotImplementedError(f"{what}: complex directions are supported by the polykern matrix product only")
+        raise NotImplementedError(f"{what}: complex directions are not supported by this operation's kernels")
     return planes
+
+
+def _cast(p, dtype):
+    """Plane p in the precision of dtype, keeping a complex plane complex (a real base with complex
+    directions stays so: the reference's per-plane dtypes, src/polytensors/_range_ops.py:46-64)."""
+    if p.is_complex() and not dtype.is_complex:
+        target = _complex_dtype(dtype) or p.dtype
+    else:
+        target = dtype
+    return p if p.dtype == target else p.to(target)
 
 
 def _write(c, target, planes):
@@ -267,6 +277,7 @@ def _write(c, target, planes):
 
 
 def _scalar(x):
+    """A real Python number (the affine fast path takes real coefficients only)."""
     return isinstance(x, (int, float, bool)) and not isinstance(x, torch.Tensor)
 
 
@@ -305,20 +316,16 @@ def _arith(c):
     # Python numbers reach dispatch as 0-dim CPU "wrapped number" tensors: read them on the
     # host instead of copying them to the device (a blocking copy per operation).
     a, b = _host_number(a), _host_number(b)
-    if dtype.is_complex or (is_poly(a) and any(p.is_complex() for p in a.coeffs)) or \
-            (is_poly(b) and any(p.is_complex() for p in b.coeffs)):
-        raise NotImplementedError("PolyTensor arithmetic with complex directions is not implemented by the "
-                                  "polykern kernels (only the matrix product supports them)")
     D = c.degree
     out = list(a.coeffs) if inplace else None
 
     def planes(x):
         if is_poly(x):
-            return [p if p.dtype == dtype else p.to(dtype) for p in x.coeffs]
+            return [_cast(p, dtype) for p in x.coeffs]
         t = x if isinstance(x, torch.Tensor) else torch.full((), x, dtype=dtype, device=c.like.device)
         if t.device != c.like.device and t.dim() == 0:
             t = t.to(c.like.device)
-        return [t.to(dtype)]
+        return [_cast(t, dtype)]
 
     sign = -alpha if func in SUB else alpha
     if func in ADD or func in SUB:
@@ -348,18 +355,17 @@ def _rsub(c):
     other = _host_number(other)
     alpha = c.kwargs.get("alpha", 1)
     if is_poly(x) and _scalar(other):
-        X = _real_planes(c.lift(x), "rsub")
-        return c.wrap(K.series_map("affine", c.degree, X, p0=-alpha, p1=other))
+        return c.wrap(K.series_map("affine", c.degree, c.lift(x), p0=-alpha, p1=other))
     # other - alpha * x with a tensor or series `other`
     dtype = torch.result_type(_rep(x), _rep(other))
-    X = [p.to(dtype) for p in c.lift(x)]
-    O = [p.to(dtype) for p in c.lift(other)]
+    X = [_cast(p, dtype) for p in c.lift(x)]
+    O = [_cast(p, dtype) for p in c.lift(other)]
     return c.wrap(K.series_map("add", c.degree, O, X, p0=-alpha))
 
 
 @rule(aten.neg.default)
 def _neg(c):
-    return c.wrap(K.series_map("affine", c.degree, _real_planes(c.lift(c.args[0]), "neg"), p0=-1.0))
+    return c.wrap(K.series_map("affine", c.degree, c.lift(c.args[0]), p0=-1.0))
 
 
 @rule(aten.pow.Tensor_Scalar)
@@ -369,12 +375,12 @@ def _pow(c):
         n = int(n)
     if not isinstance(n, int) or isinstance(n, bool) or n < 0:
         raise NotImplementedError("only nonnegative integer powers")
-    return c.wrap(K.series_map("powi", c.degree, _real_planes(c.lift(x), "pow"), p0=float(n)))
+    return c.wrap(K.series_map("powi", c.degree, c.lift(x), p0=float(n)))
 
 
 def _unary(name):
     def fn(c):
-        return c.wrap(K.series_map(name, c.degree, _real_planes(c.lift(c.args[0]), name)))
+        return c.wrap(K.series_map(name, c.degree, c.lift(c.args[0])))
     return fn
 
 
@@ -389,7 +395,7 @@ def _gelu(c):
     approximate = c.args[1] if len(c.args) > 1 else c.kwargs.get("approximate", "none")
     if approximate != "none":
         raise NotImplementedError("PolyTensor implements exact GELU (approximate='none') only")
-    return c.wrap(K.series_map("gelu", c.degree, _real_planes(c.lift(c.args[0]), "gelu")))
+    return c.wrap(K.series_map("gelu", c.degree, c.lift(c.args[0])))
 
 
 @rule(aten.gelu_backward.default)
@@ -399,19 +405,19 @@ def _gelu_backward(c):
         raise NotImplementedError("PolyTensor implements exact GELU (approximate='none') only")
     G, X = c.lift(c.args[0]), c.lift(c.args[1])
     dtype = X[0].dtype
-    return c.wrap(K.series_map("gelu_bwd", c.degree, [g.to(dtype) for g in G], X))
+    return c.wrap(K.series_map("gelu_bwd", c.degree, [_cast(g, dtype) for g in G], X))
 
 
 @rule(aten.tanh_backward.default)
 def _tanh_backward(c):
     G, Y = c.lift(c.args[0]), c.lift(c.args[1])
-    return c.wrap(K.series_map("tanh_bwd", c.degree, [g.to(Y[0].dtype) for g in G], Y))
+    return c.wrap(K.series_map("tanh_bwd", c.degree, [_cast(g, Y[0].dtype) for g in G], Y))
 
 
 @rule(aten.sigmoid_backward.default)
 def _sigmoid_backward(c):
     G, Y = c.lift(c.args[0]), c.lift(c.args[1])
-    return c.wrap(K.series_map("sigmoid_bwd", c.degree, [g.to(Y[0].dtype) for g in G], Y))
+    return c.wrap(K.series_map("sigmoid_bwd", c.degree, [_cast(g, Y[0].dtype) for g in G], Y))
 
 
 # ======================================================================================
@@ -515,8 +521,21 @@ def reduce_planes(planes, dims, keepdim, mean, dtype=None):
         src = [p.permute(*keep, *dims) for p in x]
         outer, inner = math.prod(shape[d] for d in keep), 1
     scale = (1.0 / red if red else float("nan")) if mean else 1.0
-    out = K.series_reduce(src, outer, red, inner, scale)
-    return [o.view(out_shape).to(work_dtype) for o in out]
+    if not any(p.is_complex() for p in src):
+        out = K.series_reduce(src, outer, red, inner, scale)
+        return [o.view(out_shape).to(work_dtype) for o in out]
+    # complex planes (a real base with complex directions): the sum is linear, so a complex plane
+    # is reduced as its (re, im) pairs, i.e. as a real plane with twice the inner extent
+    out = [None] * len(src)
+    for is_c in (False, True):
+        idx = [i for i, p in enumerate(src) if p.is_complex() == is_c]
+        if not idx:
+            continue
+        group = [torch.view_as_real(src[i].contiguous()) if is_c else src[i] for i in idx]
+        res = K.series_reduce(group, outer, red, inner * (2 if is_c else 1), scale)
+        for i, r in zip(idx, res):
+            out[i] = torch.view_as_complex(r.view(-1, 2)).view(out_shape) if is_c else r.view(out_shape)
+    return out
 
 
 @rule(aten.sum.default, aten.sum.dim_IntList, aten.mean.default, aten.mean.dim)
@@ -530,8 +549,7 @@ def _sum(c):
         dim = (dim,)
     keepdim = c.args[2] if len(c.args) > 2 else c.kwargs.get("keepdim", False)
     mean = c.func in (aten.mean.default, aten.mean.dim)
-    planes = _real_planes(c.lift(x), "sum")
-    return c.wrap(reduce_planes(planes, dim, keepdim, mean, c.kwargs.get("dtype")))
+    return c.wrap(reduce_planes(c.lift(x), dim, keepdim, mean, c.kwargs.get("dtype")))
 
 
 @rule(aten.sum_to_size.default, aten._grad_sum_to_size.default)
@@ -807,7 +825,7 @@ def _embedding(c):
     weight, indices = c.args[:2]
     if is_poly(indices):
         raise NotImplementedError("PolyTensor embedding indices must be ordinary tensors")
-    return c.wrap(K.gather_rows(_real_planes(c.lift(weight), "embedding"), indices))
+    return c.wrap(K.gather_rows(c.lift(weight), indices))
 
 
 @rule(aten.embedding_dense_backward.default)

@@ -283,6 +283,8 @@ def series_map(op, degree, a, b=None, p0=0.0, p1=0.0, out=None):
     opcode = _lib.OP[op]
     planes = list(a) + (list(b) if b is not None else []) + (list(out) if out is not None else [])
     _require_cuda(planes, f"series {op}")
+    if any(x.is_complex() for x in planes):
+        return _series_map_complex(op, degree, a, b, p0, p1, out)
     dtype = a[0].dtype
     code = dtype_code(dtype)
     shape = a[0].shape if b is None else torch.broadcast_shapes(a[0].shape, b[0].shape)
@@ -321,6 +323,74 @@ def series_map(op, degree, a, b=None, p0=0.0, p1=0.0, out=None):
     return out
 
 
+# operations whose output plane k depends only on the input planes k (the others mix lower planes in)
+_PLANEWISE_OPS = ("copy", "affine", "add")
+# operations whose base function is evaluated on the real part only (real base required)
+_REAL_BASE_OPS = {"tanh": 0, "gelu": 0, "gelu_bwd": 1}
+
+
+def _series_map_complex(op, degree, a, b, p0, p1, out):
+    """series_map on series with complex planes (pk_series_map_complex): a real base with complex
+    directions, or complex throughout.  Planes are brought to one precision (float64/complex128 if
+    any plane is double, else float32/complex64); an output plane is complex when an input plane
+    it depends on is (the same plane for add/affine/copy, any plane up to it otherwise), which for
+    series built by the constructor (all directions one dtype) is the reference's per-plane
+    result-type rule."""
+    np_ = degree + 1
+    ops_in = [list(a)] + ([list(b)] if b is not None else [])
+    every = [p for grp in ops_in for p in grp] + (list(out) if out is not None else [])
+    if any(p.dtype not in (torch.float32, torch.float64, torch.complex64, torch.complex128) for p in every):
+        raise NotImplementedError(f"series {op} with complex planes: float32/float64 (complex64/complex128) only")
+    if op in _REAL_BASE_OPS and ops_in[_REAL_BASE_OPS[op]][0].is_complex():
+        raise NotImplementedError(f"series {op}: a complex base (plane 0) is not supported; complex directions are")
+    wide = any(p.dtype in (torch.float64, torch.complex128) for p in every)
+    real_t, cplx_t = (torch.float64, torch.complex128) if wide else (torch.float32, torch.complex64)
+    conv = [[p.to(cplx_t if p.is_complex() else real_t) for p in grp] for grp in ops_in]
+    shape = conv[0][0].shape if b is None else torch.broadcast_shapes(conv[0][0].shape, conv[1][0].shape)
+    if out is not None:
+        shape = out[0].shape
+    conv = [[p.expand(shape) for p in grp] for grp in conv]
+    conv = [grp if _same_strides(grp) else [p.contiguous() for p in grp] for grp in conv]
+    if out is None:
+        dtypes = []
+        for k in range(np_):
+            lo = k if op in _PLANEWISE_OPS else 0
+            dep = [p for grp in conv for j, p in enumerate(grp) if lo <= j <= k]
+            dtypes.append(cplx_t if any(p.is_complex() for p in dep) else real_t)
+        out = [torch.empty(shape, dtype=dt, device=conv[0][0].device) for dt in dtypes]
+    else:
+        out = list(out)
+        if any(o.dtype not in (real_t, cplx_t) for o in out) or not _same_strides(out):
+            raise NotImplementedError(f"series {op}: in-place update into planes of another precision or layout")
+        for k, o in enumerate(out):
+            lo = k if op in _PLANEWISE_OPS else 0
+            if not o.is_complex() and any(p.is_complex() for grp in conv for j, p in enumerate(grp) if lo <= j <= k):
+                raise RuntimeError("cannot copy complex PolyTensor coefficients into real coefficient storage")
+    if out[0].numel() == 0:
+        return out
+
+    def mask(grp):
+        return sum(1 << k for k, p in enumerate(grp) if p.is_complex())
+
+    sets = [out[0].stride()] + [grp[0].stride() for grp in conv]
+    cshape, cstrides = _collapse(list(shape), *sets)
+    if len(cshape) > 6:
+        raise NotImplementedError("series operation on more than 6 non-mergeable dimensions")
+    shp, ks = _lib.int64_array(cshape)
+    so, k1 = _lib.int64_array(cstrides[0])
+    sa, k2 = _lib.int64_array(cstrides[1])
+    sb, k3 = _lib.int64_array(cstrides[2] if b is not None else [0] * len(cshape))
+    po, kp1 = _lib.pointer_array(out)
+    pa, kp2 = _lib.pointer_array(conv[0])
+    pb, kp3 = _lib.pointer_array(conv[1] if b is not None else [None])
+    status = _lib.load().pk_series_map_complex(
+        _lib.OP[op], _lib.PK_F64 if wide else _lib.PK_F32, degree, len(cshape), shp, po, so, mask(out),
+        pa, len(conv[0]), sa, mask(conv[0]), pb if b is not None else None, len(conv[1]) if b is not None else 0,
+        sb, mask(conv[1]) if b is not None else 0, float(p0), float(p1), _stream(conv[0][0].device))
+    _lib.check(status, f"pk_series_map_complex({op})")
+    return out
+
+
 def series_reduce(planes, outer, red, inner, scale=1.0):
     """out[o, i] = scale * sum_r x[o, r, i] for contiguous planes viewed as (outer, red, inner)."""
     x = [p.contiguous() for p in planes]
@@ -350,8 +420,24 @@ def _check_indices(idx, upper, what, ignore=None):
         raise IndexError(f"{what}: index {first} is out of range [0, {upper})")
 
 
+def _as_real_rows(planes, fn):
+    """Row gathers and scatters move whole rows, so a complex plane goes through as a real plane of
+    twice the width ((re, im) pairs); real and complex planes run as separate groups."""
+    out = [None] * len(planes)
+    for is_c in (False, True):
+        idx = [i for i, p in enumerate(planes) if p.is_complex() == is_c]
+        if not idx:
+            continue
+        group = [torch.view_as_real(planes[i].contiguous()).flatten(-2) if is_c else planes[i] for i in idx]
+        for i, r in zip(idx, fn(group)):
+            out[i] = torch.view_as_complex(r.unflatten(-1, (-1, 2))) if is_c else r
+    return out
+
+
 def gather_rows(weight_planes, idx):
     """out[i, :] = W[idx[i], :] per plane (embedding)."""
+    if any(p.is_complex() for p in weight_planes):
+        return _as_real_rows(list(weight_planes), lambda g: gather_rows(g, idx))
     _check_indices(idx, weight_planes[0].shape[0], "embedding")
     w = weight_planes if _same_strides(weight_planes) and weight_planes[0].stride(-1) == 1 else \
         [p.contiguous() for p in weight_planes]
@@ -369,6 +455,8 @@ def gather_rows(weight_planes, idx):
 
 def scatter_add_rows(grad_planes, idx, num_rows, padding_idx=-1):
     """out[idx[i], :] += G[i, :] over zeroed (num_rows, d) planes (embedding backward)."""
+    if any(p.is_complex() for p in grad_planes):
+        return _as_real_rows(list(grad_planes), lambda g: scatter_add_rows(g, idx, num_rows, padding_idx))
     _check_indices(idx, num_rows, "embedding backward")
     d = grad_planes[0].shape[-1]
     g = [p.reshape(-1, d) for p in grad_planes]

@@ -55,6 +55,9 @@ SIGNATURES = {
                                  _pp, _i64, _i64, _i64, _i32, _pp, _i64, _i64, _i32, _i32, _i64, _vp, _sz, _vp]),
     "pk_series_map": (_i32, [_i32, _i32, _i32, _i32, _p64, _pp, _p64, _pp, _i32, _p64, _pp, _i32, _p64,
                              ctypes.c_double, ctypes.c_double, _vp]),
+    "pk_series_map_complex": (_i32, [_i32, _i32, _i32, _i32, _p64, _pp, _p64, ctypes.c_uint32, _pp, _i32, _p64,
+                                     ctypes.c_uint32, _pp, _i32, _p64, ctypes.c_uint32, ctypes.c_double,
+                                     ctypes.c_double, _vp]),
     "pk_series_reduce": (_i32, [_i32, _i32, _i64, _i64, _i64, _pp, _pp, ctypes.c_double, _vp]),
     "pk_series_gather_rows": (_i32, [_i32, _i32, _i64, _i64, _vp, _pp, _i64, _i64, _pp, _vp]),
     "pk_series_scatter_add_rows": (_i32, [_i32, _i32, _i64, _i64, _vp, _i64, _pp, _i64, _i64, _pp, _vp]),

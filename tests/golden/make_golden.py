@@ -164,6 +164,38 @@ def case_series_ops():
     save("series_ops_f64_n5", X=X, Xp=Xp, Y=Y, Yp=Yp, **out)
 
 
+def case_series_ops_complex():
+    """Elementwise rules on a real base with complex128 directions (the constructor's model for a
+    float64 base and complex directions), degree 3, in plain range."""
+    n = 3
+    X = series((4, 6), n, 95, complex_from=1)
+    Xp = [X[0].abs() + 0.5] + X[1:]
+    Y = series((4, 6), n, 96, complex_from=1)
+    Yp = [Y[0].abs() + 0.5] + Y[1:]
+    R = series((4, 6), n, 97)                     # a real series
+    out = {}
+    with PolyTensor.plain_range():
+        x, xp, y, yp, r = PolyTensor(X), PolyTensor(Xp), PolyTensor(Y), PolyTensor(Yp), PolyTensor(R)
+        out["mul"] = coeffs(x * y)
+        out["mul_real"] = coeffs(x * r)
+        out["div"] = coeffs(x / yp)
+        out["add"] = coeffs(x + 2.5 * y)
+        out["sub_real"] = coeffs(r - x)
+        out["scale_complex"] = coeffs(x * (0.5 - 1.5j))
+        out["exp"] = coeffs(torch.exp(x))
+        out["log"] = coeffs(torch.log(xp))
+        out["sqrt"] = coeffs(torch.sqrt(xp))
+        out["rsqrt"] = coeffs(torch.rsqrt(xp))
+        out["reciprocal"] = coeffs(torch.reciprocal(xp))
+        out["tanh"] = coeffs(torch.tanh(x))
+        out["sigmoid"] = coeffs(torch.sigmoid(x))
+        out["gelu"] = coeffs(F.gelu(x))
+        out["square"] = coeffs(x.square())
+        out["sum1"] = coeffs(x.sum(dim=1))
+        out["mean0"] = coeffs(x.mean(dim=0))
+    save("series_ops_c128_n3", X=X, Xp=Xp, Y=Y, Yp=Yp, R=R, **out)
+
+
 def case_readme_fit(plain):
     """README linear-regression fit (README.md:44-68), seed 0, 10 SGD steps."""
     torch.manual_seed(0)
@@ -263,6 +295,7 @@ if __name__ == "__main__":
     case_cross_entropy()
     case_attention()
     case_series_ops()
+    case_series_ops_complex()
     case_readme_fit(plain=False)
     case_readme_fit(plain=True)
     case_tiny_transformer()

@@ -32,6 +32,63 @@ def test_elementwise_series_ops_golden(golden):
         assert_close(coeffs(value), g[key], F64, key)
 
 
+@pytest.mark.parametrize("precision", ["f64", "f32"])
+def test_complex_direction_series_ops_golden(golden, precision):
+    """Elementwise rules, sums and products on a real base with complex directions
+    (pk_series_map_complex) against the reference's own results: plane dtypes as the reference
+    gives them (real base, complex directions) and values within 1e-10 (float64 / complex128) or
+    1e-4 (float32 / complex64 inputs)."""
+    from polytensors_b200 import PolyTensor
+
+    g = golden("series_ops_c128_n3")
+    tol = F64 if precision == "f64" else F32
+
+    def dev(planes):
+        if precision == "f32":
+            planes = [p.to(torch.complex64 if p.is_complex() else torch.float32) for p in planes]
+        return poly(planes)
+
+    x, xp, y, yp, r = (dev(g[k]) for k in ("X", "Xp", "Y", "Yp", "R"))
+    with PolyTensor.plain_range():
+        got = {
+            "mul": x * y, "mul_real": x * r, "div": x / yp, "add": x + 2.5 * y, "sub_real": r - x,
+            "scale_complex": x * (0.5 - 1.5j), "exp": torch.exp(x), "log": torch.log(xp), "sqrt": torch.sqrt(xp),
+            "rsqrt": torch.rsqrt(xp), "reciprocal": torch.reciprocal(xp), "tanh": torch.tanh(x),
+            "sigmoid": torch.sigmoid(x), "gelu": F.gelu(x), "square": x.square(), "sum1": x.sum(dim=1),
+            "mean0": x.mean(dim=0),
+        }
+    for key, value in got.items():
+        want = g[key]
+        assert [c.is_complex() for c in value.coeffs] == [c.is_complex() for c in want], key
+        assert_close([c.to(torch.complex128) for c in coeffs(value)], [c.to(torch.complex128) for c in want],
+                     tol, key)
+
+
+def test_complex_directions_embedding_and_inplace_rules():
+    """Row gathers and their backward move complex planes as (re, im) pairs; an in-place update of a
+    real series with a complex one raises like the reference."""
+    from polytensors_b200 import PolyTensor
+
+    gen = torch.Generator().manual_seed(3)
+    base = torch.randn(10, 6, generator=gen, dtype=torch.float64)
+    dirs = [torch.complex(torch.randn(10, 6, generator=gen, dtype=torch.float64),
+                          torch.randn(10, 6, generator=gen, dtype=torch.float64)) for _ in range(2)]
+    w = PolyTensor(tuple(t.cuda() for t in [base] + dirs), requires_grad=True)
+    idx = torch.tensor([[1, 4, 4], [9, 0, 2]], device="cuda")
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        e = F.embedding(idx, w)
+        for got, plane in zip(e.coeffs, w.coeffs):
+            assert got.dtype == plane.dtype and torch.equal(got, plane.detach()[idx])
+        e.sum().backward()
+    counts = torch.zeros(10, dtype=torch.float64, device="cuda").index_add_(0, idx.reshape(-1),
+                                                                           torch.ones(6, dtype=torch.float64,
+                                                                                      device="cuda"))
+    assert torch.equal(w.grad.coeffs[0], counts[:, None].expand(10, 6))
+    real = PolyTensor(tuple(torch.ones(10, 6, dtype=torch.float64, device="cuda") for _ in range(3)))
+    with PolyTensor.plain_range(), pytest.raises(RuntimeError, match="complex"):
+        real.add_(PolyTensor(tuple(t.cuda() for t in [base] + dirs)))
+
+
 @pytest.mark.parametrize("n", [1, 3, 8])
 def test_elementwise_f32_against_oracle(n):
     from polytensors_b200 import PolyTensor

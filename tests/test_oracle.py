@@ -115,6 +115,25 @@ def test_series_ops(golden):
         assert_series_close(got, g[key], 1e-12)
 
 
+def test_series_ops_complex_directions(golden):
+    """The oracle's series rules on a real base with complex128 directions against the reference's
+    own results (tests/golden/series_ops_c128_n3.pt): plane dtypes and values."""
+    g = golden("series_ops_c128_n3")
+    X, Xp, Y, Yp, R = g["X"], g["Xp"], g["Y"], g["Yp"], g["R"]
+    checks = {
+        "mul": ref.cauchy(X, Y), "mul_real": ref.cauchy(X, R), "div": ref.series_quotient(X, Yp),
+        "add": [x + 2.5 * y for x, y in zip(X, Y)], "sub_real": [r - x for r, x in zip(R, X)],
+        "scale_complex": [x * (0.5 - 1.5j) for x in X], "exp": ref.series_exp(X), "log": ref.series_log(Xp),
+        "rsqrt": ref.series_rsqrt(Xp), "reciprocal": ref.series_quotient([torch.ones_like(Xp[0])] +
+                                                                        [torch.zeros_like(t) for t in Xp[1:]], Xp),
+        "tanh": ref.activation(X, "tanh"), "sigmoid": ref.activation(X, "sigmoid"), "gelu": ref.gelu(X),
+        "square": ref.cauchy(X, X), "sum1": [x.sum(dim=1) for x in X], "mean0": [x.mean(dim=0) for x in X],
+    }
+    for key, got in checks.items():
+        assert_series_close(got, g[key], 1e-12)
+    assert g["mul"][0].dtype == torch.float64 and all(c.dtype == torch.complex128 for c in g["mul"][1:])
+
+
 def test_bench_readme_fit_oracle_matches_the_reference_run(golden):
     """bench.py's configs[0] CPU leg (the README fit through the oracle) reproduces the reference's
     own README run (tests/golden/readme_fit_plain.pt): the seeded data follow the README's draws."""
