@@ -168,7 +168,6 @@ __global__ void __launch_bounds__(512, 1) rmsnorm_fwd_reg_kernel(const NormParam
     }
 }
 
-// Rows beyond the next one that the streaming kernels prefetch into L2.
 // Rows bulk-prefetched into L2 beyond the one streaming into shared memory.  Measured at 16384 x
 // 4096 float32 rows (degree 4 / degree 1): forward 0.56 / 0.20 ms with 2 rows, 0.40 / 0.18 with 1,
 // 0.45 / 0.18 with none; backward 0.78 / 0.31 ms with 1 or 2 rows, 0.72 / 0.29 with none (deeper
@@ -374,6 +373,94 @@ __global__ void __launch_bounds__(512) rmsnorm_bwd_kernel(const NormParams p) {
         for (int64_t i = threadIdx.x; i < static_cast<int64_t>(p.np) * p.cols; i += blockDim.x) {
             const int64_t k = i / p.cols, c = i % p.cols;
             out[i] = dwp[k * p.cols + (p.vec ? (c % ROW_VEC) * q + c / ROW_VEC : c)];
+        }
+    }
+}
+
+// The backward with whole rows in registers and one CTA per row (persistent over rows): for short
+// series a row's x and g fit the registers of one CTA, so no cluster exchange is needed and
+// several CTAs per SM keep rows in flight while others reduce.  Thread t owns the column quads
+// s * blockDim + t (s < STEPS) of every row; with W the weight series and the weight-gradient
+// partials of those columns stay in registers, written per CTA to dw_part[blockIdx.x] at the end.
+// Per element: rg = r (*) g, dw += rg (*) x, a = rg (*) w, row sum += a (*) x (= r (*) gy (*) x),
+// then dx = a - (r (*) r (*) sum / cols) (*) x.
+template <typename T, int NP, int STEPS, bool W>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(const NormParams p) {
+    using C = typename Compute<T>::type;
+    __shared__ C scratch[8 * NP];
+    const int64_t span = static_cast<int64_t>(blockDim.x) * ROW_VEC;
+    const C inv_cols = C(1) / C(p.cols);
+    C w[STEPS][ROW_VEC][NP], dwa[STEPS][ROW_VEC][NP];
+#pragma unroll
+    for (int s = 0; s < STEPS; ++s) {
+        const int64_t c0 = s * span + static_cast<int64_t>(threadIdx.x) * ROW_VEC;
+        if constexpr (W) load_weight4<NP, T, C>(p, c0, max(0, vec_count(p.cols, c0)), w[s]);
+#pragma unroll
+        for (int u = 0; u < ROW_VEC; ++u) {
+#pragma unroll
+            for (int k = 0; k < NP; ++k) {
+                dwa[s][u][k] = C(0);
+                if constexpr (!W) w[s][u][k] = C(k == 0 ? 1 : 0);
+            }
+        }
+    }
+    for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+        C x[STEPS][ROW_VEC][NP], g[STEPS][ROW_VEC][NP];
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+            const int64_t c0 = s * span + static_cast<int64_t>(threadIdx.x) * ROW_VEC;
+            const int valid = max(0, vec_count(p.cols, c0));
+            load_planes4<NP, T, C>(p.x, p.np, row * p.x_rs + c0, valid, p.vec != 0, x[s]);
+            load_planes4<NP, T, C>(p.g, p.np, row * p.g_rs + c0, valid, p.vec != 0, g[s]);
+        }
+        C r[NP], d[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+            r[k] = k < p.np ? static_cast<const C*>(p.rstd)[row * p.np + k] : C(0);
+            d[k] = C(0);
+        }
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+#pragma unroll
+            for (int u = 0; u < ROW_VEC; ++u) {
+                C rg[NP], a[NP];
+                s_mul<NP, C>(r, g[s][u], rg);
+                if constexpr (W) s_mul_acc<NP, C>(rg, x[s][u], dwa[s][u]);
+                s_mul<NP, C>(rg, w[s][u], a);
+                s_mul_acc<NP, C>(a, x[s][u], d);
+#pragma unroll
+                for (int k = 0; k < NP; ++k) g[s][u][k] = a[k];
+            }
+        }
+        block_sum<NP, C>(d, scratch);
+        C coef[NP];
+        s_mul<NP, C>(r, r, coef);
+        s_mul<NP, C>(coef, d, coef);
+#pragma unroll
+        for (int k = 0; k < NP; ++k) coef[k] *= inv_cols;
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+            const int64_t c0 = s * span + static_cast<int64_t>(threadIdx.x) * ROW_VEC;
+            C out[ROW_VEC][NP];
+#pragma unroll
+            for (int u = 0; u < ROW_VEC; ++u) s_sub_mul<NP, C>(g[s][u], coef, x[s][u], out[u]);
+            store_planes4<NP, T, C>(p.y, p.np, row * p.y_rs + c0, max(0, vec_count(p.cols, c0)), p.vec != 0, out);
+        }
+    }
+    if constexpr (W) {
+        if (p.dw_part != nullptr) {
+            C* part = static_cast<C*>(p.dw_part) + static_cast<int64_t>(blockIdx.x) * p.np * p.cols;
+#pragma unroll
+            for (int s = 0; s < STEPS; ++s) {
+                const int64_t c0 = s * span + static_cast<int64_t>(threadIdx.x) * ROW_VEC;
+#pragma unroll
+                for (int u = 0; u < ROW_VEC; ++u) {
+                    if (c0 + u >= p.cols) continue;
+#pragma unroll
+                    for (int k = 0; k < NP; ++k)
+                        if (k < p.np) part[k * p.cols + c0 + u] = dwa[s][u][k];
+                }
+            }
         }
     }
 }
@@ -836,6 +923,61 @@ static int bwd_stream(NormParams& p, void* const* dw, void* ws, size_t ws_bytes,
     return PK_OK;
 }
 
+// The register backward (rmsnorm_bwd_reg_kernel) for rows of at most 256 threads x 4 quads with
+// vector-aligned planes.  Returns 1 when the shape does not suit it, else a status.  Used up to
+// degree 1: at 16384 x 4096 float32 it takes 0.267 ms against 0.300 streaming at degree 1, but
+// 1.49 against 0.72 ms at degree 4 with a weight series (the registers then hold one row per SM).
+#ifndef PK_NORM_BWD_REG_MAX_NP
+#define PK_NORM_BWD_REG_MAX_NP 2
+#endif
+template <typename T, int NP>
+static int bwd_reg(NormParams& p, void* const* dw, void* ws, size_t ws_bytes, cudaStream_t s) {
+    if (p.np != NP || !p.vec || p.cols % ROW_VEC) return 1;
+    const int64_t quads = p.cols / ROW_VEC;
+    const int steps = quads <= 256 ? 1 : (quads <= 512 ? 2 : (quads <= 1024 ? 4 : 0));
+    if (!steps || quads < 32) return 1;
+    const int threads = static_cast<int>(round_up(ceil_div(quads, steps), 32));
+    const bool weighted = p.w_np != 0 || dw != nullptr;
+    const void* fn = nullptr;
+    if (weighted)
+        fn = steps == 1 ? reinterpret_cast<const void*>(rmsnorm_bwd_reg_kernel<T, NP, 1, true>)
+             : steps == 2 ? reinterpret_cast<const void*>(rmsnorm_bwd_reg_kernel<T, NP, 2, true>)
+                          : reinterpret_cast<const void*>(rmsnorm_bwd_reg_kernel<T, NP, 4, true>);
+    else
+        fn = steps == 1 ? reinterpret_cast<const void*>(rmsnorm_bwd_reg_kernel<T, NP, 1, false>)
+             : steps == 2 ? reinterpret_cast<const void*>(rmsnorm_bwd_reg_kernel<T, NP, 2, false>)
+                          : reinterpret_cast<const void*>(rmsnorm_bwd_reg_kernel<T, NP, 4, false>);
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0) != cudaSuccess || per_sm < 1) return 1;
+    // the weight-gradient partials take one [np][cols] slice per CTA of the workspace, which is
+    // sized for at most 4 CTAs per SM
+    const int64_t grid = std::min<int64_t>(p.rows, static_cast<int64_t>(num_sms()) * std::min(per_sm, 4));
+    if (dw) {
+        const size_t need = static_cast<size_t>(grid) * p.np * p.cols * sizeof(float);
+        if (!ws || ws_bytes < need) return fail(PK_ERR_WORKSPACE, "pk_rmsnorm_bwd: workspace too small");
+        p.dw_part = ws;
+    }
+    void* tok;
+    prof_begin("rmsnorm_bwd", s, &tok);
+    const int g = static_cast<int>(grid);
+    if (weighted) {
+        if (steps == 1) PK_LAUNCHED(rmsnorm_bwd_reg_kernel<T, NP, 1, true><<<g, threads, 0, s>>>(p));
+        else if (steps == 2) PK_LAUNCHED(rmsnorm_bwd_reg_kernel<T, NP, 2, true><<<g, threads, 0, s>>>(p));
+        else PK_LAUNCHED(rmsnorm_bwd_reg_kernel<T, NP, 4, true><<<g, threads, 0, s>>>(p));
+    } else {
+        if (steps == 1) PK_LAUNCHED(rmsnorm_bwd_reg_kernel<T, NP, 1, false><<<g, threads, 0, s>>>(p));
+        else if (steps == 2) PK_LAUNCHED(rmsnorm_bwd_reg_kernel<T, NP, 2, false><<<g, threads, 0, s>>>(p));
+        else PK_LAUNCHED(rmsnorm_bwd_reg_kernel<T, NP, 4, false><<<g, threads, 0, s>>>(p));
+    }
+    PK_CHECK_LAUNCH("pk_rmsnorm_bwd");
+    if (dw) {
+        const int st = reduce_dw<T, NP>(p, dw, g, s);
+        if (st != PK_OK) return st;
+    }
+    prof_end("rmsnorm_bwd", s, tok);
+    return PK_OK;
+}
+
 // Launch the streaming forward when two stages of a row fit in shared memory and the row fits
 // 512 threads x STEPS x 4 columns (vector-aligned planes, float compute, degree <= 5).  Returns
 // false when it does not apply.
@@ -919,6 +1061,10 @@ static int run_norm(bool backward, NormParams& p, void* const* dw, void* ws, siz
         prof_end("rmsnorm_fwd", s, tok);
         PK_CHECK_LAUNCH("pk_rmsnorm_fwd");
         return PK_OK;
+    }
+    if constexpr (sizeof(C) == 4 && NP <= PK_NORM_BWD_REG_MAX_NP) {
+        const int st = bwd_reg<T, NP>(p, dw, ws, ws_bytes, s);
+        if (st != 1) return st;
     }
     if constexpr (sizeof(C) == 4 && NP <= 6 && NP >= PK_NORM_BWD_STREAM_MIN_NP) {
         // next rows streamed into shared memory: half rows over 2-CTA clusters, quarter rows

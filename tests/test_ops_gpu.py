@@ -181,7 +181,9 @@ def test_rmsnorm_f32_config_width():
 
 @pytest.mark.parametrize("dtype,n,cols,weight", [
     (torch.float32, 4, 4096, "series"), (torch.float32, 5, 2048, "plain"), (torch.float32, 3, 8192, "none"),
-    (torch.bfloat16, 4, 4096, "series"), (torch.float16, 2, 1024, "plain")])
+    (torch.bfloat16, 4, 4096, "series"), (torch.float16, 2, 1024, "plain"),
+    (torch.float32, 1, 4096, "none"), (torch.float32, 1, 4096, "series"), (torch.float32, 0, 1000, "plain"),
+    (torch.bfloat16, 1, 2048, "series"), (torch.float32, 1, 1001, "series")])
 def test_rmsnorm_backward_many_rows(dtype, n, cols, weight):
     """More rows than clusters fit on the GPU at once (each cluster streams a run of rows), rows
     strided inside a wider buffer, a weight series with non-zero directions, a plain weight, none."""
