@@ -322,6 +322,12 @@ PK_API int pk_attn_probs(int dtype, int degree, int64_t rows, int64_t cols, int6
 PK_API int pk_attn_dscores(int dtype, int degree, int64_t rows, int64_t cols,
                            const void* const* probs, int64_t p_rs, const void* const* dprobs, int64_t dp_rs,
                            const void* dsum, double scale, void* const* dscores, int64_t ds_rs, void* stream);
+/* dsum[row][k] = (sum_d dO (*) O)_k over the rows of the attention output and its gradient
+ * (rows x cols planes, row strides do_rs / o_rs elements): the row term of the score gradient,
+ * sum_d dO (*) O (src/polytensors/_plain.py:342-347 applied to the attention's P V product).
+ * dsum is float32 ([rows][degree+1]; float64 for PK_F64). */
+PK_API int pk_attn_dsum(int dtype, int degree, int64_t rows, int64_t cols, const void* const* dO, int64_t do_rs,
+                        const void* const* O, int64_t o_rs, void* dsum, void* stream);
 /* float32 forms whose probabilities and score gradients are bf16 hi/lo pairs (2(n+1) planes
  * hi_0, lo_0, hi_1, ...; x ~= hi + lo), the operand form pk_poly_gemm_hilo reads without staging.
  * Scores and dprobs stay float32 (n+1 planes).  degree <= 7; outputs must not alias inputs.

@@ -325,6 +325,64 @@ __global__ void __launch_bounds__(256) attn_dscores_kernel(const SoftmaxParams p
     }
 }
 
+// dsum[row][k] = (sum_d dO (*) O)_k, the row term of the attention score gradient: one warp per
+// row, four elements per lane and step, the n+1 sums reduced across the warp.  Rows of dO and O
+// are contiguous (row strides do_rs / o_rs elements).
+struct DsumParams {
+    int np;
+    int64_t rows, cols, do_rs, o_rs;
+    const void* dO[PK_MAX_PLANES];
+    const void* O[PK_MAX_PLANES];
+    void* dsum;  // [rows][np], compute type
+    int vec;
+};
+
+template <typename T, int NP>
+__global__ void __launch_bounds__(256) attn_dsum_kernel(const DsumParams p) {
+    using C = typename Compute<T>::type;
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); row < p.rows;
+         row += warps) {
+        C acc[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) acc[k] = C(0);
+        for (int64_t c0 = static_cast<int64_t>(lane) * ROW_VEC; c0 < p.cols; c0 += 32 * ROW_VEC) {
+            const int valid = vec_count(p.cols, c0);
+            C g[ROW_VEC][NP], o[ROW_VEC][NP];
+            load_planes4<NP, T, C>(p.dO, p.np, row * p.do_rs + c0, valid, p.vec != 0, g);
+            load_planes4<NP, T, C>(p.O, p.np, row * p.o_rs + c0, valid, p.vec != 0, o);
+#pragma unroll
+            for (int u = 0; u < ROW_VEC; ++u) s_mul_acc<NP, C>(g[u], o[u], acc);
+        }
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], off);
+        }
+        if (lane < p.np) {
+#pragma unroll
+            for (int k = 0; k < NP; ++k)
+                if (k == lane) static_cast<C*>(p.dsum)[row * p.np + k] = acc[k];
+        }
+    }
+}
+
+template <typename T>
+static void launch_dsum(const DsumParams& p, cudaStream_t s) {
+    // one warp per row (no row loop): the rows are short, so parallelism, not reuse, hides latency
+    const int grid = static_cast<int>(std::min<int64_t>(ceil_div(p.rows, 8), 0x7fffffff));
+    switch (p.np) {
+        case 1: PK_LAUNCHED(attn_dsum_kernel<T, 1><<<grid, 256, 0, s>>>(p)); break;
+        case 2: PK_LAUNCHED(attn_dsum_kernel<T, 2><<<grid, 256, 0, s>>>(p)); break;
+        case 3: PK_LAUNCHED(attn_dsum_kernel<T, 3><<<grid, 256, 0, s>>>(p)); break;
+        case 4: PK_LAUNCHED(attn_dsum_kernel<T, 4><<<grid, 256, 0, s>>>(p)); break;
+        case 5: case 6: PK_LAUNCHED(attn_dsum_kernel<T, 6><<<grid, 256, 0, s>>>(p)); break;
+        case 7: case 8: case 9: PK_LAUNCHED(attn_dsum_kernel<T, 9><<<grid, 256, 0, s>>>(p)); break;
+        default: PK_LAUNCHED(attn_dsum_kernel<T, 16><<<grid, 256, 0, s>>>(p)); break;
+    }
+}
+
 enum { SM_FWD = 0, SM_BWD = 1, CE_FWD = 2, CE_BWD = 3, ATTN_P = 4, ATTN_DS = 5, ATTN_P_HILO = 6, ATTN_DS_HILO = 7 };
 
 static int row_threads(int64_t cols) { return cols >= 4096 ? 512 : (cols >= 1024 ? 256 : 128); }
@@ -536,6 +594,40 @@ int pk_attn_dscores(int dtype, int degree, int64_t rows, int64_t cols, const voi
         p.out[k] = dscores[k];
     }
     return dispatch_rows(ATTN_DS, dtype, p, stream, "attn_dscores");
+}
+
+int pk_attn_dsum(int dtype, int degree, int64_t rows, int64_t cols, const void* const* dO, int64_t do_rs,
+                 const void* const* O, int64_t o_rs, void* dsum, void* stream) {
+    if (int rc = check_common(degree, rows, cols, "pk_attn_dsum")) return rc;
+    if (!dsum || !dO || !O) return fail(PK_ERR_ARG, "pk_attn_dsum: null pointer");
+    if (rows == 0) return PK_OK;
+    DsumParams p{};
+    p.np = degree + 1;
+    p.rows = rows;
+    p.cols = cols;
+    p.do_rs = do_rs;
+    p.o_rs = o_rs;
+    p.dsum = dsum;
+    for (int k = 0; k < p.np; ++k) {
+        if (!dO[k] || !O[k]) return fail(PK_ERR_ARG, "pk_attn_dsum: null plane");
+        p.dO[k] = dO[k];
+        p.O[k] = O[k];
+    }
+    const int eb = elem_bytes(dtype);
+    p.vec = (cols % ROW_VEC == 0 && row_vec_ok(p.dO, p.np, do_rs, eb) && row_vec_ok(p.O, p.np, o_rs, eb)) ? 1 : 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    void* tok;
+    prof_begin("attn_dsum", s, &tok);
+    switch (dtype) {
+        case PK_F32: launch_dsum<float>(p, s); break;
+        case PK_F64: launch_dsum<double>(p, s); break;
+        case PK_BF16: launch_dsum<__nv_bfloat16>(p, s); break;
+        case PK_F16: launch_dsum<__half>(p, s); break;
+        default: return fail(PK_ERR_UNSUPPORTED, "pk_attn_dsum: unsupported dtype");
+    }
+    prof_end("attn_dsum", s, tok);
+    PK_CHECK_LAUNCH("pk_attn_dsum");
+    return PK_OK;
 }
 
 int pk_attn_probs_hilo(int degree, int64_t rows, int64_t cols, int64_t q_len, const void* const* scores, int64_t s_rs,

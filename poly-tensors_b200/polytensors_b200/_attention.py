@@ -410,12 +410,8 @@ def backward_planes(Q, Kp, V, O, dO, causal, scale, need, stats=None):
     BH, L, _ = Q[0].shape
     S = Kp[0].shape[1]
     D = len(Q) - 1
-    # dsum[row] = sum_d dO (*) O, as a [rows][n+1] table
-    prod = K.series_map("mul", D, dO, O)
-    if prod[0].dtype in (torch.bfloat16, torch.float16):
-        prod = [p.float() for p in prod]
-    dsum = torch.stack(K.series_reduce(prod, BH * L, prod[0].shape[-1], 1), dim=-1)
-    dsum = dsum.to(K.compute_dtype(Q[0].dtype)).contiguous().view(BH, L, D + 1)
+    # dsum[row] = sum_d dO (*) O, as a [rows][n+1] table (one fused row kernel)
+    dsum = K.attn_dsum(dO, O).view(BH, L, D + 1)
     dQ = [torch.empty_like(q) for q in Q] if need[0] else None
     dK = [torch.empty_like(k) for k in Kp] if need[1] else None
     dV = [torch.empty_like(v) for v in V] if need[2] else None

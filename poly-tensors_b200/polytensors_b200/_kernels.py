@@ -391,6 +391,26 @@ def _series_map_complex(op, degree, a, b, p0, p1, out):
     return out
 
 
+def attn_dsum(dO, O):
+    """(sum_d dO (*) O) per row of (rows..., D) planes: a (rows, n+1) table in the compute dtype
+    (pk_attn_dsum)."""
+    cols = O[0].shape[-1]
+    g = [p.reshape(-1, cols) if p.dtype == O[0].dtype else p.to(O[0].dtype).reshape(-1, cols) for p in dO]
+    o = [p.reshape(-1, cols) for p in O]
+    if not _same_strides(g) or g[0].stride(-1) != 1:
+        g = [p.contiguous() for p in g]
+    if not _same_strides(o) or o[0].stride(-1) != 1:
+        o = [p.contiguous() for p in o]
+    _require_cuda((*g, *o), "attention dsum")
+    out = torch.empty(g[0].shape[0], len(g), dtype=compute_dtype(g[0].dtype), device=g[0].device)
+    pg, k1 = _lib.pointer_array(g)
+    po, k2 = _lib.pointer_array(o)
+    status = _lib.load().pk_attn_dsum(dtype_code(g[0].dtype), len(g) - 1, g[0].shape[0], cols, pg, g[0].stride(0),
+                                      po, o[0].stride(0), out.data_ptr(), _stream(g[0].device))
+    _lib.check(status, "pk_attn_dsum")
+    return out
+
+
 def series_reduce(planes, outer, red, inner, scale=1.0):
     """out[o, i] = scale * sum_r x[o, r, i] for contiguous planes viewed as (outer, red, inner)."""
     x = [p.contiguous() for p in planes]

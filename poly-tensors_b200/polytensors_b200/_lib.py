@@ -75,6 +75,7 @@ SIGNATURES = {
                              _vp, _vp]),
     "pk_attn_dscores": (_i32, [_i32, _i32, _i64, _i64, _pp, _i64, _pp, _i64, _vp, ctypes.c_double, _pp, _i64,
                                _vp]),
+    "pk_attn_dsum": (_i32, [_i32, _i32, _i64, _i64, _pp, _i64, _pp, _i64, _vp, _vp]),
     "pk_split_hilo": (_i32, [_i32, _i64, _pp, _pp, _vp]),
     "pk_attn_probs_hilo": (_i32, [_i32, _i64, _i64, _i64, _pp, _i64, ctypes.c_double, _i32, _i64, _pp, _i64,
                                   _vp, _vp]),
