@@ -201,6 +201,33 @@ enum pk_series_op {
     PK_OP_TANH_BWD = 36,   /* a = gradient, b = output: a * (1 - b^2), src/polytensors/_plain.py:316-320 */
     PK_OP_SIGMOID_BWD = 37 /* a = gradient, b = output: a * b * (1 - b), src/polytensors/_plain.py:321-325 */
 };
+/*
+ * Extended-range series (the reference's default mode, src/polytensors/_scaled.py,
+ * src/polytensors/_range_ops.py): each coefficient element is a mantissa m (float32 for
+ * float32 / bfloat16 / float16 series, float64 for float64; |m| in [1, 2), 0 or non-finite) and an
+ * int32 binary exponent e, value m * 2^e.  Planes are contiguous (numel elements).
+ * pk_scaled_from:  values (dtype) -> (m, e + base_exponent), normalised.
+ * pk_scaled_to:    (m, e - exponent_offset) -> values of dtype (only this step can overflow or
+ *                  underflow, as the reference's to_tensor).
+ * pk_scaled_series_map: PK_OP_COPY / AFFINE (p0 a + p1) / ADD (a + p0 b) / MUL (truncated Cauchy
+ *                  product, terms added in order) / DIV (quotient recurrence) over (m, e) planes,
+ *                  strides and broadcasting as pk_series_map.
+ * pk_scaled_reduce: out[o][i] = sum_r x[o][r][i], aligned to the largest exponent of the nonzero
+ *                  terms of each sum.
+ */
+PK_API int pk_scaled_from(int dtype, int degree, int64_t numel, const void* const* x, void* const* m,
+                          int32_t* const* e, int32_t base_exponent, void* stream);
+PK_API int pk_scaled_to(int dtype, int mantissa_dtype, int degree, int64_t numel, const void* const* m,
+                        const int32_t* const* e, int32_t exponent_offset, void* const* out, void* stream);
+PK_API int pk_scaled_series_map(int op, int mantissa_dtype, int degree, int ndim, const int64_t* shape,
+                                void* const* out_m, int32_t* const* out_e, const int64_t* out_strides,
+                                const void* const* a_m, const int32_t* const* a_e, int a_planes,
+                                const int64_t* a_strides, const void* const* b_m, const int32_t* const* b_e,
+                                int b_planes, const int64_t* b_strides, double p0, double p1, void* stream);
+PK_API int pk_scaled_reduce(int mantissa_dtype, int degree, int64_t outer, int64_t red, int64_t inner,
+                            const void* const* m, const int32_t* const* e, void* const* out_m,
+                            int32_t* const* out_e, void* stream);
+
 /* float32 planes (numel contiguous elements each, degree + 1 of them) -> bf16 hi/lo pairs
  * out = [hi_0, lo_0, hi_1, ...] with hi = bf16(x) and lo = bf16(x - hi) (round to nearest): the
  * operand form read in place by pk_poly_gemm_hilo and the float32 attention kernels.  No

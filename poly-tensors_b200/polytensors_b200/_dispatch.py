@@ -15,6 +15,7 @@ import torch
 from torch.utils._python_dispatch import return_and_correct_aliasing
 
 from . import _kernels as K
+from . import _scaled
 from . import _state
 
 aten = torch.ops.aten
@@ -129,10 +130,21 @@ def dispatch(func, args, kwargs):
             f"func={func}, target_shape={getattr(target, 'shape', None)}, "
             f"target_dtype={getattr(target, 'dtype', None)}, "
             f"source_types=[{', '.join(type(a).__name__ for a in args[1:4])}]")
+    ctx = Ctx(func, args, kwargs, degree, polys[0].value)
+    default_mode = not _state.plain_range.get()
+    if default_mode:
+        # outside plain_range(): the range operations on the extended-range kernels, with hidden
+        # mantissa / exponent copies (src/polytensors/_range_ops.py:26-279)
+        out = _scaled.dispatch(ctx)
+        if out is not _scaled.NOT_HANDLED:
+            return out
     fn = _RULES.get(func)
     if fn is None:
         raise NotImplementedError(f"PolyTensor does not implement {func}")
-    return fn(Ctx(func, args, kwargs, degree, polys[0].value))
+    out = fn(ctx)
+    if default_mode and func in _scaled.CARRY:
+        out = _scaled.carry(func, args, kwargs, out)
+    return out
 
 
 # ======================================================================================

@@ -75,6 +75,11 @@ SIGNATURES = {
                              _vp, _vp]),
     "pk_attn_dscores": (_i32, [_i32, _i32, _i64, _i64, _pp, _i64, _pp, _i64, _vp, ctypes.c_double, _pp, _i64,
                                _vp]),
+    "pk_scaled_from": (_i32, [_i32, _i32, _i64, _pp, _pp, _pp, ctypes.c_int32, _vp]),
+    "pk_scaled_to": (_i32, [_i32, _i32, _i32, _i64, _pp, _pp, ctypes.c_int32, _pp, _vp]),
+    "pk_scaled_series_map": (_i32, [_i32, _i32, _i32, _i32, _p64, _pp, _pp, _p64, _pp, _pp, _i32, _p64,
+                                    _pp, _pp, _i32, _p64, ctypes.c_double, ctypes.c_double, _vp]),
+    "pk_scaled_reduce": (_i32, [_i32, _i32, _i64, _i64, _i64, _pp, _pp, _pp, _pp, _vp]),
     "pk_attn_dsum": (_i32, [_i32, _i32, _i64, _i64, _pp, _i64, _pp, _i64, _vp, _vp]),
     "pk_split_hilo": (_i32, [_i32, _i64, _pp, _pp, _vp]),
     "pk_attn_probs_hilo": (_i32, [_i32, _i64, _i64, _i64, _pp, _i64, ctypes.c_double, _i32, _i64, _pp, _i64,

@@ -196,6 +196,36 @@ def case_series_ops_complex():
     save("series_ops_c128_n3", X=X, Xp=Xp, Y=Y, Yp=Yp, R=R, **out)
 
 
+def case_default_mode_range():
+    """Default (extended-range) mode with float32 values beyond float32's range: the reference keeps
+    hidden mantissa/exponent coefficients, so intermediates that overflow or underflow in the public
+    tensors come back finite.  Degree 3."""
+    n = 3
+    g = torch.Generator().manual_seed(120)
+    big = [torch.randn(4, 5, generator=g) * 1e30 for _ in range(n + 1)]
+    small = [torch.randn(4, 5, generator=g) * 1e-30 for _ in range(n + 1)]
+    W = [torch.randn(5, 3, generator=g) * 1e25 for _ in range(n + 1)]
+    Wt = [torch.randn(3, 5, generator=g) * 1e25 for _ in range(n + 1)]
+    x, s, w, wt = PolyTensor(big), PolyTensor(small), PolyTensor(W), PolyTensor(Wt)
+    out = {}
+    y = x * x
+    out["square_public"] = coeffs(y)
+    out["square_back"] = coeffs(y / x)
+    out["square_back_t"] = coeffs(y.t() / x.t())
+    out["tiny_back"] = coeffs((s * s) / s)
+    out["sub"] = coeffs((y - 0.5 * y) / x)
+    out["matmul_scaled"] = coeffs((x @ w) * 1e-35)
+    out["linear_scaled"] = coeffs(F.linear(x, wt) * 1e-35)
+    out["sum_scaled"] = coeffs((x * x).sum(dim=1) * 1e-35)
+    out["mean_scaled"] = coeffs((x * x).mean() * 1e-35)
+    out["reciprocal_back"] = coeffs(torch.reciprocal(y) * 1e30 * 1e30)
+    z = x * 1.0
+    z.mul_(x)
+    z.div_(x)
+    out["inplace_back"] = coeffs(z)
+    save("default_mode_range_f32_n3", X=big, S=small, W=W, Wt=Wt, **out)
+
+
 def case_readme_fit(plain):
     """README linear-regression fit (README.md:44-68), seed 0, 10 SGD steps."""
     torch.manual_seed(0)
@@ -296,6 +326,7 @@ if __name__ == "__main__":
     case_attention()
     case_series_ops()
     case_series_ops_complex()
+    case_default_mode_range()
     case_readme_fit(plain=False)
     case_readme_fit(plain=True)
     case_tiny_transformer()
