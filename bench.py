@@ -849,6 +849,48 @@ def readme_fit_line(device, steps, warmup):
                              "sample": "the whole fit through the oracle, float32"}}
 
 
+def default_mode_line(device, steps, warmup, M=2048, n=4, sample_rows=1024):
+    """§8(f)3: the series matrix product in the reference's default (extended-range) mode, i.e.
+    outside plain_range(): float32 M x M x M, degree 4, each of the (n+1)(n+2)/2 products rescaled
+    by its operands' largest exponents on the product kernel, sums kept as mantissa / exponent
+    pairs.  Parity: against the reference's own default-mode product on the host (a row sample of
+    A) and against the plain-range product; the CPU leg times that reference run."""
+    from polytensors_b200 import PolyTensor
+    from oracle import polyref as R
+
+    A_host = make_series((M, M), n, 1, torch.float32)
+    B_host = make_series((M, M), n, 2, torch.float32)
+    a = PolyTensor(tuple(p.to(device) for p in A_host))
+    b = PolyTensor(tuple(p.to(device) for p in B_host))
+    ms, clocks = _timed(lambda: a @ b, steps, warmup, device, 1)
+    c = a @ b
+    with PolyTensor.plain_range():
+        c_plain = a @ b
+    vs_plain = max(R.plane_errors([x.cpu() for x in c.coeffs], [x.cpu().double() for x in c_plain.coeffs]))
+    line = {"metric": f"default-mode poly-matmul coeff TFLOP/s (float32, M=N=K={M}, degree {n})",
+            "value": matmul_flops(M, M, M, n) / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+            "steps": steps, "clocks": clocks,
+            "config": {"workload": f"default-mode (extended-range) poly_matmul M=N=K={M} degree {n} float32"},
+            "parity": {"vs_plain_range_product": vs_plain}}
+    ref = _reference_package()
+    if ref is not None:
+        torch.set_num_threads(os.cpu_count() or 1)
+        ra = ref.PolyTensor(tuple(p[:sample_rows] for p in A_host))
+        rb = ref.PolyTensor(tuple(B_host))
+        t0 = time.perf_counter()
+        rc = ra @ rb
+        dt = time.perf_counter() - t0
+        err = R.plane_errors([x[:sample_rows].cpu().double() for x in c.coeffs], [x.double() for x in rc.coeffs])
+        line["parity"].update({"max_plane_err": max(err), "tol": 1e-4, "within_tolerance": bool(max(err) <= 1e-4),
+                               "against": "the reference's own default-mode product (its ScaledTensor rules), "
+                                          f"CPU, rows 0..{sample_rows - 1} of A"})
+        line["cpu_baseline"] = {"value": matmul_flops(sample_rows, M, M, n) / dt / 1e12, "unit": "TFLOP/s",
+                                "cores": os.cpu_count() or 1, "kind": "reference",
+                                "sample": f"{sample_rows} of {M} rows of A, the reference's default mode, "
+                                          f"{dt:.1f} s"}
+    return line
+
+
 def run_train(args, rank, world, device):
     """configs[4] (the default workload): global batch 64 x seq 1024 sharded over the ranks,
     micro-batches of args.micro sequences per rank with gradient accumulation, one bucketed
@@ -873,6 +915,8 @@ def run_train(args, rank, world, device):
         torch.cuda.empty_cache()
     if world == 1 and not args.no_extras:
         extras["readme_fit"] = readme_fit_line(device, min(args.steps, 5), args.warmup)
+        extras["default_mode"] = default_mode_line(device, min(args.steps, 5), max(args.warmup, 2))
+        torch.cuda.empty_cache()
         # configs[2] and configs[3] on the same GPU, a few steps each (per-op lines carried here so
         # that every config is measured in the default run)
         ns = argparse.Namespace(steps=min(args.steps, 3), warmup=2, rows=16384, seq=4096, batch=8,
@@ -1268,7 +1312,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="train",
                     choices=sorted(WORKLOADS) + ["norm_ce", "attention", "attention_fwd", "train",
-                                                 "poly_matmul_sweep", "degree1"])
+                                                 "poly_matmul_sweep", "degree1", "default_mode"])
     ap.add_argument("--no-matmul", action="store_true", help="train: skip the configs[1] product line")
     ap.add_argument("--no-extras", action="store_true", help="train: skip the configs[2] / configs[3] lines")
     ap.add_argument("--impl", default="polykern", choices=["polykern", "reference"])
@@ -1316,7 +1360,8 @@ def main():
                                              device_id=device)
     secondary = {"norm_ce": run_norm_ce, "attention": run_attention, "attention_fwd": run_attention_fwd,
                  "train": run_train, "degree1": run_degree1,
-                 "poly_matmul_sweep": run_matmul_sweep}
+                 "poly_matmul_sweep": run_matmul_sweep,
+                 "default_mode": lambda a, r, w, d: default_mode_line(d, a.steps, max(a.warmup, 2))}
     if args.workload in secondary:
         result = secondary[args.workload](args, rank, world, device)
         if rank == 0:
