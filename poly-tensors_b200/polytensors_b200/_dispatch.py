@@ -131,7 +131,7 @@ def dispatch(func, args, kwargs):
             f"target_dtype={getattr(target, 'dtype', None)}, "
             f"source_types=[{', '.join(type(a).__name__ for a in args[1:4])}]")
     ctx = Ctx(func, args, kwargs, degree, polys[0].value)
-    default_mode = not _state.plain_range.get()
+    default_mode = not _state.plain_mode()
     if default_mode:
         # outside plain_range(): the range operations on the extended-range kernels, with hidden
         # mantissa / exponent copies (src/polytensors/_range_ops.py:26-279)

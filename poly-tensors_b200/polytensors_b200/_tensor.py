@@ -204,9 +204,11 @@ class PolyTensor(torch.Tensor):
         """Ordinary floating-point range for coefficient arithmetic (the mode the kernels
         implement).  Context-local; run backward inside the same context."""
         token = _state.plain_range.set(True)
+        _state.enter_plain()
         try:
             yield
         finally:
+            _state.exit_plain()
             _state.plain_range.reset(token)
 
     @classmethod

@@ -73,3 +73,28 @@ def test_hidden_copy_is_dropped_after_a_public_write(golden):
     back = y / x
     want = 2.0 / g["X"][0]
     assert torch.allclose(back.coeffs[0].cpu(), want, rtol=1e-5)
+
+
+def test_backward_inside_plain_range_stays_plain():
+    """CUDA backward runs on the autograd engine's threads; started inside plain_range() it keeps
+    plain-range arithmetic (no extended-range kernel launches), as the forward did."""
+    from polytensors_b200 import PolyTensor, _lib
+
+    g = torch.Generator().manual_seed(5)
+    planes = lambda *shape: tuple(torch.randn(*shape, generator=g).cuda() for _ in range(3))  # noqa: E731
+    a = PolyTensor(planes(16, 8), requires_grad=True)
+    b = PolyTensor(planes(8, 4), requires_grad=True)
+    _lib.profile_query("scaled_map")
+    _lib.profile_enable(True)
+    try:
+        with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+            ((a @ b) * (a @ b)).sum().backward()
+        torch.cuda.synchronize()
+        assert _lib.profile_query("scaled_map")[1] == 0
+        assert a.grad is not None and torch.isfinite(a.grad.coeffs[2]).all()
+        with PolyTensor.retain_wrappers():
+            (a.detach() * 2.0).sum()
+        torch.cuda.synchronize()
+        assert _lib.profile_query("scaled_map")[1] > 0
+    finally:
+        _lib.profile_enable(False)
