@@ -210,7 +210,8 @@ enum pk_series_op {
  * pk_scaled_to:    (m, e - exponent_offset) -> values of dtype (only this step can overflow or
  *                  underflow, as the reference's to_tensor).
  * pk_scaled_series_map: PK_OP_COPY / AFFINE (p0 a + p1) / ADD (a + p0 b) / MUL (truncated Cauchy
- *                  product, terms added in order) / DIV (quotient recurrence) over (m, e) planes,
+ *                  product, terms added in order) / DIV (quotient recurrence) / EXP (exp of the base
+ *                  from its logarithm, then the exponential recurrence) over (m, e) planes,
  *                  strides and broadcasting as pk_series_map.
  * pk_scaled_reduce: out[o][i] = sum_r x[o][r][i], aligned to the largest exponent of the nonzero
  *                  terms of each sum.

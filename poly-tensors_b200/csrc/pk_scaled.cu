@@ -146,6 +146,32 @@ __global__ void __launch_bounds__(256) scaled_map_kernel(const ScaledMapParams p
                     y[k] = sc_div<C>(r, b[0]);
                 }
                 break;
+            case PK_OP_EXP: {
+                // y_0 = exp(x_0) from its logarithm: 2^floor(x_0 / ln 2) times exp of the remainder,
+                // in double, so exp(x_0) beyond the dtype's range stays finite (the reference's
+                // ScaledTensor.from_log, src/polytensors/_scaled.py:226-250); then
+                // y_k = (x_1 / k) y_{k-1} + sum_{i=2..k} (x_i (i/k)) y_{k-i} in scaled arithmetic
+                // (src/polytensors/_series.py:31-42)
+                const double v = static_cast<double>(sc_value<C>(a[0].m, a[0].e));
+                if (isfinite(v)) {
+                    const double ln2 = 0.69314718055994530942;
+                    const double E = floor(v / ln2);
+                    const double E_c = fmax(fmin(E, 1.0e9), -1.0e9);
+                    const double r = v - E_c * ln2;
+                    y[0] = sc_norm<C>(static_cast<C>(exp(r)), static_cast<long long>(E_c));
+                } else {
+                    y[0] = sc_norm<C>(static_cast<C>(exp(v)), 0);
+                }
+#pragma unroll
+                for (int k = 1; k < NP; ++k) {
+                    SV<C> acc = sc_mul<C>(sc_div<C>(a[1], sc_norm<C>(C(k), 0)), y[k - 1]);
+#pragma unroll
+                    for (int i = 2; i <= k; ++i)
+                        acc = sc_add<C>(acc, sc_mul<C>(sc_mul<C>(a[i], sc_norm<C>(C(i) / C(k), 0)), y[k - i]));
+                    y[k] = acc;
+                }
+                break;
+            }
             default:  // copy
 #pragma unroll
                 for (int k = 0; k < NP; ++k) y[k] = a[k];
@@ -321,8 +347,9 @@ int pk_scaled_series_map(int op, int mantissa_dtype, int degree, int ndim, const
                          double p0, double p1, void* stream) {
     if (degree < 0 || degree >= PK_MAX_PLANES) return fail(PK_ERR_UNSUPPORTED, "pk_scaled_series_map: degree out of range");
     if (ndim < 0 || ndim > 6) return fail(PK_ERR_UNSUPPORTED, "pk_scaled_series_map: more than 6 dimensions");
-    if (op != PK_OP_COPY && op != PK_OP_AFFINE && op != PK_OP_ADD && op != PK_OP_MUL && op != PK_OP_DIV)
-        return fail(PK_ERR_UNSUPPORTED, "pk_scaled_series_map: copy, affine, add, mul and div only");
+    if (op != PK_OP_COPY && op != PK_OP_AFFINE && op != PK_OP_ADD && op != PK_OP_MUL && op != PK_OP_DIV &&
+        op != PK_OP_EXP)
+        return fail(PK_ERR_UNSUPPORTED, "pk_scaled_series_map: copy, affine, add, mul, div and exp only");
     const bool binary = op == PK_OP_ADD || op == PK_OP_MUL || op == PK_OP_DIV;
     const int np = degree + 1;
     if (!out_m || !out_e || !a_m || !a_e || (binary && (!b_m || !b_e)))

@@ -9,8 +9,9 @@ operations on the kernels: each coefficient is a pair of device tensors, a float
 mantissa and an int32 exponent (``csrc/pk_scaled.cu``), attached to the PolyTensor it belongs to
 with a snapshot of its coefficients' version counters (a write to a public coefficient invalidates
 it, as in the reference).  Handled: add / sub / mul / div (series and constants, in place too),
-neg, rsub, reciprocal, mm / bmm / matmul / mv / dot / linear / addmm, sum / mean, views, clone,
-detach, copy_ and zero_.  Other operations run on the public coefficients (the hidden copy is not
+exp (the base's exponential from its logarithm, the series in scaled arithmetic), neg, rsub,
+reciprocal, mm / bmm / matmul / mv / dot / linear / addmm, sum / mean, views, clone,
+detach and copy_.  Other operations run on the public coefficients (the hidden copy is not
 carried through them).  Complex coefficients run on the public coefficients as well.
 """
 
@@ -305,6 +306,13 @@ def dispatch(c):
         else:
             out = series_op("div", D, A, B)
         return _write(a, out) if inplace else _output(c, out, dtype)
+    if func is aten.exp.default and not _complex(args[0]):
+        # the series from the public input coefficients in scaled arithmetic, the public coefficients
+        # converted from it, so that overflowing directions are +-inf rather than inf - inf
+        # (src/polytensors/_dispatch.py:431-437, _series.py:23-42)
+        x = args[0]
+        scs = series_op("exp", D, from_planes(list(x.coeffs)))
+        return _output(c, scs, x.coeffs[0].dtype)
     if func is aten.neg.default and not _complex(args[0]):
         return _output(c, series_op("affine", D, lift(args[0], like), p0=-1.0), args[0].coeffs[0].dtype)
     if func is aten.rsub.Scalar and not _complex(*args[:2]) and not isinstance(args[1], torch.Tensor):

@@ -223,7 +223,13 @@ def case_default_mode_range():
     z.mul_(x)
     z.div_(x)
     out["inplace_back"] = coeffs(z)
-    save("default_mode_range_f32_n3", X=big, S=small, W=W, Wt=Wt, **out)
+    # exp of a base around 100: exp(100) ~ 2.7e43 overflows float32's public coefficients
+    E = [torch.full((4, 5), 100.0) + torch.randn(4, 5, generator=g)] + [torch.randn(4, 5, generator=g) / (k + 1)
+                                                                          for k in range(n)]
+    e = torch.exp(PolyTensor(E))
+    out["exp_public"] = coeffs(e)
+    out["exp_scaled"] = coeffs(e * 1e-30)
+    save("default_mode_range_f32_n3", X=big, S=small, W=W, Wt=Wt, E=E, **out)
 
 
 def case_readme_fit(plain):

@@ -47,6 +47,9 @@ def test_default_mode_range_matches_the_reference(golden):
     z.mul_(x)
     z.div_(x)
     got["inplace_back"] = z
+    e = torch.exp(_cuda(g["E"]))
+    got["exp_public"] = e
+    got["exp_scaled"] = e * 1e-30
     for key, value in got.items():
         _same(value, g[key], 1e-5, key)
 
