@@ -232,6 +232,13 @@ def lift(x, like):
     return from_planes([x])
 
 
+def constant(value, dtype):
+    """A Python scalar rounded to `dtype`, as the reference lifts a constant operand
+    (torch.full((), value, dtype=result_type(like, value)), src/polytensors/_range_ops.py:40-42),
+    returned as the float the kernels take."""
+    return float(torch.tensor(value, dtype=dtype))
+
+
 def _padded(scs, degree):
     zero = SC(torch.zeros_like(scs[0].m), torch.zeros_like(scs[0].e))
     return scs + [zero] * (degree + 1 - len(scs))
@@ -318,7 +325,8 @@ def dispatch(c):
     if func is aten.rsub.Scalar and not _complex(*args[:2]) and not isinstance(args[1], torch.Tensor):
         x, other = args[:2]
         dtype = torch.result_type(_rep(x), other)
-        return _output(c, series_op("affine", D, lift(x, like), p0=-kwargs.get("alpha", 1), p1=other), dtype)
+        return _output(c, series_op("affine", D, lift(x, like), p0=-kwargs.get("alpha", 1), p1=constant(other, dtype)),
+                       dtype)
     if func is aten.reciprocal.default and not _complex(args[0]):
         x = args[0]
         one = from_planes([torch.ones((), dtype=x.coeffs[0].dtype, device=like.device)])

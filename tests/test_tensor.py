@@ -223,3 +223,16 @@ def test_construction_matches_the_reference_rules():
         for cls in (PolyTensor, ref.PolyTensor):
             with pytest.raises(kind):
                 cls(list(bad), degree=degree)
+
+
+def test_default_mode_constants_round_like_the_reference():
+    """A scalar operand of the extended-range rules is rounded to the operation's dtype first, as
+    the reference lifts it (torch.full((), value, dtype=result_type(like, value)))."""
+    from polytensors_b200 import _scaled
+
+    for dtype in (torch.float32, torch.bfloat16, torch.float16, torch.float64):
+        like = torch.zeros((), dtype=dtype)
+        for value in (0.1, 1 / 3, 1e30, 7, -2.5):
+            want = torch.full((), value, dtype=torch.result_type(like, value)).item()
+            assert _scaled.constant(value, torch.result_type(like, value)) == want
+    assert _scaled.constant(0.1, torch.bfloat16) != 0.1
