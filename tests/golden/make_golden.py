@@ -214,6 +214,7 @@ def case_default_mode_range():
     out["square_back_t"] = coeffs(y.t() / x.t())
     out["tiny_back"] = coeffs((s * s) / s)
     out["sub"] = coeffs((y - 0.5 * y) / x)
+    out["rsub_back"] = coeffs((1.0 - y) / x)
     out["matmul_scaled"] = coeffs((x @ w) * 1e-35)
     out["linear_scaled"] = coeffs(F.linear(x, wt) * 1e-35)
     out["sum_scaled"] = coeffs((x * x).sum(dim=1) * 1e-35)

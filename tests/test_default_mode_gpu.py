@@ -39,7 +39,7 @@ def test_default_mode_range_matches_the_reference(golden):
     y = x * x
     got = {
         "square_public": y, "square_back": y / x, "square_back_t": y.t() / x.t(), "tiny_back": (s * s) / s,
-        "sub": (y - 0.5 * y) / x, "matmul_scaled": (x @ w) * 1e-35, "linear_scaled": F.linear(x, wt) * 1e-35,
+        "sub": (y - 0.5 * y) / x, "rsub_back": (1.0 - y) / x, "matmul_scaled": (x @ w) * 1e-35, "linear_scaled": F.linear(x, wt) * 1e-35,
         "sum_scaled": (x * x).sum(dim=1) * 1e-35, "mean_scaled": (x * x).mean() * 1e-35,
         "reciprocal_back": torch.reciprocal(y) * 1e30 * 1e30,
     }

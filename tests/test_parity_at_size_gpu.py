@@ -81,21 +81,23 @@ def check_product(M, n, dtype, tol, rows, complex_from=None, seed=0):
     return errs
 
 
-@pytest.mark.parametrize("M,n", [(8192, 4), (4096, 8), (8192, 8)])
+@pytest.mark.parametrize("M,n", [(8192, 4), (4096, 2), (8192, 2), (4096, 8), (8192, 8)])
 def test_float32_product_at_config_size(M, n):
-    """configs[1] float32: the benchmark configuration (8192^3, degree 4) and degree 8."""
+    """configs[1] float32: the benchmark configuration (8192^3, degree 4), degrees 2 and 8."""
     check_product(M, n, torch.float32, 1e-4, rows=32)
 
 
-@pytest.mark.parametrize("M,n", [(1024, 2), (1024, 4), (4096, 2), (4096, 4)])
+@pytest.mark.parametrize("M,n", [(1024, 2), (1024, 4), (1024, 8), (4096, 2), (4096, 4), (4096, 8), (8192, 2),
+                                 (8192, 4)])
 def test_float64_product_at_config_size(M, n):
     """configs[1] float64 on the DMMA path."""
     check_product(M, n, torch.float64, 1e-10, rows=64)
 
 
-def test_complex_directions_product_at_config_size():
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_complex_directions_product_at_config_size(n):
     """configs[1] complex128 directions at 4096: real float64 base, complex128 planes k >= 1."""
-    check_product(4096, 2, torch.float64, 1e-10, rows=64, complex_from=1)
+    check_product(4096, n, torch.float64, 1e-10, rows=64, complex_from=1)
 
 
 # ----------------------------------------------------------------------------------------
