@@ -236,3 +236,31 @@ def test_default_mode_constants_round_like_the_reference():
             want = torch.full((), value, dtype=torch.result_type(like, value)).item()
             assert _scaled.constant(value, torch.result_type(like, value)) == want
     assert _scaled.constant(0.1, torch.bfloat16) != 0.1
+
+
+def test_default_mode_hidden_copy_bookkeeping():
+    """Default mode's hidden extended-range coefficients, host bookkeeping only (no kernel runs):
+    views of a series carry the same view of the mantissas and exponents (the reference's
+    map_tensor over its hidden copy), and an in-place write to a public coefficient drops the copy
+    from the series and from its views (version snapshots, src/polytensors/_range.py:40-52)."""
+    from polytensors_b200 import PolyTensor, _scaled
+
+    g = torch.Generator().manual_seed(3)
+    x = PolyTensor(tuple(torch.randn(3, 4, generator=g) for _ in range(3)))
+    scs = [_scaled.SC(torch.randn(3, 4, generator=g), torch.randint(-9, 9, (3, 4), generator=g, dtype=torch.int32))
+           for _ in range(3)]
+    _scaled.attach(x, scs)
+    assert _scaled.get(x) is not None
+    views = {"t": (x.t(), lambda t: t.t()), "slice": (x[1:], lambda t: t[1:]),
+             "detach": (x.detach(), lambda t: t)}
+    for name, (v, fn) in views.items():
+        got = _scaled.get(v)
+        assert got is not None, name
+        for a, s in zip(got, scs):
+            assert torch.equal(a.m, fn(s.m)) and torch.equal(a.e, fn(s.e)), name
+    with PolyTensor.plain_range():
+        plain_view = x.t()
+    assert _scaled.get(plain_view) is None
+    x.coeffs[0].add_(1.0)
+    assert _scaled.get(x) is None
+    assert _scaled.get(views["t"][0]) is None
