@@ -59,14 +59,15 @@ enum pk_status {
 
 #define PK_MAX_PLANES 16   /* degree <= 15 */
 
-/* Library identification and diagnostics. */
+/* Library identification and diagnostics (no counterpart in the reference: its rules are Python
+ * that raises on failure, where these entry points return status codes). */
 PK_API const char* pk_version(void);
 PK_API const char* pk_last_error(void);
 
 /*
  * Device-side status word: kernels whose internal waits time out write a nonzero
  * code here instead of hanging.  pk_device_status() synchronises the current
- * device and returns (and with reset != 0, clears) that word.
+ * device and returns (and with reset != 0, clears) that word.  No counterpart in the reference.
  */
 PK_API int pk_device_status(int reset);
 
