@@ -164,6 +164,29 @@ def case_series_ops():
     save("series_ops_f64_n5", X=X, Xp=Xp, Y=Y, Yp=Yp, **out)
 
 
+def case_series_rules_backward():
+    """Forward rules the series_ops case leaves out (sqrt, reciprocal, an integer power) and the
+    backward rules of tanh, sigmoid, GELU, softmax and log-softmax (y.backward(G) in plain range),
+    degree 4."""
+    n = 4
+    X = series((5, 7), n, 130)
+    Xp = [X[0].abs() + 0.5] + X[1:]
+    G = series((5, 7), n, 131)
+    out = {}
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        x, xp = PolyTensor(X), PolyTensor(Xp)
+        out["sqrt"] = coeffs(torch.sqrt(xp))
+        out["reciprocal"] = coeffs(torch.reciprocal(xp))
+        out["cube"] = coeffs(x ** 3)
+        rules = (("tanh", torch.tanh), ("sigmoid", torch.sigmoid), ("gelu", F.gelu),
+                 ("softmax", lambda t: torch.softmax(t, dim=-1)), ("log_softmax", lambda t: torch.log_softmax(t, dim=-1)))
+        for name, fn in rules:
+            xg = PolyTensor(X, requires_grad=True)
+            fn(xg).backward(PolyTensor(G))
+            out[f"d_{name}"] = coeffs(xg.grad)
+    save("series_rules_bwd_f64_n4", X=X, Xp=Xp, G=G, **out)
+
+
 def case_series_ops_complex():
     """Elementwise rules on a real base with complex128 directions (the constructor's model for a
     float64 base and complex directions), degree 3, in plain range."""
@@ -333,6 +356,7 @@ if __name__ == "__main__":
     case_attention()
     case_series_ops()
     case_series_ops_complex()
+    case_series_rules_backward()
     case_default_mode_range()
     case_readme_fit(plain=False)
     case_readme_fit(plain=True)

@@ -146,3 +146,25 @@ def test_bench_readme_fit_oracle_matches_the_reference_run(golden):
         w, c = bench.oracle_readme_fit(data, dtype)
         assert max(ref.plane_errors(w, g["w"])) <= 1e-5, dtype
         assert max(ref.plane_errors(c, g["c"])) <= 1e-5, dtype
+
+
+def test_series_rules_and_backward_rules(golden):
+    """sqrt, reciprocal, an integer power and the backward rules of tanh, sigmoid, GELU, softmax
+    and log-softmax against the reference's own plain-range run (tests/golden/
+    series_rules_bwd_f64_n4.pt: y.backward(G) for every rule)."""
+    g = golden("series_rules_bwd_f64_n4")
+    X, Xp, G = g["X"], g["Xp"], g["G"]
+    one = [torch.ones_like(Xp[0])] + [torch.zeros_like(t) for t in Xp[1:]]
+    sm, lsm, _ = ref.softmax_family(X, -1)
+    checks = {
+        "sqrt": ref.series_exp([0.5 * t for t in ref.series_log(Xp)]),
+        "reciprocal": ref.series_quotient(one, Xp),
+        "cube": ref.cauchy(ref.cauchy(X, X), X),
+        "d_tanh": ref.cauchy(G, ref.activation(X, "tanh", derivative_order=1)),
+        "d_sigmoid": ref.cauchy(G, ref.activation(X, "sigmoid", derivative_order=1)),
+        "d_gelu": ref.gelu_backward(G, X),
+        "d_softmax": ref.softmax_backward(G, sm, -1),
+        "d_log_softmax": ref.log_softmax_backward(G, lsm, -1),
+    }
+    for key, got in checks.items():
+        assert_series_close(got, g[key], 1e-12)
