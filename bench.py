@@ -594,9 +594,10 @@ class TinyGPT:
     """decoder-only transformer with PolyTensor parameters (degree 3, float32):
     embedding, L x [RMSNorm, q/k/v/o linears, causal SDPA, RMSNorm, GELU MLP], RMSNorm, untied head."""
 
-    def __init__(self, device, init, layers=12, d=768, heads=12, vocab=32000, degree=3):
-        from polytensors_b200 import PolyTensor
+    def __init__(self, device, init, layers=12, d=768, heads=12, vocab=32000, degree=3, poly_cls=None):
+        from polytensors_b200 import PolyTensor as Ours
 
+        PolyTensor = poly_cls or Ours   # the reference arm passes the reference's own class
         self.layers, self.d, self.heads, self.vocab, self.degree = layers, d, heads, vocab, degree
         self.p = {}
         for name, planes in init.items():
@@ -676,6 +677,25 @@ def oracle_train_sample(init, ids, layers, dtype, threads, d=768, heads=12, voca
     return dt, [c.detach() for c in out], result
 
 
+def reference_train_sample(init, ids, layers, threads, lam=0.5):
+    """The reference's own CPU implementation of one configs[4] forward + backward: its PolyTensor
+    (the package pip-installed in baseline/_ref) on host tensors inside plain_range(), through the
+    same model code (TinyGPT) and inputs as the GPU arm.  Returns the seconds it took, or None
+    when the package is absent."""
+    pt = _reference_package()
+    if pt is None:
+        return None
+    RP = pt.PolyTensor
+    torch.set_num_threads(threads)
+    model = TinyGPT(torch.device("cpu"), init, layers=layers, poly_cls=RP)
+    Z = RP((torch.tensor(0.0), 1.0), degree=3)
+    t0 = time.perf_counter()
+    with RP.plain_range(), RP.retain_wrappers():
+        loss = model.loss(ids[:, :-1], ids[:, 1:], Z, lam)
+        loss.backward()
+    return time.perf_counter() - t0
+
+
 def train_config(layers):
     """The configs[4] workload description, identical in both arms of the bench."""
     return {"workload": f"train transformer layers={layers} d=768 heads=12 mlp=3072 vocab=32000 seq=1024 "
@@ -744,6 +764,15 @@ def train_parity_and_cpu(layers, device, threads, batch=4, seq=256):
            "sample": f"oracle forward + series backward, full width ({layers} layers), {batch} x {seq} tokens, "
                      f"float32, {dt:.1f} s",
            "extrapolated_s_per_step": dt * 64 * 1024 / tokens}
+    # the reference's own code on the same sample (zero higher weight coefficients, as the bench's
+    # model), when its package is installed
+    dt_ref = reference_train_sample(transformer_init(layers=layers, seed=0), ids, layers, threads)
+    if dt_ref is not None:
+        cpu = {"value": tokens / dt_ref, "unit": "tokens/s", "cores": threads, "kind": "reference",
+               "sample": f"the reference's PolyTensor (baseline/_ref) forward + backward on host tensors, full width "
+                         f"({layers} layers), {batch} x {seq} tokens, float32, {dt_ref:.1f} s",
+               "extrapolated_s_per_step": dt_ref * 64 * 1024 / tokens,
+               "oracle_port_tokens_per_s": tokens / dt}
     return parity, cpu
 
 
@@ -1271,25 +1300,35 @@ def reference_arm(args, cfg):
 
 
 def reference_arm_train(args, budget_s=150.0):
-    """--impl reference for the default (configs[4] training) workload: the reference algorithm
-    (oracle restatement of its plain-range rules) for the full-width model's forward and series
-    backward on the host cores, each step a bounded sample of 4 x 256 tokens; steps beyond a
-    ~150 s budget are not run (the count is reported)."""
+    """--impl reference for the default (configs[4] training) workload: the reference's own CPU
+    implementation (its PolyTensor from baseline/_ref on host tensors, the same model code) for the
+    full-width model's forward and backward on the host cores, each step a bounded sample of
+    4 x 256 tokens; without the package, the oracle restatement of its plain-range rules.  Steps
+    beyond a ~150 s budget are not run (the count is reported)."""
     threads = os.cpu_count() or 1
     init = transformer_init(layers=args.layers, seed=0)
     ids = train_sample_ids(4, 256)
+    use_ref = _reference_package() is not None
+
+    def one():
+        if use_ref:
+            return reference_train_sample(init, ids, args.layers, threads)
+        return oracle_train_sample(init, ids, args.layers, torch.float32, threads)[0]
+
     for _ in range(min(args.warmup, 1)):
-        oracle_train_sample(init, ids, args.layers, torch.float32, threads)
+        one()
     rates, used = [], 0.0
     for _ in range(args.steps):
-        dt, _, _ = oracle_train_sample(init, ids, args.layers, torch.float32, threads)
+        dt = one()
         rates.append(ids[:, 1:].numel() / dt)
         used += dt
         if used > budget_s:
             break
     value = statistics.median(rates)
-    sample = (f"oracle forward + series backward of the full-width model ({args.layers} layers), 4 x 256 tokens "
-              f"per step, float32, {len(rates)} of {args.steps} steps run")
+    what = ("the reference's PolyTensor (baseline/_ref) forward + backward on host tensors" if use_ref
+            else "oracle forward + series backward")
+    sample = (f"{what} of the full-width model ({args.layers} layers), 4 x 256 tokens per step, float32, "
+              f"{len(rates)} of {args.steps} steps run")
     return {
         "impl": "reference",
         "metric": "train tokens/s (configs[4]: 12-layer d768 PolyTensor transformer, degree 3, float32, "
@@ -1300,7 +1339,8 @@ def reference_arm_train(args, budget_s=150.0):
         "config": train_config(args.layers),
         "parallelism": "host CPU",
         "extrapolated_s_per_step": 64 * 1024 / value,
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference" if use_ref else "port",
+                         "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
