@@ -423,8 +423,8 @@ def run_norm_ce(args, rank, world, device):
         # 1024 of the 16384 rows (the full batch's softmax-series intermediates would not fit in host
         # memory); about 20 s on 16 host cores
         cpu_rows = 1024
-        rate, dt, desc = cpu_norm_ce_rate(cpu_rows, os.cpu_count() or 1)
-        cpu = {"value": rate, "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port", "sample": desc,
+        rate, dt, desc, kind = cpu_norm_ce_rate(cpu_rows, os.cpu_count() or 1)
+        cpu = {"value": rate, "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": kind, "sample": desc,
                "ms_per_step_extrapolated": dt * 1e3 * 16384 / cpu_rows}
     return {
         "cpu_baseline": cpu,
@@ -446,9 +446,11 @@ def run_norm_ce(args, rank, world, device):
 
 
 def cpu_norm_ce_rate(rows, threads):
-    """Reference algorithm (oracle restatement of the plain-range rules) for configs[2] on the host
-    CPU at `rows` rows: RMSNorm -> GELU -> linear(32000) -> CE forward and its series backward.
-    Returns (GB/s of the norm/CE algorithmic bytes scaled to the sample, seconds, description)."""
+    """The reference's own plain-range chain for configs[2] on the host CPU at `rows` rows (its
+    PolyTensor from baseline/_ref: F.rms_norm -> F.gelu -> F.linear(32000) -> F.cross_entropy, forward
+    and backward; without the package, the oracle restatement of those rules).  Returns (GB/s of
+    the norm/CE algorithmic bytes scaled to the sample, seconds, description, kind)."""
+    import torch.nn.functional as F
     from oracle import polyref
 
     torch.set_num_threads(threads)
@@ -458,33 +460,70 @@ def cpu_norm_ce_rate(rows, threads):
     W0 = [1 + 0.02 * torch.randn(H, generator=g)] + [torch.zeros(H) for _ in range(n)]
     Wl = [0.02 * torch.randn(V, H, generator=g)] + [torch.zeros(V, H) for _ in range(n)]
     target = torch.randint(0, V, (rows,), generator=g)
+    pt = _reference_package()
+    if pt is not None:
+        RP = pt.PolyTensor
 
-    def loss_fn(Xs, ws, wl):
-        h = polyref.gelu(polyref.rms_norm(Xs, (H,), ws))
-        logits = polyref.cauchy(h, [w.t() for w in wl], lambda a, b: a @ b)
-        return polyref.cross_entropy(logits, target)
+        def run(r):
+            x = RP(tuple(t[:r] for t in X), requires_grad=True)
+            ws, wl = RP(tuple(W0), requires_grad=True), RP(tuple(Wl), requires_grad=True)
+            with RP.plain_range(), RP.retain_wrappers():
+                F.cross_entropy(F.linear(F.gelu(F.rms_norm(x, (H,), ws)), wl), target[:r]).backward()
 
-    seed = [torch.tensor(1.0)] + [torch.tensor(0.0)] * n
+        run(8)   # untimed: the first call's one-time setup
+        kind, what = "reference", "the reference's PolyTensor chain"
+    else:
+        def loss_fn(Xs, ws, wl):
+            h = polyref.gelu(polyref.rms_norm(Xs, (H,), ws))
+            logits = polyref.cauchy(h, [w.t() for w in wl], lambda a, b: a @ b)
+            return polyref.cross_entropy(logits, target)
+
+        def run(r):
+            seed = [torch.tensor(1.0)] + [torch.tensor(0.0)] * n
+            polyref.series_vjp(loss_fn, [X, W0, Wl], seed)
+
+        kind, what = "port", "oracle restatement"
     t0 = time.perf_counter()
-    polyref.series_vjp(loss_fn, [X, W0, Wl], seed)
+    run(rows)
     dt = time.perf_counter() - t0
     P = n + 1
     nbytes = (2 + 3) * P * rows * H * 4 + 3 * P * rows * V * 4
-    return nbytes / dt / 1e9, dt, f"{rows} of 16384 rows, fwd + series backward, float32, {dt:.1f} s"
+    return nbytes / dt / 1e9, dt, f"{what}: {rows} of 16384 rows, fwd + backward, float32, {dt:.1f} s", kind
 
 
 def cpu_attention_rate(L, threads, D=128):
-    """Reference SDPA decomposition (oracle) on a (1, 4, L, D) head slice, causal, degree 3,
-    forward + series backward, float32.  Returns (coefficient TFLOP/s, description)."""
+    """The reference's SDPA on a (1, 4, L, D) head slice, causal, degree 3, forward + backward,
+    float32, in plain range (its PolyTensor from baseline/_ref, which evaluates its decomposition on
+    host tensors; without the package, the oracle restatement).  Returns (coefficient TFLOP/s,
+    description, kind)."""
+    import torch.nn.functional as F
     from oracle import polyref
 
     torch.set_num_threads(threads)
     n, shape = 3, (1, 4, L, D)
     Q, Kp, V, G = (make_series(shape, n, s, torch.float32) for s in (1, 2, 3, 4))
+    pt = _reference_package()
+    if pt is not None:
+        RP = pt.PolyTensor
+
+        def run(length):
+            q, k, v = (RP(tuple(t[:, :, :length] for t in X), requires_grad=True) for X in (Q, Kp, V))
+            with RP.plain_range(), RP.retain_wrappers():
+                F.scaled_dot_product_attention(q, k, v, is_causal=True).backward(
+                    RP(tuple(t[:, :, :length] for t in G)))
+
+        run(16)   # untimed: the first call's one-time setup
+        kind, what = "reference", "the reference's PolyTensor SDPA"
+    else:
+        def run(length):
+            polyref.series_vjp(lambda q, k, v: polyref.attention(q, k, v, is_causal=True), [Q, Kp, V], G)
+
+        kind, what = "port", "oracle restatement"
     t0 = time.perf_counter()
-    polyref.series_vjp(lambda q, k, v: polyref.attention(q, k, v, is_causal=True), [Q, Kp, V], G)
+    run(L)
     dt = time.perf_counter() - t0
-    return attention_flops(1, 4, L, D, n) / dt / 1e12, f"(1, 4, {L}, {D}) head slice, fwd + backward, {dt:.1f} s"
+    return (attention_flops(1, 4, L, D, n) / dt / 1e12,
+            f"{what}: (1, 4, {L}, {D}) head slice, fwd + backward, {dt:.1f} s", kind)
 
 
 def attention_flops(B, H, L, D, n):
@@ -562,8 +601,8 @@ def run_attention(args, rank, world, device):
     value = world * flops / (ms / 1e3) / 1e12
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, desc = cpu_attention_rate(min(L, 1024), os.cpu_count() or 1, D)
-        cpu = {"value": rate, "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": "port", "sample": desc}
+        rate, desc, kind = cpu_attention_rate(min(L, 1024), os.cpu_count() or 1, D)
+        cpu = {"value": rate, "unit": "TFLOP/s", "cores": os.cpu_count() or 1, "kind": kind, "sample": desc}
     return {
         "cpu_baseline": cpu,
         "metric": f"poly-attention coeff TFLOP/s (causal, ({B}, {H}, {L}, {D}), degree 3, {args.dtype}, fwd+bwd)",
@@ -812,11 +851,13 @@ def readme_fit_data(seed=0):
     return X, Y, Xp, Yp, batches
 
 
-def gpu_readme_fit(device, data, degree=5):
+def gpu_readme_fit(device, data, degree=5, poly_cls=None):
     """The README fit through this package's API on the GPU (plain range): 10 SGD steps of
-    loss = (signal + (1 - Z) noise) / 2; returns the coefficient planes of w and c."""
-    from polytensors_b200 import PolyTensor
+    loss = (signal + (1 - Z) noise) / 2; returns the coefficient planes of w and c.  With the
+    reference's PolyTensor class and a CPU device it is the reference's own fit on the host."""
+    from polytensors_b200 import PolyTensor as Ours
 
+    PolyTensor = poly_cls or Ours
     X, Y, Xp, Yp = (t.to(device) for t in data[:4])
     batches = [(i.to(device), j.to(device)) for i, j in data[4]]
     Z = PolyTensor((torch.tensor(0.0, device=device), 1.0), degree=degree)
@@ -884,6 +925,15 @@ def readme_fit_line(device, steps, warmup):
     t0 = time.perf_counter()
     w32, c32 = oracle_readme_fit(data, torch.float32)
     cpu_ms = (time.perf_counter() - t0) * 1e3
+    cpu_kind, cpu_what = "port", "the whole fit through the oracle, float32"
+    pt = _reference_package()
+    if pt is not None:
+        # the reference's own fit on host tensors (after an untimed first fit)
+        gpu_readme_fit(torch.device("cpu"), data, poly_cls=pt.PolyTensor)
+        t0 = time.perf_counter()
+        gpu_readme_fit(torch.device("cpu"), data, poly_cls=pt.PolyTensor)
+        cpu_ms = (time.perf_counter() - t0) * 1e3
+        cpu_kind, cpu_what = "reference", "the whole fit through the reference's PolyTensor on host tensors, float32"
     worst, ok = 0.0, True
     for got, r32, want in ((gw, w32, w64), (gc, c32, c64)):
         for a, b in zip(R.plane_errors([x.cpu() for x in got], want), R.plane_errors(r32, want)):
@@ -895,8 +945,8 @@ def readme_fit_line(device, steps, warmup):
             "parity": {"max_plane_err": worst, "within_tolerance": bool(ok),
                        "tol": "per plane: err <= max(1e-4, 3 x the float32 oracle's err)",
                        "against": "oracle restatement of the fit, float64, CPU"},
-            "cpu_baseline": {"value": cpu_ms, "unit": "ms", "cores": 1, "kind": "port",
-                             "sample": "the whole fit through the oracle, float32"}}
+            "cpu_baseline": {"value": cpu_ms, "unit": "ms", "cores": torch.get_num_threads(), "kind": cpu_kind,
+                             "sample": cpu_what}}
 
 
 def default_mode_line(device, steps, warmup, M=2048, n=4, sample_rows=1024):
