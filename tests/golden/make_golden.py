@@ -119,6 +119,31 @@ def case_cross_entropy():
         save("ce_none_f64_n4", X=X, target=target, G=G, CE=coeffs(per_row), dX=coeffs(x.grad))
 
 
+def case_cross_entropy_softcap_and_embedding():
+    """PolyTensor.cross_entropy with a softcap (the public API, src/polytensors/_tensor.py:255-269)
+    and reduction 'sum', and F.embedding with padding_idx, forward and backward in plain range,
+    degree 3."""
+    n = 3
+    X = series((6, 40), n, 140)
+    target = torch.randint(0, 40, (6,), generator=torch.Generator().manual_seed(141))
+    target[2] = -100
+    G = [t.reshape(()) for t in series((1,), n, 142)]
+    W = series((10, 4), n, 143)
+    idx = torch.tensor([[1, 0, 3], [0, 9, 1]])
+    GE = series((2, 3, 4), n, 144)
+    out = {}
+    with PolyTensor.plain_range(), PolyTensor.retain_wrappers():
+        x = PolyTensor(X, requires_grad=True)
+        loss = PolyTensor.cross_entropy(x, target, softcap=5.0, reduction="sum")
+        loss.backward(PolyTensor(G))
+        out["softcap_sum"], out["d_softcap_sum"] = coeffs(loss), coeffs(x.grad)
+        w = PolyTensor(W, requires_grad=True)
+        e = F.embedding(idx, w, padding_idx=0)
+        e.backward(PolyTensor(GE))
+        out["embedding"], out["d_embedding"] = coeffs(e), coeffs(w.grad)
+    save("ce_softcap_embedding_f64_n3", X=X, target=target, G=G, W=W, idx=idx, GE=GE, **out)
+
+
 def case_attention():
     n = 3
     shape = (1, 2, 9, 4)
@@ -353,6 +378,7 @@ if __name__ == "__main__":
     case_rmsnorm(torch.float32, "rmsnorm_f32_n3")
     case_gelu()
     case_cross_entropy()
+    case_cross_entropy_softcap_and_embedding()
     case_attention()
     case_series_ops()
     case_series_ops_complex()

@@ -168,3 +168,26 @@ def test_series_rules_and_backward_rules(golden):
     }
     for key, got in checks.items():
         assert_series_close(got, g[key], 1e-12)
+
+
+def test_softcap_cross_entropy_sum_and_embedding(golden):
+    """PolyTensor.cross_entropy with a softcap and reduction 'sum', and F.embedding with
+    padding_idx, forward and backward, against the reference's own plain-range run
+    (tests/golden/ce_softcap_embedding_f64_n3.pt)."""
+    g = golden("ce_softcap_embedding_f64_n3")
+    X, target, G, W, idx, GE = g["X"], g["target"], g["G"], g["W"], g["idx"], g["GE"]
+    cap = 5.0
+
+    def capped_loss(Xs):
+        capped = [cap * t for t in ref.activation([p / cap for p in Xs], "tanh")]
+        return ref.cross_entropy(capped, target, reduction="sum")
+
+    assert_series_close(capped_loss(X), g["softcap_sum"], 1e-12)
+    assert_series_close(ref.series_vjp(capped_loss, [X], G)[0], g["d_softcap_sum"], 1e-12)
+    assert_series_close([w[idx] for w in W], g["embedding"], 1e-12)
+    want = []
+    for ge in GE:
+        d = torch.zeros_like(W[0]).index_add_(0, idx.reshape(-1), ge.reshape(-1, W[0].shape[1]))
+        d[0] = 0.0   # padding_idx rows get no gradient
+        want.append(d)
+    assert_series_close(want, g["d_embedding"], 1e-12)
