@@ -264,3 +264,19 @@ def test_default_mode_hidden_copy_bookkeeping():
     x.coeffs[0].add_(1.0)
     assert _scaled.get(x) is None
     assert _scaled.get(views["t"][0]) is None
+
+
+def test_plain_range_block_count_survives_exceptions():
+    """The process-wide count of open plain_range() blocks (which decides plain-range arithmetic
+    inside backward on the autograd engine's threads) is restored when a block exits by an
+    exception, and nesting counts each block."""
+    from polytensors_b200 import PolyTensor, _state
+
+    before = _state._plain_open
+    with pytest.raises(ValueError):
+        with PolyTensor.plain_range():
+            with PolyTensor.plain_range():
+                assert _state._plain_open == before + 2
+            raise ValueError
+    assert _state._plain_open == before
+    assert not _state.plain_mode()
